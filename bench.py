@@ -1,0 +1,467 @@
+#!/usr/bin/env python3
+"""Benchmark of the charlotte_b200 hot path on B200.
+
+Headline (BASELINE.json metric "Q4_0/Q6_K GEMV HBM GB/s"): one step is one
+pass of the decode GEMVs of a Qwen3-0.6B token over seeded random-init
+weights (configs[1] at M = 1): 28 layers x [QKV 4096x1024, O 1024x2048,
+gate|up 2x3072x1024, down 1024x3072] in Q4_0 and the 151,936x1024 Q6_K
+head — 113 launches, 375.3 MB of weights a step (larger than the 126 MB L2,
+so every step streams from HBM). The step is captured once as a CUDA graph
+(PDL launches) and replayed. `value` = algorithmic bytes (weights + x + y)
+/ time. `e2e` runs the same GEMVs through the C ABI with host buffers:
+each step copies every x host->device and every y back inside the timed
+region.
+
+`--impl reference` times the reference path's CPU restatement (the oracle:
+the reference's order of operations over its dequantizers, all host
+threads) on a bounded sample of the same step.
+
+Multi-GPU: the GEMV set does not shard (replicas only): each rank runs its
+own replica, `value` is the sum over ranks, time the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from charlotte_b200 import synth  # noqa: E402
+
+Q4_0, Q6_K = 2, 14
+LAYERS, HIDDEN, FFN, VOCAB = 28, 1024, 3072, 151936
+QKV_ROWS, ATT = 4096, 2048
+SEED = 20261201
+
+
+def qwen3_gemv_set():
+    """(name, format, rows, K, members) of one decode token's products."""
+    layer = [("qkv", Q4_0, [2048, 1024, 1024], HIDDEN), ("o", Q4_0, [HIDDEN], ATT),
+             ("gate_up", Q4_0, [FFN, FFN], HIDDEN), ("down", Q4_0, [HIDDEN], FFN)]
+    out = []
+    for l in range(LAYERS):
+        for name, fmt, rows, K in layer:
+            out.append((f"{name}.{l}", fmt, rows, K))
+    out.append(("head", Q6_K, [VOCAB], HIDDEN))
+    return out
+
+
+def algorithmic_bytes(fmt, rows_list, K):
+    per_weight = 18 / 32 if fmt == Q4_0 else 210 / 256
+    rows = sum(rows_list)
+    out_rows = rows_list[0] if len(rows_list) == 2 else rows
+    return rows * K * per_weight + 4 * K + 4 * out_rows
+
+
+class Clocks:
+    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class GemvSet:
+    """Device weights, inputs and outputs of one decode token's products."""
+
+    def __init__(self, seed):
+        import torch
+        import charlotte_b200 as cb
+        self.cb = cb
+        rng = np.random.default_rng(seed)
+        self.items = []
+        self.bytes = 0.0
+        for name, fmt, rows, K in qwen3_gemv_set():
+            members = []
+            for r in rows:   # distinct weights for every layer and member
+                stored = synth.blocks(rng, fmt, r, K)
+                nb = stored.size // synth.BLOCK_BYTES[fmt]
+                members.append((torch.from_numpy(synth.to_piece(fmt, stored)).cuda(), nb, 0, r, 0))
+            kind = name.split(".")[0]
+            epi = {"qkv": cb.QKV, "gate_up": cb.GATED}.get(kind, cb.WRITE)
+            x = torch.from_numpy(synth.activations(rng, 1, K)).cuda()
+            if epi == cb.QKV:
+                outs = [torch.zeros((1, r), dtype=torch.float32, device="cuda") for r in rows]
+            else:
+                outs = [torch.zeros((1, rows[0]), dtype=torch.float32, device="cuda")]
+            self.items.append(dict(name=name, kind=kind, fmt=fmt, K=K, rows=rows, members=members, epi=epi, x=x,
+                                   outs=outs, bytes=algorithmic_bytes(fmt, rows, K)))
+            self.bytes += self.items[-1]["bytes"]
+
+    def launch(self, item, stream, pdl=True):
+        cb = self.cb
+        cb.matmul(item["fmt"], item["K"], item["members"], item["x"], item["outs"], epilogue=item["epi"],
+                  activation=cb.SILU, flags=cb.MATMUL_PDL if pdl else 0, stream=stream)
+
+    def step(self, stream, events=None):
+        for it in self.items:
+            if events is not None and it["kind"] in events:
+                ev = events[it["kind"]]
+                ev[0].append(self._event(stream))
+                self.launch(it, stream)
+                ev[1].append(self._event(stream))
+            else:
+                self.launch(it, stream)
+
+    @staticmethod
+    def _event(stream):
+        import torch
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    import charlotte_b200 as cb
+    cb.lib()
+    gs = GemvSet(SEED + rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    # warm-up (eager), then capture one step as a graph
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            gs.step(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        gs.step(stream)
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # Timed: K graph replays, CUDA events on the replay stream.
+    clocks = Clocks(torch.cuda.current_device() if world == 1 else local)
+    with clocks:
+        time.sleep(0.3)
+        barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream()
+        start.record(cur)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(cur)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_total = start.elapsed_time(end)
+        time.sleep(0.25)
+    ms_total = max_over_ranks(ms_total, world)
+    ms_per_step = ms_total / args.steps
+    value = gs.bytes * world / (ms_per_step * 1e-3) / 1e9
+
+    # Roofline of the dominant kernel: per-launch CUDA events around the Q4_0
+    # and Q6_K launches over a further timed pass (same stream, eager).
+    events = {"qkv": ([], []), "o": ([], []), "gate_up": ([], []), "down": ([], []), "head": ([], [])}
+    with torch.cuda.stream(stream):
+        for _ in range(20):
+            gs.step(stream, events)
+    torch.cuda.synchronize()
+    per_kind = {}
+    for kind, (s, e) in events.items():
+        ms = [a.elapsed_time(b) for a, b in zip(s, e)]
+        by = [it["bytes"] for it in gs.items if it["kind"] == kind]
+        per_kind[kind] = dict(launches=len(ms), ms=float(np.mean(ms)),
+                              gbs=float(np.mean(by)) / (float(np.mean(ms)) * 1e-3) / 1e9)
+    q4_ms = sum(per_kind[k]["ms"] * per_kind[k]["launches"] for k in ("qkv", "o", "gate_up", "down"))
+    q4_bytes = sum(it["bytes"] for it in gs.items if it["fmt"] == Q4_0) * 20
+    q4_launches = sum(per_kind[k]["launches"] for k in ("qkv", "o", "gate_up", "down"))
+    head = per_kind["head"]
+    share_q4 = q4_ms / (q4_ms + head["ms"] * head["launches"])
+    peaks = read_peaks()
+    dom = "decode_kernel<Q4_0>" if share_q4 >= 0.5 else "decode_kernel<Q6_K>"
+    if share_q4 >= 0.5:
+        achieved = (q4_bytes / q4_launches) / (q4_ms / q4_launches * 1e-3) / 1e9
+        per_launch_bytes = q4_bytes / q4_launches
+    else:
+        achieved = head["gbs"]
+        per_launch_bytes = gs.items[-1]["bytes"]
+    peak = peaks.get("hbm_gbs", 6650.0)
+
+    # e2e: the same products through the C ABI with host buffers.
+    e2e = None if args.no_e2e else run_e2e(gs, stream, max(args.steps // 20, 5), world)
+
+    result = {
+        "metric": "Q4_0/Q6_K GEMV HBM GB/s",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (Q4_0/Q6_K weights)",
+        "data": "synthetic: seeded random-init weights and N(0,1) activations",
+        "config": {"workload": "qwen3-0.6b decode-token GEMV set (configs[1], M=1): 28x[QKV,O,gate|up,down] Q4_0 + head Q6_K",
+                   "bytes_per_step": int(gs.bytes), "launches_per_step": len(gs.items),
+                   "l2": "inputs larger than L2 (375 MB weights a step vs 126 MB L2)",
+                   "parallelism": f"replicas x{world}", "graph": "CUDA graph of PDL launches"},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "bytes_per_launch": round(per_launch_bytes), "peak_source": "measured" if peaks else "fallback"},
+        "per_product": {k: {kk: round(vv, 4) for kk, vv in v.items()} for k, v in per_kind.items()},
+        "e2e": e2e,
+        "gpu_launches": len(gs.items) * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_e2e(gs, stream, steps, world):
+    """Every x host->device and every y device->host in the timed region,
+    pinned host buffers, one copy a buffer, through the same C ABI calls."""
+    import torch
+    hx = [it["x"].cpu().pin_memory() for it in gs.items]
+    hy = [[torch.empty_like(o, device="cpu").pin_memory() for o in it["outs"]] for it in gs.items]
+    h2d = sum(x.numel() * 4 for x in hx)
+    d2h = sum(o.numel() * 4 for ys in hy for o in ys)
+
+    def one():
+        with torch.cuda.stream(stream):
+            for it, x in zip(gs.items, hx):
+                it["x"].copy_(x, non_blocking=True)
+            gs.step(stream)
+            for it, ys in zip(gs.items, hy):
+                for o, y in zip(it["outs"], ys):
+                    y.copy_(o, non_blocking=True)
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        one()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    return {"value": round(gs.bytes * world / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4)}
+
+
+def read_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+def cpu_sample_items(fraction=1.0):
+    """A bounded sample of the step for the CPU: one layer's four products
+    and 1/16 of the head's rows, each cut to `fraction` of its rows."""
+    f = lambda r: max(32, int(r * fraction) // 32 * 32)
+    return [("qkv", Q4_0, [f(2048), f(1024), f(1024)], HIDDEN), ("o", Q4_0, [f(HIDDEN)], ATT),
+            ("gate_up", Q4_0, [f(FFN), f(FFN)], HIDDEN), ("down", Q4_0, [f(HIDDEN)], FFN),
+            ("head/16", Q6_K, [f(VOCAB // 16)], HIDDEN)]
+
+
+def cpu_baseline(seconds, repeat=None, fraction=1.0):
+    import oracle as O
+    rng = np.random.default_rng(SEED)
+    prepared = []
+    total_bytes = 0.0
+    for name, fmt, rows_list, K in cpu_sample_items(fraction):
+        for rows in rows_list:
+            stored = synth.blocks(rng, fmt, rows, K)
+            nb = stored.size // synth.BLOCK_BYTES[fmt]
+            prepared.append((fmt, O.to_piece(fmt, stored), nb, rows, K, synth.activations(rng, 1, K)))
+        total_bytes += algorithmic_bytes(fmt, rows_list, K)
+    threads = os.cpu_count() or 1
+    O.lib()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        for fmt, piece, nb, rows, K, x in prepared:
+            O.matmul(fmt, piece, nb, rows, K, x, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if (repeat is not None and n >= repeat) or (repeat is None and el >= seconds):
+            break
+    gbs = total_bytes * n / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "seconds": el,
+            "sample": f"{fraction:g} of one Qwen3 layer's 4 Q4_0 products + 1/16 of the Q6_K head "
+                      f"({total_bytes / 1e6:.2f} MB) x{n}, {el:.1f} s, oracle (reference order of operations), "
+                      f"{threads} threads"}
+
+
+def run_reference(args):
+    """The reference path's CPU restatement on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    # Size each step so that the whole run stays near a minute of CPU time:
+    # the full sample takes ~0.12 s on 8 cores.
+    probe = cpu_baseline(0, repeat=1)
+    fraction = min(1.0, max(1.0 / 64, 45.0 / (max(args.steps + args.warmup, 1) * max(probe["seconds"], 1e-3))))
+    for _ in range(args.warmup):
+        cpu_baseline(0, repeat=1, fraction=fraction)
+    t0 = time.perf_counter()
+    vals = [cpu_baseline(0, repeat=1, fraction=fraction) for _ in range(args.steps)]
+    el = time.perf_counter() - t0
+    value = float(np.median([v["value"] for v in vals]))
+    line = {
+        "impl": "reference",
+        "metric": "Q4_0/Q6_K GEMV HBM GB/s",
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(el / max(args.steps, 1) * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (Q4_0/Q6_K weights)",
+        "data": "synthetic: seeded random-init weights and N(0,1) activations",
+        "config": {"workload": "qwen3-0.6b decode-token GEMV set (configs[1], M=1): 28x[QKV,O,gate|up,down] Q4_0 + head Q6_K",
+                   "sample": "each step: one layer's 4 products + 1/16 of the head"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": vals[0]["sample"]},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_case(spec, iters):
+    """One product launched `iters` times (for profiling): spec is
+    format:rows:K[:epilogue], e.g. q4_0:1024:2048 or q6_k:151936:1024."""
+    import torch
+    import charlotte_b200 as cb
+    fmt_name, rows, K, *rest = spec.split(":")
+    fmt = {"q4_0": Q4_0, "q6_k": Q6_K, "q8_0": 8}[fmt_name]
+    rows, K = int(rows), int(K)
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(SEED)
+    stored = synth.blocks(rng, fmt, rows, K)
+    nb = stored.size // synth.BLOCK_BYTES[fmt]
+    piece = torch.from_numpy(synth.to_piece(fmt, stored)).cuda()
+    x = torch.from_numpy(synth.activations(rng, 1, K)).cuda()
+    y = torch.zeros((1, rows), dtype=torch.float32, device="cuda")
+    for _ in range(iters):
+        cb.matmul(fmt, K, [(piece, nb, 0, rows, 0)], x, [y])
+    torch.cuda.synchronize()
+    cb.check(cb.lib().cb_fault_check(None))
+    print(json.dumps({"case": spec, "iters": iters, "ok": True}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--case", default=None, help="profile one product: format:rows:K")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.case:
+        run_case(args.case, args.steps)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+"""charlotte_b200: a B200 (sm_100a) CUDA backend for the hot path of Charlotte
+(plainsight-systems/charlotte) — GGUF dequant-matmul, RMSNorm, QK-norm + RoPE
++ KV append, chunked attention, gather, top-k and the draw — behind a C ABI
+(include/charlotte_b200.h).
+
+This module is the host-side binding of that C ABI (ctypes over
+libcharlotte_b200.so), taking torch CUDA tensors for device memory and
+streams. There is no CPU path: every call runs the CUDA kernels, and loading
+fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libcharlotte_b200.so")
+
+F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
+WRITE, QKV, GATED, GATED_BY_INPUT = 0, 1, 2, 3
+SILU, GELU_TANH, SIGMOID = 0, 1, 2
+MATMUL_PDL, MATMUL_TENSOR = 1, 2
+OK, ERROR_BUILD, ERROR_STEP, ERROR_DEVICE_LOST, ERROR_CANCELLED, ERROR_INVALID = range(6)
+
+
+class CharlotteError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[status {status}] {message}")
+        self.status = status
+
+
+class Member(ctypes.Structure):
+    _fields_ = [("piece", ctypes.c_void_p), ("blocks", ctypes.c_uint32), ("first_row", ctypes.c_uint32),
+                ("rows", ctypes.c_uint32), ("out_offset", ctypes.c_uint32)]
+
+
+class Matmul(ctypes.Structure):
+    _fields_ = [("format", ctypes.c_uint32), ("columns", ctypes.c_uint32), ("members", ctypes.c_uint32),
+                ("epilogue", ctypes.c_uint32), ("activation", ctypes.c_uint32), ("member", Member * 3),
+                ("gate_input", ctypes.c_void_p), ("gate_input_stride", ctypes.c_uint32),
+                ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32)]
+
+
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C ABI library. Raises when it has not been built: there is
+    no fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m charlotte_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        L.cb_last_error.restype = ctypes.c_size_t
+        L.cb_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+        L.cb_version.restype = ctypes.c_char_p
+        L.cb_device_sm_count.restype = ctypes.c_int
+        L.cb_fault_check.restype = ctypes.c_int
+        L.cb_fault_check.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+        L.cb_matmul_run.restype = ctypes.c_int
+        L.cb_matmul_run.argtypes = [ctypes.POINTER(Matmul), ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                                    ctypes.POINTER(ctypes.c_void_p * 3), ctypes.POINTER(ctypes.c_uint32 * 3),
+                                    ctypes.c_uint32, ctypes.c_void_p]
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    lib().cb_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise CharlotteError(status, last_error())
+
+
+def _stream(stream) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, activation: int = SILU,
+           tokens: int | None = None, x_stride: int | None = None, out_stride=None, flags: int = 0,
+           gate_input=None, gate_input_stride: int = 0, gate_input_column: int = 0, gate_input_token: int = 0,
+           stream=None) -> None:
+    """Runs cb_matmul_run. `members`: list of (piece tensor (uint8, cuda), blocks,
+    first_row, rows, out_offset). `x`: f32 cuda tensor [tokens, x_stride].
+    `out`: list of up to 3 f32 cuda tensors."""
+    m = Matmul()
+    m.format = fmt
+    m.columns = columns
+    m.members = len(members)
+    m.epilogue = epilogue
+    m.activation = activation
+    for i, (piece, blocks, first_row, rows, out_offset) in enumerate(members):
+        m.member[i] = Member(piece.data_ptr(), blocks, first_row, rows, out_offset)
+    m.gate_input = _ptr(gate_input)
+    m.gate_input_stride = gate_input_stride
+    m.gate_input_column = gate_input_column
+    m.gate_input_token = gate_input_token
+    if tokens is None:
+        tokens = x.shape[0] if x.dim() > 1 else 1
+    if x_stride is None:
+        x_stride = x.shape[-1]
+    outs = (ctypes.c_void_p * 3)(*[_ptr(o) for o in (list(out) + [None, None, None])[:3]])
+    if out_stride is None:
+        out_stride = [o.shape[-1] if o is not None else 0 for o in (list(out) + [None, None, None])[:3]]
+    strides = (ctypes.c_uint32 * 3)(*out_stride)
+    check(lib().cb_matmul_run(ctypes.byref(m), x.data_ptr(), x_stride, tokens, ctypes.byref(outs),
+                              ctypes.byref(strides), flags, _stream(stream)))

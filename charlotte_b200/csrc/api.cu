@@ -1,0 +1,173 @@
+// C ABI entry points: argument checks, dispatch to the kernels, status codes.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "api_common.h"
+#include "charlotte_b200.h"
+#include "matmul.h"
+
+namespace cb {
+
+namespace {
+thread_local std::string g_error;
+// One word a device: set by a kernel whose bounded wait ran out.
+__device__ unsigned int g_fault_word;
+}
+
+int fail(int status, const char* format, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, format);
+    vsnprintf(buf, sizeof buf, format, ap);
+    va_end(ap);
+    g_error = buf;
+    return status;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+    // Errors that leave the context unusable (sticky) are the device lost.
+    const bool sticky = e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure ||
+                        e == cudaErrorIllegalInstruction || e == cudaErrorMisalignedAddress ||
+                        e == cudaErrorHardwareStackError || e == cudaErrorAssert ||
+                        e == cudaErrorDevicesUnavailable || e == cudaErrorECCUncorrectable;
+    return fail(sticky ? CB_ERROR_DEVICE_LOST : CB_ERROR_STEP, "%s: %s (%s)", what, cudaGetErrorString(e),
+                cudaGetErrorName(e));
+}
+
+int sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
+unsigned int* fault_word() {
+    static unsigned int* words[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!words[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_fault_word) != cudaSuccess) return nullptr;
+        words[dev] = static_cast<unsigned int*>(p);
+    }
+    return words[dev];
+}
+
+}  // namespace cb
+
+extern "C" {
+
+int cb_fault_check(unsigned int* faults) {
+    unsigned int* w = cb::fault_word();
+    if (!w) return cb::fail(CB_ERROR_STEP, "cb_fault_check: no CUDA device");
+    unsigned int h = 0;
+    cudaError_t e = cudaMemcpy(&h, w, sizeof h, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cb::fail_cuda(e, "cb_fault_check");
+    if (h) {
+        const unsigned int zero = 0;
+        e = cudaMemcpy(w, &zero, sizeof zero, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cb::fail_cuda(e, "cb_fault_check");
+    }
+    if (faults) *faults = h;
+    return h ? cb::fail(CB_ERROR_STEP, "a kernel's bounded wait ran out (fault word 0x%x)", h) : CB_OK;
+}
+
+
+size_t cb_last_error(char* buffer, size_t capacity) {
+    const std::string& e = cb::g_error;
+    if (buffer && capacity) {
+        const size_t n = e.size() < capacity - 1 ? e.size() : capacity - 1;
+        std::memcpy(buffer, e.data(), n);
+        buffer[n] = '\0';
+    }
+    return e.size();
+}
+
+const char* cb_version(void) { return "0.1.0"; }
+
+int cb_device_sm_count(void) {
+    const int n = cb::sm_count();
+    return n > 0 ? n : cb::fail(CB_ERROR_STEP, "no CUDA device");
+}
+
+int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_t tokens, float* const out[3],
+                  const uint32_t out_stride[3], uint32_t flags, void* stream) {
+    using namespace cb;
+    if (!m || !x || !out) return fail(CB_ERROR_INVALID, "cb_matmul_run: null argument");
+    if (m->format != CB_Q4_0 && m->format != CB_Q8_0 && m->format != CB_Q6_K)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: format %u has no matmul kernel", m->format);
+    if (m->columns == 0 || m->columns % 32 != 0)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: columns %u is not a whole number of 32-weight groups",
+                    m->columns);
+    if (m->format == CB_Q6_K && m->columns % 256 != 0)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: Q6_K rows of %u are not whole 256-weight super-blocks",
+                    m->columns);
+    if (m->members < 1 || m->members > 3) return fail(CB_ERROR_INVALID, "cb_matmul_run: %u members", m->members);
+    if (m->epilogue > CB_EPILOGUE_GATED_BY_INPUT)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: epilogue %u", m->epilogue);
+    if (m->activation > CB_ACT_SIGMOID) return fail(CB_ERROR_INVALID, "cb_matmul_run: activation %u", m->activation);
+    if (m->epilogue == CB_EPILOGUE_GATED && (m->members != 2 || m->member[0].rows != m->member[1].rows))
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: a gated product is a gate and an up of equal rows");
+    if (m->epilogue == CB_EPILOGUE_GATED_BY_INPUT && !m->gate_input)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: GATED_BY_INPUT without its input u");
+    if (flags & CB_MATMUL_TENSOR)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: the tensor-core form is not built in this library version");
+    if (tokens == 0) return CB_OK;
+    if (x_stride < m->columns) return fail(CB_ERROR_INVALID, "cb_matmul_run: x_stride %u < columns", x_stride);
+    MatmulArgs a{};
+    a.format = m->format;
+    a.columns = m->columns;
+    a.members = m->members;
+    a.epilogue = m->epilogue;
+    a.activation = m->activation;
+    a.token = m->gate_input_token;
+    a.tokens = tokens;
+    a.x = x;
+    a.x_stride = x_stride;
+    a.gate_input = m->gate_input;
+    a.gate_input_stride = m->gate_input_stride;
+    a.gate_input_column = m->gate_input_column;
+    a.fault = fault_word();
+    if (matmul_decode_smem_bytes(m->format, m->columns) > 220u * 1024u)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: rows of %u are wider than the decode form stages", m->columns);
+    uint32_t total = 0;
+    for (uint32_t i = 0; i < m->members; ++i) {
+        const cb_member& s = m->member[i];
+        if (!s.piece || !aligned16(s.piece))
+            return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u's piece is null or not 16-byte aligned", i);
+        if (s.rows == 0) return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u has no rows", i);
+        const uint64_t groups = static_cast<uint64_t>(s.first_row + s.rows) * (m->columns / 32);
+        const uint64_t needed_blocks = m->format == CB_Q6_K ? groups / 8 : groups;
+        if (needed_blocks > s.blocks)
+            return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u reads rows past its piece (%llu of %u blocks)", i,
+                        static_cast<unsigned long long>(needed_blocks), s.blocks);
+        a.member[i] = {static_cast<const uint8_t*>(s.piece), s.blocks, s.first_row, s.rows, s.out_offset};
+        total += s.rows;
+    }
+    a.total_rows = m->epilogue == CB_EPILOGUE_GATED ? m->member[0].rows : total;
+    const uint32_t outputs = m->epilogue == CB_EPILOGUE_QKV ? m->members : 1;
+    for (uint32_t i = 0; i < outputs; ++i) {
+        if (!out[i]) return fail(CB_ERROR_INVALID, "cb_matmul_run: output %u is null", i);
+        a.out[i] = out[i];
+        a.out_stride[i] = out_stride ? out_stride[i] : 0;
+        if (tokens > 1 && a.out_stride[i] == 0)
+            return fail(CB_ERROR_INVALID, "cb_matmul_run: output %u has no stride for %u tokens", i, tokens);
+    }
+    const int sms = sm_count();
+    if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
+    cudaError_t e = matmul_decode(a, sms, static_cast<cudaStream_t>(stream), (flags & CB_MATMUL_PDL) != 0);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_matmul_run: launch");
+    return CB_OK;
+}
+
+}  // extern "C"

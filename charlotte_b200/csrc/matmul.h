@@ -1,0 +1,51 @@
+// Arguments of the matrix-product kernels: the device form of the
+// reference's `Matmul` constants struct (plainsight-systems/charlotte,
+// src/core/kernels/matmul/matmul.wgsl:28-40: members[3] of {first word,
+// blocks, first output row, rows}) plus the bindings it reads and writes.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace cb {
+
+// What a product writes (matmul.h:594-599).
+enum Epilogue : uint32_t { kWrite = 0, kQKV = 1, kGated = 2, kGatedByInput = 3 };
+
+struct MemberArgs {
+    const uint8_t* piece;   // the member's piece, 16-byte aligned, in the device layout
+    uint32_t blocks;        // blocks in the piece (locates each stream)
+    uint32_t first_row;     // first weight row read (a GLU half's first row)
+    uint32_t rows;          // rows of the product this member gives
+    uint32_t out_offset;    // Write: first output column; QKV: 0
+};
+
+struct MatmulArgs {
+    uint32_t format;        // GGUF type: 2 Q4_0, 8 Q8_0, 14 Q6_K
+    uint32_t columns;       // K, a multiple of 32
+    uint32_t members;       // 1 to 3
+    uint32_t total_rows;    // the members' rows together
+    uint32_t epilogue;
+    uint32_t activation;    // Gated and GatedByInput: 0 SiLU, 1 GELU tanh, 2 sigmoid
+    uint32_t token;         // GatedByInput: the first token's row of u
+    uint32_t tokens;        // rows of x (grid y)
+    MemberArgs member[3];
+    const float* x;         // [tokens][x_stride]
+    uint32_t x_stride;
+    float* out[3];          // [tokens][out_stride[m]]
+    uint32_t out_stride[3];
+    const float* gate_input;
+    uint32_t gate_input_stride;
+    uint32_t gate_input_column;
+    unsigned int* fault;    // device word: a bounded wait that ran out sets a bit
+};
+
+// Decode form over `tokens` rows of x (each token its own grid row): the
+// reference's per-output order. PDL when `pdl`.
+cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
+
+// Shared memory the decode form needs at its smallest batch, for a width.
+size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns);
+
+}  // namespace cb

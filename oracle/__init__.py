@@ -1,0 +1,177 @@
+"""ctypes bindings for the CPU oracle (oracle.c) and for oracle/_ref, the
+reference's own CPU code compiled from its sources — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this package; the product (charlotte_b200) never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libcharlotte_ref.so")
+
+F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
+SILU, GELU_TANH, SIGMOID = 0, 1, 2
+BLOCK_BYTES = {F32: 4, F16: 2, Q4_0: 18, Q8_0: 34, Q6_K: 210}
+BLOCK_WEIGHTS = {F32: 1, F16: 1, Q4_0: 32, Q8_0: 32, Q6_K: 256}
+
+_lib = None
+_ref = None
+
+c_u8p = ctypes.POINTER(ctypes.c_uint8)
+c_f32p = ctypes.POINTER(ctypes.c_float)
+c_u16p = ctypes.POINTER(ctypes.c_uint16)
+c_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+
+def build() -> None:
+    """Compile liboracle.so (and oracle/_ref when the reference is present)."""
+    subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
+    if os.path.isdir(os.environ.get("CHARLOTTE_REFERENCE", "/root/reference")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref",
+                        "REF=" + os.environ.get("CHARLOTTE_REFERENCE", "/root/reference")], check=True)
+
+
+def ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.or_fp16_to_fp32.restype = ctypes.c_float
+        L.or_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.or_fp32_to_fp16_sat.restype = ctypes.c_uint16
+        L.or_fp32_to_fp16_sat.argtypes = [ctypes.c_float]
+        for name in ("or_exp_nonpositive", "or_exp2"):
+            getattr(L, name).restype = ctypes.c_float
+            getattr(L, name).argtypes = [ctypes.c_float]
+        L.or_activate.restype = ctypes.c_float
+        L.or_activate.argtypes = [ctypes.c_int, ctypes.c_float]
+        L.or_sincos.argtypes = [ctypes.c_float, c_f32p, c_f32p]
+        L.or_dequant_stored.argtypes = [ctypes.c_int, c_u8p, ctypes.c_size_t, c_f32p]
+        L.or_piece_bytes.restype = ctypes.c_size_t
+        L.or_piece_bytes.argtypes = [ctypes.c_int, ctypes.c_size_t]
+        L.or_to_piece.argtypes = [ctypes.c_int, c_u8p, ctypes.c_size_t, c_u8p]
+        L.or_unpack.argtypes = [ctypes.c_int, c_u8p, ctypes.c_uint32, ctypes.c_uint32, c_f32p]
+        L.or_matmul.argtypes = [ctypes.c_int, c_u8p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                ctypes.c_uint32, c_f32p, ctypes.c_uint32, c_f32p, ctypes.c_uint32, ctypes.c_int]
+        L.or_norm_row.argtypes = [c_f32p, c_f32p, c_f32p, c_f32p, ctypes.c_uint32, ctypes.c_float,
+                                  ctypes.c_int, c_f32p]
+        L.or_rope_turns.argtypes = [ctypes.c_double, ctypes.c_uint32, c_f32p]
+        L.or_topk64.argtypes = [c_f32p, ctypes.c_uint32, c_u32p]
+        L.or_philox4x32_10.argtypes = [c_u32p, c_u32p, c_u32p]
+        L.or_attention_row.argtypes = [c_f32p, ctypes.c_uint32, c_u16p, c_u16p, ctypes.c_uint32,
+                                       ctypes.c_uint32, ctypes.c_float, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_uint32, c_f32p]
+        _lib = L
+    return _lib
+
+
+def ref():
+    """The reference's own CPU code (oracle/_ref), or None where it was not built."""
+    global _ref
+    if _ref is None and os.path.exists(REF_PATH):
+        R = ctypes.CDLL(REF_PATH)
+        for name in ("ref_dequant_q4_0", "ref_dequant_q8_0", "ref_dequant_q6_k"):
+            getattr(R, name).restype = ctypes.c_int
+            getattr(R, name).argtypes = [c_u8p, ctypes.c_size_t, c_f32p]
+        R.ref_fp16_to_fp32.restype = ctypes.c_float
+        R.ref_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        R.ref_fp32_to_fp16_saturating.restype = ctypes.c_uint16
+        R.ref_fp32_to_fp16_saturating.argtypes = [ctypes.c_float]
+        R.ref_repack_q6_k.argtypes = [c_u8p, ctypes.c_size_t, c_u8p, c_u8p, c_u8p, c_u8p]
+        R.ref_philox.argtypes = [c_u32p, ctypes.c_uint32, ctypes.c_uint32, c_u32p]
+        _ref = R
+    return _ref
+
+
+# ---- numpy helpers ----------------------------------------------------------
+
+def dequant_stored(fmt: int, stored: np.ndarray) -> np.ndarray:
+    stored = np.ascontiguousarray(stored, dtype=np.uint8)
+    blocks = stored.size // BLOCK_BYTES[fmt]
+    out = np.empty(blocks * BLOCK_WEIGHTS[fmt], np.float32)
+    rc = lib().or_dequant_stored(fmt, ptr(stored, ctypes.c_uint8), blocks, ptr(out, ctypes.c_float))
+    assert rc == 0
+    return out
+
+
+def to_piece(fmt: int, stored: np.ndarray) -> np.ndarray:
+    stored = np.ascontiguousarray(stored, dtype=np.uint8)
+    blocks = stored.size // BLOCK_BYTES[fmt]
+    out = np.zeros(lib().or_piece_bytes(fmt, blocks), np.uint8)
+    assert lib().or_to_piece(fmt, ptr(stored, ctypes.c_uint8), blocks, ptr(out, ctypes.c_uint8)) == 0
+    return out
+
+
+def unpack(fmt: int, piece: np.ndarray, blocks: int, group: int) -> np.ndarray:
+    out = np.empty(32, np.float32)
+    assert lib().or_unpack(fmt, ptr(piece, ctypes.c_uint8), blocks, group, ptr(out, ctypes.c_float)) == 0
+    return out
+
+
+def matmul(fmt: int, piece: np.ndarray, blocks: int, rows: int, K: int, x: np.ndarray,
+           threads: int = 0) -> np.ndarray:
+    """y[t, o] in the reference's order; x is [tokens, K] float32."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K)
+    tokens = x.shape[0]
+    y = np.empty((tokens, rows), np.float32)
+    threads = threads or os.cpu_count() or 1
+    rc = lib().or_matmul(fmt, ptr(piece, ctypes.c_uint8), blocks, 0, rows, K, ptr(x, ctypes.c_float), tokens,
+                         ptr(y, ctypes.c_float), rows, threads)
+    assert rc == 0
+    return y
+
+
+def norm_row(hidden: np.ndarray, output, gain: np.ndarray, post_gain, epsilon: float, add: bool):
+    """Returns (new hidden, normed) for one row."""
+    h = np.array(hidden, np.float32, copy=True)
+    width = h.size
+    normed = np.empty(width, np.float32)
+    out = np.ascontiguousarray(output if output is not None else np.zeros(width), np.float32)
+    g = np.ascontiguousarray(gain, np.float32)
+    pg = np.ascontiguousarray(post_gain, np.float32) if post_gain is not None else None
+    lib().or_norm_row(ptr(h, ctypes.c_float), ptr(out, ctypes.c_float), ptr(g, ctypes.c_float),
+                      ptr(pg, ctypes.c_float) if pg is not None else None, width, epsilon, int(add),
+                      ptr(normed, ctypes.c_float))
+    return h, normed
+
+
+def rope_turns(base: float, head_dim: int) -> np.ndarray:
+    t = np.empty(head_dim // 2, np.float32)
+    lib().or_rope_turns(base, head_dim, ptr(t, ctypes.c_float))
+    return t
+
+
+def topk64(logits: np.ndarray) -> np.ndarray:
+    logits = np.ascontiguousarray(logits, np.float32)
+    out = np.empty(128, np.uint32)
+    lib().or_topk64(ptr(logits, ctypes.c_float), logits.size, ptr(out, ctypes.c_uint32))
+    return out
+
+
+def philox(counter, key) -> np.ndarray:
+    c = np.array(counter, np.uint32)
+    k = np.array(key, np.uint32)
+    out = np.empty(4, np.uint32)
+    lib().or_philox4x32_10(ptr(c, ctypes.c_uint32), ptr(k, ctypes.c_uint32), ptr(out, ctypes.c_uint32))
+    return out
+
+
+def attention_row(q, p, key_cache, value_cache, slots, window, scale_log2e, head_dim, query_heads, kv_heads):
+    q = np.ascontiguousarray(q, np.float32)
+    out = np.empty(query_heads * head_dim, np.float32)
+    lib().or_attention_row(ptr(q, ctypes.c_float), p, ptr(key_cache, ctypes.c_uint16),
+                           ptr(value_cache, ctypes.c_uint16), slots, window, scale_log2e, head_dim,
+                           query_heads, kv_heads, ptr(out, ctypes.c_float))
+    return out

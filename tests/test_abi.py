@@ -1,0 +1,56 @@
+"""The C ABI library loads and exports every function include/*.h declares
+(no GPU: nothing here launches a kernel)."""
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+import charlotte_b200 as cb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(header).read()
+        names.update(re.findall(r"CB_API\s+[\w\s\*]+?\b(cb_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_headers_declare_functions():
+    assert "cb_matmul_run" in declared_functions()
+
+
+def test_library_exports_every_declared_function():
+    out = subprocess.run(["nm", "-D", "--defined-only", cb.library_path()], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\sT\s(cb_\w+)$", out, re.M))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+
+
+def test_library_loads_and_names_itself():
+    L = cb.lib()
+    for name in declared_functions():
+        assert hasattr(L, name)
+    assert L.cb_version().decode().count(".") == 2
+
+
+def test_invalid_arguments_are_a_status_not_a_fault():
+    """Argument checks run before any device work: no GPU needed."""
+    import ctypes
+    m = cb.Matmul()
+    m.format = 3            # Q4_1: no kernel here
+    m.columns = 64
+    m.members = 1
+    outs = (ctypes.c_void_p * 3)(1, 0, 0)
+    st = (ctypes.c_uint32 * 3)(0, 0, 0)
+    rc = cb.lib().cb_matmul_run(ctypes.byref(m), 16, 64, 1, ctypes.byref(outs), ctypes.byref(st), 0, None)
+    assert rc == cb.ERROR_INVALID and "format 3" in cb.last_error()
+    m.format = cb.Q4_0
+    m.columns = 33
+    rc = cb.lib().cb_matmul_run(ctypes.byref(m), 16, 64, 1, ctypes.byref(outs), ctypes.byref(st), 0, None)
+    assert rc == cb.ERROR_INVALID and "32-weight" in cb.last_error()

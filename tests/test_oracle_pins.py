@@ -1,0 +1,158 @@
+"""Pins the CPU oracle before it is trusted: against the reference's own CPU
+code compiled from its sources (oracle/_ref: its tests/support dequantizers,
+f16 conversions, Philox, and its Q6_K repack), and against the known answers
+its tests state (tests/quant_q4_0_test.cpp, tests/sampler_test.cpp,
+tests/formats_q6_k_repack_test.cpp). No GPU."""
+import ctypes
+import struct
+
+import numpy as np
+import pytest
+
+import oracle as O
+from charlotte_b200 import synth
+
+REF = O.ref()
+needs_ref = pytest.mark.skipif(REF is None, reason="oracle/_ref not built (the reference sources are absent)")
+
+
+def _ref_dequant(fmt, stored):
+    out = np.empty(stored.size // O.BLOCK_BYTES[fmt] * O.BLOCK_WEIGHTS[fmt], np.float32)
+    fn = {O.Q4_0: REF.ref_dequant_q4_0, O.Q8_0: REF.ref_dequant_q8_0, O.Q6_K: REF.ref_dequant_q6_k}[fmt]
+    fn(O.ptr(stored, ctypes.c_uint8), stored.size, O.ptr(out, ctypes.c_float))
+    return out
+
+
+@needs_ref
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+@pytest.mark.parametrize("gen", ["random_bytes", "config"])
+def test_dequant_matches_reference_bit_for_bit(fmt, gen):
+    rng = np.random.default_rng(fmt * 7 + len(gen))
+    n = 257
+    stored = (synth.random_bytes_blocks(rng, fmt, n) if gen == "random_bytes"
+              else synth.blocks(rng, fmt, n * O.BLOCK_WEIGHTS[fmt] // 32, 32))
+    ours = O.dequant_stored(fmt, stored)
+    theirs = _ref_dequant(fmt, stored)
+    assert np.array_equal(ours, theirs)   # zeros compare by value, as format.h states
+
+
+@needs_ref
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+def test_unpack_from_device_layout_equals_reference_dequant(fmt):
+    rng = np.random.default_rng(100 + fmt)
+    n = 64
+    stored = synth.random_bytes_blocks(rng, fmt, n)
+    piece = O.to_piece(fmt, stored)
+    groups = n * O.BLOCK_WEIGHTS[fmt] // 32
+    got = np.concatenate([O.unpack(fmt, piece, n, g) for g in range(groups)])
+    assert np.array_equal(got, _ref_dequant(fmt, stored))
+
+
+@needs_ref
+def test_q6_k_repack_matches_reference_repack():
+    rng = np.random.default_rng(5)
+    n = 33
+    stored = synth.random_bytes_blocks(rng, O.Q6_K, n)
+    lo, hi, sc, d = (np.zeros(n * w, np.uint8) for w in (128, 64, 16, 2))
+    REF.ref_repack_q6_k(O.ptr(stored, ctypes.c_uint8), n, O.ptr(lo, ctypes.c_uint8), O.ptr(hi, ctypes.c_uint8),
+                        O.ptr(sc, ctypes.c_uint8), O.ptr(d, ctypes.c_uint8))
+    piece = O.to_piece(O.Q6_K, stored)
+    assert np.array_equal(piece[: 210 * n], np.concatenate([lo, hi, sc, d]))
+    assert np.array_equal(synth.to_piece(O.Q6_K, stored), piece)
+
+
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+def test_synth_device_layout_equals_oracle_layout(fmt):
+    rng = np.random.default_rng(9)
+    stored = synth.random_bytes_blocks(rng, fmt, 40)
+    assert np.array_equal(synth.to_piece(fmt, stored), O.to_piece(fmt, stored))
+
+
+@needs_ref
+def test_fp16_conversions_match_reference():
+    L = O.lib()
+    for h in range(1 << 16):
+        a, b = L.or_fp16_to_fp32(h), REF.ref_fp16_to_fp32(h)
+        assert (np.isnan(a) and np.isnan(b)) or np.float32(a).view(np.uint32) == np.float32(b).view(np.uint32)
+    rng = np.random.default_rng(3)
+    xs = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s
+                         for s in (1e-9, 1e-7, 1e-5, 1e-3, 1.0, 1e2, 6.5e4, 1e6)])
+    xs = np.concatenate([xs, np.float32([65504, 65519, 65520, 70000, -65520, 2.0 ** -24, 2.0 ** -25, 0.0, -0.0])])
+    for x in xs:
+        assert L.or_fp32_to_fp16_sat(float(x)) == REF.ref_fp32_to_fp16_saturating(float(x))
+
+
+def test_q4_0_known_answers():
+    """tests/quant_q4_0_test.cpp: scale 1 gives nibble - 8; nibble 8 is zero;
+    element 16 is the high nibble of byte 0; scale applies per block."""
+    def block(scale_bits, nibbles):
+        qs = bytes((nibbles[j] & 0xF) | ((nibbles[j + 16] & 0xF) << 4) for j in range(16))
+        return np.frombuffer(struct.pack("<H", scale_bits) + qs, np.uint8)
+    out = O.dequant_stored(O.Q4_0, block(0x3C00, [i % 16 for i in range(32)]))
+    assert out.tolist() == [float(i % 16 - 8) for i in range(32)]
+    assert not O.dequant_stored(O.Q4_0, block(0x4900, [8] * 32)).any()
+    n = [8] * 32
+    n[16] = 15
+    out = O.dequant_stored(O.Q4_0, block(0x3C00, n))
+    assert out[16] == 7.0 and out[0] == 0.0 and out[1] == 0.0 and out[8] == 0.0
+    two = np.concatenate([block(0x3C00, [9] * 32), block(0x4000, [9] * 32)])
+    out = O.dequant_stored(O.Q4_0, two)
+    assert out[0] == 1.0 and out[32] == 2.0
+
+
+def test_fp16_classes():
+    """tests/quant_q4_0_test.cpp:41-65."""
+    f = O.lib().or_fp16_to_fp32
+    assert f(0x0000) == 0.0 and np.signbit(np.float32(f(0x8000)))
+    assert f(0x3C00) == 1.0 and f(0xBC00) == -1.0 and f(0x7BFF) == 65504.0
+    assert f(0x0001) == 2.0 ** -24 and f(0x0002) == 2.0 ** -23
+    assert np.isinf(f(0x7C00)) and np.isnan(f(0x7E00))
+
+
+def test_philox_random123_known_answers():
+    """tests/sampler_test.cpp:15-31 (Random123's published vectors)."""
+    cases = [
+        ([0, 0, 0, 0], [0, 0], [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]),
+        ([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2, [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]),
+        ([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0],
+         [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]),
+    ]
+    for counter, key, want in cases:
+        assert O.philox(counter, key).tolist() == want
+
+
+def test_q6_k_repack_known_placement():
+    """tests/formats_q6_k_repack_test.cpp:40-67: every weight's six bits where
+    q6_k.h says, from where ggml's block_q6_K stores them."""
+    rng = np.random.default_rng(11)
+    st = synth.random_bytes_blocks(rng, O.Q6_K, 3).reshape(3, 210)
+    piece = O.to_piece(O.Q6_K, st.reshape(-1))
+    n = 3
+    for b in range(n):
+        lo = piece[128 * b: 128 * b + 128]
+        hi = piece[128 * n + 64 * b: 128 * n + 64 * b + 64]
+        for k in range(8):
+            h, r = divmod(k, 4)
+            for l in range(32):
+                stored = ((st[b, 64 * h + 32 * (r % 2) + l] >> (4 * (r // 2))) & 0xF) | \
+                         (((st[b, 128 + 32 * h + l] >> (2 * r)) & 3) << 4)
+                rep = ((lo[16 * k + l % 16] >> (4 * (l // 16))) & 0xF) | (((hi[8 * k + l % 8] >> (2 * (l // 8))) & 3) << 4)
+                assert stored == rep
+        assert np.array_equal(piece[192 * n + 16 * b: 192 * n + 16 * b + 16], st[b, 192:208])
+        assert np.array_equal(piece[208 * n + 2 * b: 208 * n + 2 * b + 2], st[b, 208:210])
+
+
+def test_matmul_order_against_f64_bound():
+    """matmul.h:'Accuracy': each output within gamma(2K)*sum|w x| of the f64 sum."""
+    rng = np.random.default_rng(21)
+    rows, K = 96, 3072
+    st = synth.blocks(rng, O.Q4_0, rows, K)
+    piece = O.to_piece(O.Q4_0, st)
+    x = rng.standard_normal((2, K)).astype(np.float32)
+    y = O.matmul(O.Q4_0, piece, rows * K // 32, rows, K, x)
+    W = O.dequant_stored(O.Q4_0, st).reshape(rows, K).astype(np.float64)
+    exact = x.astype(np.float64) @ W.T
+    u = 2.0 ** -24
+    gamma = 2 * K * u / (1 - 2 * K * u)
+    bound = gamma * (np.abs(x.astype(np.float64)) @ np.abs(W).T)
+    assert np.all(np.abs(y - exact) <= bound)
