@@ -41,6 +41,48 @@ class Matmul(ctypes.Structure):
                 ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32)]
 
 
+class Norm(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_void_p), ("output", ctypes.c_void_p), ("gain", ctypes.c_void_p),
+                ("post_gain", ctypes.c_void_p), ("normed", ctypes.c_void_p), ("width", ctypes.c_uint32),
+                ("tokens", ctypes.c_uint32), ("add", ctypes.c_uint32), ("last_token", ctypes.c_uint32),
+                ("epsilon", ctypes.c_float)]
+
+
+class Rope(ctypes.Structure):
+    _fields_ = [("query", ctypes.c_void_p), ("key", ctypes.c_void_p), ("value", ctypes.c_void_p),
+                ("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p), ("query_gain", ctypes.c_void_p),
+                ("key_gain", ctypes.c_void_p), ("factors", ctypes.c_void_p), ("turns", ctypes.c_void_p),
+                ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
+                ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
+                ("halves", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("epsilon", ctypes.c_float)]
+
+
+class Attention(ctypes.Structure):
+    _fields_ = [("query", ctypes.c_void_p), ("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
+                ("out", ctypes.c_void_p), ("partials", ctypes.c_void_p), ("stats", ctypes.c_void_p),
+                ("tickets", ctypes.c_void_p), ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32),
+                ("tokens", ctypes.c_uint32), ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32),
+                ("kv_heads", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("window", ctypes.c_uint32),
+                ("max_chunks", ctypes.c_uint32), ("scale_log2e", ctypes.c_float)]
+
+
+class Gather(ctypes.Structure):
+    _fields_ = [("piece", ctypes.c_void_p), ("format", ctypes.c_uint32), ("blocks", ctypes.c_uint32),
+                ("width", ctypes.c_uint32), ("first_row", ctypes.c_uint32), ("row_count", ctypes.c_uint32),
+                ("ids", ctypes.c_void_p), ("sampled", ctypes.c_void_p), ("fed", ctypes.c_uint32),
+                ("tokens", ctypes.c_uint32), ("scale", ctypes.c_float), ("hidden", ctypes.c_void_p)]
+
+
+class Select(ctypes.Structure):
+    _fields_ = [("logits", ctypes.c_void_p), ("count", ctypes.c_uint32), ("partials", ctypes.c_void_p),
+                ("ticket", ctypes.c_void_p), ("candidates", ctypes.c_void_p), ("sampled", ctypes.c_void_p),
+                ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
+                ("seed0", ctypes.c_uint32), ("seed1", ctypes.c_uint32), ("top_k", ctypes.c_uint32),
+                ("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("min_p", ctypes.c_float),
+                ("log_min_p", ctypes.c_float)]
+
+
+RUN_PDL = 1
 _lib = None
 
 
@@ -66,6 +108,16 @@ def lib() -> ctypes.CDLL:
         L.cb_matmul_run.argtypes = [ctypes.POINTER(Matmul), ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                     ctypes.POINTER(ctypes.c_void_p * 3), ctypes.POINTER(ctypes.c_uint32 * 3),
                                     ctypes.c_uint32, ctypes.c_void_p]
+        for name, struct in (("cb_norm_run", Norm), ("cb_rope_run", Rope), ("cb_attention_run", Attention),
+                             ("cb_gather_run", Gather), ("cb_select_run", Select)):
+            fn = getattr(L, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [ctypes.POINTER(struct), ctypes.c_uint32, ctypes.c_void_p]
+        L.cb_rope_turns.argtypes = [ctypes.c_double, ctypes.c_uint32, ctypes.POINTER(ctypes.c_float)]
+        L.cb_attention_tickets.restype = ctypes.c_uint32
+        L.cb_attention_tickets.argtypes = [ctypes.c_uint32] * 3
+        L.cb_select_tiles.restype = ctypes.c_uint32
+        L.cb_select_tiles.argtypes = [ctypes.c_uint32]
         _lib = L
     return _lib
 
@@ -120,3 +172,24 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
     strides = (ctypes.c_uint32 * 3)(*out_stride)
     check(lib().cb_matmul_run(ctypes.byref(m), x.data_ptr(), x_stride, tokens, ctypes.byref(outs),
                               ctypes.byref(strides), flags, _stream(stream)))
+
+
+def run(kind: str, **fields) -> None:
+    """Runs one kernel entry point: kind in norm, rope, attention, gather,
+    select; fields are the C struct's (tensors become device pointers)."""
+    struct = {"norm": Norm, "rope": Rope, "attention": Attention, "gather": Gather, "select": Select}[kind]
+    stream = fields.pop("stream", None)
+    flags = fields.pop("flags", 0)
+    v = struct()
+    for name, value in fields.items():
+        if hasattr(value, "data_ptr"):
+            value = value.data_ptr()
+        setattr(v, name, value)
+    check(getattr(lib(), f"cb_{kind}_run")(ctypes.byref(v), flags, _stream(stream)))
+
+
+def rope_turns(base: float, head_dim: int):
+    import numpy as np
+    t = np.empty(head_dim // 2, np.float32)
+    lib().cb_rope_turns(base, head_dim, t.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return t

@@ -1,0 +1,100 @@
+// C ABI entry points of the norm, rope, attention, gather and select
+// kernels: argument checks (the reference launchers' preconditions), then
+// the launch. A bad argument is CB_ERROR_INVALID before anything runs.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "api_common.h"
+#include "charlotte_b200.h"
+#include "formats.cuh"
+#include "kernels.h"
+
+using namespace cb;
+
+namespace {
+
+int launched(cudaError_t e, const char* what) { return e == cudaSuccess ? CB_OK : fail_cuda(e, what); }
+
+bool head_dim_ok(uint32_t d) { return d == 64 || d == 128 || d == 256; }
+
+}  // namespace
+
+extern "C" {
+
+int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream) {
+    if (!n || !n->hidden || !n->gain || !n->normed) return fail(CB_ERROR_INVALID, "cb_norm_run: null argument");
+    if (n->width == 0 || n->width % 4 != 0 || n->width > 4096)
+        return fail(CB_ERROR_INVALID, "cb_norm_run: width %u is not a multiple of 4 up to 4096", n->width);
+    if (n->add && !n->output) return fail(CB_ERROR_INVALID, "cb_norm_run: add without the block's output");
+    if (n->post_gain && !n->add) return fail(CB_ERROR_INVALID, "cb_norm_run: a post-norm needs the add");
+    if (n->tokens == 0) return CB_OK;
+    return launched(norm_run(*n, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_norm_run");
+}
+
+void cb_rope_turns(double base, uint32_t head_dim, float* turns) {
+    for (uint32_t k = 0; k < head_dim / 2; ++k) {
+        const double theta = std::pow(base, -2.0 * k / head_dim);
+        turns[k] = static_cast<float>(theta / (2 * 3.14159265358979323846));
+    }
+}
+
+int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream) {
+    if (!r || !r->query || !r->key || !r->value || !r->key_cache || !r->value_cache || !r->turns)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: null argument");
+    if (!head_dim_ok(r->head_dim)) return fail(CB_ERROR_INVALID, "cb_rope_run: head dimension %u", r->head_dim);
+    if (r->kv_heads == 0 || r->query_heads % r->kv_heads != 0)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: %u query heads over %u kv heads", r->query_heads, r->kv_heads);
+    if ((r->query_heads + 2 * r->kv_heads) * (r->head_dim / 8) % 32 != 0)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: (Hq + 2 Hkv) * d / 8 is not a multiple of 32");
+    if ((r->query_heads + 2 * r->kv_heads) * (r->head_dim / 8) > 1024)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: more than 1024 lanes a token");
+    if ((r->query_gain == nullptr) != (r->key_gain == nullptr))
+        return fail(CB_ERROR_INVALID, "cb_rope_run: QK-norm on queries or keys alone");
+    if (r->slots == 0) return fail(CB_ERROR_INVALID, "cb_rope_run: no cache slots");
+    if (r->tokens == 0) return CB_OK;
+    return launched(rope_run(*r, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_rope_run");
+}
+
+uint32_t cb_attention_tickets(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads) {
+    if (kv_heads == 0) return 0;
+    return attention_row_tiles(tokens, query_heads, kv_heads) * kv_heads;
+}
+
+int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
+    if (!a || !a->query || !a->key_cache || !a->value_cache || !a->out || !a->partials || !a->stats || !a->tickets)
+        return fail(CB_ERROR_INVALID, "cb_attention_run: null argument");
+    if (!head_dim_ok(a->head_dim)) return fail(CB_ERROR_INVALID, "cb_attention_run: head dimension %u", a->head_dim);
+    if (a->kv_heads == 0 || a->query_heads % a->kv_heads != 0 || a->query_heads / a->kv_heads > 16)
+        return fail(CB_ERROR_INVALID, "cb_attention_run: %u query heads over %u kv heads", a->query_heads,
+                    a->kv_heads);
+    if (a->slots == 0 || a->window == 0) return fail(CB_ERROR_INVALID, "cb_attention_run: no slots or no window");
+    if (!a->position && static_cast<uint64_t>(a->position0) + a->tokens > static_cast<uint64_t>(a->max_chunks) * 64)
+        return fail(CB_ERROR_INVALID, "cb_attention_run: positions past max_chunks");
+    if (a->tokens == 0) return CB_OK;
+    return launched(attention_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_attention_run");
+}
+
+int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream) {
+    if (!g || !g->piece || !g->hidden || (!g->fed && !g->ids) || (g->fed && !g->sampled))
+        return fail(CB_ERROR_INVALID, "cb_gather_run: null argument");
+    if (g->format != CB_Q4_0 && g->format != CB_Q8_0 && g->format != CB_Q6_K)
+        return fail(CB_ERROR_INVALID, "cb_gather_run: format %u", g->format);
+    if (g->width == 0 || g->width % (g->format == CB_Q6_K ? 256 : 32) != 0)
+        return fail(CB_ERROR_INVALID, "cb_gather_run: width %u is not whole blocks", g->width);
+    if (g->fed && g->tokens != 1) return fail(CB_ERROR_INVALID, "cb_gather_run: a fed step has one token");
+    if (g->tokens == 0) return CB_OK;
+    return launched(gather_run(*g, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_gather_run");
+}
+
+uint32_t cb_select_tiles(uint32_t count) { return select_tiles(count); }
+
+int cb_select_run(const cb_select* s, uint32_t flags, void* stream) {
+    if (!s || !s->logits || !s->partials || !s->ticket || !s->candidates || !s->sampled)
+        return fail(CB_ERROR_INVALID, "cb_select_run: null argument");
+    if (s->count == 0 || s->count > 262144)
+        return fail(CB_ERROR_INVALID, "cb_select_run: %u entries (1 to 262,144)", s->count);
+    return launched(select_run(*s, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_select_run");
+}
+
+}  // extern "C"

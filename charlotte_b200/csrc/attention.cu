@@ -1,0 +1,265 @@
+// Attention over the f16 KV cache (plainsight-systems/charlotte,
+// src/core/kernels/attention/attention.wgsl main :138-360, combine :363-392;
+// launcher attention.h:304-320, attention.cpp:27-86).
+//
+// The reference's arithmetic, per query row at position p and query head h
+// (kv head h / G): keys live for p are earliest..p (earliest = p+1-W when
+// p+1 > W, else 0). Keys are taken in 64-key chunks fixed by position
+// (key_chunks, interface.h:243); within a chunk, in tiles of B = 2048/d keys
+// aligned to B, an online softmax in log2 units: the tile's top over its
+// live scores, a = 2^(old−top) (1 when equal), e_b = 2^(s_b − top), the
+// sum in key order, l = fma(l, a, sum), and O = O·a then O = fma(p_b, v_b, O)
+// in key order. s = Σ_w dot(q_w·scale·log2e, k_w) in quads, in order. The
+// chunks' (O, m, l) are folded in chunk order with fold_factors/fold_sum/fold
+// (:101-127), then O / l. Keys and chunks that are not live contribute
+// exactly nothing (a zero weight's product added to a sum that is never −0),
+// so they are skipped.
+//
+// B200 mapping: one CTA a (kv head, chunk, tile of rows): the chunk's 64
+// keys and values staged in shared memory once for all its G·rows queries;
+// a thread a (query, key) score; a thread a query for the sequential softmax
+// steps; threads over (query, dimension) for P·V. Every CTA writes its
+// chunk's partial state; the last CTA of a (row tile, kv head) to finish —
+// found by an atomic ticket, no waiting — folds the chunks in order and
+// resets the ticket. So a decode step is one launch, split over every chunk
+// (flash-decoding), and a prefill step the same launch with more row tiles.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "numerics.cuh"
+#include "tma.cuh"
+
+namespace cb {
+
+namespace {
+
+constexpr uint32_t kChunk = 64;
+constexpr uint32_t kAttnThreads = 128;
+constexpr uint32_t kMaxQueries = 16;   // queries (rows × G) a CTA works
+
+struct Geometry {
+    uint32_t rows_per_tile;   // query rows a CTA takes
+    uint32_t G;               // query heads a kv head
+};
+
+__host__ __device__ inline Geometry geometry_of(uint32_t query_heads, uint32_t kv_heads) {
+    Geometry g;
+    g.G = query_heads / kv_heads;
+    g.rows_per_tile = kMaxQueries / g.G > 0 ? kMaxQueries / g.G : 1;
+    return g;
+}
+
+__host__ __device__ inline size_t attention_smem(uint32_t d, uint32_t queries) {
+    return 2ull * kChunk * d * 2u            // K and V, f16
+           + static_cast<size_t>(queries) * d * 4u   // q·scale·log2e
+           + static_cast<size_t>(queries) * kChunk * 4u   // scores, then weights
+           + static_cast<size_t>(queries) * 8u * 4u       // a tile's alpha (≤ 8 tiles)
+           + static_cast<size_t>(queries) * 4u * 4u;      // m, l, live, spare
+}
+
+__device__ __forceinline__ uint32_t earliest_of(uint32_t p, uint32_t window) {
+    return p + 1u > window ? p + 1u - window : 0u;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    grid_dependency_wait();
+    const uint32_t d = a.head_dim;
+    const uint32_t B = 2048u / d;
+    const uint32_t tiles = kChunk / B;
+    const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
+    const uint32_t G = geo.G;
+    const uint32_t kvh = blockIdx.x;
+    const uint32_t c = blockIdx.y;
+    const uint32_t rt = blockIdx.z;
+    const uint32_t pos0 = a.position ? *a.position : a.position0;
+    const uint32_t row0 = rt * geo.rows_per_tile;
+    const uint32_t rows = min(geo.rows_per_tile, a.tokens - row0);
+    const uint32_t Q = rows * G;
+    const uint32_t key0 = c * kChunk;
+
+    uint16_t* ks = reinterpret_cast<uint16_t*>(smem);
+    uint16_t* vs = ks + kChunk * d;
+    float* qs = reinterpret_cast<float*>(vs + kChunk * d);
+    float* ps = qs + kMaxQueries * d;                 // [Q][64]
+    float* alpha = ps + kMaxQueries * kChunk;         // [Q][8]
+    float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l, live
+
+    // Does any of the tile's rows have a live key in this chunk?
+    const uint32_t p_first = pos0 + row0, p_last = pos0 + row0 + rows - 1u;
+    const bool any = key0 <= p_last && key0 + kChunk > earliest_of(p_first, a.window);
+    if (any) {
+        // Stage the chunk's keys and values (keys past p_last are never live).
+        const uint32_t words = d / 8u;   // uint4 per key row
+        for (uint32_t i = threadIdx.x; i < kChunk * words; i += kAttnThreads) {
+            const uint32_t b = i / words, w = i % words;
+            const uint32_t j = key0 + b;
+            uint4 kv = make_uint4(0, 0, 0, 0), vv = kv;
+            if (j <= p_last) {
+                const size_t at = (static_cast<size_t>(j % a.slots) * a.kv_heads + kvh) * d;
+                kv = reinterpret_cast<const uint4*>(a.key_cache + at)[w];
+                vv = reinterpret_cast<const uint4*>(a.value_cache + at)[w];
+            }
+            reinterpret_cast<uint4*>(ks + b * d)[w] = kv;
+            reinterpret_cast<uint4*>(vs + b * d)[w] = vv;
+        }
+        // Queries m = r·G + g: row r, head kvh·G + g, scaled into log2 units.
+        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+            const uint32_t m = i / d, e = i % d;
+            const uint32_t r = m / G, h = kvh * G + m % G;
+            qs[m * d + e] = a.query[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] * a.scale_log2e;
+        }
+        __syncthreads();
+        // Scores: s = Σ_w dot(q_w, k_w) in quads, in order.
+        for (uint32_t i = threadIdx.x; i < Q * kChunk; i += kAttnThreads) {
+            const uint32_t m = i / kChunk, b = i % kChunk;
+            const uint32_t p = pos0 + row0 + m / G;
+            const uint32_t j = key0 + b;
+            float s = 0.0f;
+            if (j <= p && j >= earliest_of(p, a.window)) {
+                const float4* q4 = reinterpret_cast<const float4*>(qs + m * d);
+                const uint2* k4 = reinterpret_cast<const uint2*>(ks + b * d);
+                for (uint32_t w = 0; w < d / 4u; ++w) {
+                    const uint2 kw = k4[w];
+                    const float4 kk = make_float4(fp16_bits_to_f32(kw.x & 0xFFFF), fp16_bits_to_f32(kw.x >> 16),
+                                                  fp16_bits_to_f32(kw.y & 0xFFFF), fp16_bits_to_f32(kw.y >> 16));
+                    s = s + dot4(q4[w], kk);
+                }
+            }
+            ps[m * kChunk + b] = s;
+        }
+        __syncthreads();
+        // The online softmax, a thread a query, tile by tile in key order.
+        for (uint32_t m = threadIdx.x; m < Q; m += kAttnThreads) {
+            const uint32_t p = pos0 + row0 + m / G;
+            const uint32_t early = earliest_of(p, a.window);
+            bool chunk_live = false;
+            float chunk_m = 0.0f, chunk_l = 0.0f;
+            for (uint32_t t = 0; t < tiles; ++t) {
+                float top_tile = 0.0f;
+                bool seen = false;
+                for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
+                    const uint32_t j = key0 + b;
+                    if (j <= p && j >= early) {
+                        const float s = ps[m * kChunk + b];
+                        top_tile = seen ? fmaxf(top_tile, s) : s;
+                        seen = true;
+                    }
+                }
+                float al = 1.0f;
+                if (seen) {
+                    const float old = chunk_live ? chunk_m : top_tile;
+                    chunk_live = true;
+                    const float top = fmaxf(old, top_tile);
+                    al = old == top ? 1.0f : exp2_np(old - top);
+                    float sum = 0.0f;
+                    for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
+                        const uint32_t j = key0 + b;
+                        float e = 0.0f;
+                        if (j <= p && j >= early) e = exp2_np(ps[m * kChunk + b] - top);
+                        ps[m * kChunk + b] = e;
+                        sum = sum + e;
+                    }
+                    chunk_l = fmaf(chunk_l, al, sum);
+                    chunk_m = top;
+                } else {
+                    for (uint32_t b = t * B; b < (t + 1u) * B; ++b) ps[m * kChunk + b] = 0.0f;
+                }
+                alpha[m * 8u + t] = al;
+            }
+            stat[m * 4u + 0] = chunk_m;
+            stat[m * 4u + 1] = chunk_live ? chunk_l : 0.0f;
+        }
+        __syncthreads();
+        // O = O·a_t, then fma(p_b, v_b, O) in key order; the chunk's partial.
+        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+            const uint32_t m = i / d, e = i % d;
+            float o = 0.0f;
+            for (uint32_t t = 0; t < tiles; ++t) {
+                o = o * alpha[m * 8u + t];
+                for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
+                    const float pb = ps[m * kChunk + b];
+                    if (pb != 0.0f) o = fmaf(pb, fp16_bits_to_f32(vs[b * d + e]), o);
+                }
+            }
+            const uint32_t r = m / G, h = kvh * G + m % G;
+            const size_t at = (static_cast<size_t>(c) * a.tokens + row0 + r) * a.query_heads + h;
+            a.partials[at * d + e] = o;
+            if (e == 0) {
+                a.stats[at * 2u] = stat[m * 4u];
+                a.stats[at * 2u + 1u] = stat[m * 4u + 1u];
+            }
+        }
+    }
+    grid_dependents_launch();
+
+    // The last CTA of this (row tile, kv head) folds the chunks in order.
+    __shared__ unsigned int last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int* ticket = a.tickets + rt * a.kv_heads + kvh;
+        const unsigned int seen = atomicAdd(ticket, 1u);
+        last = seen == gridDim.y - 1u;
+        if (last) *ticket = 0u;   // ready for the next step
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+        const uint32_t m = i / d, e = i % d;
+        const uint32_t r = m / G, h = kvh * G + m % G;
+        const uint32_t p = pos0 + row0 + r;
+        bool live = false;
+        float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
+        for (uint32_t cc = earliest_of(p, a.window) / kChunk; cc <= p / kChunk; ++cc) {
+            const size_t at = (static_cast<size_t>(cc) * a.tokens + row0 + r) * a.query_heads + h;
+            const float cm = __ldcg(a.stats + at * 2u), cl = __ldcg(a.stats + at * 2u + 1u);
+            const float co = __ldcg(a.partials + at * d + e);
+            float fa, fb, fm;
+            if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
+            else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
+            else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
+            else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
+            run_l = fmaf(run_l, fa, cl * fb);
+            o = fmaf(o, fa, co * fb);
+            run_m = fm;
+            live = true;
+        }
+        a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
+    }
+}
+
+}  // namespace
+
+uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads) {
+    const Geometry g = geometry_of(query_heads, kv_heads);
+    return (tokens + g.rows_per_tile - 1) / g.rows_per_tile;
+}
+
+cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+    const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
+    const size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
+                        kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.kv_heads, a.max_chunks, (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_kernel, a);
+}
+
+}  // namespace cb

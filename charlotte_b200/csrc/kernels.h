@@ -1,0 +1,29 @@
+// The non-matmul kernels of the hot path. Their arguments are the public C
+// structs (include/charlotte_b200.h), each the device form of a reference
+// launcher's constants and bindings (plainsight-systems/charlotte,
+// src/core/kernels/<op>/<op>.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "charlotte_b200.h"
+
+namespace cb {
+
+using NormArgs = cb_norm;
+using RopeArgs = cb_rope;
+using AttentionArgs = cb_attention;
+using GatherArgs = cb_gather;
+using SelectArgs = cb_select;
+
+cudaError_t norm_run(const NormArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t rope_run(const RopeArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads);
+cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl);
+uint32_t select_tiles(uint32_t count);
+
+}  // namespace cb

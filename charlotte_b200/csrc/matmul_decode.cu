@@ -12,7 +12,7 @@
 // oracle's and to the reference's prefill form of the same token.
 //
 // B200 mapping.
-//  - A warp owns batches of R rows (R = 2, 4 or 8, chosen by the product's
+//  - A warp owns batches of R rows (R = 1, 2, 4 or 8, chosen by the product's
 //    size so that small products still spread over every SM). Each batch's
 //    row streams (codes, scales, ...) are brought into the warp's shared
 //    memory by bulk asynchronous copies (cp.async.bulk, the untiled TMA),
@@ -24,8 +24,8 @@
 //    only x, the previous launch's output, waits.
 //  - Rows are worked two at a time sharing each x read: one fma decodes a
 //    weight exactly (formats.cuh), one fma accumulates it.
-//  - A batch's rows that are consecutive in one weight (all of them, but at
-//    a member's edge or the product's end) come in one bulk copy per stream.
+//  - Batches never straddle members, so a batch's rows come in one bulk copy
+//    per stream (two for a gated batch: its gate rows and its up rows).
 //  - x is staged once per CTA in shared memory range-major, a 16-byte skew
 //    per range, so the lanes' 128-bit reads fall in distinct banks.
 //  - Every mbarrier wait is bounded (tma.cuh): a copy that never lands sets
@@ -57,125 +57,107 @@ __device__ __forceinline__ uint32_t lane_of(uint32_t g, uint32_t G) { return (32
 // Floats of x a range holds in shared memory: its most groups, and a 16-byte skew.
 __host__ __device__ __forceinline__ uint32_t x_lane_stride(uint32_t G) { return (G + 31u) / 32u * 32u + 4u; }
 
-struct Slot {
-    const uint8_t* piece;
-    uint32_t blocks;
-    uint32_t row;     // row within the piece
-    uint32_t member;
-    uint32_t out;     // output column
-    bool live;
+// A batch: up to R consecutive rows of one member (non-gated), or R/2
+// outputs' gate rows then the same up rows (gated). Batches never straddle
+// members, so a batch's rows of each stream are one contiguous run.
+struct Batch {
+    uint32_t member;   // non-gated: the member; gated: 0
+    uint32_t local;    // first row's index within the member's rows (gated: first output)
+    uint32_t live;     // rows live (gated: outputs live)
 };
 
-// Slot s (0..R-1) of batch b. Write/QKV/GatedByInput: the product's rows in
-// order, members concatenated. Gated: R/2 outputs a batch, gate rows in slots
-// 0..R/2-1 and the same up rows in R/2..R-1.
 template <int R>
-__device__ __forceinline__ Slot locate_slot(const MatmulArgs& a, uint32_t batch, uint32_t s) {
-    Slot r{};
+__device__ __forceinline__ uint32_t batch_count(const MatmulArgs& a) {
+    if (a.epilogue == kGated) return (a.member[0].rows + (R > 1 ? R / 2 : 1) - 1) / (R > 1 ? R / 2 : 1);
+    uint32_t n = 0;
+    for (uint32_t m = 0; m < a.members; ++m) n += (a.member[m].rows + R - 1) / R;
+    return n;
+}
+
+template <int R>
+__device__ __forceinline__ Batch locate_batch(const MatmulArgs& a, uint32_t b) {
+    Batch r{0, 0, 0};
     if (a.epilogue == kGated) {
-        constexpr uint32_t H = R / 2;
-        const uint32_t m = s / H;
-        const uint32_t row = batch * H + (s % H);
-        r.member = m;
-        r.live = row < a.member[0].rows;
-        r.piece = a.member[m].piece;
-        r.blocks = a.member[m].blocks;
-        r.row = a.member[m].first_row + row;
-        r.out = a.member[0].out_offset + row;
+        constexpr uint32_t H = R > 1 ? R / 2 : 1;
+        r.local = b * H;
+        r.live = min(H, a.member[0].rows - r.local);
         return r;
     }
-    uint32_t v = batch * R + s;
     for (uint32_t m = 0; m < a.members; ++m) {
-        if (v < a.member[m].rows) {
+        const uint32_t nb = (a.member[m].rows + R - 1) / R;
+        if (b < nb) {
             r.member = m;
-            r.live = true;
-            r.piece = a.member[m].piece;
-            r.blocks = a.member[m].blocks;
-            r.row = a.member[m].first_row + v;
-            r.out = a.member[m].out_offset + v;
+            r.local = b * R;
+            r.live = min(static_cast<uint32_t>(R), a.member[m].rows - r.local);
             return r;
         }
-        v -= a.member[m].rows;
+        b -= nb;
     }
-    r.live = false;
-    r.piece = a.member[0].piece;
-    r.blocks = a.member[0].blocks;
     return r;
 }
 
-// Whether slot j continues the segment of slot j-1: both live, one member,
-// consecutive rows (always so within a member).
-__device__ __forceinline__ bool continues(const Slot& prev, const Slot& cur) {
-    return prev.live && cur.live && prev.member == cur.member && prev.row + 1u == cur.row;
-}
-
-// A batch's stage is stream-major: stream s's region holds R slots of
-// RowStreams<F>::slot(s) bytes. A segment of consecutive rows starting at
-// slot j0 is one bulk copy per stream, rounded out to 16-byte bounds, placed
-// at slot j0 of each region; slot j of the segment then lies
-// (off(j0) mod 16) + (j - j0)·row_bytes past that.
+// The stage is stream-major: stream s's region holds R slots of
+// RowStreams<F>::slot(s) bytes. A run of consecutive rows (a segment) is one
+// bulk copy per stream, rounded out to 16-byte bounds, at the region's slot
+// `j0`; its row i lies (off mod 16) + i·row_bytes past that.
 template <typename F>
 struct Stage {
-    __device__ __forceinline__ static uint64_t offset(const Slot& sl, int s, uint32_t G) {
-        return RowStreams<F>::base(s, sl.blocks) + static_cast<uint64_t>(sl.row) * RowStreams<F>::row_bytes(s, G);
-    }
     __device__ __forceinline__ static uint32_t region(int s, uint32_t G, int R) {
         uint32_t at = 0;
         for (int t = 0; t < s; ++t) at += R * RowStreams<F>::slot(t, G);
         return at;
     }
-    // Copies a segment of `len` rows starting at slot j0 (`first` its first row).
-    __device__ __forceinline__ static uint32_t copy_segment(uint8_t* stage, const Slot& first, uint32_t j0,
-                                                            uint32_t len, uint32_t G, int R, uint64_t* bar,
-                                                            bool issue) {
+    __device__ __forceinline__ static uint32_t copy_segment(uint8_t* stage, const MemberArgs& m, uint32_t row,
+                                                            uint32_t j0, uint32_t len, uint32_t G, int R,
+                                                            uint64_t* bar, bool issue) {
         uint32_t bytes = 0;
 #pragma unroll
         for (int s = 0; s < F::kStreams; ++s) {
-            const uint64_t off = offset(first, s, G);
+            const uint64_t off = RowStreams<F>::base(s, m.blocks) + static_cast<uint64_t>(row) * RowStreams<F>::row_bytes(s, G);
             const uint64_t start = off & ~15ull;
             const uint64_t end = (off + static_cast<uint64_t>(len) * RowStreams<F>::row_bytes(s, G) + 15ull) & ~15ull;
             if (issue)
-                bulk_g2s(stage + region(s, G, R) + j0 * RowStreams<F>::slot(s, G), first.piece + start,
+                bulk_g2s(stage + region(s, G, R) + j0 * RowStreams<F>::slot(s, G), m.piece + start,
                          static_cast<uint32_t>(end - start), bar);
             bytes += static_cast<uint32_t>(end - start);
         }
         return bytes;
     }
-    // Slot j's stream pointers, given its segment's first slot j0 and row.
-    __device__ __forceinline__ static void pointers(const uint8_t* stage, const Slot& first, uint32_t j0, uint32_t j,
-                                                    uint32_t G, int R, const uint8_t** p) {
+    // Stream pointers of row i of the segment copied at slot j0 from `row`.
+    __device__ __forceinline__ static void pointers(const uint8_t* stage, const MemberArgs& m, uint32_t row,
+                                                    uint32_t j0, uint32_t i, uint32_t G, int R, const uint8_t** p) {
 #pragma unroll
-        for (int s = 0; s < F::kStreams; ++s)
-            p[s] = stage + region(s, G, R) + j0 * RowStreams<F>::slot(s, G) +
-                   static_cast<uint32_t>(offset(first, s, G) & 15ull) + (j - j0) * RowStreams<F>::row_bytes(s, G);
+        for (int s = 0; s < F::kStreams; ++s) {
+            const uint64_t off = RowStreams<F>::base(s, m.blocks) + static_cast<uint64_t>(row) * RowStreams<F>::row_bytes(s, G);
+            p[s] = stage + region(s, G, R) + j0 * RowStreams<F>::slot(s, G) + static_cast<uint32_t>(off & 15ull) +
+                   i * RowStreams<F>::row_bytes(s, G);
+        }
     }
 };
 
-// Issues batch `batch`'s copies into `stage` (warp-cooperative): lane j < R
-// holds slot j; each segment's first lane copies the segment; lane 0 arms
-// the barrier with the batch's bytes first.
+// Issues batch b's copies into `stage`: lane 0 arms the barrier with the
+// batch's bytes, then issues one copy per stream per segment (gated: the
+// gate run and the up run).
 template <typename F, int R>
-__device__ __forceinline__ void issue_batch(const MatmulArgs& a, uint32_t batch, uint8_t* stage, uint64_t* bar,
+__device__ __forceinline__ void issue_batch(const MatmulArgs& a, uint32_t b, uint8_t* stage, uint64_t* bar,
                                             uint32_t G, uint32_t lane) {
-    Slot mine{};
-    if (lane < static_cast<uint32_t>(R)) mine = locate_slot<R>(a, batch, lane);
-    // The previous slot's member and row, to find segment starts.
-    const uint32_t prev_member = __shfl_up_sync(0xFFFFFFFFu, mine.member, 1);
-    const uint32_t prev_row = __shfl_up_sync(0xFFFFFFFFu, mine.row, 1);
-    const bool prev_live = __shfl_up_sync(0xFFFFFFFFu, mine.live ? 1u : 0u, 1) != 0u && lane > 0;
-    const bool cont = lane < static_cast<uint32_t>(R) && mine.live && prev_live && prev_member == mine.member &&
-                      prev_row + 1u == mine.row;
-    const bool start = lane < static_cast<uint32_t>(R) && mine.live && !cont;
-    const uint32_t cont_mask = __ballot_sync(0xFFFFFFFFu, cont);
-    // Rows of my segment: me and the run of continuing lanes after me.
-    const uint32_t after = ~(cont_mask >> (lane + 1u));
-    const uint32_t len = lane < 31u ? 1u + (__ffs(after) - 1u) : 1u;
-    uint32_t bytes = start ? Stage<F>::copy_segment(stage, mine, lane, len, G, R, bar, false) : 0u;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xFFFFFFFFu, bytes, o);
-    if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
-    __syncwarp();
-    if (start) Stage<F>::copy_segment(stage, mine, lane, len, G, R, bar, true);
+    if (lane != 0) return;
+    const Batch bt = locate_batch<R>(a, b);
+    if (a.epilogue == kGated) {
+        const MemberArgs& g = a.member[0];
+        const MemberArgs& u = a.member[1];
+        const uint32_t bytes = Stage<F>::copy_segment(stage, g, g.first_row + bt.local, 0, bt.live, G, R, bar, false) +
+                               Stage<F>::copy_segment(stage, u, u.first_row + bt.local, R / 2, bt.live, G, R, bar, false);
+        static_assert(R >= 2 || true, "");
+        mbar_arrive_expect_tx(bar, bytes);
+        Stage<F>::copy_segment(stage, g, g.first_row + bt.local, 0, bt.live, G, R, bar, true);
+        Stage<F>::copy_segment(stage, u, u.first_row + bt.local, R / 2, bt.live, G, R, bar, true);
+    } else {
+        const MemberArgs& m = a.member[bt.member];
+        const uint32_t bytes = Stage<F>::copy_segment(stage, m, m.first_row + bt.local, 0, bt.live, G, R, bar, false);
+        mbar_arrive_expect_tx(bar, bytes);
+        Stage<F>::copy_segment(stage, m, m.first_row + bt.local, 0, bt.live, G, R, bar, true);
+    }
 }
 
 template <typename F, int k>
@@ -197,6 +179,20 @@ __device__ __forceinline__ void chain_group(const F& A, const F& B, const float4
     (chain_step<F, ks>(A, B, ca, cbb, x4, acc_a, acc_b), ...);
 }
 
+template <typename F, int k>
+__device__ __forceinline__ void chain_step1(const F& A, const typename F::Consts& ca, const float4* x4, float& acc) {
+    const float4 xq = x4[k / 4];
+    const float xk = (k % 4 == 0) ? xq.x : ((k % 4 == 1) ? xq.y : ((k % 4 == 2) ? xq.z : xq.w));
+    acc = fmaf(fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca)), xk, acc);
+}
+
+template <typename F, int... ks>
+__device__ __forceinline__ void chain_group1(const F& A, const float4* x4, float& acc,
+                                             std::integer_sequence<int, ks...>) {
+    const typename F::Consts ca = A.consts();
+    (chain_step1<F, ks>(A, ca, x4, acc), ...);
+}
+
 template <typename F, int R>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -204,9 +200,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t lane_stride = x_lane_stride(G);
     const uint32_t stage_bytes = RowStreams<F>::row_stage(G) * R;
-    const uint32_t batches = a.epilogue == kGated ? (a.member[0].rows + R / 2 - 1) / (R / 2)
-                                                  : (a.total_rows + R - 1) / R;
+    const uint32_t batches = batch_count<R>(a);
     const uint32_t stride = gridDim.x * kWarps;
+    const bool gated = a.epilogue == kGated;
 
     // Shared memory: x (range-major floats), then per warp: 2 barriers,
     // range sums, 2 stages.
@@ -245,35 +241,75 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     grid_dependents_launch();
     const float4* xl = reinterpret_cast<const float4*>(xs + lane * lane_stride);
 
+    // Per stream: a row's bytes, a slot's bytes, the region's offset in a stage.
+    uint32_t rb[F::kStreams], sl[F::kStreams], reg[F::kStreams];
+#pragma unroll
+    for (int q = 0; q < F::kStreams; ++q) {
+        rb[q] = RowStreams<F>::row_bytes(q, G);
+        sl[q] = RowStreams<F>::slot(q, G);
+        reg[q] = q == 0 ? 0u : reg[q - 1] + R * sl[q - 1];
+    }
+
     uint32_t i = 0;
-    for (uint32_t batch = first; batch < batches; batch += stride, ++i) {
+    for (uint32_t b = first; b < batches; b += stride, ++i) {
         const uint32_t s = i & 1u;
         uint8_t* stage = stages + s * stage_bytes;
         if (!mbar_wait(&bars[s], (i >> 1) & 1u, a.fault)) {
             // A copy did not land in time: the fault word is set. Wait (bounded)
             // for the other stage's copy so none is left writing this CTA's
             // shared memory, then leave.
-            if (batch + stride < batches) mbar_wait(&bars[s ^ 1u], ((i + 1) >> 1) & 1u, nullptr);
+            if (b + stride < batches) mbar_wait(&bars[s ^ 1u], ((i + 1) >> 1) & 1u, nullptr);
             return;
         }
-        // Each slot, its segment's first slot (static indices only).
-        Slot sl[R], head[R];
-        uint32_t j0[R];
+        const Batch bt = locate_batch<R>(a, b);
+        // The batch's segments' stream pointers, once a batch: non-gated one
+        // segment (the member's rows from bt.local); gated the gate run at
+        // slot 0 and the up run at slot R/2.
+        const uint8_t* seg[2][F::kStreams];
+        {
+            const MemberArgs& m0 = gated ? a.member[0] : a.member[bt.member];
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-            sl[j] = locate_slot<R>(a, batch, j);
-            const bool c = j > 0 && continues(sl[j > 0 ? j - 1 : 0], sl[j]);
-            head[j] = c ? head[j > 0 ? j - 1 : 0] : sl[j];
-            j0[j] = c ? j0[j > 0 ? j - 1 : 0] : static_cast<uint32_t>(j);
+            for (int q = 0; q < F::kStreams; ++q) {
+                const uint64_t off = RowStreams<F>::base(q, m0.blocks) +
+                                     static_cast<uint64_t>(m0.first_row + bt.local) * rb[q];
+                seg[0][q] = stage + reg[q] + static_cast<uint32_t>(off & 15ull);
+            }
+            if (gated) {
+                const MemberArgs& m1 = a.member[1];
+#pragma unroll
+                for (int q = 0; q < F::kStreams; ++q) {
+                    const uint64_t off = RowStreams<F>::base(q, m1.blocks) +
+                                         static_cast<uint64_t>(m1.first_row + bt.local) * rb[q];
+                    seg[1][q] = stage + reg[q] + (R > 1 ? R / 2 : 0) * sl[q] + static_cast<uint32_t>(off & 15ull);
+                }
+            }
         }
-        float acc[R];
-#pragma unroll
+        if constexpr (R == 1) {
+            // One row a batch: the smallest products, spread over the most warps.
+            float acc = 0.0f;
+            for (uint32_t g = lo; g < hi; ++g) {
+                F A;
+                A.load(seg[0], g);
+                chain_group1<F>(A, xl + (g - lo) * 8u, acc, std::make_integer_sequence<int, 32>{});
+            }
+            red[lane] = acc;
+        } else {
+        // Pairs of slots: non-gated rows (2p, 2p+1) of the segment. Gated:
+        // with R = 2 the pair is the output's gate row and up row; otherwise
+        // pairs p < R/4 are gate rows (2p, 2p+1), then the same up rows.
+#pragma unroll 1
         for (int p = 0; p < R / 2; ++p) {
+            const bool upper = gated && R > 2 && p >= R / 4;
+            const uint32_t ia = upper ? 2u * p - R / 2 : 2u * p;
+            const bool la = ia < bt.live;
+            const bool lb = (gated && R == 2) ? la : ia + 1u < bt.live;
             const uint8_t* pa[F::kStreams];
             const uint8_t* pb[F::kStreams];
-            Stage<F>::pointers(stage, head[2 * p], j0[2 * p], 2 * p, G, R, pa);
-            Stage<F>::pointers(stage, head[2 * p + 1], j0[2 * p + 1], 2 * p + 1, G, R, pb);
-            const bool la = sl[2 * p].live, lb = sl[2 * p + 1].live;
+#pragma unroll
+            for (int q = 0; q < F::kStreams; ++q) {
+                pa[q] = (upper ? seg[1][q] : seg[0][q]) + ia * rb[q];
+                pb[q] = (gated && R == 2) ? seg[1][q] : pa[q] + rb[q];
+            }
             float aa = 0.0f, ab = 0.0f;
             for (uint32_t g = lo; g < hi; ++g) {
                 F A, B;
@@ -281,16 +317,14 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
                 if (lb) B.load(pb, g); else B.zero();
                 chain_group<F>(A, B, xl + (g - lo) * 8u, aa, ab, std::make_integer_sequence<int, 32>{});
             }
-            acc[2 * p] = aa;
-            acc[2 * p + 1] = ab;
+            red[(2 * p) * kRedStride + lane] = aa;
+            red[(2 * p + 1) * kRedStride + lane] = ab;
+        }
         }
         // The stage is read: let the copy engine refill it with batch i+2.
         fence_proxy_async();
         __syncwarp();
-        if (batch + 2u * stride < batches) issue_batch<F, R>(a, batch + 2u * stride, stage, &bars[s], G, lane);
-#pragma unroll
-        for (int j = 0; j < R; ++j) red[j * kRedStride + lane] = acc[j];
-        __syncwarp();
+        if (b + 2u * stride < batches) issue_batch<F, R>(a, b + 2u * stride, stage, &bars[s], G, lane);
         // Slot `lane`'s total: its 32 range sums added in order (slot_total, :237).
         float total = 0.0f;
         if (lane < static_cast<uint32_t>(R)) {
@@ -304,20 +338,23 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
                 total = total + v.w;
             }
         }
-        const Slot me = locate_slot<R>(a, batch, lane < static_cast<uint32_t>(R) ? lane : 0u);
-        if (a.epilogue == kGated) {
-            const float up = __shfl_down_sync(0xFFFFFFFFu, total, R / 2);
-            if (lane < static_cast<uint32_t>(R / 2) && me.live)
-                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + me.out] = activate(a.activation, total) * up;
-        } else if (lane < static_cast<uint32_t>(R) && me.live) {
+        if (gated) {
+            const float up = __shfl_down_sync(0xFFFFFFFFu, total, R > 1 ? R / 2 : 1);
+            if (lane < bt.live) {
+                const uint32_t o = a.member[0].out_offset + bt.local + lane;
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * up;
+            }
+        } else if (lane < bt.live) {
+            const MemberArgs& m = a.member[bt.member];
+            const uint32_t o = m.out_offset + bt.local + lane;
             if (a.epilogue == kWrite) {
-                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + me.out] = total;
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = total;
             } else if (a.epilogue == kQKV) {
-                a.out[me.member][static_cast<size_t>(t) * a.out_stride[me.member] + me.out] = total;
+                a.out[bt.member][static_cast<size_t>(t) * a.out_stride[bt.member] + o] = total;
             } else {   // kGatedByInput (matmul.wgsl:346-350)
                 const float u = a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride +
-                                             a.gate_input_column + me.out];
-                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + me.out] = activate(a.activation, total) * u;
+                                             a.gate_input_column + o];
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * u;
             }
         }
         __syncwarp();
@@ -334,12 +371,17 @@ cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
     const uint32_t G = a.columns / 32u;
     const size_t smem = decode_smem<F, R>(G);
     if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
-    const uint32_t batches = a.epilogue == kGated ? (a.member[0].rows + R / 2 - 1) / (R / 2)
-                                                  : (a.total_rows + R - 1) / R;
+    uint32_t batches = 0;
+    if (a.epilogue == kGated) batches = (a.member[0].rows + (R > 1 ? R / 2 : 1) - 1) / (R > 1 ? R / 2 : 1);
+    else for (uint32_t m = 0; m < a.members; ++m) batches += (a.member[m].rows + R - 1) / R;
     auto kernel = decode_kernel<F, R>;
     static bool configured = false;   // per instantiation
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDecodeSmem);
+        if (e != cudaSuccess) return e;
+        // The whole unified L1/shared carveout to shared memory, so that
+        // launches of different sizes never flip the SM's configuration.
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
         configured = true;
     }
@@ -371,12 +413,14 @@ cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
 template <typename F>
 cudaError_t dispatch(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    const uint64_t slots = a.epilogue == kGated ? 2ull * a.member[0].rows : a.total_rows;
+    const bool gated = a.epilogue == kGated;
+    const uint64_t slots = gated ? 2ull * a.member[0].rows : a.total_rows;
     const uint64_t warps_wanted = static_cast<uint64_t>(sm_count) * 16u;
     const size_t budget = 110u * 1024u;   // two CTAs an SM at least
     if (slots >= warps_wanted * 8u && decode_smem<F, 8>(G) <= budget) return launch_decode<F, 8>(a, sm_count, stream, pdl);
     if (slots >= warps_wanted * 4u && decode_smem<F, 4>(G) <= budget) return launch_decode<F, 4>(a, sm_count, stream, pdl);
-    return launch_decode<F, 2>(a, sm_count, stream, pdl);
+    if (slots >= warps_wanted * 2u || gated) return launch_decode<F, 2>(a, sm_count, stream, pdl);
+    return launch_decode<F, 1>(a, sm_count, stream, pdl);
 }
 
 }  // namespace
@@ -384,9 +428,9 @@ cudaError_t dispatch(const MatmulArgs& a, int sm_count, cudaStream_t stream, boo
 size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns) {
     const uint32_t G = columns / 32u;
     switch (format) {
-        case kQ4_0: return decode_smem<Q4_0, 2>(G);
-        case kQ8_0: return decode_smem<Q8_0, 2>(G);
-        case kQ6_K: return decode_smem<Q6_K, 2>(G);
+        case kQ4_0: return decode_smem<Q4_0, 1>(G);
+        case kQ8_0: return decode_smem<Q8_0, 1>(G);
+        case kQ6_K: return decode_smem<Q6_K, 1>(G);
         default: return 0;
     }
 }

@@ -1,0 +1,140 @@
+// QK-norm, RoPE and the KV append (plainsight-systems/charlotte,
+// src/core/kernels/rope/rope.wgsl + rope_cache.wgsl:11-89; launcher
+// rope.h:282-300, rope.cpp:76-87, 107-130).
+//
+// One CTA a token row: (Hq + 2·Hkv) heads × d/8 lanes, lane i of a head
+// holding its vec4s i and i + d/8, as the reference's invocations do. The
+// token's angles are computed once into shared memory: t = p·turn_k (then
+// t/factor_k with llama3 factors), angle = 2π·(t − round_even(t)), and its
+// sine and cosine by the Cody–Waite/Taylor method of numerics.cuh. A query
+// or key head with QK-norm sums dot(a,a) + dot(b,b) over its lanes in the
+// reference's halving tree (reduce_head, rope.wgsl:62-73; a shuffle-down by
+// `stride` within the head's lanes pairs the same elements), then
+// (x·r)·g. Query and key pairs turn by their angle — NEOX halves or
+// adjacent pairs — queries written back f32, keys and values packed f16
+// (saturated, round-to-nearest-even) into slot p mod slots.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "numerics.cuh"
+#include "tma.cuh"
+
+namespace cb {
+
+namespace {
+
+__device__ __forceinline__ void store_f16x4(uint16_t* dst, float4 v) {
+    const uint32_t lo = static_cast<uint32_t>(f32_to_f16_sat(v.x)) | (static_cast<uint32_t>(f32_to_f16_sat(v.y)) << 16);
+    const uint32_t hi = static_cast<uint32_t>(f32_to_f16_sat(v.z)) | (static_cast<uint32_t>(f32_to_f16_sat(v.w)) << 16);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+}
+
+__global__ void rope_kernel(RopeArgs a) {
+    extern __shared__ float angles[];   // cos then sin, d/2 each
+    grid_dependency_wait();
+    const uint32_t d = a.head_dim;
+    const uint32_t lanes = d / 8u;
+    const uint32_t row = blockIdx.x;
+    const uint32_t p = (a.position ? *a.position : a.position0) + row;
+    float* cosines = angles;
+    float* sines = angles + d / 2u;
+    for (uint32_t k = threadIdx.x; k < d / 2u; k += blockDim.x) {
+        float t = static_cast<float>(p) * a.turns[k];
+        if (a.factors) t = t / a.factors[k];
+        const float angle = 6.283185307179586f * (t - rintf(t));
+        sincos_turn(angle, &sines[k], &cosines[k]);
+    }
+    __syncthreads();
+    grid_dependents_launch();
+
+    const uint32_t head = threadIdx.x / lanes;
+    const uint32_t lane = threadIdx.x % lanes;
+    const uint32_t hq = a.query_heads, hkv = a.kv_heads;
+    if (head >= hq + 2u * hkv) return;
+    const bool is_query = head < hq;
+    const bool is_value = head >= hq + hkv;
+    const uint32_t kvh = is_value ? head - hq - hkv : head - hq;
+    const float4* src;
+    if (is_query) src = reinterpret_cast<const float4*>(a.query + (static_cast<size_t>(row) * hq + head) * d);
+    else if (is_value) src = reinterpret_cast<const float4*>(a.value + (static_cast<size_t>(row) * hkv + kvh) * d);
+    else src = reinterpret_cast<const float4*>(a.key + (static_cast<size_t>(row) * hkv + kvh) * d);
+    float4 x0 = src[lane];
+    float4 x1 = src[lane + lanes];
+
+    // QK-norm (uniform over the CTA: both gains or neither). Every lane takes
+    // part in the shuffles — a warp may hold a key head and a value head —
+    // and value heads discard the result.
+    float r = 1.0f;
+    if (a.query_gain) {
+        float v = dot4(x0, x0) + dot4(x1, x1);
+        for (uint32_t stride = lanes / 2u; stride > 0; stride >>= 1)
+            v = v + __shfl_down_sync(0xFFFFFFFFu, v, stride, lanes);
+        const float total = __shfl_sync(0xFFFFFFFFu, v, 0, lanes);
+        r = 1.0f / sqrtf(total / static_cast<float>(d) + a.epsilon);
+    }
+    if (!is_value) {
+        const float* gain = is_query ? a.query_gain : a.key_gain;
+        if (gain) {
+            const float4 g0 = reinterpret_cast<const float4*>(gain)[lane];
+            const float4 g1 = reinterpret_cast<const float4*>(gain)[lane + lanes];
+            x0 = make_float4((x0.x * r) * g0.x, (x0.y * r) * g0.y, (x0.z * r) * g0.z, (x0.w * r) * g0.w);
+            x1 = make_float4((x1.x * r) * g1.x, (x1.y * r) * g1.y, (x1.z * r) * g1.z, (x1.w * r) * g1.w);
+        }
+        if (a.halves) {
+            // pairs k = 4·lane + c: (x0.c, x1.c) turned by angle k
+            float* e0 = &x0.x;
+            float* e1 = &x1.x;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t k = 4u * lane + c;
+                const float u = e0[c], w = e1[c];
+                e0[c] = fmaf(u, cosines[k], -(w * sines[k]));
+                e1[c] = fmaf(u, sines[k], w * cosines[k]);
+            }
+        } else {
+            // adjacent pairs: x0 holds pairs 2·lane, 2·lane+1; x1 pairs d/4 + 2·lane, +1
+            float* e[2] = {&x0.x, &x1.x};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t k = (h ? d / 4u : 0u) + 2u * lane + c;
+                    const float u = e[h][2 * c], w = e[h][2 * c + 1];
+                    e[h][2 * c] = fmaf(u, cosines[k], (-w) * sines[k]);
+                    e[h][2 * c + 1] = fmaf(w, cosines[k], u * sines[k]);
+                }
+            }
+        }
+    }
+    if (is_query) {
+        float4* dst = reinterpret_cast<float4*>(a.query + (static_cast<size_t>(row) * hq + head) * d);
+        dst[lane] = x0;
+        dst[lane + lanes] = x1;
+    } else {
+        uint16_t* cache = is_value ? a.value_cache : a.key_cache;
+        uint16_t* dst = cache + (static_cast<size_t>(p % a.slots) * hkv + kvh) * d;
+        store_f16x4(dst + 4u * lane, x0);
+        store_f16x4(dst + 4u * (lane + lanes), x1);
+    }
+}
+
+}  // namespace
+
+cudaError_t rope_run(const RopeArgs& a, cudaStream_t stream, bool pdl) {
+    const uint32_t threads = (a.query_heads + 2u * a.kv_heads) * (a.head_dim / 8u);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.tokens);
+    cfg.blockDim = dim3((threads + 31u) / 32u * 32u);
+    cfg.dynamicSmemBytes = a.head_dim * sizeof(float);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rope_kernel, a);
+}
+
+}  // namespace cb

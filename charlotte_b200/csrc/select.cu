@@ -1,0 +1,238 @@
+// Top-k selection and the draw (plainsight-systems/charlotte,
+// src/core/kernels/topk/topk.wgsl first/merge :131-165, key_of :28,
+// before :55; launcher topk.cpp:21; src/core/sampler/draw.wgsl:71-163).
+//
+// The reference keeps the top 64 of the vocabulary under one total order —
+// larger logit first, of equal logits the lower token; −0 = +0; every NaN
+// above +∞ — as (logit bits, token) pairs, a NaN's bits canonical
+// (0x7FC00000), padding (0xFFFFFFFF, 0xFFFFFFFF) when fewer than 64 exist.
+// That order is one comparison here: the 64-bit key
+//     key_of(bits) << 32 | (0xFFFFFFFF − token)
+// descending, padding 0. Any exact selection of the 64 largest keys gives
+// the reference's candidates, in its order.
+//
+// B200 mapping: one launch. Each CTA sorts a tile of 1,024 keys (bitonic, in
+// shared memory) and writes its top 64; the last CTA to finish (an atomic
+// ticket, no waiting) merges the tiles' sorted lists pairwise, round by
+// round, by rank, then runs the draw on the 64 candidates and writes the
+// 16-byte sampled record. The ticket is reset for the next step.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "numerics.cuh"
+#include "tma.cuh"
+
+namespace cb {
+
+namespace {
+
+constexpr uint32_t kTile = 1024;
+constexpr uint32_t kKeep = 64;
+constexpr uint32_t kSelThreads = 1024;
+constexpr uint32_t kMaxTiles = 256;   // vocabularies up to 262,144
+
+__device__ __forceinline__ uint64_t entry_key(uint32_t bits, uint32_t id) {
+    return (static_cast<uint64_t>(key_of(bits)) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - id);
+}
+
+__device__ __forceinline__ void entry_pair(uint64_t k, uint32_t* out) {
+    out[0] = bits_of(static_cast<uint32_t>(k >> 32));
+    out[1] = 0xFFFFFFFFu - static_cast<uint32_t>(k);
+}
+
+// Bitonic sort of 1,024 keys in shared memory, descending.
+__device__ void sort_tile(uint64_t* keys) {
+    const uint32_t t = threadIdx.x;
+    for (uint32_t k = 2; k <= kTile; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            const uint32_t ixj = t ^ j;
+            if (ixj > t) {
+                const uint64_t a = keys[t], b = keys[ixj];
+                const bool descending = (t & k) == 0;
+                if (descending ? a < b : a > b) {
+                    keys[t] = b;
+                    keys[ixj] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t count_greater(const uint64_t* list, uint64_t v, bool or_equal) {
+    // list descending, 64 long: how many come before v
+    uint32_t lo = 0, hi = kKeep;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        const bool before = or_equal ? list[mid] >= v : list[mid] > v;
+        if (before) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ uint32_t philox_word0(uint32_t c0, uint32_t k0, uint32_t k1) {
+    uint32_t c[4] = {c0, 0, 0, 0};
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]), lo0 = 0xD2511F53u * c[0];
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]), lo1 = 0xCD9E8D57u * c[2];
+        const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return c[0];
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
+    extern __shared__ __align__(16) uint64_t buf[];   // 16,384 + 8,192 keys
+    __shared__ unsigned int last;
+    grid_dependency_wait();
+    const uint32_t t = threadIdx.x;
+    const uint32_t tile = blockIdx.x;
+    {
+        const uint32_t e = tile * kTile + t;
+        uint64_t k = 0;
+        if (e < a.count) k = entry_key(__float_as_uint(a.logits[e]), e);
+        buf[t] = k;
+    }
+    __syncthreads();
+    sort_tile(buf);
+    if (t < kKeep) entry_pair(buf[t], a.partials + 2u * (tile * kKeep + t));
+    grid_dependents_launch();
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+        const unsigned int seen = atomicAdd(a.ticket, 1u);
+        last = seen == gridDim.x - 1u;
+        if (last) *a.ticket = 0u;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+
+    // Merge the tiles' sorted lists pairwise, round by round.
+    uint32_t lists = gridDim.x;
+    uint64_t* src = buf;
+    uint64_t* dst = buf + kMaxTiles * kKeep;
+    for (uint32_t i = t; i < lists * kKeep; i += kSelThreads) {
+        const uint32_t bits = __ldcg(a.partials + 2u * i), id = __ldcg(a.partials + 2u * i + 1u);
+        src[i] = id == 0xFFFFFFFFu ? 0ull : entry_key(bits, id);
+    }
+    __syncthreads();
+    while (lists > 1) {
+        const uint32_t out_lists = (lists + 1u) / 2u;
+        for (uint32_t i = t; i < out_lists * 2u * kKeep; i += kSelThreads) {
+            const uint32_t pair = i / (2u * kKeep), w = i % (2u * kKeep);
+            const uint64_t* A = src + (2u * pair) * kKeep;
+            uint64_t* out = dst + pair * kKeep;
+            if (2u * pair + 1u >= lists) {   // an odd list out passes through
+                if (w < kKeep) out[w] = A[w];
+                continue;
+            }
+            const uint64_t* Bl = A + kKeep;
+            uint32_t pos;
+            uint64_t v;
+            if (w < kKeep) { v = A[w]; pos = w + count_greater(Bl, v, false); }
+            else { v = Bl[w - kKeep]; pos = (w - kKeep) + count_greater(A, v, true); }
+            if (pos < kKeep) out[pos] = v;
+        }
+        __syncthreads();
+        uint64_t* tmp = src; src = dst; dst = tmp;
+        lists = out_lists;
+    }
+    // src[0..63]: the candidates, in the reference's order.
+    __shared__ uint32_t cand[2 * kKeep];
+    __shared__ float weight[kKeep], tempered[kKeep], running[kKeep];
+    __shared__ uint32_t above[kKeep];
+    __shared__ float total_s;
+    if (t < kKeep) {
+        entry_pair(src[t], cand + 2u * t);
+        a.candidates[2u * t] = cand[2u * t];
+        a.candidates[2u * t + 1u] = cand[2u * t + 1u];
+    }
+    __syncthreads();
+    // The draw (draw.wgsl:71-163); temperature 0 keeps candidate 0 (greedy).
+    const uint32_t k = min(a.top_k ? a.top_k : 1u, kKeep);
+    const bool top_p = a.top_p < 1.0f;
+    const uint32_t first_bits = cand[0];
+    const bool failed = (first_bits & 0x7F800000u) == 0x7F800000u;
+    if (t < k) {
+        const uint32_t mine_bits = cand[2u * t];
+        weight[t] = 0.0f;
+        tempered[t] = 0.0f;
+        above[t] = 0u;
+        if (!failed && mine_bits != 0xFF800000u) {
+            const float first = __uint_as_float(first_bits), mine = __uint_as_float(mine_bits);
+            if (top_p) weight[t] = exp_nonpositive(mine - first);
+            if (a.temperature > 0.0f) tempered[t] = exp_nonpositive((mine - first) / a.temperature);
+            above[t] = (a.min_p == 0.0f || mine >= first + a.log_min_p) ? 1u : 0u;
+        }
+    }
+    __syncthreads();
+    if (t == 0) {
+        const uint32_t pos = a.position ? *a.position : a.position0;
+        const uint32_t w0 = philox_word0(pos + a.tokens, a.seed0, a.seed1);
+        const float u = static_cast<float>(w0 >> 9) * (1.0f / 8388608.0f) + (1.0f / 16777216.0f);
+        if (top_p) {
+            float sum = 0.0f;
+            for (uint32_t i = 0; i < k; ++i) sum = sum + weight[i];
+            if (!failed)
+                for (uint32_t i = 0; i < k; ++i) weight[i] = weight[i] / sum;
+        }
+        uint32_t kept = k;
+        float cumulative = 0.0f, tempered_sum = 0.0f;
+        for (uint32_t i = 0; i < k; ++i) {
+            tempered_sum = tempered_sum + tempered[i];
+            running[i] = tempered_sum;
+            if (top_p) {
+                cumulative = cumulative + weight[i];
+                if (cumulative >= a.top_p) { kept = i + 1u; break; }
+            }
+        }
+        uint32_t survivors = 1;
+        while (survivors < kept && above[survivors] == 1u) survivors++;
+        uint32_t chosen = 0;
+        if (a.temperature > 0.0f) {
+            const float goal = u * running[survivors - 1u];
+            chosen = survivors - 1u;
+            for (uint32_t i = 0; i < survivors; ++i)
+                if (running[i] > goal) { chosen = i; break; }
+        }
+        a.sampled[0] = failed ? 0u : cand[2u * chosen + 1u];
+        a.sampled[1] = failed ? 1u : 0u;
+        a.sampled[2] = __float_as_uint(u);
+        a.sampled[3] = 0u;
+    }
+}
+
+}  // namespace
+
+uint32_t select_tiles(uint32_t count) { return (count + kTile - 1u) / kTile; }
+
+cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl) {
+    const uint32_t tiles = select_tiles(a.count);
+    if (tiles == 0 || tiles > kMaxTiles) return cudaErrorInvalidValue;
+    const size_t smem = (kMaxTiles * kKeep + (kMaxTiles / 2u) * kKeep) * sizeof(uint64_t);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles);
+    cfg.blockDim = dim3(kSelThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, select_kernel, a);
+}
+
+}  // namespace cb

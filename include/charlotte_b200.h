@@ -114,6 +114,141 @@ typedef struct cb_matmul {
 CB_API int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_t tokens, float* const out[3],
                   const uint32_t out_stride[3], uint32_t flags, void* stream);
 
+
+/* ---- RMSNorm ------------------------------------------------------------------
+ * Replaces norm.wgsl:80 behind norm_launch (src/core/kernels/norm/norm.h:220):
+ * with `add`, hidden += y (y post-normed with post_gain first when given —
+ * Gemma 3), the new hidden row written back; then normed = (x·r)·gain,
+ * r = 1/sqrt(mean(x²) + epsilon), the sum of squares in the reference's
+ * 256-way tree. `last_token`: the final norm, the step's last row only.
+ * Rows up to 4096 wide, a multiple of 4. */
+typedef struct cb_norm {
+    float* hidden;            /* [tokens][width]                          */
+    const float* output;      /* y, [tokens][width], with add             */
+    const float* gain;        /* [width]                                  */
+    const float* post_gain;   /* [width] or NULL                          */
+    float* normed;            /* [tokens][width]                          */
+    uint32_t width;
+    uint32_t tokens;
+    uint32_t add;
+    uint32_t last_token;
+    float epsilon;
+} cb_norm;
+CB_API int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream);
+
+/* ---- QK-norm + RoPE + KV append -----------------------------------------------
+ * Replaces rope.wgsl + rope_cache.wgsl behind rope_launch
+ * (src/core/kernels/rope/rope.h:300): per token at position p = position +
+ * row, query and key heads QK-normed (when gains are given) and turned by
+ * p·θ_k (NEOX halves or adjacent pairs; llama3 factors divide the turns),
+ * queries written back in place, keys and values packed f16 into cache slot
+ * p mod slots ([slots][kv_heads][head_dim]). `turns` holds θ_k/2π rounded
+ * once from f64 (rope.cpp:76; cb_rope_turns computes it). (Hq + 2·Hkv)·d/8
+ * must be a multiple of 32; d is 64, 128 or 256. */
+typedef struct cb_rope {
+    float* query;
+    const float* key;
+    const float* value;
+    uint16_t* key_cache;
+    uint16_t* value_cache;
+    const float* query_gain;
+    const float* key_gain;
+    const float* factors;
+    const float* turns;
+    const uint32_t* position;   /* device word holding the step's position, or NULL */
+    uint32_t position0;         /* the position when `position` is NULL            */
+    uint32_t tokens;
+    uint32_t head_dim;
+    uint32_t query_heads;
+    uint32_t kv_heads;
+    uint32_t halves;
+    uint32_t slots;
+    float epsilon;
+} cb_rope;
+CB_API int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream);
+/* θ_k / 2π for k < d/2, base^(−2k/d) in f64 rounded once to f32 (host). */
+CB_API void cb_rope_turns(double base, uint32_t head_dim, float* turns_host);
+
+/* ---- attention ----------------------------------------------------------------
+ * Replaces attention.wgsl main and combine behind attention_launches
+ * (src/core/kernels/attention/attention.h:320): each query row at position
+ * p attends keys p−window+1..p of the layer's f16 cache in 64-key chunks,
+ * each chunk an online softmax in tiles of 2048/d keys, the chunks folded in
+ * order — one launch, split over every chunk. `partials` holds
+ * max_chunks·tokens·Hq·d floats, `stats` max_chunks·tokens·Hq·2, `tickets`
+ * ceil(tokens/rows_per_tile)·Hkv zeroed words (left zero after each run);
+ * max_chunks ≥ ceil((position + tokens)/64). scale_log2e = scale·log2(e). */
+typedef struct cb_attention {
+    const float* query;
+    const uint16_t* key_cache;
+    const uint16_t* value_cache;
+    float* out;
+    float* partials;
+    float* stats;
+    unsigned int* tickets;
+    const uint32_t* position;
+    uint32_t position0;
+    uint32_t tokens;
+    uint32_t head_dim;
+    uint32_t query_heads;
+    uint32_t kv_heads;
+    uint32_t slots;
+    uint32_t window;
+    uint32_t max_chunks;
+    float scale_log2e;
+} cb_attention;
+CB_API int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream);
+/* Ticket words cb_attention needs for `tokens` rows. */
+CB_API uint32_t cb_attention_tickets(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads);
+
+/* ---- embedding gather -----------------------------------------------------------
+ * Replaces gather.wgsl:25 behind gather_launches (src/core/kernels/gather/
+ * gather.h:124): hidden[t] = unpack(table row of ids[t])·scale; a fed step
+ * reads its one token from the last draw's record on the device. */
+typedef struct cb_gather {
+    const void* piece;
+    uint32_t format;
+    uint32_t blocks;
+    uint32_t width;
+    uint32_t first_row;
+    uint32_t row_count;
+    const uint32_t* ids;
+    const uint32_t* sampled;
+    uint32_t fed;
+    uint32_t tokens;
+    float scale;
+    float* hidden;
+} cb_gather;
+CB_API int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream);
+
+/* ---- top-k selection and the draw -------------------------------------------------
+ * Replaces topk.wgsl first/merge and draw.wgsl behind topk_launches
+ * (src/core/kernels/topk/topk.h:113) and sampler::draw_launch
+ * (src/core/sampler/sampler.h:274): the 64 largest logits under the
+ * reference's total order as (bits, token) candidates, then the draw
+ * (temperature 0: candidate 0) into the 16-byte record {token, failed, u, 0}.
+ * `partials` holds cb_select_tiles(count)·128 words, `ticket` one zeroed
+ * word. count ≤ 262,144. */
+typedef struct cb_select {
+    const float* logits;
+    uint32_t count;
+    uint32_t* partials;
+    unsigned int* ticket;
+    uint32_t* candidates;       /* [64][2] */
+    uint32_t* sampled;          /* [4]     */
+    const uint32_t* position;
+    uint32_t position0;
+    uint32_t tokens;
+    uint32_t seed0, seed1;
+    uint32_t top_k;
+    float temperature, top_p, min_p, log_min_p;
+} cb_select;
+CB_API int cb_select_run(const cb_select* s, uint32_t flags, void* stream);
+CB_API uint32_t cb_select_tiles(uint32_t count);
+
+/* Flags of the kernel entry points above. */
+enum { CB_RUN_PDL = 1u };
+
 #ifdef __cplusplus
 }
 #endif

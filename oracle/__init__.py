@@ -175,3 +175,43 @@ def attention_row(q, p, key_cache, value_cache, slots, window, scale_log2e, head
                            ptr(value_cache, ctypes.c_uint16), slots, window, scale_log2e, head_dim,
                            query_heads, kv_heads, ptr(out, ctypes.c_float))
     return out
+
+
+class RopeShape(ctypes.Structure):
+    _fields_ = [("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
+                ("halves", ctypes.c_int), ("qk_norm", ctypes.c_int), ("slots", ctypes.c_uint32),
+                ("epsilon", ctypes.c_float), ("turns", c_f32p), ("factors", c_f32p),
+                ("query_gain", c_f32p), ("key_gain", c_f32p)]
+
+
+class DrawSettings(ctypes.Structure):
+    _fields_ = [("position", ctypes.c_uint32), ("tokens", ctypes.c_uint32), ("seed0", ctypes.c_uint32),
+                ("seed1", ctypes.c_uint32), ("top_k", ctypes.c_uint32), ("temperature", ctypes.c_float),
+                ("top_p", ctypes.c_float), ("min_p", ctypes.c_float), ("log_min_p", ctypes.c_float)]
+
+
+def rope_token(q, k, v, p, key_cache, value_cache, *, head_dim, query_heads, kv_heads, halves, slots, epsilon,
+               turns, factors=None, query_gain=None, key_gain=None):
+    """One token in place: q (f32 [Hq*d]) rotated; k, v packed into the caches."""
+    keep = [np.ascontiguousarray(a, np.float32) if a is not None else None
+            for a in (turns, factors, query_gain, key_gain)]
+    s = RopeShape(head_dim, query_heads, kv_heads, int(halves), int(query_gain is not None), slots, epsilon,
+                  *[ptr(a, ctypes.c_float) if a is not None else None for a in keep])
+    L = lib()
+    L.or_rope_token.argtypes = [ctypes.POINTER(RopeShape), ctypes.c_uint32, c_f32p, c_f32p, c_f32p, c_u16p, c_u16p]
+    kk = np.ascontiguousarray(k, np.float32)
+    vv = np.ascontiguousarray(v, np.float32)
+    L.or_rope_token(ctypes.byref(s), p, ptr(q, ctypes.c_float), ptr(kk, ctypes.c_float), ptr(vv, ctypes.c_float),
+                    ptr(key_cache, ctypes.c_uint16), ptr(value_cache, ctypes.c_uint16))
+
+
+def draw(pairs128, position, tokens, seed=(0, 0), top_k=40, temperature=0.0, top_p=1.0, min_p=0.0):
+    import math
+    s = DrawSettings(position, tokens, seed[0], seed[1], top_k, temperature, top_p, min_p,
+                     math.log(min_p) if min_p > 0 else 0.0)
+    pairs = np.ascontiguousarray(pairs128, np.uint32)
+    rec = np.zeros(4, np.uint32)
+    L = lib()
+    L.or_draw.argtypes = [c_u32p, ctypes.POINTER(DrawSettings), c_u32p]
+    L.or_draw(ptr(pairs, ctypes.c_uint32), ctypes.byref(s), ptr(rec, ctypes.c_uint32))
+    return rec

@@ -156,3 +156,29 @@ def test_matmul_order_against_f64_bound():
     gamma = 2 * K * u / (1 - 2 * K * u)
     bound = gamma * (np.abs(x.astype(np.float64)) @ np.abs(W).T)
     assert np.all(np.abs(y - exact) <= bound)
+
+
+def test_sincos_against_libm():
+    """The rotation's sine/cosine method stays within a few ulps of libm."""
+    import math
+    s = np.empty(1, np.float32)
+    c = np.empty(1, np.float32)
+    worst = 0.0
+    for a in np.linspace(-math.pi, math.pi, 20001, dtype=np.float32):
+        O.lib().or_sincos(float(a), O.ptr(s, ctypes.c_float), O.ptr(c, ctypes.c_float))
+        worst = max(worst, abs(float(s[0]) - math.sin(float(a))), abs(float(c[0]) - math.cos(float(a))))
+    assert worst < 4e-7
+
+
+def test_exp2_and_exp_against_libm():
+    import math
+    worst2 = worst = 0.0
+    # results in binary32's normal range (below it the result is subnormal)
+    for x in np.linspace(-87.0, 0.0, 50001, dtype=np.float32):
+        a = O.lib().or_exp2(float(x))
+        e = 2.0 ** float(x)
+        worst2 = max(worst2, abs(a - e) / e)
+        b = O.lib().or_exp_nonpositive(float(x))
+        e = math.exp(float(x))
+        worst = max(worst, abs(b - e) / e)
+    assert worst2 < 4e-7 and worst < 4e-7
