@@ -1,0 +1,494 @@
+// A whole decoder on the hot path's kernels: the launches the reference's
+// graph builds (plainsight-systems/charlotte, src/core/graph/graph.cpp:
+// Builder::embed :155, attention :159-230, gated_feed_forward :232-262,
+// output :264-292; the architectures' orders in src/core/arch/{qwen3,llama,
+// gemma3}), each step in that order on one stream, every launch with
+// programmatic dependent launch.
+//
+// Buffers follow the reference's working set (graph.cpp decoder_working_set:
+// hidden, normed, query, key, value, attention, partials, partial_stats,
+// output, activation, logits, the selection's partials, candidates,
+// sampled) sized for a step of max_step_tokens; an f16 KV cache per layer of
+// `context` slots, or, for a sliding-window layer, a ring of window + step
+// slots (src/core/cache/kv.h:13-34: position p in slot p mod slots).
+//
+// Decode: the step's position lives in a device word and its one token is
+// the last draw's (gather's fed form), so a decode step is captured once as
+// a CUDA graph and replayed; a closing launch records the drawn token and
+// advances the position.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "api_common.h"
+#include "charlotte_b200.h"
+#include "kernels.h"
+#include "matmul.h"
+
+namespace cb {
+
+namespace {
+
+struct DevWeight {
+    uint8_t* piece = nullptr;
+    uint32_t format = 0, rows = 0, cols = 0, blocks = 0;
+};
+
+struct DevLayer {
+    float* attn_norm = nullptr;
+    DevWeight q, k, v, o, gate, up, down;
+    float* q_norm = nullptr;
+    float* k_norm = nullptr;
+    float* post_attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    float* post_ffn_norm = nullptr;
+    float* turns = nullptr;
+    uint16_t* key_cache = nullptr;
+    uint16_t* value_cache = nullptr;
+    uint32_t window = 0, slots = 0;
+};
+
+// Records the drawn token and advances the step's position (decode graph).
+__global__ void advance_kernel(uint32_t* state, const uint32_t* sampled, uint32_t* tokens_out, uint32_t* failed_out,
+                               uint32_t capacity) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t step = state[1];
+    if (step < capacity) {
+        tokens_out[step] = sampled[0];
+        failed_out[step] = sampled[1];
+    }
+    state[0] += 1u;   // position
+    state[1] = step + 1u;
+}
+
+}  // namespace
+
+}  // namespace cb
+
+struct cb_decoder {
+    cb_model model{};
+    uint32_t max_tokens = 0;
+    uint32_t max_chunks = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocations;
+    cb::DevWeight token_embd, output;
+    float* output_norm = nullptr;
+    float* factors = nullptr;
+    std::vector<cb::DevLayer> layers;
+    // working set
+    float *hidden = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *out = nullptr, *act = nullptr, *logits = nullptr, *partials = nullptr, *stats = nullptr;
+    unsigned int* tickets = nullptr;
+    uint32_t* sel_partials = nullptr;
+    unsigned int* sel_ticket = nullptr;
+    uint32_t* candidates = nullptr;
+    uint32_t* sampled = nullptr;
+    uint32_t* ids = nullptr;
+    uint32_t* state = nullptr;       // [0] position, [1] decode step index
+    uint32_t* gen_tokens = nullptr;  // generate's drawn tokens
+    uint32_t* gen_failed = nullptr;
+    uint32_t gen_capacity = 0;
+    cudaGraphExec_t decode_graph = nullptr;
+    cb_sampling graph_sampling{};
+    bool has_step = false;
+    uint32_t next_position = 0;   // the position after the last step's tokens
+};
+
+namespace {
+
+using namespace cb;
+
+template <typename T>
+int dalloc(cb_decoder* d, T** p, size_t count) {
+    void* q = nullptr;
+    const cudaError_t e = cudaMalloc(&q, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_create: cudaMalloc");
+    d->allocations.push_back(q);
+    *p = static_cast<T*>(q);
+    return CB_OK;
+}
+
+int upload_f32(cb_decoder* d, float** dst, const float* host, size_t n) {
+    if (!host) { *dst = nullptr; return CB_OK; }
+    if (int rc = dalloc(d, dst, n)) return rc;
+    const cudaError_t e = cudaMemcpy(*dst, host, n * sizeof(float), cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? CB_OK : fail_cuda(e, "cb_decoder_create: upload");
+}
+
+uint32_t weights_per_block(uint32_t f) { return f == CB_Q6_K ? 256u : (f == CB_Q4_0 || f == CB_Q8_0 ? 32u : 1u); }
+
+int upload_weight(cb_decoder* d, DevWeight* w, const cb_weight& src, const char* name) {
+    if (src.rows == 0) return CB_OK;
+    if (src.format != CB_Q4_0 && src.format != CB_Q8_0 && src.format != CB_Q6_K)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: %s's format %u has no matmul kernel", name, src.format);
+    if (src.cols % weights_per_block(src.format) != 0)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: %s's rows of %u are not whole blocks", name, src.cols);
+    if (!src.stored_host) return fail(CB_ERROR_BUILD, "cb_decoder_create: %s has no data", name);
+    const uint64_t blocks = static_cast<uint64_t>(src.rows) * src.cols / weights_per_block(src.format);
+    if (blocks > 0xFFFFFFFFull) return fail(CB_ERROR_BUILD, "cb_decoder_create: %s is too large for one piece", name);
+    const size_t bytes = cb_piece_bytes(src.format, blocks);
+    std::vector<uint8_t> host(bytes);
+    if (int rc = cb_piece_from_stored(src.format, src.stored_host, blocks, host.data())) return rc;
+    if (int rc = dalloc(d, &w->piece, bytes)) return rc;
+    const cudaError_t e = cudaMemcpy(w->piece, host.data(), bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_create: upload");
+    w->format = src.format;
+    w->rows = src.rows;
+    w->cols = src.cols;
+    w->blocks = static_cast<uint32_t>(blocks);
+    return CB_OK;
+}
+
+cb_member member_of(const DevWeight& w) { return {w.piece, w.blocks, 0, w.rows, 0}; }
+
+int launched(cudaError_t e, const char* what) { return e == cudaSuccess ? CB_OK : fail_cuda(e, what); }
+
+// One matmul launch through the same path as cb_matmul_run.
+int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, const float* x,
+            uint32_t x_stride, uint32_t tokens, float* const outs[3], const uint32_t strides[3]) {
+    cb_matmul m{};
+    const DevWeight* first = *ws.begin();
+    m.format = first->format;
+    m.columns = first->cols;
+    m.members = static_cast<uint32_t>(ws.size());
+    m.epilogue = epilogue;
+    m.activation = d->model.activation;
+    uint32_t i = 0;
+    for (const DevWeight* w : ws) m.member[i++] = member_of(*w);
+    return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, CB_MATMUL_PDL, d->stream);
+}
+
+// The step's launches (graph.cpp's order). `fed`: the token is the last draw.
+int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb_sampling& s) {
+    const cb_model& m = d->model;
+    const uint32_t H = m.hidden, dh = m.head_dim, qd = m.query_heads * dh, kvd = m.kv_heads * dh;
+    const uint32_t* pos = d->state;
+    // embed
+    {
+        cb_gather g{};
+        g.piece = d->token_embd.piece;
+        g.format = d->token_embd.format;
+        g.blocks = d->token_embd.blocks;
+        g.width = H;
+        g.first_row = 0;
+        g.row_count = d->token_embd.rows;
+        g.ids = d->ids;
+        g.sampled = d->sampled;
+        g.fed = fed ? 1u : 0u;
+        g.tokens = tokens;
+        g.scale = m.embed_scale;
+        g.hidden = d->hidden;
+        if (int rc = launched(gather_run(g, d->stream, true), "step: gather")) return rc;
+    }
+    const float* pending_post = nullptr;
+    bool pending_add = false;
+    for (uint32_t l = 0; l < m.layers; ++l) {
+        const DevLayer& L = d->layers[l];
+        cb_norm n{d->hidden, d->out, L.attn_norm, pending_post, d->normed, H, tokens, pending_add ? 1u : 0u, 0u,
+                  m.epsilon};
+        if (int rc = launched(norm_run(n, d->stream, true), "step: attention norm")) return rc;
+        {
+            float* outs[3] = {d->q, d->k, d->v};
+            const uint32_t strides[3] = {qd, kvd, kvd};
+            if (int rc = product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, d->normed, H, tokens, outs, strides))
+                return rc;
+        }
+        cb_rope r{};
+        r.query = d->q;
+        r.key = d->k;
+        r.value = d->v;
+        r.key_cache = L.key_cache;
+        r.value_cache = L.value_cache;
+        r.query_gain = L.q_norm;
+        r.key_gain = L.k_norm;
+        r.factors = d->factors;
+        r.turns = L.turns;
+        r.position = pos;
+        r.tokens = tokens;
+        r.head_dim = dh;
+        r.query_heads = m.query_heads;
+        r.kv_heads = m.kv_heads;
+        r.halves = m.halves;
+        r.slots = L.slots;
+        r.epsilon = m.epsilon;
+        if (int rc = launched(rope_run(r, d->stream, true), "step: rope")) return rc;
+        cb_attention at{};
+        at.query = d->q;
+        at.key_cache = L.key_cache;
+        at.value_cache = L.value_cache;
+        at.out = d->att;
+        at.partials = d->partials;
+        at.stats = d->stats;
+        at.tickets = d->tickets;
+        at.position = pos;
+        at.tokens = tokens;
+        at.head_dim = dh;
+        at.query_heads = m.query_heads;
+        at.kv_heads = m.kv_heads;
+        at.slots = L.slots;
+        at.window = L.window;
+        at.max_chunks = d->max_chunks;
+        at.scale_log2e = static_cast<float>(static_cast<double>(m.attention_scale) * 1.4426950408889634);
+        if (int rc = launched(attention_run(at, d->stream, true), "step: attention")) return rc;
+        {
+            float* outs[3] = {d->out, nullptr, nullptr};
+            const uint32_t strides[3] = {H, 0, 0};
+            if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides)) return rc;
+        }
+        cb_norm n2{d->hidden, d->out, L.ffn_norm, L.post_attn_norm, d->normed, H, tokens, 1u, 0u, m.epsilon};
+        if (int rc = launched(norm_run(n2, d->stream, true), "step: feed-forward norm")) return rc;
+        {
+            float* outs[3] = {d->act, nullptr, nullptr};
+            const uint32_t strides[3] = {m.ffn, 0, 0};
+            if (int rc = product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, d->normed, H, tokens, outs, strides))
+                return rc;
+        }
+        {
+            float* outs[3] = {d->out, nullptr, nullptr};
+            const uint32_t strides[3] = {H, 0, 0};
+            if (int rc = product(d, {&L.down}, CB_EPILOGUE_WRITE, d->act, m.ffn, tokens, outs, strides)) return rc;
+        }
+        pending_add = true;
+        pending_post = L.post_ffn_norm;
+    }
+    if (!logits) return CB_OK;
+    cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, 1u, m.epsilon};
+    if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
+    {
+        const DevWeight& head = d->output.piece ? d->output : d->token_embd;
+        float* outs[3] = {d->logits, nullptr, nullptr};
+        const uint32_t strides[3] = {m.vocab, 0, 0};
+        if (int rc = product(d, {&head}, CB_EPILOGUE_WRITE, d->normed + static_cast<size_t>(tokens - 1) * H, H, 1,
+                             outs, strides))
+            return rc;
+    }
+    cb_select sel{};
+    sel.logits = d->logits;
+    sel.count = m.vocab;
+    sel.partials = d->sel_partials;
+    sel.ticket = d->sel_ticket;
+    sel.candidates = d->candidates;
+    sel.sampled = d->sampled;
+    sel.position = pos;
+    sel.tokens = tokens;
+    sel.seed0 = s.seed0;
+    sel.seed1 = s.seed1;
+    sel.top_k = s.top_k ? s.top_k : 1;
+    sel.temperature = s.temperature;
+    sel.top_p = s.top_p;
+    sel.min_p = s.min_p;
+    sel.log_min_p = s.min_p > 0.0f ? std::log(s.min_p) : 0.0f;
+    return launched(select_run(sel, d->stream, true), "step: select");
+}
+
+bool same_sampling(const cb_sampling& a, const cb_sampling& b) { return std::memcmp(&a, &b, sizeof a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flags, cb_decoder** out) {
+    (void)flags;
+    if (!m || !out || !m->layer) return fail(CB_ERROR_INVALID, "cb_decoder_create: null argument");
+    *out = nullptr;
+    if (m->layers == 0 || m->hidden == 0 || m->hidden % 32 != 0 || m->hidden > 4096)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: hidden width %u", m->hidden);
+    if (m->head_dim != 64 && m->head_dim != 128 && m->head_dim != 256)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: head dimension %u is not 64, 128 or 256", m->head_dim);
+    if (m->kv_heads == 0 || m->query_heads % m->kv_heads != 0)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: %u query heads do not share %u kv heads evenly",
+                    m->query_heads, m->kv_heads);
+    if (m->vocab < 64) return fail(CB_ERROR_BUILD, "cb_decoder_create: a vocabulary under the 64 candidates");
+    if (m->context == 0 || max_step_tokens == 0 || max_step_tokens > 4096)
+        return fail(CB_ERROR_BUILD, "cb_decoder_create: context %u, step tokens %u", m->context, max_step_tokens);
+    cb_decoder* d = new (std::nothrow) cb_decoder();
+    if (!d) return fail(CB_ERROR_BUILD, "cb_decoder_create: out of host memory");
+    d->model = *m;
+    d->max_tokens = max_step_tokens;
+    d->sms = sm_count();
+    auto bail = [&](int rc) { cb_decoder_destroy(d); return rc; };
+    if (d->sms <= 0) return bail(fail(CB_ERROR_BUILD, "cb_decoder_create: no CUDA device"));
+    cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return bail(fail_cuda(e, "cb_decoder_create: stream"));
+    const uint32_t H = m->hidden, dh = m->head_dim, T = max_step_tokens;
+    if (int rc = upload_weight(d, &d->token_embd, m->token_embd, "token_embd")) return bail(rc);
+    if (int rc = upload_weight(d, &d->output, m->output, "output")) return bail(rc);
+    if (int rc = upload_f32(d, &d->output_norm, m->output_norm, H)) return bail(rc);
+    if (int rc = upload_f32(d, &d->factors, m->rope_factors, dh / 2)) return bail(rc);
+    d->layers.resize(m->layers);
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        const cb_layer_weights& s = m->layer[l];
+        DevLayer& L = d->layers[l];
+        const char* names[7] = {"q", "k", "v", "o", "gate", "up", "down"};
+        const cb_weight* srcs[7] = {&s.q, &s.k, &s.v, &s.o, &s.gate, &s.up, &s.down};
+        DevWeight* dsts[7] = {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down};
+        for (int i = 0; i < 7; ++i) {
+            if (srcs[i]->rows == 0) return bail(fail(CB_ERROR_BUILD, "cb_decoder_create: layer %u has no %s", l, names[i]));
+            if (int rc = upload_weight(d, dsts[i], *srcs[i], names[i])) return bail(rc);
+        }
+        if (L.q.format != L.k.format || L.q.format != L.v.format || L.gate.format != L.up.format)
+            return bail(fail(CB_ERROR_BUILD, "cb_decoder_create: layer %u's fused members differ in format", l));
+        if (int rc = upload_f32(d, &L.attn_norm, s.attn_norm, H)) return bail(rc);
+        if (int rc = upload_f32(d, &L.ffn_norm, s.ffn_norm, H)) return bail(rc);
+        if (int rc = upload_f32(d, &L.post_attn_norm, s.post_attn_norm, H)) return bail(rc);
+        if (int rc = upload_f32(d, &L.post_ffn_norm, s.post_ffn_norm, H)) return bail(rc);
+        if (int rc = upload_f32(d, &L.q_norm, s.q_norm, dh)) return bail(rc);
+        if (int rc = upload_f32(d, &L.k_norm, s.k_norm, dh)) return bail(rc);
+        if (!L.attn_norm || !L.ffn_norm) return bail(fail(CB_ERROR_BUILD, "cb_decoder_create: layer %u norms", l));
+        std::vector<float> turns(dh / 2);
+        cb_rope_turns(s.rope_base, dh, turns.data());
+        if (int rc = upload_f32(d, &L.turns, turns.data(), dh / 2)) return bail(rc);
+        L.window = s.window ? s.window : m->context;
+        // A sliding-window layer keeps a ring of its window and a step
+        // (kv.h:13-34); a global layer the whole context.
+        const uint64_t ring = static_cast<uint64_t>(L.window) + T;
+        L.slots = static_cast<uint32_t>(L.window < m->context && ring < m->context ? ring : m->context);
+        const size_t cache = static_cast<size_t>(L.slots) * m->kv_heads * dh;
+        if (int rc = dalloc(d, &L.key_cache, cache)) return bail(rc);
+        if (int rc = dalloc(d, &L.value_cache, cache)) return bail(rc);
+    }
+    d->max_chunks = (m->context + 63u) / 64u;
+    const size_t qd = static_cast<size_t>(m->query_heads) * dh, kvd = static_cast<size_t>(m->kv_heads) * dh;
+    if (int rc = dalloc(d, &d->hidden, static_cast<size_t>(T) * H)) return bail(rc);
+    if (int rc = dalloc(d, &d->normed, static_cast<size_t>(T) * H)) return bail(rc);
+    if (int rc = dalloc(d, &d->q, T * qd)) return bail(rc);
+    if (int rc = dalloc(d, &d->k, T * kvd)) return bail(rc);
+    if (int rc = dalloc(d, &d->v, T * kvd)) return bail(rc);
+    if (int rc = dalloc(d, &d->att, T * qd)) return bail(rc);
+    if (int rc = dalloc(d, &d->out, static_cast<size_t>(T) * H)) return bail(rc);
+    if (int rc = dalloc(d, &d->act, static_cast<size_t>(T) * m->ffn)) return bail(rc);
+    if (int rc = dalloc(d, &d->logits, m->vocab)) return bail(rc);
+    if (int rc = dalloc(d, &d->partials, static_cast<size_t>(d->max_chunks) * T * qd)) return bail(rc);
+    if (int rc = dalloc(d, &d->stats, static_cast<size_t>(d->max_chunks) * T * m->query_heads * 2)) return bail(rc);
+    const uint32_t tickets = cb_attention_tickets(T, m->query_heads, m->kv_heads);
+    if (int rc = dalloc(d, &d->tickets, tickets)) return bail(rc);
+    if (int rc = dalloc(d, &d->sel_partials, static_cast<size_t>(select_tiles(m->vocab)) * 128)) return bail(rc);
+    if (int rc = dalloc(d, &d->sel_ticket, 1)) return bail(rc);
+    if (int rc = dalloc(d, &d->candidates, 128)) return bail(rc);
+    if (int rc = dalloc(d, &d->sampled, 4)) return bail(rc);
+    if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
+    if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
+    e = cudaMemset(d->tickets, 0, tickets * sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(d->sel_ticket, 0, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(d->state, 0, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(d->sampled, 0, 4 * sizeof(uint32_t));
+    if (e != cudaSuccess) return bail(fail_cuda(e, "cb_decoder_create: memset"));
+    *out = d;
+    return CB_OK;
+}
+
+void cb_decoder_destroy(cb_decoder* d) {
+    if (!d) return;
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
+    for (void* p : d->allocations) cudaFree(p);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    delete d;
+}
+
+int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, uint32_t position, uint32_t logits,
+                    const cb_sampling* s, uint32_t* record_host) {
+    if (!d || !ids_host || tokens == 0) return fail(CB_ERROR_INVALID, "cb_decoder_step: null argument or no tokens");
+    if (tokens > d->max_tokens)
+        return fail(CB_ERROR_INVALID, "cb_decoder_step: %u tokens over the step's %u", tokens, d->max_tokens);
+    if (static_cast<uint64_t>(position) + tokens > d->model.context)
+        return fail(CB_ERROR_STEP, "cb_decoder_step: positions past the context of %u", d->model.context);
+    for (uint32_t i = 0; i < tokens; ++i)
+        if (ids_host[i] >= d->model.vocab) return fail(CB_ERROR_INVALID, "cb_decoder_step: token %u", ids_host[i]);
+    const cb_sampling greedy{0, 0, 1, 0.0f, 1.0f, 0.0f};
+    const uint32_t st[2] = {position, 0};
+    cudaError_t e = cudaMemcpyAsync(d->ids, ids_host, tokens * sizeof(uint32_t), cudaMemcpyHostToDevice, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: upload");
+    if (int rc = enqueue_step(d, tokens, false, logits != 0, s ? *s : greedy)) return rc;
+    if (logits && record_host) {
+        e = cudaMemcpyAsync(record_host, d->sampled, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: readback");
+    }
+    e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step");
+    d->has_step = logits != 0;
+    d->next_position = position + tokens;
+    return cb_fault_check(nullptr);
+}
+
+int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uint32_t* tokens_host,
+                        uint32_t* failed_host) {
+    if (!d || !tokens_host) return fail(CB_ERROR_INVALID, "cb_decoder_generate: null argument");
+    if (!d->has_step) return fail(CB_ERROR_INVALID, "cb_decoder_generate: no drawn token to feed");
+    if (steps == 0) return CB_OK;
+    const cb_sampling greedy{0, 0, 1, 0.0f, 1.0f, 0.0f};
+    const cb_sampling smp = s ? *s : greedy;
+    cudaError_t e;
+    if (steps > d->gen_capacity) {
+        const uint32_t cap = steps < 4096 ? 4096 : steps;
+        if (int rc = dalloc(d, &d->gen_tokens, cap)) return rc;
+        if (int rc = dalloc(d, &d->gen_failed, cap)) return rc;
+        d->gen_capacity = cap;
+        if (d->decode_graph) { cudaGraphExecDestroy(d->decode_graph); d->decode_graph = nullptr; }
+    }
+    if (d->decode_graph && !same_sampling(smp, d->graph_sampling)) {
+        cudaGraphExecDestroy(d->decode_graph);
+        d->decode_graph = nullptr;
+    }
+    if (static_cast<uint64_t>(d->next_position) + steps > d->model.context)
+        return fail(CB_ERROR_STEP, "cb_decoder_generate: positions past the context of %u", d->model.context);
+    if (!d->decode_graph) {
+        cudaGraph_t g = nullptr;
+        e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: capture");
+        int rc = enqueue_step(d, 1, true, true, smp);
+        if (rc == CB_OK) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1);
+            cfg.blockDim = dim3(1);
+            cfg.stream = d->stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, advance_kernel, d->state, static_cast<const uint32_t*>(d->sampled),
+                                   d->gen_tokens, d->gen_failed, d->gen_capacity);
+            if (e != cudaSuccess) rc = fail_cuda(e, "cb_decoder_generate: advance");
+        }
+        const cudaError_t end = cudaStreamEndCapture(d->stream, &g);
+        if (rc != CB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+        if (end != cudaSuccess) return fail_cuda(end, "cb_decoder_generate: end capture");
+        e = cudaGraphInstantiate(&d->decode_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: instantiate");
+        d->graph_sampling = smp;
+    }
+    // Fed steps start after the last step's tokens; the closing launch of
+    // each advances the position and counts the step.
+    const uint32_t st[2] = {d->next_position, 0};
+    e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: state");
+    for (uint32_t i = 0; i < steps; ++i) {
+        e = cudaGraphLaunch(d->decode_graph, d->stream);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: launch");
+    }
+    e = cudaMemcpyAsync(tokens_host, d->gen_tokens, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess && failed_host)
+        e = cudaMemcpyAsync(failed_host, d->gen_failed, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate");
+    d->next_position += steps;
+    return cb_fault_check(nullptr);
+}
+
+int cb_decoder_logits(cb_decoder* d, float* logits_host) {
+    if (!d || !logits_host) return fail(CB_ERROR_INVALID, "cb_decoder_logits: null argument");
+    const cudaError_t e = cudaMemcpy(logits_host, d->logits, d->model.vocab * sizeof(float), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? CB_OK : fail_cuda(e, "cb_decoder_logits");
+}
+
+const float* cb_decoder_device_logits(cb_decoder* d) { return d ? d->logits : nullptr; }
+
+}  // extern "C"

@@ -249,6 +249,91 @@ CB_API uint32_t cb_select_tiles(uint32_t count);
 /* Flags of the kernel entry points above. */
 enum { CB_RUN_PDL = 1u };
 
+/* ---- weight layout ------------------------------------------------------------
+ * The device layout of a weight piece (src/core/formats/device_layout.h:
+ * 121-136; Q6_K repacked as src/core/formats/q6_k/q6_k.h:9-21 describes),
+ * made on the host from the file's stored blocks — what the reference's
+ * PieceWriter writes (src/core/residency/piece_writer.h). `piece_host`
+ * holds cb_piece_bytes(format, blocks) bytes (the stored size rounded up to
+ * 16). */
+CB_API size_t cb_piece_bytes(uint32_t format, uint64_t blocks);
+CB_API int cb_piece_from_stored(uint32_t format, const void* stored_host, uint64_t blocks, void* piece_host);
+
+/* ---- a whole decoder ------------------------------------------------------------
+ * The pass the reference's graph builds (src/core/graph/graph.cpp: embed,
+ * per layer attention then gated feed-forward, output) for Qwen3, Llama 3
+ * and Gemma 3 shaped models, run on the CUDA kernels above: weights uploaded
+ * once, an f16 KV cache per layer (a ring of window + step slots for a
+ * sliding-window layer), each step's launches in the reference's order, a
+ * decode step captured once as a CUDA graph and replayed (its position and
+ * fed token read on the device). Stands in for Program + Upload
+ * (src/core/kernels/program.h:262-331, residency/upload.h) for a caller that
+ * brings its weights as host memory. */
+typedef struct cb_weight {
+    uint32_t format;             /* CB_Q4_0, CB_Q8_0, CB_Q6_K (matmuls); rows=0: absent */
+    uint32_t rows, cols;         /* rows of cols weights (cols a multiple of the block) */
+    const void* stored_host;     /* the file's stored blocks                        */
+} cb_weight;
+
+typedef struct cb_layer_weights {
+    const float* attn_norm;      /* [hidden]                                       */
+    cb_weight q, k, v, o;
+    const float* q_norm;         /* [head_dim] or NULL (no QK-norm)                */
+    const float* k_norm;
+    const float* post_attn_norm; /* [hidden] or NULL (Gemma 3's post-norms)        */
+    const float* ffn_norm;
+    cb_weight gate, up, down;
+    const float* post_ffn_norm;
+    uint32_t window;             /* keys a query reads: the context for a global layer */
+    float rope_base;
+} cb_layer_weights;
+
+typedef struct cb_model {
+    uint32_t layers, hidden, query_heads, kv_heads, head_dim, ffn, vocab, context;
+    float epsilon, attention_scale, embed_scale;
+    uint32_t halves;             /* 1 NEOX (Qwen3, Gemma 3), 0 adjacent (Llama)   */
+    uint32_t activation;         /* CB_ACT_SILU or CB_ACT_GELU_TANH                */
+    const float* rope_factors;   /* [head_dim/2] or NULL (llama3 rope_freqs)      */
+    cb_weight token_embd;
+    const float* output_norm;
+    cb_weight output;            /* rows = 0: tied to token_embd                   */
+    const cb_layer_weights* layer;
+} cb_model;
+
+/* The draw's settings (policy::SamplingSettings through sampler::apply into
+ * the Step, src/core/kernels/interface.h:165-192). temperature 0: greedy. */
+typedef struct cb_sampling {
+    uint32_t seed0, seed1;
+    uint32_t top_k;
+    float temperature, top_p, min_p;
+} cb_sampling;
+
+typedef struct cb_decoder cb_decoder;
+
+/* Uploads the model and allocates its caches and working buffers for steps
+ * of up to max_step_tokens (the reference's prefill block is 512). */
+CB_API int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flags, cb_decoder** out);
+CB_API void cb_decoder_destroy(cb_decoder* d);
+
+/* One step (Program::run(Step)): `tokens` ids from host memory at
+ * `position`; with `logits`, the last token's head, top-k and draw, its
+ * 16-byte record {token, failed, u, 0} copied to record_host. Synchronous. */
+CB_API int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, uint32_t position,
+                           uint32_t logits, const cb_sampling* s, uint32_t* record_host);
+
+/* `steps` fed decode steps after the last step (each reads the last draw's
+ * token on the device), from one CUDA graph replayed back to back; the
+ * drawn tokens (and each step's failed flag) copied to tokens_host. */
+CB_API int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uint32_t* tokens_host,
+                               uint32_t* failed_host);
+
+/* The last step's logits [vocab] to host memory. */
+CB_API int cb_decoder_logits(cb_decoder* d, float* logits_host);
+
+/* Device pointers of the decoder's working buffers, for callers that feed
+ * it from their own kernels: the logits [vocab] and the sampled record [4]. */
+CB_API const float* cb_decoder_device_logits(cb_decoder* d);
+
 #ifdef __cplusplus
 }
 #endif
