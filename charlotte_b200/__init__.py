@@ -109,7 +109,8 @@ def lib() -> ctypes.CDLL:
                                     ctypes.POINTER(ctypes.c_void_p * 3), ctypes.POINTER(ctypes.c_uint32 * 3),
                                     ctypes.c_uint32, ctypes.c_void_p]
         for name, struct in (("cb_norm_run", Norm), ("cb_rope_run", Rope), ("cb_attention_run", Attention),
-                             ("cb_gather_run", Gather), ("cb_select_run", Select)):
+                             ("cb_gather_run", Gather), ("cb_select_run", Select),
+                             ("cb_select_run_static", Select)):
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(struct), ctypes.c_uint32, ctypes.c_void_p]
@@ -176,8 +177,11 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
 
 def run(kind: str, **fields) -> None:
     """Runs one kernel entry point: kind in norm, rope, attention, gather,
-    select; fields are the C struct's (tensors become device pointers)."""
-    struct = {"norm": Norm, "rope": Rope, "attention": Attention, "gather": Gather, "select": Select}[kind]
+    select, select_static; fields are the C struct's (tensors become device
+    pointers)."""
+    struct = {"norm": Norm, "rope": Rope, "attention": Attention, "gather": Gather, "select": Select,
+              "select_static": Select}[kind]
+    fn = {"select_static": "cb_select_run_static"}.get(kind, f"cb_{kind}_run")
     stream = fields.pop("stream", None)
     flags = fields.pop("flags", 0)
     v = struct()
@@ -185,7 +189,7 @@ def run(kind: str, **fields) -> None:
         if hasattr(value, "data_ptr"):
             value = value.data_ptr()
         setattr(v, name, value)
-    check(getattr(lib(), f"cb_{kind}_run")(ctypes.byref(v), flags, _stream(stream)))
+    check(getattr(lib(), fn)(ctypes.byref(v), flags, _stream(stream)))
 
 
 def rope_turns(base: float, head_dim: int):

@@ -246,6 +246,19 @@ typedef struct cb_select {
 CB_API int cb_select_run(const cb_select* s, uint32_t flags, void* stream);
 CB_API uint32_t cb_select_tiles(uint32_t count);
 
+/* cb_select_run for callers that cannot allocate device memory — a host
+ * that plans every device byte up front against a budget, code where
+ * cudaMalloc is not allowed or would stall the device, a plugin whose host
+ * owns the allocator. No counterpart in the reference (its selection's
+ * buffers are planned working buffers). Same inputs, outputs and results as
+ * cb_select_run; `partials` and `ticket` must be NULL: the scratch is a
+ * fixed 128 KiB array inside the library (every GPU that loads the library
+ * holds it until the process exits), so count is at most 262,144. Allocates
+ * nothing. The first call on a device looks up the array's address (make it
+ * before any stream capture). All calls share the array: calls that overlap
+ * on the GPU race — order them on one stream. */
+CB_API int cb_select_run_static(const cb_select* s, uint32_t flags, void* stream);
+
 /* Flags of the kernel entry points above. */
 enum { CB_RUN_PDL = 1u };
 

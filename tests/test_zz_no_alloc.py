@@ -1,0 +1,55 @@
+"""cb_select_run_static — top-k and the draw for callers that cannot
+allocate device memory (their host plans every device byte up front, or
+cudaMalloc is not allowed where they run) — against cb_select_run, the entry
+point that takes caller-allocated scratch. Through the C ABI, two calls in a
+row, each's candidates and sampled record identical bit for bit (the
+tolerance every selection test here uses). Collected last on purpose: it
+runs on its own in a fresh process, and after every other test."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import charlotte_b200 as cb
+
+pytestmark = pytest.mark.gpu
+
+
+def _select(kind, logits, position, **settings):
+    count = logits.numel()
+    cand = torch.zeros(128, dtype=torch.int32, device="cuda")
+    rec = torch.zeros(4, dtype=torch.int32, device="cuda")
+    scratch = {}
+    if kind == "select":
+        scratch = dict(partials=torch.zeros(cb.lib().cb_select_tiles(count) * 128, dtype=torch.int32, device="cuda"),
+                       ticket=torch.zeros(1, dtype=torch.int32, device="cuda"))
+    min_p = settings.get("min_p", 0.0)
+    cb.run(kind, logits=logits, count=count, candidates=cand, sampled=rec, position=0, position0=position, tokens=1,
+           seed0=settings.get("seed0", 0), seed1=settings.get("seed1", 0), top_k=settings.get("top_k", 40),
+           temperature=settings.get("temperature", 0.0), top_p=settings.get("top_p", 1.0), min_p=min_p,
+           log_min_p=math.log(min_p) if min_p > 0 else 0.0, **scratch)
+    torch.cuda.synchronize()
+    cb.check(cb.lib().cb_fault_check(None))
+    return cand.cpu().numpy(), rec.cpu().numpy()
+
+
+def test_static_scratch_matches_caller_scratch_twice_in_a_row(cuda):
+    rng = np.random.default_rng(2026)
+    calls = [
+        (151936, 10, dict(temperature=0.0, top_k=1)),                                   # greedy, Qwen3's vocabulary
+        (262144, 11, dict(temperature=0.8, top_k=40, top_p=0.9, min_p=0.05, seed0=3)),  # the largest it holds
+    ]
+    for count, position, settings in calls:
+        logits = torch.from_numpy((rng.standard_normal(count) * 4).astype(np.float32)).cuda()
+        want_cand, want_rec = _select("select", logits, position, **settings)
+        got_cand, got_rec = _select("select_static", logits, position, **settings)
+        np.testing.assert_array_equal(got_cand, want_cand)
+        np.testing.assert_array_equal(got_rec, want_rec)
+
+
+def test_static_scratch_refuses_what_it_cannot_hold(cuda):
+    logits = torch.zeros(262145, dtype=torch.float32, device="cuda")
+    with pytest.raises(cb.CharlotteError) as e:
+        _select("select_static", logits, 0)
+    assert e.value.status == cb.ERROR_INVALID and "262144" in str(e.value)
