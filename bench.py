@@ -294,8 +294,12 @@ def run_ours(args):
         "gpu_launches": len(gs.items) * args.steps,
         "clocks": clocks.summary(),
     }
+    if not args.no_decode:
+        result["qwen3_decode"] = decode_bench(args.decode_steps, 512, SEED + 7 + rank, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        if "qwen3_decode" in result:
+            result["qwen3_decode"]["cpu_baseline"] = cpu_decode_baseline(SEED + 7)
     if rank == 0:
         print(json.dumps(result), flush=True)
     del graph
@@ -334,6 +338,74 @@ def run_e2e(gs, stream, steps, world):
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
     return {"value": round(gs.bytes * world / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4)}
+
+
+def decode_bench(steps, prompt_len, seed, world):
+    """Qwen3-0.6B greedy decode, a 512-token prompt then `steps`
+    fed decode steps (one CUDA graph replayed), random-init weights."""
+    import torch
+    from charlotte_b200 import model as M
+    arch = M.qwen3_0_6b(context=4096)
+    m = M.synthesize(arch, seed=seed)
+    dec = M.Decoder(m, max_step_tokens=512)
+    rng = np.random.default_rng(seed + 1)
+    prompt = rng.integers(0, arch.vocab, prompt_len).astype(np.uint32)
+    t0 = time.perf_counter()
+    rec = dec.prefill(prompt)
+    prefill_s = time.perf_counter() - t0
+    dec.generate(4)   # capture and warm the decode graph
+    # restart from the prompt so the timed run is the configured one
+    rec = dec.prefill(prompt)
+    barrier(world)
+    toks, failed, dev_ms = dec.generate(steps, timed=True)
+    dev_ms = max_over_ranks(dev_ms, world)
+    # e2e: the same steps driven from the host one at a time through
+    # cb_decoder_step (each step: the token id host->device, the 16-byte
+    # record device->host), after the same prompt.
+    rec = dec.prefill(prompt)
+    tok = int(rec[0])
+    barrier(world)
+    t0 = time.perf_counter()
+    host_toks = []
+    for i in range(steps):
+        r = dec.step(np.array([tok], np.uint32), prompt_len + i)
+        tok = int(r[0])
+        host_toks.append(tok)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    dec.close()
+    return {
+        "workload": "qwen3-0.6b greedy decode (configs[2]): 512-token prompt, %d steps, f16 KV, context 4096" % steps,
+        "tok_s": round(steps * world / (dev_ms * 1e-3), 1),
+        "ms_per_token": round(dev_ms / steps, 4),
+        "launches_per_token": 4 + 8 * arch.layers + 1,
+        "prefill_512_ms_wall": round(prefill_s * 1e3, 1),
+        "host_driven_matches_graph": bool(host_toks == toks.tolist()),
+        "failed_steps": int(failed.sum()),
+        "e2e": {"value": round(steps * world / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 16, "how": "cb_decoder_step per token from host ids, record read back"},
+    }
+
+
+def cpu_decode_baseline(seed):
+    """The oracle's pass (the reference's order of operations) on all host
+    cores: a 16-token prompt then 4 decode steps of Qwen3-0.6B."""
+    from charlotte_b200 import model as M
+    from oracle.model import OracleDecoder
+    m = M.synthesize(M.qwen3_0_6b(context=64), seed=seed)
+    od = OracleDecoder(m)
+    rng = np.random.default_rng(seed + 1)
+    rec, _ = od.step(rng.integers(0, 151936, 16).astype(np.uint32), 0, logits=False)
+    rec, _ = od.step([1], 16)
+    t0 = time.perf_counter()
+    n = 4
+    tok = rec[0]
+    for i in range(n):
+        rec, _ = od.step([tok], 17 + i)
+        tok = rec[0]
+    el = time.perf_counter() - t0
+    od.close()
+    return {"value": round(n / el, 2), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"Qwen3-0.6B decode, 4 steps after 17 positions, oracle, {os.cpu_count()} threads, {el:.1f} s"}
 
 
 def read_peaks():
@@ -452,10 +524,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--case", default=None, help="profile one product: format:rows:K")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--case", default=None, help="profile one product (format:rows:K) or 'decode'")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
-    if args.case:
+    if args.case == "decode":
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(decode_bench(args.decode_steps, 512, SEED + 7, 1)))
+    elif args.case:
         run_case(args.case, args.steps)
     elif args.impl == "reference":
         run_reference(args)

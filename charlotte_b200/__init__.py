@@ -119,6 +119,8 @@ def lib() -> ctypes.CDLL:
         L.cb_attention_tickets.argtypes = [ctypes.c_uint32] * 3
         L.cb_select_tiles.restype = ctypes.c_uint32
         L.cb_select_tiles.argtypes = [ctypes.c_uint32]
+        L.cb_select_tickets.restype = ctypes.c_uint32
+        L.cb_select_tickets.argtypes = [ctypes.c_uint32]
         _lib = L
     return _lib
 

@@ -89,6 +89,8 @@ int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream) {
 
 uint32_t cb_select_tiles(uint32_t count) { return select_tiles(count); }
 
+uint32_t cb_select_tickets(uint32_t count) { return 1u + (select_tiles(count) + 15u) / 16u; }
+
 int cb_select_run(const cb_select* s, uint32_t flags, void* stream) {
     if (!s || !s->logits || !s->partials || !s->ticket || !s->candidates || !s->sampled)
         return fail(CB_ERROR_INVALID, "cb_select_run: null argument");

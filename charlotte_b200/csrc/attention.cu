@@ -15,13 +15,16 @@
 // exactly nothing (a zero weight's product added to a sum that is never −0),
 // so they are skipped.
 //
-// B200 mapping: one CTA a (kv head, chunk, tile of rows): the chunk's 64
-// keys and values staged in shared memory once for all its G·rows queries;
-// a thread a (query, key) score; a thread a query for the sequential softmax
-// steps; threads over (query, dimension) for P·V. Every CTA writes its
-// chunk's partial state; the last CTA of a (row tile, kv head) to finish —
-// found by an atomic ticket, no waiting — folds the chunks in order and
-// resets the ticket. So a decode step is one launch, split over every chunk
+// B200 mapping: CTAs a (kv head, tile of rows), at most 16 of them striding
+// over the tile's live chunks; each chunk's 64 keys and values staged in
+// shared memory once for all its G·rows queries;
+// a thread a (query, key) score; a warp a query for the softmax (the tile's
+// max and exponentials across lanes, the in-order sums by one lane);
+// threads over (query, dimension) for P·V. Every live CTA writes its
+// chunk's partial state; the last of the tile's live chunks to finish —
+// found by an atomic ticket, no waiting — folds them in order and resets
+// the ticket. CTAs of chunks no row reaches (the grid spans the context, so
+// a decode graph replays at any position) leave at once. So a decode step is one launch, split over every chunk
 // (flash-decoding), and a prefill step the same launch with more row tiles.
 #include <cuda_runtime.h>
 
@@ -63,53 +66,82 @@ __device__ __forceinline__ uint32_t earliest_of(uint32_t p, uint32_t window) {
     return p + 1u > window ? p + 1u - window : 0u;
 }
 
+constexpr uint32_t kChunkSlots = 16;   // CTAs a (kv head, row tile) takes, striding over its live chunks
+
+// Stages keys and values j_lo..j_hi-1 (absolute positions) of the chunk at
+// key0 into its shared tiles.
+__device__ __forceinline__ void stage_keys(const AttentionArgs& a, uint16_t* ks, uint16_t* vs, uint32_t key0,
+                                           uint32_t j_lo, uint32_t j_hi, uint32_t kvh, uint32_t d) {
+    const uint32_t words = d / 8u;   // uint4 per key row
+    const uint32_t b_lo = j_lo - key0, n = (j_hi - j_lo) * words;
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n; i += kAttnThreads) {
+        const uint32_t b = b_lo + i / words, w = i % words;
+        const size_t at = (static_cast<size_t>((key0 + b) % a.slots) * a.kv_heads + kvh) * d;
+        reinterpret_cast<uint4*>(ks + b * d)[w] = reinterpret_cast<const uint4*>(a.key_cache + at)[w];
+        reinterpret_cast<uint4*>(vs + b * d)[w] = reinterpret_cast<const uint4*>(a.value_cache + at)[w];
+    }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    grid_dependency_wait();
     const uint32_t d = a.head_dim;
     const uint32_t B = 2048u / d;
     const uint32_t tiles = kChunk / B;
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
     const uint32_t G = geo.G;
     const uint32_t kvh = blockIdx.x;
-    const uint32_t c = blockIdx.y;
     const uint32_t rt = blockIdx.z;
+    // The step's position was written before the launches preceding this one
+    // (by the host, or by the last step's closing launch), so it is read
+    // before the dependency wait, as are the keys of earlier steps.
     const uint32_t pos0 = a.position ? *a.position : a.position0;
     const uint32_t row0 = rt * geo.rows_per_tile;
     const uint32_t rows = min(geo.rows_per_tile, a.tokens - row0);
     const uint32_t Q = rows * G;
-    const uint32_t key0 = c * kChunk;
+    const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
 
     uint16_t* ks = reinterpret_cast<uint16_t*>(smem);
     uint16_t* vs = ks + kChunk * d;
     float* qs = reinterpret_cast<float*>(vs + kChunk * d);
     float* ps = qs + kMaxQueries * d;                 // [Q][64]
     float* alpha = ps + kMaxQueries * kChunk;         // [Q][8]
-    float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l, live
+    float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l
 
-    // Does any of the tile's rows have a live key in this chunk?
+    // The tile's live chunks: every chunk some row's keys reach.
     const uint32_t p_first = pos0 + row0, p_last = pos0 + row0 + rows - 1u;
-    const bool any = key0 <= p_last && key0 + kChunk > earliest_of(p_first, a.window);
-    if (any) {
-        // Stage the chunk's keys and values (keys past p_last are never live).
-        const uint32_t words = d / 8u;   // uint4 per key row
-        for (uint32_t i = threadIdx.x; i < kChunk * words; i += kAttnThreads) {
-            const uint32_t b = i / words, w = i % words;
-            const uint32_t j = key0 + b;
-            uint4 kv = make_uint4(0, 0, 0, 0), vv = kv;
-            if (j <= p_last) {
-                const size_t at = (static_cast<size_t>(j % a.slots) * a.kv_heads + kvh) * d;
-                kv = reinterpret_cast<const uint4*>(a.key_cache + at)[w];
-                vv = reinterpret_cast<const uint4*>(a.value_cache + at)[w];
-            }
-            reinterpret_cast<uint4*>(ks + b * d)[w] = kv;
-            reinterpret_cast<uint4*>(vs + b * d)[w] = vv;
-        }
-        // Queries m = r·G + g: row r, head kvh·G + g, scaled into log2 units.
-        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
-            const uint32_t m = i / d, e = i % d;
-            const uint32_t r = m / G, h = kvh * G + m % G;
-            qs[m * d + e] = a.query[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] * a.scale_log2e;
+    const uint32_t live_first = earliest_of(p_first, a.window) / kChunk;
+    const uint32_t live_chunks = p_last / kChunk - live_first + 1u;
+    if (blockIdx.y >= live_chunks) {   // no chunk for this slot: no ticket either
+        grid_dependency_wait();
+        return;
+    }
+    // This slot's first chunk's keys of earlier steps (below pos0), staged
+    // while the launch before this one (rope) finishes.
+    const uint32_t c_first = live_first + blockIdx.y;
+    {
+        const uint32_t key0 = c_first * kChunk;
+        const uint32_t j_hi = min(key0 + kChunk, max(pos0, key0));
+        if (j_hi > key0) stage_keys(a, ks, vs, key0, key0, j_hi, kvh, d);
+    }
+    grid_dependency_wait();
+
+    // Queries m = r·G + g: row r, head kvh·G + g, scaled into log2 units.
+    for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+        const uint32_t m = i / d, e = i % d;
+        const uint32_t r = m / G, h = kvh * G + m % G;
+        qs[m * d + e] = a.query[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] * a.scale_log2e;
+    }
+    for (uint32_t c = c_first; c <= p_last / kChunk; c += gridDim.y) {
+        const uint32_t key0 = c * kChunk;
+        const bool first_chunk = c == c_first;
+        if (!first_chunk) __syncthreads();   // the last chunk's reads of ks, vs, ps are done
+        // The chunk's keys this step wrote (for later chunks, all of them);
+        // positions past p_last are never live and are not staged.
+        {
+            const uint32_t j_lo = first_chunk ? max(key0, min(pos0, key0 + kChunk)) : key0;
+            const uint32_t j_hi = min(key0 + kChunk, p_last + 1u);
+            if (j_hi > j_lo) stage_keys(a, ks, vs, key0, j_lo, j_hi, kvh, d);
         }
         __syncthreads();
         // Scores: s = Σ_w dot(q_w, k_w) in quads, in order.
@@ -121,6 +153,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             if (j <= p && j >= earliest_of(p, a.window)) {
                 const float4* q4 = reinterpret_cast<const float4*>(qs + m * d);
                 const uint2* k4 = reinterpret_cast<const uint2*>(ks + b * d);
+#pragma unroll 8
                 for (uint32_t w = 0; w < d / 4u; ++w) {
                     const uint2 kw = k4[w];
                     const float4 kk = make_float4(fp16_bits_to_f32(kw.x & 0xFFFF), fp16_bits_to_f32(kw.x >> 16),
@@ -131,58 +164,62 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             ps[m * kChunk + b] = s;
         }
         __syncthreads();
-        // The online softmax, a thread a query, tile by tile in key order.
-        for (uint32_t m = threadIdx.x; m < Q; m += kAttnThreads) {
+    // The online softmax, a warp a query, tile by tile in key order: the
+        // tile's top (a max: any order gives its bits) and each live key's
+        // 2^(s − top) across lanes; the sum of a tile's weights, and the
+        // running l and m, by lane 0 in key order.
+        for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
             const uint32_t p = pos0 + row0 + m / G;
             const uint32_t early = earliest_of(p, a.window);
             bool chunk_live = false;
             float chunk_m = 0.0f, chunk_l = 0.0f;
             for (uint32_t t = 0; t < tiles; ++t) {
-                float top_tile = 0.0f;
-                bool seen = false;
-                for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
-                    const uint32_t j = key0 + b;
-                    if (j <= p && j >= early) {
-                        const float s = ps[m * kChunk + b];
-                        top_tile = seen ? fmaxf(top_tile, s) : s;
-                        seen = true;
-                    }
-                }
+                const uint32_t b = t * B + lane;
+                const uint32_t j = key0 + b;
+                const bool live = lane < B && j <= p && j >= early;
+                const float s = live ? ps[m * kChunk + b] : 0.0f;
+                float top_tile = live ? s : -INFINITY;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) top_tile = fmaxf(top_tile, __shfl_xor_sync(0xFFFFFFFFu, top_tile, o));
+                const bool seen = __any_sync(0xFFFFFFFFu, live);
                 float al = 1.0f;
                 if (seen) {
                     const float old = chunk_live ? chunk_m : top_tile;
                     chunk_live = true;
                     const float top = fmaxf(old, top_tile);
                     al = old == top ? 1.0f : exp2_np(old - top);
-                    float sum = 0.0f;
-                    for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
-                        const uint32_t j = key0 + b;
-                        float e = 0.0f;
-                        if (j <= p && j >= early) e = exp2_np(ps[m * kChunk + b] - top);
-                        ps[m * kChunk + b] = e;
-                        sum = sum + e;
-                    }
+                    const float e = live ? exp2_np(s - top) : 0.0f;
+                    if (lane < B) ps[m * kChunk + b] = e;
+                    float sum = 0.0f;   // in key order, on every lane alike
+                    for (uint32_t i = 0; i < B; ++i) sum = sum + __shfl_sync(0xFFFFFFFFu, e, i);
                     chunk_l = fmaf(chunk_l, al, sum);
                     chunk_m = top;
-                } else {
-                    for (uint32_t b = t * B; b < (t + 1u) * B; ++b) ps[m * kChunk + b] = 0.0f;
+                } else if (lane < B) {
+                    ps[m * kChunk + b] = 0.0f;
                 }
-                alpha[m * 8u + t] = al;
+                if (lane == 0) alpha[m * 8u + t] = al;
             }
-            stat[m * 4u + 0] = chunk_m;
-            stat[m * 4u + 1] = chunk_live ? chunk_l : 0.0f;
+            if (lane == 0) {
+                stat[m * 4u + 0] = chunk_m;
+                stat[m * 4u + 1] = chunk_live ? chunk_l : 0.0f;
+            }
         }
         __syncthreads();
         // O = O·a_t, then fma(p_b, v_b, O) in key order; the chunk's partial.
         for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
             const uint32_t m = i / d, e = i % d;
             float o = 0.0f;
+            // A key of weight 0 (not live for this query) adds exactly
+            // nothing — fma(0, v, o) = o for the finite values the cache
+            // holds — so the loop needs no test; keys past p_last, never
+            // staged, are left out.
+            const uint32_t valid = min(kChunk, p_last + 1u - key0);
             for (uint32_t t = 0; t < tiles; ++t) {
                 o = o * alpha[m * 8u + t];
-                for (uint32_t b = t * B; b < (t + 1u) * B; ++b) {
-                    const float pb = ps[m * kChunk + b];
-                    if (pb != 0.0f) o = fmaf(pb, fp16_bits_to_f32(vs[b * d + e]), o);
-                }
+                const uint32_t b_end = min((t + 1u) * B, valid);
+#pragma unroll 8
+                for (uint32_t b = t * B; b < b_end; ++b)
+                    o = fmaf(ps[m * kChunk + b], fp16_bits_to_f32(vs[b * d + e]), o);
             }
             const uint32_t r = m / G, h = kvh * G + m % G;
             const size_t at = (static_cast<size_t>(c) * a.tokens + row0 + r) * a.query_heads + h;
@@ -195,38 +232,59 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     }
     grid_dependents_launch();
 
-    // The last CTA of this (row tile, kv head) folds the chunks in order.
+    // The last of the tile's chunk CTAs to finish folds the chunks in order.
     __shared__ unsigned int last;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned int* ticket = a.tickets + rt * a.kv_heads + kvh;
         const unsigned int seen = atomicAdd(ticket, 1u);
-        last = seen == gridDim.y - 1u;
+        last = seen == min(gridDim.y, live_chunks) - 1u;
         if (last) *ticket = 0u;   // ready for the next step
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // Stage every live chunk's (m, l) for the tile's queries in shared memory.
+    float* fstat = reinterpret_cast<float*>(smem);   // [chunks][Q][2], over ks/vs
+    for (uint32_t i = threadIdx.x; i < live_chunks * Q; i += kAttnThreads) {
+        const uint32_t cc = live_first + i / Q, m = i % Q;
+        const uint32_t r = m / G, h = kvh * G + m % G;
+        const size_t at = (static_cast<size_t>(cc) * a.tokens + row0 + r) * a.query_heads + h;
+        fstat[2u * i] = __ldcg(a.stats + at * 2u);
+        fstat[2u * i + 1u] = __ldcg(a.stats + at * 2u + 1u);
+    }
+    __syncthreads();
     for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
         const uint32_t m = i / d, e = i % d;
         const uint32_t r = m / G, h = kvh * G + m % G;
         const uint32_t p = pos0 + row0 + r;
+        const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
         bool live = false;
         float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
-        for (uint32_t cc = earliest_of(p, a.window) / kChunk; cc <= p / kChunk; ++cc) {
-            const size_t at = (static_cast<size_t>(cc) * a.tokens + row0 + r) * a.query_heads + h;
-            const float cm = __ldcg(a.stats + at * 2u), cl = __ldcg(a.stats + at * 2u + 1u);
-            const float co = __ldcg(a.partials + at * d + e);
-            float fa, fb, fm;
-            if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
-            else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
-            else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
-            else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
-            run_l = fmaf(run_l, fa, cl * fb);
-            o = fmaf(o, fa, co * fb);
-            run_m = fm;
-            live = true;
+        for (uint32_t cc = c0; cc <= c1; cc += 4u) {
+            // four chunks' partials in flight at once, then folded in order
+            float co[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const size_t at = (static_cast<size_t>(cc + k) * a.tokens + row0 + r) * a.query_heads + h;
+                co[k] = cc + k <= c1 ? __ldcg(a.partials + at * d + e) : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (cc + k > c1) break;
+                const uint32_t si = (cc + k - live_first) * Q + m;
+                const float cm = fstat[2u * si], cl = fstat[2u * si + 1u];
+                float fa, fb, fm;
+                if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
+                else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
+                else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
+                else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
+                run_l = fmaf(run_l, fa, cl * fb);
+                o = fmaf(o, fa, co[k] * fb);
+                run_m = fm;
+                live = true;
+            }
         }
         a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
     }
@@ -241,8 +299,11 @@ uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_
 
 cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
-    const size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
-                        kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
+    size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
+                  kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
+    const size_t fold = static_cast<size_t>(a.max_chunks) * kMaxQueries * 2u * sizeof(float);   // the fold's stats
+    if (fold > smem) smem = fold;
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -250,7 +311,8 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads, a.max_chunks, (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
+    cfg.gridDim = dim3(a.kv_heads, a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots,
+                       (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

@@ -93,8 +93,10 @@ struct cb_decoder {
     uint32_t* gen_tokens = nullptr;  // generate's drawn tokens
     uint32_t* gen_failed = nullptr;
     uint32_t gen_capacity = 0;
-    cudaGraphExec_t decode_graph = nullptr;
+    cudaGraphExec_t decode_graph = nullptr;   // fed step + advance (generate)
     cb_sampling graph_sampling{};
+    cudaGraphExec_t step_graph = nullptr;     // one host-fed token with logits (step)
+    cb_sampling step_sampling{};
     bool has_step = false;
     uint32_t next_position = 0;   // the position after the last step's tokens
 };
@@ -288,6 +290,36 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
 
 bool same_sampling(const cb_sampling& a, const cb_sampling& b) { return std::memcmp(&a, &b, sizeof a) == 0; }
 
+// Captures one decode step (one token, logits and draw) as a graph: fed
+// (the token is the last draw) and closed by `advance` for generate, or
+// reading its token from the ids buffer for a host-driven step.
+int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return fail_cuda(e, "decoder: capture");
+    int rc = enqueue_step(d, 1, fed, true, smp);
+    if (rc == CB_OK && fed) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1);
+        cfg.blockDim = dim3(1);
+        cfg.stream = d->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, advance_kernel, d->state, static_cast<const uint32_t*>(d->sampled),
+                               d->gen_tokens, d->gen_failed, d->gen_capacity);
+        if (e != cudaSuccess) rc = fail_cuda(e, "decoder: advance");
+    }
+    const cudaError_t end = cudaStreamEndCapture(d->stream, &g);
+    if (rc != CB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+    if (end != cudaSuccess) return fail_cuda(end, "decoder: end capture");
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return e == cudaSuccess ? CB_OK : fail_cuda(e, "decoder: instantiate");
+}
+
 }  // namespace
 
 extern "C" {
@@ -368,13 +400,13 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
     const uint32_t tickets = cb_attention_tickets(T, m->query_heads, m->kv_heads);
     if (int rc = dalloc(d, &d->tickets, tickets)) return bail(rc);
     if (int rc = dalloc(d, &d->sel_partials, static_cast<size_t>(select_tiles(m->vocab)) * 128)) return bail(rc);
-    if (int rc = dalloc(d, &d->sel_ticket, 1)) return bail(rc);
+    if (int rc = dalloc(d, &d->sel_ticket, cb_select_tickets(m->vocab))) return bail(rc);
     if (int rc = dalloc(d, &d->candidates, 128)) return bail(rc);
     if (int rc = dalloc(d, &d->sampled, 4)) return bail(rc);
     if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
     e = cudaMemset(d->tickets, 0, tickets * sizeof(unsigned int));
-    if (e == cudaSuccess) e = cudaMemset(d->sel_ticket, 0, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(d->sel_ticket, 0, cb_select_tickets(m->vocab) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->state, 0, 2 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(d->sampled, 0, 4 * sizeof(uint32_t));
     if (e != cudaSuccess) return bail(fail_cuda(e, "cb_decoder_create: memset"));
@@ -386,6 +418,7 @@ void cb_decoder_destroy(cb_decoder* d) {
     if (!d) return;
     if (d->stream) cudaStreamSynchronize(d->stream);
     if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
+    if (d->step_graph) cudaGraphExecDestroy(d->step_graph);
     for (void* p : d->allocations) cudaFree(p);
     if (d->stream) cudaStreamDestroy(d->stream);
     delete d;
@@ -405,7 +438,22 @@ int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, ui
     cudaError_t e = cudaMemcpyAsync(d->ids, ids_host, tokens * sizeof(uint32_t), cudaMemcpyHostToDevice, d->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: upload");
-    if (int rc = enqueue_step(d, tokens, false, logits != 0, s ? *s : greedy)) return rc;
+    const cb_sampling smp = s ? *s : greedy;
+    if (tokens == 1 && logits) {
+        // A decode step: the captured graph, replayed.
+        if (d->step_graph && !same_sampling(smp, d->step_sampling)) {
+            cudaGraphExecDestroy(d->step_graph);
+            d->step_graph = nullptr;
+        }
+        if (!d->step_graph) {
+            if (int rc = capture_step(d, false, smp, &d->step_graph)) return rc;
+            d->step_sampling = smp;
+        }
+        e = cudaGraphLaunch(d->step_graph, d->stream);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: launch");
+    } else if (int rc = enqueue_step(d, tokens, false, logits != 0, smp)) {
+        return rc;
+    }
     if (logits && record_host) {
         e = cudaMemcpyAsync(record_host, d->sampled, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
         if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: readback");
@@ -418,7 +466,7 @@ int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, ui
 }
 
 int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uint32_t* tokens_host,
-                        uint32_t* failed_host) {
+                        uint32_t* failed_host, float* device_ms) {
     if (!d || !tokens_host) return fail(CB_ERROR_INVALID, "cb_decoder_generate: null argument");
     if (!d->has_step) return fail(CB_ERROR_INVALID, "cb_decoder_generate: no drawn token to feed");
     if (steps == 0) return CB_OK;
@@ -439,30 +487,7 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
     if (static_cast<uint64_t>(d->next_position) + steps > d->model.context)
         return fail(CB_ERROR_STEP, "cb_decoder_generate: positions past the context of %u", d->model.context);
     if (!d->decode_graph) {
-        cudaGraph_t g = nullptr;
-        e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
-        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: capture");
-        int rc = enqueue_step(d, 1, true, true, smp);
-        if (rc == CB_OK) {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(1);
-            cfg.blockDim = dim3(1);
-            cfg.stream = d->stream;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            e = cudaLaunchKernelEx(&cfg, advance_kernel, d->state, static_cast<const uint32_t*>(d->sampled),
-                                   d->gen_tokens, d->gen_failed, d->gen_capacity);
-            if (e != cudaSuccess) rc = fail_cuda(e, "cb_decoder_generate: advance");
-        }
-        const cudaError_t end = cudaStreamEndCapture(d->stream, &g);
-        if (rc != CB_OK) { if (g) cudaGraphDestroy(g); return rc; }
-        if (end != cudaSuccess) return fail_cuda(end, "cb_decoder_generate: end capture");
-        e = cudaGraphInstantiate(&d->decode_graph, g, 0);
-        cudaGraphDestroy(g);
-        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: instantiate");
+        if (int rc = capture_step(d, true, smp, &d->decode_graph)) return rc;
         d->graph_sampling = smp;
     }
     // Fed steps start after the last step's tokens; the closing launch of
@@ -470,14 +495,26 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
     const uint32_t st[2] = {d->next_position, 0};
     e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: state");
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    if (device_ms) {
+        for (auto& x : ev)
+            if ((e = cudaEventCreate(&x)) != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: event");
+        cudaEventRecord(ev[0], d->stream);
+    }
     for (uint32_t i = 0; i < steps; ++i) {
         e = cudaGraphLaunch(d->decode_graph, d->stream);
         if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: launch");
     }
+    if (device_ms) cudaEventRecord(ev[1], d->stream);
     e = cudaMemcpyAsync(tokens_host, d->gen_tokens, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess && failed_host)
         e = cudaMemcpyAsync(failed_host, d->gen_failed, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (device_ms) {
+        if (e == cudaSuccess) e = cudaEventElapsedTime(device_ms, ev[0], ev[1]);
+        cudaEventDestroy(ev[0]);
+        cudaEventDestroy(ev[1]);
+    }
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate");
     d->next_position += steps;
     return cb_fault_check(nullptr);

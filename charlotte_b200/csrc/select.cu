@@ -12,10 +12,12 @@
 // the reference's candidates, in its order.
 //
 // B200 mapping: one launch. Each CTA sorts a tile of 1,024 keys (bitonic, in
-// shared memory) and writes its top 64; the last CTA to finish (an atomic
-// ticket, no waiting) merges the tiles' sorted lists pairwise, round by
-// round, by rank, then runs the draw on the 64 candidates and writes the
-// 16-byte sampled record. The ticket is reset for the next step.
+// shared memory) and writes its top 64. The last CTA of each group of 16
+// tiles to finish (an atomic ticket, no waiting) merges the group's sorted
+// lists pairwise by rank; the last group to finish merges the groups' lists
+// the same way and runs the draw on the 64 candidates, writing the 16-byte
+// sampled record. Tickets (one a group and one overall) are reset for the
+// next step.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -31,7 +33,8 @@ namespace {
 constexpr uint32_t kTile = 1024;
 constexpr uint32_t kKeep = 64;
 constexpr uint32_t kSelThreads = 1024;
-constexpr uint32_t kMaxTiles = 256;   // vocabularies up to 262,144
+constexpr uint32_t kMaxTiles = 256;   // vocabularies up to 262,144 (the partials a caller provides)
+constexpr uint32_t kGroup = 16;       // tiles a first-level merge takes (256 tiles: 16 groups)
 
 __device__ __forceinline__ uint64_t entry_key(uint32_t bits, uint32_t id) {
     return (static_cast<uint64_t>(key_of(bits)) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - id);
@@ -61,8 +64,9 @@ __device__ void sort_tile(uint64_t* keys) {
     }
 }
 
-__device__ __forceinline__ uint32_t count_greater(const uint64_t* list, uint64_t v, bool or_equal) {
-    // list descending, 64 long: how many come before v
+// How many of a descending 64-key list come before v (ties: list first
+// when `or_equal`), by binary search.
+__device__ __forceinline__ uint32_t count_before(const uint64_t* list, uint64_t v, bool or_equal) {
     uint32_t lo = 0, hi = kKeep;
     while (lo < hi) {
         const uint32_t mid = (lo + hi) >> 1;
@@ -70,6 +74,56 @@ __device__ __forceinline__ uint32_t count_greater(const uint64_t* list, uint64_t
         if (before) lo = mid + 1; else hi = mid;
     }
     return lo;
+}
+
+// Merges `lists` descending 64-key lists held in `src` (shared memory)
+// pairwise, round by round, each output the pair's top 64 by rank; the
+// result is left in src[0..63]. `dst` holds lists/2 + 1 lists.
+__device__ void merge_lists(uint64_t* src, uint64_t* dst, uint32_t lists) {
+    const uint32_t t = threadIdx.x;
+    while (lists > 1) {
+        const uint32_t out_lists = (lists + 1u) / 2u;
+        for (uint32_t i = t; i < out_lists * 2u * kKeep; i += kSelThreads) {
+            const uint32_t pair = i / (2u * kKeep), w = i % (2u * kKeep);
+            const uint64_t* A = src + (2u * pair) * kKeep;
+            uint64_t* out = dst + pair * kKeep;
+            if (2u * pair + 1u >= lists) {   // an odd list out passes through
+                if (w < kKeep) out[w] = A[w];
+                continue;
+            }
+            const uint64_t* Bl = A + kKeep;
+            uint32_t pos;
+            uint64_t v;
+            if (w < kKeep) { v = A[w]; pos = w + count_before(Bl, v, false); }
+            else { v = Bl[w - kKeep]; pos = (w - kKeep) + count_before(A, v, true); }
+            if (pos < kKeep) out[pos] = v;
+        }
+        __syncthreads();
+        for (uint32_t i = t; i < out_lists * kKeep; i += kSelThreads) src[i] = dst[i];
+        __syncthreads();
+        lists = out_lists;
+    }
+}
+
+// Takes this CTA's ticket among `of`; true for the last to arrive (which
+// resets the ticket for the next step).
+__device__ __forceinline__ bool last_to_arrive(unsigned int* ticket, uint32_t of, unsigned int* flag) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int seen = atomicAdd(ticket, 1u);
+        *flag = seen == of - 1u;
+        if (*flag) *ticket = 0u;
+    }
+    __syncthreads();
+    const bool last = *flag != 0u;
+    if (last) __threadfence();
+    return last;
+}
+
+__device__ __forceinline__ uint64_t load_key(const uint32_t* pairs, uint32_t i) {
+    const uint32_t bits = __ldcg(pairs + 2u * i), id = __ldcg(pairs + 2u * i + 1u);
+    return id == 0xFFFFFFFFu ? 0ull : entry_key(bits, id);
 }
 
 __device__ __forceinline__ uint32_t philox_word0(uint32_t c0, uint32_t k0, uint32_t k1) {
@@ -86,7 +140,7 @@ __device__ __forceinline__ uint32_t philox_word0(uint32_t c0, uint32_t k0, uint3
 }
 
 __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
-    extern __shared__ __align__(16) uint64_t buf[];   // 16,384 + 8,192 keys
+    extern __shared__ __align__(16) uint64_t buf[];   // a tile of keys
     __shared__ unsigned int last;
     grid_dependency_wait();
     const uint32_t t = threadIdx.x;
@@ -101,47 +155,27 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
     sort_tile(buf);
     if (t < kKeep) entry_pair(buf[t], a.partials + 2u * (tile * kKeep + t));
     grid_dependents_launch();
-    __threadfence();
-    __syncthreads();
-    if (t == 0) {
-        const unsigned int seen = atomicAdd(a.ticket, 1u);
-        last = seen == gridDim.x - 1u;
-        if (last) *a.ticket = 0u;
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
 
-    // Merge the tiles' sorted lists pairwise, round by round.
-    uint32_t lists = gridDim.x;
-    uint64_t* src = buf;
-    uint64_t* dst = buf + kMaxTiles * kKeep;
-    for (uint32_t i = t; i < lists * kKeep; i += kSelThreads) {
-        const uint32_t bits = __ldcg(a.partials + 2u * i), id = __ldcg(a.partials + 2u * i + 1u);
-        src[i] = id == 0xFFFFFFFFu ? 0ull : entry_key(bits, id);
-    }
+    // Level 1: the last tile of each group of kGroup merges the group's
+    // lists into the group's first slot. Level 2: the last group merges the
+    // groups' lists. Both merge pairwise by rank (merge_lists).
+    __shared__ unsigned int flag;
+    const uint32_t group = tile / kGroup;
+    const uint32_t groups = (gridDim.x + kGroup - 1u) / kGroup;
+    const uint32_t in_group = min(kGroup, gridDim.x - group * kGroup);
+    if (!last_to_arrive(a.ticket + 1u + group, in_group, &flag)) return;
+    uint64_t* work = buf;                   // kGroup lists
+    uint64_t* tmp = buf + kGroup * kKeep;   // half as many
+    for (uint32_t i = t; i < in_group * kKeep; i += kSelThreads) work[i] = load_key(a.partials, group * kGroup * kKeep + i);
     __syncthreads();
-    while (lists > 1) {
-        const uint32_t out_lists = (lists + 1u) / 2u;
-        for (uint32_t i = t; i < out_lists * 2u * kKeep; i += kSelThreads) {
-            const uint32_t pair = i / (2u * kKeep), w = i % (2u * kKeep);
-            const uint64_t* A = src + (2u * pair) * kKeep;
-            uint64_t* out = dst + pair * kKeep;
-            if (2u * pair + 1u >= lists) {   // an odd list out passes through
-                if (w < kKeep) out[w] = A[w];
-                continue;
-            }
-            const uint64_t* Bl = A + kKeep;
-            uint32_t pos;
-            uint64_t v;
-            if (w < kKeep) { v = A[w]; pos = w + count_greater(Bl, v, false); }
-            else { v = Bl[w - kKeep]; pos = (w - kKeep) + count_greater(A, v, true); }
-            if (pos < kKeep) out[pos] = v;
-        }
-        __syncthreads();
-        uint64_t* tmp = src; src = dst; dst = tmp;
-        lists = out_lists;
-    }
+    merge_lists(work, tmp, in_group);
+    if (t < kKeep) entry_pair(work[t], a.partials + 2u * (group * kGroup * kKeep + t));
+    if (!last_to_arrive(a.ticket, groups, &flag)) return;
+    for (uint32_t i = t; i < groups * kKeep; i += kSelThreads)
+        work[i] = load_key(a.partials, (i / kKeep) * kGroup * kKeep + i % kKeep);
+    __syncthreads();
+    merge_lists(work, tmp, groups);
+    uint64_t* src = work;
     // src[0..63]: the candidates, in the reference's order.
     __shared__ uint32_t cand[2 * kKeep];
     __shared__ float weight[kKeep], tempered[kKeep], running[kKeep];
@@ -214,7 +248,7 @@ uint32_t select_tiles(uint32_t count) { return (count + kTile - 1u) / kTile; }
 cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl) {
     const uint32_t tiles = select_tiles(a.count);
     if (tiles == 0 || tiles > kMaxTiles) return cudaErrorInvalidValue;
-    const size_t smem = (kMaxTiles * kKeep + (kMaxTiles / 2u) * kKeep) * sizeof(uint64_t);
+    const size_t smem = (kTile > kGroup * kKeep * 3 / 2 ? kTile : kGroup * kKeep * 3 / 2) * sizeof(uint64_t);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -2,7 +2,7 @@
 // memory.
 //
 // cb_select_run needs scratch beside its inputs and outputs: each
-// 1,024-logit tile's 64 candidates, and a ticket word that finds the tile
+// 1,024-logit tile's 64 candidates, and ticket words that find the tiles
 // finishing last. Most callers hand in buffers they allocated once. Some
 // cannot: a host that plans every byte of device memory up front and counts
 // it against a budget (as Charlotte's residency plan does for every working
@@ -11,13 +11,13 @@
 // synchronize the device); a plugin whose host owns the allocator. For them,
 // cb_select_run_static keeps its scratch in a fixed array compiled into the
 // library: 128 KiB of candidates (256 tiles, vocabularies up to 262,144)
-// and the ticket word, held by every GPU that loads the library until the
+// and its ticket words, held by every GPU that loads the library until the
 // process exits. It allocates nothing.
 //
 // The first call on a device looks up the array's device address
 // (cudaGetSymbolAddress, with that device current) and keeps it; make that
 // first call before any stream capture. Every call shares the one array,
-// which keeps the last call's contents: each call clears the ticket before
+// which keeps the last call's contents: each call clears the tickets before
 // its launch, and calls that overlap on the GPU (on two streams at once)
 // race on the array — order them on one stream.
 #include <cuda_runtime.h>
@@ -36,7 +36,8 @@ constexpr uint32_t kStaticCount = kStaticTiles * 1024u;
 constexpr uint32_t kCandidateWords = kStaticTiles * 64u * 2u;   // (bits, token) pairs
 constexpr uint32_t kTicketWord = kCandidateWords;             // after the candidates
 
-// The scratch: every tile's candidates, then the ticket (and padding).
+// The scratch: every tile's candidates, then the tickets (at most 17 words
+// of the 64).
 static __device__ __align__(256) uint32_t g_select_scratch[kCandidateWords + 64u];
 
 constexpr int kMaxDevices = 64;
@@ -79,8 +80,8 @@ int cb_select_run_static(const cb_select* s, uint32_t flags, void* stream) {
     a.partials = base;
     a.ticket = reinterpret_cast<unsigned int*>(base + kTicketWord);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(a.ticket, 0, sizeof(unsigned int), st);
-    if (e != cudaSuccess) return cb::fail_cuda(e, "cb_select_run_static: clearing the ticket");
+    cudaError_t e = cudaMemsetAsync(a.ticket, 0, cb_select_tickets(s->count) * sizeof(unsigned int), st);
+    if (e != cudaSuccess) return cb::fail_cuda(e, "cb_select_run_static: clearing the tickets");
     e = cb::select_run(a, st, (flags & CB_RUN_PDL) != 0);
     return e == cudaSuccess ? CB_OK : cb::fail_cuda(e, "cb_select_run_static");
 }

@@ -248,7 +248,7 @@ class Decoder:
                                       ctypes.c_uint32, ctypes.POINTER(CSampling), ctypes.c_void_p]
         L.cb_decoder_generate.restype = ctypes.c_int
         L.cb_decoder_generate.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(CSampling),
-                                          ctypes.c_void_p, ctypes.c_void_p]
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)]
         L.cb_decoder_logits.restype = ctypes.c_int
         L.cb_decoder_logits.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         self.lib = L
@@ -289,13 +289,16 @@ class Decoder:
             rec = self.step(part, position + at, logits=at + part.size >= ids.size, sampling=sampling)
         return rec
 
-    def generate(self, steps: int, sampling: CSampling | None = None):
+    def generate(self, steps: int, sampling: CSampling | None = None, timed: bool = False):
+        """Fed greedy (or sampled) decode steps as one replayed CUDA graph.
+        Returns (tokens, failed) or, when timed, (tokens, failed, device_ms)."""
         toks = np.zeros(steps, np.uint32)
         failed = np.zeros(steps, np.uint32)
         s = sampling or self.sampling()
+        ms = ctypes.c_float(0.0)
         _check(self.lib.cb_decoder_generate(self.handle, steps, ctypes.byref(s), toks.ctypes.data,
-                                            failed.ctypes.data))
-        return toks, failed
+                                            failed.ctypes.data, ctypes.byref(ms) if timed else None))
+        return (toks, failed, ms.value) if timed else (toks, failed)
 
     def logits(self) -> np.ndarray:
         out = np.empty(self.model.arch.vocab, np.float32)

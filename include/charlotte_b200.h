@@ -227,8 +227,9 @@ CB_API int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream);
  * (src/core/sampler/sampler.h:274): the 64 largest logits under the
  * reference's total order as (bits, token) candidates, then the draw
  * (temperature 0: candidate 0) into the 16-byte record {token, failed, u, 0}.
- * `partials` holds cb_select_tiles(count)·128 words, `ticket` one zeroed
- * word. count ≤ 262,144. */
+ * `partials` holds cb_select_tiles(count)·128 words, `ticket`
+ * cb_select_tickets(count) zeroed words (left zero after each run).
+ * count ≤ 262,144. */
 typedef struct cb_select {
     const float* logits;
     uint32_t count;
@@ -245,6 +246,7 @@ typedef struct cb_select {
 } cb_select;
 CB_API int cb_select_run(const cb_select* s, uint32_t flags, void* stream);
 CB_API uint32_t cb_select_tiles(uint32_t count);
+CB_API uint32_t cb_select_tickets(uint32_t count);
 
 /* cb_select_run for callers that cannot allocate device memory — a host
  * that plans every device byte up front against a budget, code where
@@ -336,9 +338,10 @@ CB_API int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tok
 
 /* `steps` fed decode steps after the last step (each reads the last draw's
  * token on the device), from one CUDA graph replayed back to back; the
- * drawn tokens (and each step's failed flag) copied to tokens_host. */
+ * drawn tokens (and each step's failed flag) copied to tokens_host. With
+ * device_ms, the replays' device time (CUDA events around them). */
 CB_API int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uint32_t* tokens_host,
-                               uint32_t* failed_host);
+                               uint32_t* failed_host, float* device_ms);
 
 /* The last step's logits [vocab] to host memory. */
 CB_API int cb_decoder_logits(cb_decoder* d, float* logits_host);

@@ -232,7 +232,7 @@ def select(logits, **draw):
     count = logits.size
     tiles = cb.lib().cb_select_tiles(count)
     partials = torch.zeros(tiles * 128, dtype=torch.int32, device="cuda")
-    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ticket = torch.zeros(cb.lib().cb_select_tickets(count), dtype=torch.int32, device="cuda")
     cand = torch.zeros(128, dtype=torch.int32, device="cuda")
     rec = torch.zeros(4, dtype=torch.int32, device="cuda")
     min_p = draw.get("min_p", 0.0)

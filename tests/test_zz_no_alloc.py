@@ -23,7 +23,7 @@ def _select(kind, logits, position, **settings):
     scratch = {}
     if kind == "select":
         scratch = dict(partials=torch.zeros(cb.lib().cb_select_tiles(count) * 128, dtype=torch.int32, device="cuda"),
-                       ticket=torch.zeros(1, dtype=torch.int32, device="cuda"))
+                       ticket=torch.zeros(cb.lib().cb_select_tickets(count), dtype=torch.int32, device="cuda"))
     min_p = settings.get("min_p", 0.0)
     cb.run(kind, logits=logits, count=count, candidates=cand, sampled=rec, position=0, position0=position, tokens=1,
            seed0=settings.get("seed0", 0), seed1=settings.get("seed1", 0), top_k=settings.get("top_k", 40),
