@@ -496,19 +496,20 @@ def run_reference(args):
 
 def run_case(spec, iters):
     """One product launched `iters` times (for profiling): spec is
-    format:rows:K[:epilogue], e.g. q4_0:1024:2048 or q6_k:151936:1024."""
+    format:rows:K[:tokens], e.g. q4_0:1024:2048 or q4_0:4096:1024:512."""
     import torch
     import charlotte_b200 as cb
     fmt_name, rows, K, *rest = spec.split(":")
     fmt = {"q4_0": Q4_0, "q6_k": Q6_K, "q8_0": 8}[fmt_name]
     rows, K = int(rows), int(K)
+    tokens = int(rest[0]) if rest else 1
     torch.cuda.set_device(0)
     rng = np.random.default_rng(SEED)
     stored = synth.blocks(rng, fmt, rows, K)
     nb = stored.size // synth.BLOCK_BYTES[fmt]
     piece = torch.from_numpy(synth.to_piece(fmt, stored)).cuda()
-    x = torch.from_numpy(synth.activations(rng, 1, K)).cuda()
-    y = torch.zeros((1, rows), dtype=torch.float32, device="cuda")
+    x = torch.from_numpy(synth.activations(rng, tokens, K)).cuda()
+    y = torch.zeros((tokens, rows), dtype=torch.float32, device="cuda")
     for _ in range(iters):
         cb.matmul(fmt, K, [(piece, nb, 0, rows, 0)], x, [y])
     torch.cuda.synchronize()

@@ -124,6 +124,8 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
         return fail(CB_ERROR_INVALID, "cb_matmul_run: the tensor-core form is not built in this library version");
     if (tokens == 0) return CB_OK;
     if (x_stride < m->columns) return fail(CB_ERROR_INVALID, "cb_matmul_run: x_stride %u < columns", x_stride);
+    if (!aligned16(x) || x_stride % 4 != 0)
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: x must be 16-byte aligned with a stride of whole float4s");
     MatmulArgs a{};
     a.format = m->format;
     a.columns = m->columns;
@@ -165,7 +167,9 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
     }
     const int sms = sm_count();
     if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
-    cudaError_t e = matmul_decode(a, sms, static_cast<cudaStream_t>(stream), (flags & CB_MATMUL_PDL) != 0);
+    const bool pdl = (flags & CB_MATMUL_PDL) != 0;
+    cudaError_t e = tokens >= kTiledMinTokens ? matmul_tiled(a, sms, static_cast<cudaStream_t>(stream), pdl)
+                                              : matmul_decode(a, sms, static_cast<cudaStream_t>(stream), pdl);
     if (e != cudaSuccess) return fail_cuda(e, "cb_matmul_run: launch");
     return CB_OK;
 }

@@ -45,6 +45,13 @@ struct MatmulArgs {
 // reference's per-output order. PDL when `pdl`.
 cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
 
+// Tiled form over a step of `tokens` rows of x: the same sums, bit for bit,
+// as a register-tiled GEMM on the CUDA cores. PDL when `pdl`.
+cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
+
+// Steps of at least this many tokens take the tiled form.
+constexpr uint32_t kTiledMinTokens = 8;
+
 // Shared memory the decode form needs at its smallest batch, for a width.
 size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns);
 
