@@ -298,6 +298,7 @@ uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_
 }
 
 cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+    if (a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a)) return attention_prefill_run(a, stream, pdl);
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
     size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
                   kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;

@@ -22,6 +22,11 @@ cudaError_t norm_run(const NormArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t rope_run(const RopeArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads);
+// The many-query form (attention_prefill.cu): same bits, a CTA per query tile.
+bool attention_prefill_fits(const AttentionArgs& a);
+cudaError_t attention_prefill_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+// Steps of at least this many rows take the many-query form.
+constexpr uint32_t kPrefillAttentionRows = 32;
 cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl);
 uint32_t select_tiles(uint32_t count);

@@ -155,7 +155,9 @@ def f16_cache(rng, slots, hkv, d, scale=1.0):
 
 
 @pytest.mark.parametrize("case", ATT, ids=[f"d{c[0]}_{c[1]}x{c[2]}_w{min(c[3], 9999)}" for c in ATT])
-@pytest.mark.parametrize("position,tokens", [(0, 1), (63, 1), (64, 1), (700, 1), (1000, 5), (40, 30)])
+# steps of 32 rows or more take the many-query (prefill) kernel: same bits
+@pytest.mark.parametrize("position,tokens", [(0, 1), (63, 1), (64, 1), (700, 1), (1000, 5), (40, 30),
+                                             (0, 64), (40, 100), (500, 33), (1000, 130)])
 def test_attention_bit_exact(cuda, case, position, tokens):
     d, hq, hkv, window = case
     rng = np.random.default_rng(position * 7 + tokens + d)
