@@ -523,51 +523,69 @@ def run_case(spec, iters):
 SWEEP_SHAPES = [("qkv", 4096, 1024), ("o", 1024, 2048), ("gate_up", 6144, 1024), ("down", 1024, 3072)]
 SWEEP_M = [1, 16, 128, 512, 2048]
 BYTES_PER_WEIGHT = {2: 18 / 32, 8: 34 / 32, 14: 210 / 256}
+FORMAT_NAME = {2: "Q4_0", 8: "Q8_0", 14: "Q6_K"}
 
 
-def sweep_bench(iters=20, warmup=3, flags=0):
+def graph_time_ms(launch, n):
+    """Mean device ms of `launch(i)` for i in range(n), captured once as a CUDA
+    graph (no host launch cost in the timing) and replayed after a warm
+    replay, timed with CUDA events on the replay stream."""
+    import torch
+    launch(0)   # first calls outside capture (kernel attributes)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            launch(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / n
+
+
+def sweep_bench(iters=20, flags=0, ms=None, formats=(8, 2, 14), head=True):
     """the Qwen3-shape product sweep. Each (format, shape, M):
-    `iters` launches timed with CUDA events after `warmup`, weights rotated
-    over copies totalling more than 2x L2 so that every launch reads them
-    from HBM. Reports GB/s (weights + x + y) and TFLOP/s (2MNK)."""
+    `iters` launches in a CUDA graph, weights rotated over copies totalling
+    more than 2x L2 so that every launch reads them from HBM. Reports GB/s
+    (weights + x + y) and TFLOP/s (2MNK)."""
     import torch
     import charlotte_b200 as cb
     torch.cuda.set_device(0)
     rng = np.random.default_rng(SEED + 3)
-    cases = [(fmt, name, rows, K) for fmt in (8, 2, 14) for name, rows, K in SWEEP_SHAPES]
-    cases.append((14, "head", VOCAB, HIDDEN))
+    cases = [(fmt, name, rows, K) for fmt in formats for name, rows, K in SWEEP_SHAPES]
+    if head:
+        cases.append((14, "head", VOCAB, HIDDEN))
     rows_out = []
     for fmt, name, rows, K in cases:
         stored = synth.blocks(rng, fmt, rows, K)
         nb = stored.size // synth.BLOCK_BYTES[fmt]
         piece = torch.from_numpy(synth.to_piece(fmt, stored)).cuda()
-        wbytes = piece.numel()
-        copies = max(1, min(64, int(np.ceil(256e6 / wbytes))))
+        copies = max(1, min(64, int(np.ceil(256e6 / piece.numel()))))
         pieces = [piece] + [piece.clone() for _ in range(copies - 1)]
-        for M in SWEEP_M:
+        for M in (ms or SWEEP_M):
             x = torch.from_numpy(synth.activations(rng, M, K)).cuda()
             y = torch.empty((M, rows), dtype=torch.float32, device="cuda")
-            for i in range(warmup):
+            n = iters if M * rows < 2048 * 8192 else 4
+
+            def launch(i):
                 cb.matmul(fmt, K, [(pieces[i % copies], nb, 0, rows, 0)], x, [y], flags=flags)
-            torch.cuda.synchronize()
-            n = iters if M < 2048 or rows < VOCAB else 5
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(n):
-                cb.matmul(fmt, K, [(pieces[i % copies], nb, 0, rows, 0)], x, [y], flags=flags)
-            e1.record()
-            torch.cuda.synchronize()
+            t = graph_time_ms(launch, n)
             cb.check(cb.lib().cb_fault_check(None))
-            ms = e0.elapsed_time(e1) / n
             nbytes = rows * K * BYTES_PER_WEIGHT[fmt] + 4 * M * (K + rows)
-            rows_out.append({"format": {2: "Q4_0", 8: "Q8_0", 14: "Q6_K"}[fmt], "product": name, "N": rows, "K": K,
-                             "M": M, "us": round(ms * 1e3, 2), "gbs": round(nbytes / ms / 1e6, 1),
-                             "tflops": round(2 * M * rows * K / ms / 1e9, 2)})
+            rows_out.append({"format": FORMAT_NAME[fmt], "product": name, "N": rows, "K": K, "M": M,
+                             "us": round(t * 1e3, 2), "gbs": round(nbytes / t / 1e6, 1),
+                             "tflops": round(2 * M * rows * K / t / 1e9, 2)})
             del x, y
         del pieces, piece
         torch.cuda.empty_cache()
-    return {"workload": "configs[1]: Qwen3-shape product sweep, M in {1,16,128,512,2048}", "form":
-            "tensor" if flags & 2 else "exact (CUDA cores, the reference's order)", "results": rows_out}
+    form = ("tensor" if flags & 2 else "streamed" if flags & 4 else "tiled" if flags & 8 else
+            "exact, form chosen by size")
+    return {"workload": "configs[1]: Qwen3-shape product sweep", "form": form, "results": rows_out}
 
 
 def main():
@@ -585,6 +603,10 @@ def main():
     args = ap.parse_args()
     if args.case in ("sweep", "sweep-tensor"):
         print(json.dumps(sweep_bench(flags=2 if args.case == "sweep-tensor" else 0)))
+    elif args.case == "sweep-forms":
+        ms = [16, 128, 256, 512, 2048]
+        for f in (4, 8):
+            print(json.dumps(sweep_bench(flags=f, ms=ms, formats=(2,), head=False)))
     elif args.case == "decode":
         import torch
         torch.cuda.set_device(0)

@@ -19,7 +19,7 @@ LIB_PATH = os.path.join(HERE, "libcharlotte_b200.so")
 F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
 WRITE, QKV, GATED, GATED_BY_INPUT = 0, 1, 2, 3
 SILU, GELU_TANH, SIGMOID = 0, 1, 2
-MATMUL_PDL, MATMUL_TENSOR = 1, 2
+MATMUL_PDL, MATMUL_TENSOR, MATMUL_STREAMED, MATMUL_TILED = 1, 2, 4, 8
 OK, ERROR_BUILD, ERROR_STEP, ERROR_DEVICE_LOST, ERROR_CANCELLED, ERROR_INVALID = range(6)
 
 

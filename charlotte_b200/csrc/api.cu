@@ -168,8 +168,11 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
     const int sms = sm_count();
     if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
     const bool pdl = (flags & CB_MATMUL_PDL) != 0;
-    cudaError_t e = tokens >= kTiledMinTokens ? matmul_tiled(a, sms, static_cast<cudaStream_t>(stream), pdl)
-                                              : matmul_decode(a, sms, static_cast<cudaStream_t>(stream), pdl);
+    bool tiled = tiled_form(tokens, m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : total);
+    if (flags & CB_MATMUL_STREAMED) tiled = false;
+    if (flags & CB_MATMUL_TILED) tiled = true;
+    cudaError_t e = tiled ? matmul_tiled(a, sms, static_cast<cudaStream_t>(stream), pdl)
+                          : matmul_decode(a, sms, static_cast<cudaStream_t>(stream), pdl);
     if (e != cudaSuccess) return fail_cuda(e, "cb_matmul_run: launch");
     return CB_OK;
 }

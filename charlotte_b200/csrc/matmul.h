@@ -49,8 +49,13 @@ cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
 // as a register-tiled GEMM on the CUDA cores. PDL when `pdl`.
 cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
 
-// Steps of at least this many tokens take the tiled form.
-constexpr uint32_t kTiledMinTokens = 8;
+// Which exact form a step takes by default: the streamed (decode-layout)
+// form keeps every SM busy on short steps and narrow products, the tiled
+// GEMM wins once the step has enough tiles (measured on B200: for 1,024-row
+// products from 512 tokens, for 4,096 rows and more from 256).
+inline bool tiled_form(uint32_t tokens, uint32_t slots) {
+    return tokens >= 512 || (tokens >= 256 && slots >= 4096);
+}
 
 // Shared memory the decode form needs at its smallest batch, for a width.
 size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns);

@@ -361,6 +361,259 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     }
 }
 
+// ---- several tokens a weight pass ------------------------------------------
+// The same warp layout with R = 2 (a pair of rows, or a gated output's gate
+// and up rows) and MT tokens: each weight is decoded once and multiplied
+// into MT chains, one per token, each still the reference's chain for that
+// (row, token). x of the CTA's MT tokens is staged range-major, token after
+// token. The 2·MT range-sum rows meet in shared memory, and lane slot·MT + i
+// adds row `slot`'s range sums for token i in range order.
+template <typename F, int MT>
+__device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const float4* x4, uint32_t tok4,
+                                               float (&aa)[MT], float (&ab)[MT]) {
+    const typename F::Consts ca = A.consts(), cbb = B.consts();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        float wa[4], wb[4];
+        auto dec = [&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            wa[k % 4] = fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca));
+            wb[k % 4] = fmaf(__uint_as_float(B.template magic<k>()), F::template S<k>(cbb), F::template C<k>(cbb));
+        };
+        // k = 4q .. 4q+3 as compile-time constants
+        if (q == 0) { dec(std::integral_constant<int, 0>{}); dec(std::integral_constant<int, 1>{}); dec(std::integral_constant<int, 2>{}); dec(std::integral_constant<int, 3>{}); }
+        if (q == 1) { dec(std::integral_constant<int, 4>{}); dec(std::integral_constant<int, 5>{}); dec(std::integral_constant<int, 6>{}); dec(std::integral_constant<int, 7>{}); }
+        if (q == 2) { dec(std::integral_constant<int, 8>{}); dec(std::integral_constant<int, 9>{}); dec(std::integral_constant<int, 10>{}); dec(std::integral_constant<int, 11>{}); }
+        if (q == 3) { dec(std::integral_constant<int, 12>{}); dec(std::integral_constant<int, 13>{}); dec(std::integral_constant<int, 14>{}); dec(std::integral_constant<int, 15>{}); }
+        if (q == 4) { dec(std::integral_constant<int, 16>{}); dec(std::integral_constant<int, 17>{}); dec(std::integral_constant<int, 18>{}); dec(std::integral_constant<int, 19>{}); }
+        if (q == 5) { dec(std::integral_constant<int, 20>{}); dec(std::integral_constant<int, 21>{}); dec(std::integral_constant<int, 22>{}); dec(std::integral_constant<int, 23>{}); }
+        if (q == 6) { dec(std::integral_constant<int, 24>{}); dec(std::integral_constant<int, 25>{}); dec(std::integral_constant<int, 26>{}); dec(std::integral_constant<int, 27>{}); }
+        if (q == 7) { dec(std::integral_constant<int, 28>{}); dec(std::integral_constant<int, 29>{}); dec(std::integral_constant<int, 30>{}); dec(std::integral_constant<int, 31>{}); }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            const float4 xq = x4[i * tok4 + q];
+            aa[i] = fmaf(wa[0], xq.x, aa[i]);
+            ab[i] = fmaf(wb[0], xq.x, ab[i]);
+            aa[i] = fmaf(wa[1], xq.y, aa[i]);
+            ab[i] = fmaf(wb[1], xq.y, ab[i]);
+            aa[i] = fmaf(wa[2], xq.z, aa[i]);
+            ab[i] = fmaf(wb[2], xq.z, ab[i]);
+            aa[i] = fmaf(wa[3], xq.w, aa[i]);
+            ab[i] = fmaf(wb[3], xq.w, ab[i]);
+        }
+    }
+}
+
+template <typename F, int MT>
+__global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a) {
+    constexpr int R = 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t G = a.columns / 32u;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t lane_stride = x_lane_stride(G);
+    const uint32_t tok_floats = 32u * lane_stride;   // one token's staged x
+    const uint32_t stage_bytes = RowStreams<F>::row_stage(G) * R;
+    const uint32_t batches = batch_count<R>(a);
+    const uint32_t stride = gridDim.x * kWarps;
+    const bool gated = a.epilogue == kGated;
+
+    float* xs = reinterpret_cast<float*>(smem);
+    const uint32_t x_bytes = MT * tok_floats * 4u;
+    const uint32_t warp_bytes = 16u + R * MT * kRedStride * 4u + 2u * stage_bytes;
+    uint8_t* wbase = smem + x_bytes + warp * warp_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
+    float* red = reinterpret_cast<float*>(wbase + 16);
+    uint8_t* stages = wbase + 16u + R * MT * kRedStride * 4u;
+
+    if (lane == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    const uint32_t first = blockIdx.x * kWarps + warp;
+    if (first < batches) issue_batch<F, R>(a, first, stages, &bars[0], G, lane);
+    if (first + stride < batches) issue_batch<F, R>(a, first + stride, stages + stage_bytes, &bars[1], G, lane);
+
+    grid_dependency_wait();
+
+    const uint32_t t0 = blockIdx.y * MT;
+    const uint32_t nt = min(static_cast<uint32_t>(MT), a.tokens - t0);
+    const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
+    for (uint32_t i = 0; i < MT; ++i) {
+        float4* dst = reinterpret_cast<float4*>(xs + i * tok_floats + lane * lane_stride);
+        if (i < nt) {
+            const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i) * a.x_stride);
+            for (uint32_t g = lo + warp; g < hi; g += kWarps)
+#pragma unroll
+                for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = xg[g * 8u + v];
+        } else {
+            for (uint32_t g = lo + warp; g < hi; g += kWarps)
+#pragma unroll
+                for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    __syncthreads();
+    grid_dependents_launch();
+    const float4* xl = reinterpret_cast<const float4*>(xs + lane * lane_stride);
+    const uint32_t tok4 = tok_floats / 4u;
+
+    uint32_t rb[F::kStreams], sl[F::kStreams], reg[F::kStreams];
+#pragma unroll
+    for (int q = 0; q < F::kStreams; ++q) {
+        rb[q] = RowStreams<F>::row_bytes(q, G);
+        sl[q] = RowStreams<F>::slot(q, G);
+        reg[q] = q == 0 ? 0u : reg[q - 1] + R * sl[q - 1];
+    }
+
+    uint32_t it = 0;
+    for (uint32_t b = first; b < batches; b += stride, ++it) {
+        const uint32_t s = it & 1u;
+        uint8_t* stage = stages + s * stage_bytes;
+        if (!mbar_wait(&bars[s], (it >> 1) & 1u, a.fault)) {
+            if (b + stride < batches) mbar_wait(&bars[s ^ 1u], ((it + 1) >> 1) & 1u, nullptr);
+            return;
+        }
+        const Batch bt = locate_batch<R>(a, b);
+        // Stream pointers of the batch's two rows: non-gated rows 0 and 1 of
+        // one segment; gated the gate row at slot 0 and the up row at slot 1.
+        const uint8_t* pa[F::kStreams];
+        const uint8_t* pb[F::kStreams];
+        {
+            const MemberArgs& m0 = gated ? a.member[0] : a.member[bt.member];
+#pragma unroll
+            for (int q = 0; q < F::kStreams; ++q) {
+                const uint64_t off = RowStreams<F>::base(q, m0.blocks) +
+                                     static_cast<uint64_t>(m0.first_row + bt.local) * rb[q];
+                pa[q] = stage + reg[q] + static_cast<uint32_t>(off & 15ull);
+                pb[q] = pa[q] + rb[q];
+            }
+            if (gated) {
+                const MemberArgs& m1 = a.member[1];
+#pragma unroll
+                for (int q = 0; q < F::kStreams; ++q) {
+                    const uint64_t off = RowStreams<F>::base(q, m1.blocks) +
+                                         static_cast<uint64_t>(m1.first_row + bt.local) * rb[q];
+                    pb[q] = stage + reg[q] + sl[q] + static_cast<uint32_t>(off & 15ull);
+                }
+            }
+        }
+        const bool la = bt.live > 0;
+        const bool lb = gated ? la : bt.live > 1;
+        float aa[MT], ab[MT];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) { aa[i] = 0.0f; ab[i] = 0.0f; }
+        for (uint32_t g = lo; g < hi; ++g) {
+            F A, B;
+            if (la) A.load(pa, g); else A.zero();
+            if (lb) B.load(pb, g); else B.zero();
+            chain_group_mt<F, MT>(A, B, xl + (g - lo) * 8u, tok4, aa, ab);
+        }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            red[i * kRedStride + lane] = aa[i];
+            red[(MT + i) * kRedStride + lane] = ab[i];
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (b + 2u * stride < batches) issue_batch<F, R>(a, b + 2u * stride, stage, &bars[s], G, lane);
+        // Lane slot·MT + i: row `slot`, token i, its 32 range sums in order.
+        float total = 0.0f;
+        if (lane < static_cast<uint32_t>(R * MT)) {
+            const float4* rs = reinterpret_cast<const float4*>(red + lane * kRedStride);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = rs[q];
+                total = total + v.x;
+                total = total + v.y;
+                total = total + v.z;
+                total = total + v.w;
+            }
+        }
+        const uint32_t slot = lane / MT, ti = lane % MT;
+        const uint32_t t = t0 + ti;
+        if (gated) {
+            const float up = __shfl_down_sync(0xFFFFFFFFu, total, MT);
+            if (slot == 0 && ti < nt && bt.live > 0) {
+                const uint32_t o = a.member[0].out_offset + bt.local;
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * up;
+            }
+        } else if (slot < min(bt.live, 2u) && lane < static_cast<uint32_t>(R * MT) && ti < nt) {
+            const MemberArgs& m = a.member[bt.member];
+            const uint32_t o = m.out_offset + bt.local + slot;
+            if (a.epilogue == kWrite) {
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = total;
+            } else if (a.epilogue == kQKV) {
+                a.out[bt.member][static_cast<size_t>(t) * a.out_stride[bt.member] + o] = total;
+            } else {   // kGatedByInput (matmul.wgsl:346-350)
+                const float u = a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride +
+                                             a.gate_input_column + o];
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * u;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+template <typename F, int MT>
+size_t decode_mt_smem(uint32_t G) {
+    return static_cast<size_t>(MT) * 32u * x_lane_stride(G) * 4u +
+           kWarps * (16u + 2u * MT * kRedStride * 4u + 2ull * 2u * RowStreams<F>::row_stage(G));
+}
+
+template <typename F, int MT>
+cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    const uint32_t G = a.columns / 32u;
+    const size_t smem = decode_mt_smem<F, MT>(G);
+    if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
+    const uint32_t batches = a.epilogue == kGated ? a.member[0].rows
+                                                  : [&] { uint32_t n = 0; for (uint32_t m = 0; m < a.members; ++m) n += (a.member[m].rows + 1) / 2; return n; }();
+    auto kernel = decode_mt_kernel<F, MT>;
+    static bool configured = false;   // per instantiation
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDecodeSmem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const uint32_t groups = (a.tokens + MT - 1) / MT;
+    uint32_t ctas = (batches + kWarps - 1) / kWarps;
+    uint32_t per_sm = static_cast<uint32_t>((227u * 1024u) / (smem + 1024u));
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm > 16) per_sm = 16;
+    // Enough CTAs across the token groups to fill the SMs, no more.
+    const uint32_t cap = (static_cast<uint32_t>(sm_count) * per_sm + groups - 1) / groups;
+    if (ctas > cap) ctas = cap;
+    if (ctas == 0) ctas = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas, groups);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+// Tokens a weight pass: 2, 4, 8 or 16 — the fewest that cover a short step,
+// 16 for longer ones — stepping down while x of that many tokens and the
+// stages do not fit shared memory (wide rows).
+template <typename F>
+cudaError_t dispatch_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    const uint32_t G = a.columns / 32u;
+    const size_t budget = static_cast<size_t>(kMaxDecodeSmem);
+    const uint32_t want = a.tokens > 8 ? 16u : (a.tokens > 4 ? 8u : (a.tokens > 2 ? 4u : 2u));
+    if (want >= 16 && decode_mt_smem<F, 16>(G) <= budget) return launch_decode_mt<F, 16>(a, sm_count, stream, pdl);
+    if (want >= 8 && decode_mt_smem<F, 8>(G) <= budget) return launch_decode_mt<F, 8>(a, sm_count, stream, pdl);
+    if (want >= 4 && decode_mt_smem<F, 4>(G) <= budget) return launch_decode_mt<F, 4>(a, sm_count, stream, pdl);
+    if (decode_mt_smem<F, 2>(G) <= budget) return launch_decode_mt<F, 2>(a, sm_count, stream, pdl);
+    return cudaErrorInvalidValue;
+}
+
 template <typename F, int R>
 size_t decode_smem(uint32_t G) {
     return 32ull * x_lane_stride(G) * 4u + kWarps * (16u + R * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
@@ -436,6 +689,14 @@ size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns) {
 }
 
 cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    if (a.tokens > 1) {
+        switch (a.format) {
+            case kQ4_0: return dispatch_mt<Q4_0>(a, sm_count, stream, pdl);
+            case kQ8_0: return dispatch_mt<Q8_0>(a, sm_count, stream, pdl);
+            case kQ6_K: return dispatch_mt<Q6_K>(a, sm_count, stream, pdl);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (a.format) {
         case kQ4_0: return dispatch<Q4_0>(a, sm_count, stream, pdl);
         case kQ8_0: return dispatch<Q8_0>(a, sm_count, stream, pdl);

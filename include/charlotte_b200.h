@@ -83,7 +83,12 @@ enum { CB_ACT_SILU = 0, CB_ACT_GELU_TANH = 1, CB_ACT_SIGMOID = 2 };
 /* Flags of cb_matmul_run. */
 enum {
     CB_MATMUL_PDL = 1u,      /* launch with programmatic dependent launch   */
-    CB_MATMUL_TENSOR = 2u    /* tokens > 1: the tcgen05 tensor-core form     */
+    CB_MATMUL_TENSOR = 2u,   /* tokens > 1: the tcgen05 tensor-core form     */
+    /* The exact forms give the same bits; these pick one (for benchmarks):
+     * STREAMED decodes each weight once a pass of up to 16 tokens (decode
+     * GEMV layout), TILED is the register-tiled GEMM. Default: by size. */
+    CB_MATMUL_STREAMED = 4u,
+    CB_MATMUL_TILED = 8u
 };
 
 typedef struct cb_member {

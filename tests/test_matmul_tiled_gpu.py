@@ -1,8 +1,8 @@
 """The tiled (prefill) form of the matrix products against the CPU oracle.
 
-Parity tier: bit-exact. Steps of kTiledMinTokens (8) tokens or more take the
-tiled kernel; every output must equal the oracle's — the reference's prefill
-order, which is its decode order (matmul.wgsl tile_range :410, matmul.h
+Parity tier: bit-exact. Long steps take the tiled kernel by default, and any
+step with CB_MATMUL_TILED, which these tests set. Every output must equal the
+oracle's — the reference's prefill order, which is its decode order (matmul.wgsl tile_range :410, matmul.h
 34-50) — bit for bit, and a token's outputs must be the bits the decode form
 gives it alone. Shapes cover each tile shape the dispatch picks (long and
 short steps, wide and narrow products), ragged token and row tails, ranges of
@@ -29,6 +29,7 @@ def weight(rng, fmt, rows, K):
 
 
 def run(fmt, K, members, x, outs, **kw):
+    kw.setdefault("flags", cb.MATMUL_TILED)
     cb.matmul(fmt, K, members, x, outs, **kw)
     torch.cuda.synchronize()
     cb.check(cb.lib().cb_fault_check(None))
@@ -83,7 +84,7 @@ def test_tiled_rows_equal_decoded_rows(cuda):
     run(O.Q4_0, K, [(p, nb, 0, rows, 0)], xd, [yT])
     for t in (0, 17, 39):
         y1 = torch.zeros((1, rows), dtype=torch.float32, device="cuda")
-        run(O.Q4_0, K, [(p, nb, 0, rows, 0)], xd[t:t + 1], [y1])
+        run(O.Q4_0, K, [(p, nb, 0, rows, 0)], xd[t:t + 1], [y1], flags=0)
         assert_exact(yT[t].cpu().numpy(), y1.cpu().numpy())
 
 
@@ -158,7 +159,7 @@ def test_tiled_strided_input_and_output(cuda):
     xw = synth.activations(rng, T, K + 64)
     y = torch.zeros((T, rows + 100), dtype=torch.float32, device="cuda")
     cb.matmul(O.Q6_K, K, [(dev(piece), nb, 0, rows, 100)], dev(xw), [y], x_stride=K + 64,
-              out_stride=[rows + 100, 0, 0])
+              out_stride=[rows + 100, 0, 0], flags=cb.MATMUL_TILED)
     torch.cuda.synchronize()
     want = O.matmul(O.Q6_K, piece, nb, rows, K, np.ascontiguousarray(xw[:, :K]))
     got = y.cpu().numpy()
