@@ -38,7 +38,8 @@ class Matmul(ctypes.Structure):
     _fields_ = [("format", ctypes.c_uint32), ("columns", ctypes.c_uint32), ("members", ctypes.c_uint32),
                 ("epilogue", ctypes.c_uint32), ("activation", ctypes.c_uint32), ("member", Member * 3),
                 ("gate_input", ctypes.c_void_p), ("gate_input_stride", ctypes.c_uint32),
-                ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32)]
+                ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32),
+                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64)]
 
 
 class Norm(ctypes.Structure):
@@ -121,6 +122,8 @@ def lib() -> ctypes.CDLL:
         L.cb_select_tiles.argtypes = [ctypes.c_uint32]
         L.cb_select_tickets.restype = ctypes.c_uint32
         L.cb_select_tickets.argtypes = [ctypes.c_uint32]
+        L.cb_matmul_scratch_bytes.restype = ctypes.c_uint64
+        L.cb_matmul_scratch_bytes.argtypes = [ctypes.c_uint32] * 3
         _lib = L
     return _lib
 
@@ -149,10 +152,11 @@ def _ptr(t) -> int:
 def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, activation: int = SILU,
            tokens: int | None = None, x_stride: int | None = None, out_stride=None, flags: int = 0,
            gate_input=None, gate_input_stride: int = 0, gate_input_column: int = 0, gate_input_token: int = 0,
-           stream=None) -> None:
+           stream=None, scratch=None) -> None:
     """Runs cb_matmul_run. `members`: list of (piece tensor (uint8, cuda), blocks,
     first_row, rows, out_offset). `x`: f32 cuda tensor [tokens, x_stride].
-    `out`: list of up to 3 f32 cuda tensors."""
+    `out`: list of up to 3 f32 cuda tensors. With MATMUL_TENSOR, `scratch`
+    (a cuda tensor of cb_matmul_scratch_bytes) or one allocated here."""
     m = Matmul()
     m.format = fmt
     m.columns = columns
@@ -169,6 +173,13 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
         tokens = x.shape[0] if x.dim() > 1 else 1
     if x_stride is None:
         x_stride = x.shape[-1]
+    if flags & MATMUL_TENSOR:
+        need = lib().cb_matmul_scratch_bytes(flags, tokens, columns)
+        if scratch is None:
+            import torch
+            scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        m.scratch = scratch.data_ptr()
+        m.scratch_bytes = scratch.numel() * scratch.element_size()
     outs = (ctypes.c_void_p * 3)(*[_ptr(o) for o in (list(out) + [None, None, None])[:3]])
     if out_stride is None:
         out_stride = [o.shape[-1] if o is not None else 0 for o in (list(out) + [None, None, None])[:3]]

@@ -100,6 +100,10 @@ int cb_device_sm_count(void) {
     return n > 0 ? n : cb::fail(CB_ERROR_STEP, "no CUDA device");
 }
 
+uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t columns) {
+    return (flags & CB_MATMUL_TENSOR) ? cb::matmul_tensor_scratch_bytes(tokens, columns) : 0u;
+}
+
 int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_t tokens, float* const out[3],
                   const uint32_t out_stride[3], uint32_t flags, void* stream) {
     using namespace cb;
@@ -120,8 +124,6 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
         return fail(CB_ERROR_INVALID, "cb_matmul_run: a gated product is a gate and an up of equal rows");
     if (m->epilogue == CB_EPILOGUE_GATED_BY_INPUT && !m->gate_input)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: GATED_BY_INPUT without its input u");
-    if (flags & CB_MATMUL_TENSOR)
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: the tensor-core form is not built in this library version");
     if (tokens == 0) return CB_OK;
     if (x_stride < m->columns) return fail(CB_ERROR_INVALID, "cb_matmul_run: x_stride %u < columns", x_stride);
     if (!aligned16(x) || x_stride % 4 != 0)
@@ -165,14 +167,23 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
         if (tokens > 1 && a.out_stride[i] == 0)
             return fail(CB_ERROR_INVALID, "cb_matmul_run: output %u has no stride for %u tokens", i, tokens);
     }
+    if (flags & CB_MATMUL_TENSOR) {
+        const uint64_t need = matmul_tensor_scratch_bytes(tokens, m->columns);
+        if (!m->scratch || !aligned16(m->scratch) || m->scratch_bytes < need)
+            return fail(CB_ERROR_INVALID, "cb_matmul_run: the tensor form needs %llu bytes of 16-byte aligned scratch",
+                        static_cast<unsigned long long>(need));
+        a.scratch = m->scratch;
+    }
     const int sms = sm_count();
     if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
     const bool pdl = (flags & CB_MATMUL_PDL) != 0;
     bool tiled = tiled_form(tokens, m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : total);
     if (flags & CB_MATMUL_STREAMED) tiled = false;
     if (flags & CB_MATMUL_TILED) tiled = true;
-    cudaError_t e = tiled ? matmul_tiled(a, sms, static_cast<cudaStream_t>(stream), pdl)
-                          : matmul_decode(a, sms, static_cast<cudaStream_t>(stream), pdl);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = (flags & CB_MATMUL_TENSOR) ? matmul_tensor(a, st, pdl)
+                    : tiled                    ? matmul_tiled(a, sms, st, pdl)
+                                               : matmul_decode(a, sms, st, pdl);
     if (e != cudaSuccess) return fail_cuda(e, "cb_matmul_run: launch");
     return CB_OK;
 }

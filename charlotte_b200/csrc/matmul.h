@@ -39,6 +39,7 @@ struct MatmulArgs {
     uint32_t gate_input_stride;
     uint32_t gate_input_column;
     unsigned int* fault;    // device word: a bounded wait that ran out sets a bit
+    void* scratch;          // tensor form: x rounded to f16, [tokens][columns]
 };
 
 // Decode form over `tokens` rows of x (each token its own grid row): the
@@ -48,6 +49,10 @@ cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
 // Tiled form over a step of `tokens` rows of x: the same sums, bit for bit,
 // as a register-tiled GEMM on the CUDA cores. PDL when `pdl`.
 cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
+
+// Tensor-core form (tolerance tier, f16 operands, f32 accumulation in TMEM).
+cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl);
+uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns);
 
 // Which exact form a step takes by default: the streamed (decode-layout)
 // form keeps every SM busy on short steps and narrow products, the tiled

@@ -1,0 +1,412 @@
+// The tensor-core form of the matrix products (CB_MATMUL_TENSOR): Y = X·Wᵀ
+// for steps of many tokens on the 5th-generation tensor cores, at the
+// BASELINE tolerance tier (max |y − y_exact| ≤ 1e-3·max |y|), not bit-exact:
+// X and the decoded weights are rounded to f16 (round to nearest even) and
+// the products accumulate in f32 in tensor memory, in the tensor core's own
+// order. Each weight is decoded exactly (formats.cuh) before that rounding.
+// Inputs beyond ±65,504 do not fit f16; the exact forms serve those.
+//
+// B200 mapping, two launches:
+//  1. x is rounded to f16 once, into the caller's scratch ([tokens][K]);
+//  2. one CTA a 128-token × 128-slot tile:
+//     - a TMA warp loads each 128 × 64 block of x16 with a tiled bulk tensor
+//       copy (128-byte swizzle, no multicast) straight into the K-major
+//       layout the MMA reads;
+//     - eight producer warps decode the tile's weight blocks (four blocks of
+//       codes in flight in registers a thread) to f16 and store them in the
+//       same swizzled layout;
+//     - one warp issues tcgen05.mma (M = 128, N = 128, K = 16, four a block)
+//       into a 128-column f32 accumulator in tensor memory; tcgen05.commit
+//       hands each of the 6 ring stages back;
+//     - after the last block the producer warps read the accumulator
+//       (tcgen05.ld) and apply the epilogue: write, QKV, gated (the tile's
+//       first 64 slots are gate rows, the last 64 the same outputs' up rows)
+//       or gated by input.
+// Every wait is bounded; a wait that runs out sets the fault word, the
+// pipeline drains, and the accumulator is still freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <utility>
+
+#include "formats.cuh"
+#include "matmul.h"
+#include "numerics.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace cb {
+
+namespace {
+
+constexpr uint32_t kBM = 128, kBN = 128, kBK = 64, kStages = 6;
+constexpr uint32_t kProducerWarps = 8, kProducers = kProducerWarps * 32;
+constexpr uint32_t kMmaWarp = kProducerWarps, kTmaWarp = kProducerWarps + 1;
+constexpr uint32_t kThreadsT = kProducers + 64;                 // + the MMA warp and the TMA warp
+constexpr uint32_t kTileA = kBM * kBK * 2, kTileB = kBN * kBK * 2;   // 16 KB each
+constexpr uint32_t kStageBytes = kTileA + kTileB;
+constexpr uint32_t kTmemColumns = 128;
+constexpr size_t kTensorSmem = 1024 + kStages * kStageBytes + 256;
+
+// Byte offset of 16-byte chunk c of row r in a K-major 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Weights [K0, K0+16) of a group, exactly decoded, as eight packed f16 pairs.
+template <typename F, int K0, int... ks>
+__device__ __forceinline__ void decode16(const F& f, const typename F::Consts& c, uint32_t (&h)[8],
+                                         std::integer_sequence<int, ks...>) {
+    float w[16];
+    ((w[ks] = fmaf(__uint_as_float(f.template magic<K0 + ks>()), F::template S<K0 + ks>(c),
+                   F::template C<K0 + ks>(c))),
+     ...);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = pack_half2(w[2 * i], w[2 * i + 1]);
+}
+
+// x rounded to f16 (round to nearest even), [tokens][K].
+__global__ void to_f16_kernel(const float* x, uint32_t x_stride, uint32_t K, uint32_t tokens, __half2* x16) {
+    grid_dependency_wait();
+    const uint32_t quads = K / 4u;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * quads; i += gridDim.x * blockDim.x) {
+        const uint32_t t = i / quads, q = i % quads;
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * x_stride) + q);
+        x16[2u * i] = __floats2half2_rn(v.x, v.y);
+        x16[2u * i + 1u] = __floats2half2_rn(v.z, v.w);
+    }
+    grid_dependents_launch();
+}
+
+// Tiled TMA load of box {64, 128} at (k0, row0) of the x16 map into `dst`,
+// completing on `bar`. No cluster multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t k0, int32_t row0,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(k0), "r"(row0), "r"(smem_addr(bar))
+        : "memory");
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kThreadsT, 1) tensor_kernel(const MatmulArgs a, const __grid_constant__ CUtensorMap x16map) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* done = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t G = a.columns / 32u;
+    const uint32_t kblocks = (G + 1u) / 2u;
+    const bool gated = a.epilogue == kGated;
+    const uint32_t m0 = blockIdx.x * kBM;
+    const uint32_t n0 = blockIdx.y * (gated ? kBN / 2 : kBN);   // first slot (gated: first output)
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], kProducers + 1u);   // the producers, and the TMA warp's expect-tx
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, kTmemColumns);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    grid_dependency_wait();
+
+    if (warp < kProducerWarps) {
+        // ---- producers: row r of B, half h of each K block ---------------------
+        const uint32_t tid = threadIdx.x;
+        const uint32_t r = tid % 128u, h = tid / 128u;
+        // B: slot r's weight row (members picked by value, see matmul_tiled.cu).
+        const uint8_t* sp[F::kStreams];
+        bool live = false;
+        {
+            int q = -1;
+            uint32_t row = 0;
+            if (gated) {
+                const uint32_t o = n0 + (r < kBN / 2 ? r : r - kBN / 2);
+                if (o < a.member[0].rows) {
+                    q = r < kBN / 2 ? 0 : 1;
+                    row = (q == 0 ? a.member[0].first_row : a.member[1].first_row) + o;
+                }
+            } else {
+                uint32_t n = n0 + r;
+#pragma unroll
+                for (int i = 0; i < 3; ++i) {
+                    if (q < 0 && i < static_cast<int>(a.members)) {
+                        if (n < a.member[i].rows) {
+                            q = i;
+                            row = a.member[i].first_row + n;
+                        } else {
+                            n -= a.member[i].rows;
+                        }
+                    }
+                }
+            }
+            live = q >= 0;
+            const uint8_t* piece = q == 1 ? a.member[1].piece : (q == 2 ? a.member[2].piece : a.member[0].piece);
+            const uint32_t blocks = q == 1 ? a.member[1].blocks : (q == 2 ? a.member[2].blocks : a.member[0].blocks);
+#pragma unroll
+            for (int s = 0; s < F::kStreams; ++s)
+                sp[s] = piece + RowStreams<F>::base(s, blocks) +
+                        static_cast<uint64_t>(live ? row : 0u) * RowStreams<F>::row_bytes(s, G);
+        }
+        // Four blocks' codes in flight in registers: block kb+4 is read from
+        // global memory while block kb is decoded and stored.
+        auto fetch = [&](uint32_t kb, F& f) {
+            const uint32_t g = 2u * kb + h;   // this thread's 32-wide group of the block
+            if (live && g < G) f.load(sp, g);
+            else f.zero();
+        };
+        // Stores block kb (stage kb mod kStages): the slot's group decoded
+        // exactly and rounded to f16, as four 16-byte swizzled chunks.
+        auto put = [&](uint32_t kb, const F& f) -> bool {
+            const uint32_t s = kb % kStages;
+            if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1u) & 1u, a.fault)) return false;
+            uint8_t* tileB = base + s * kStageBytes + kTileA;
+            const typename F::Consts c = f.consts();
+            uint32_t lo[8], hi[8];
+            decode16<F, 0>(f, c, lo, std::make_integer_sequence<int, 16>{});
+            decode16<F, 16>(f, c, hi, std::make_integer_sequence<int, 16>{});
+            *reinterpret_cast<uint4*>(tileB + sw128(r, 4u * h + 0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4*>(tileB + sw128(r, 4u * h + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+            *reinterpret_cast<uint4*>(tileB + sw128(r, 4u * h + 2)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(tileB + sw128(r, 4u * h + 3)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+            fence_proxy_async();   // generic-proxy stores, then the tensor core's reads
+            mbar_arrive(&full[s]);
+            return true;
+        };
+        F f0, f1, f2, f3;
+        fetch(0u, f0);
+        fetch(1u, f1);
+        fetch(2u, f2);
+        fetch(3u, f3);
+        for (uint32_t kb = 0; kb < kblocks; kb += 4u) {
+            if (!put(kb, f0)) break;
+            fetch(kb + 4u, f0);
+            if (kb + 1u >= kblocks || !put(kb + 1u, f1)) break;
+            fetch(kb + 5u, f1);
+            if (kb + 2u >= kblocks || !put(kb + 2u, f2)) break;
+            fetch(kb + 6u, f2);
+            if (kb + 3u >= kblocks || !put(kb + 3u, f3)) break;
+            fetch(kb + 7u, f3);
+        }
+    } else if (warp == kTmaWarp) {
+        // ---- the TMA warp: x16 blocks ------------------------------------------
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < kblocks; ++kb) {
+                const uint32_t s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1u) & 1u, a.fault)) break;
+                mbar_arrive_expect_tx(&full[s], kTileA);
+                tma_load_2d(base + s * kStageBytes, &x16map, static_cast<int32_t>(kb * kBK), static_cast<int32_t>(m0),
+                            &full[s]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- the MMA warp ---------------------------------------------------------
+        constexpr uint32_t idesc = umma_idesc_f16(kBM, kBN);
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            const uint32_t s = kb % kStages;
+            if (!mbar_wait(&full[s], (kb / kStages) & 1u, a.fault)) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a_addr = smem_addr(base + s * kStageBytes);
+                const uint64_t da = umma_desc_sw128(a_addr), db = umma_desc_sw128(a_addr + kTileA);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kBK / 16u; ++kk)   // 32 bytes of K an MMA
+                    umma_f16(tmem, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0u ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) umma_commit(done);   // when every MMA issued has completed
+        __syncwarp();
+    }
+    grid_dependents_launch();
+
+    // ---- epilogue: producer warp w reads TMEM lanes 32·(w mod 4), columns
+    //      [32·(w/4), +32) and [64 + 32·(w/4), +32), into a 128 × 128 tile in
+    //      the drained ring; then each warp writes whole output rows, its
+    //      lanes over consecutive columns (coalesced) ------------------------
+    if (warp < kProducerWarps) {
+        const bool ok = mbar_wait(done, 0u, a.fault);
+        constexpr uint32_t kCs = kBN + 1u;   // floats a staged row: conflict-free column writes
+        float* cs = reinterpret_cast<float*>(base);
+        if (ok) {
+            tc_fence_after();
+            const uint32_t quarter = warp & 3u, half = warp >> 2;
+            const uint32_t row = 32u * quarter + lane;
+            float lo[32], hi[32];
+            const uint32_t lane_addr = tmem + ((32u * quarter) << 16);
+            tmem_ld32(lane_addr + 32u * half, lo);
+            tmem_ld32(lane_addr + 64u + 32u * half, hi);
+            fence_proxy_async();   // the ring was last written by the copy engine and read by the MMA
+#pragma unroll
+            for (uint32_t c = 0; c < 32; ++c) {
+                cs[row * kCs + 32u * half + c] = lo[c];
+                cs[row * kCs + 64u + 32u * half + c] = hi[c];
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kProducers) : "memory");
+        if (ok) {
+            if (gated) {
+                for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += kProducerWarps) {
+                    const size_t rowbase = static_cast<size_t>(m0 + r) * a.out_stride[0] + a.member[0].out_offset;
+#pragma unroll
+                    for (uint32_t j = 0; j < 2; ++j) {
+                        const uint32_t c = lane + 32u * j, o = n0 + c;
+                        if (o < a.member[0].rows)
+                            a.out[0][rowbase + o] = activate(a.activation, cs[r * kCs + c]) * cs[r * kCs + 64u + c];
+                    }
+                }
+            } else {
+                // Column lane + 32j of the tile: its member and output column.
+                int qj[4];
+                uint32_t oj[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t n = n0 + lane + 32u * j;
+                    int q = -1;
+#pragma unroll
+                    for (int m = 0; m < 3; ++m) {
+                        if (q < 0 && m < static_cast<int>(a.members)) {
+                            if (n < a.member[m].rows) q = m;
+                            else n -= a.member[m].rows;
+                        }
+                    }
+                    qj[j] = q;
+                    oj[j] = (q == 1 ? a.member[1].out_offset : (q == 2 ? a.member[2].out_offset : a.member[0].out_offset)) + n;
+                }
+                for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += kProducerWarps) {
+                    const uint32_t t = m0 + r;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int q = qj[j];
+                        if (q < 0) continue;
+                        const float v = cs[r * kCs + lane + 32u * j];
+                        const uint32_t o = oj[j];
+                        if (a.epilogue == kQKV) {
+                            float* out = q == 1 ? a.out[1] : (q == 2 ? a.out[2] : a.out[0]);
+                            const uint32_t st = q == 1 ? a.out_stride[1] : (q == 2 ? a.out_stride[2] : a.out_stride[0]);
+                            out[static_cast<size_t>(t) * st + o] = v;
+                        } else if (a.epilogue == kWrite) {
+                            a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = v;
+                        } else {   // kGatedByInput
+                            const float u = a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride +
+                                                         a.gate_input_column + o];
+                            a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, v) * u;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemColumns);
+    }
+}
+
+template <typename F>
+cudaError_t launch_tensor(const MatmulArgs& a, const CUtensorMap& map, cudaStream_t stream, bool pdl) {
+    auto kernel = tensor_kernel<F>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTensorSmem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const bool gated = a.epilogue == kGated;
+    const uint32_t slots = gated ? a.member[0].rows : a.total_rows;
+    const uint32_t per_tile = gated ? kBN / 2 : kBN;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.tokens + kBM - 1) / kBM, (slots + per_tile - 1) / per_tile);
+    cfg.blockDim = dim3(kThreadsT);
+    cfg.dynamicSmemBytes = kTensorSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a, map);
+}
+
+}  // namespace
+
+uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns) {
+    return (static_cast<uint64_t>(tokens) * columns * 2u + 255u) / 256u * 256u;
+}
+
+cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
+    // 1. x to f16 in the scratch.
+    {
+        const uint32_t quads = a.tokens * (a.columns / 4u);
+        uint32_t blocks = (quads + 255u) / 256u;
+        if (blocks > 4096u) blocks = 4096u;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(blocks);
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, to_f16_kernel, a.x, a.x_stride, a.columns, a.tokens,
+                                           static_cast<__half2*>(a.scratch));
+        if (e != cudaSuccess) return e;
+    }
+    // 2. The map of x16: [tokens][K] f16, boxes of 64 × 128 with the 128-byte
+    //    swizzle; rows past `tokens` and columns past K read as zero.
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {a.columns, a.tokens};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.columns) * 2u};
+    const cuuint32_t box[2] = {kBK, kBM};
+    const cuuint32_t elem[2] = {1, 1};
+    // The driver's encoder, looked up through the runtime once (the library
+    // does not link the driver library, so it still loads where there is no
+    // GPU driver).
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return cudaErrorNotSupported;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.scratch, dims, strides, box,
+                                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    switch (a.format) {
+        case kQ4_0: return launch_tensor<Q4_0>(a, map, stream, pdl);
+        case kQ8_0: return launch_tensor<Q8_0>(a, map, stream, pdl);
+        case kQ6_K: return launch_tensor<Q6_K>(a, map, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace cb

@@ -110,6 +110,10 @@ typedef struct cb_matmul {
     uint32_t gate_input_stride;    /* floats between u's token rows                      */
     uint32_t gate_input_column;    /* u's first column                                   */
     uint32_t gate_input_token;     /* u's row of the first token                         */
+    void* scratch;                 /* CB_MATMUL_TENSOR: cb_matmul_scratch_bytes() of
+                                      device memory, 16-byte aligned (x rounded to f16);
+                                      the exact forms ignore it                          */
+    uint64_t scratch_bytes;
 } cb_matmul;
 
 /* y[t][o] = Σ_k W[o][k]·x[t][k] for tokens t in [0, tokens), each output
@@ -118,6 +122,10 @@ typedef struct cb_matmul {
  * entries may be NULL). */
 CB_API int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_t tokens, float* const out[3],
                   const uint32_t out_stride[3], uint32_t flags, void* stream);
+/* Scratch a product of `tokens` rows and `columns` K needs under `flags`
+ * (0 for the exact forms). No counterpart in the reference (its prefill is
+ * exact f32 only). */
+CB_API uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t columns);
 
 
 /* ---- RMSNorm ------------------------------------------------------------------
