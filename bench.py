@@ -389,6 +389,42 @@ def decode_bench(steps, prompt_len, seed, world):
     }
 
 
+def llama_bench(decode_steps, seed):
+    """Llama-3.2-1B shapes, random-init weights, a 2,048-token
+    prompt as four 512-token steps on the tcgen05 path
+    (CB_DECODER_TENSOR_PREFILL), then `decode_steps` greedy decode steps
+    (exact form, one CUDA graph replayed). The same prompt through the exact
+    forms is timed beside it."""
+    import torch
+    from charlotte_b200 import model as M
+    arch = M.llama_3_2_1b(context=2048 + decode_steps + 64)
+    m = M.synthesize(arch, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    prompt = rng.integers(0, arch.vocab, 2048).astype(np.uint32)
+    out = {"workload": "llama-3.2-1b shapes (configs[3]): 2048-token prompt as 4x512 steps, "
+                       "then %d greedy steps" % decode_steps}
+    flops_per_token = 2.0 * sum(w.rows * w.cols for L in m.layers for w in (L.q, L.k, L.v, L.o, L.gate, L.up,
+                                                                           L.down))
+    for tensor in (True, False):
+        dec = M.Decoder(m, max_step_tokens=512, tensor_prefill=tensor)
+        dec.prefill(prompt)   # warm
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        rec = dec.prefill(prompt)
+        s = time.perf_counter() - t0
+        key = "prefill_tensor" if tensor else "prefill_exact"
+        out[key] = {"ms": round(s * 1e3, 2), "tok_s": round(2048 / s, 1),
+                    "matmul_tflops": round(2048 * flops_per_token / s / 1e12, 1)}
+        if tensor:
+            dec.generate(4)
+            dec.prefill(prompt)
+            toks, failed, dev_ms = dec.generate(decode_steps, timed=True)
+            out["decode"] = {"tok_s": round(decode_steps / (dev_ms * 1e-3), 1),
+                             "ms_per_token": round(dev_ms / decode_steps, 4), "failed_steps": int(failed.sum())}
+        dec.close()
+    return out
+
+
 def cpu_decode_baseline(seed):
     """The oracle's pass (the reference's order of operations) on all host
     cores: a 16-token prompt then 4 decode steps of Qwen3-0.6B."""
@@ -609,6 +645,10 @@ def main():
         ms = [16, 128, 256, 512, 2048]
         for f in (4, 8):
             print(json.dumps(sweep_bench(flags=f, ms=ms, formats=(2,), head=False)))
+    elif args.case == "llama":
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(llama_bench(128, SEED + 11)))
     elif args.case == "decode":
         import torch
         torch.cuda.set_device(0)

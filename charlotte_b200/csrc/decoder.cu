@@ -18,6 +18,7 @@
 // advances the position.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -99,6 +100,9 @@ struct cb_decoder {
     cb_sampling step_sampling{};
     bool has_step = false;
     uint32_t next_position = 0;   // the position after the last step's tokens
+    bool tensor_prefill = false;  // CB_DECODER_TENSOR_PREFILL
+    void* tensor_scratch = nullptr;
+    uint64_t tensor_scratch_bytes = 0;
 };
 
 namespace {
@@ -150,6 +154,10 @@ cb_member member_of(const DevWeight& w) { return {w.piece, w.blocks, 0, w.rows, 
 
 int launched(cudaError_t e, const char* what) { return e == cudaSuccess ? CB_OK : fail_cuda(e, what); }
 
+// Steps of this many tokens or more take the tensor form under
+// CB_DECODER_TENSOR_PREFILL.
+constexpr uint32_t kDecoderTensorTokens = 128;
+
 // One matmul launch through the same path as cb_matmul_run.
 int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, const float* x,
             uint32_t x_stride, uint32_t tokens, float* const outs[3], const uint32_t strides[3]) {
@@ -162,7 +170,13 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
     m.activation = d->model.activation;
     uint32_t i = 0;
     for (const DevWeight* w : ws) m.member[i++] = member_of(*w);
-    return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, CB_MATMUL_PDL, d->stream);
+    uint32_t flags = CB_MATMUL_PDL;
+    if (d->tensor_prefill && tokens >= kDecoderTensorTokens) {
+        flags |= CB_MATMUL_TENSOR;
+        m.scratch = d->tensor_scratch;
+        m.scratch_bytes = d->tensor_scratch_bytes;
+    }
+    return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, flags, d->stream);
 }
 
 // The step's launches (graph.cpp's order). `fed`: the token is the last draw.
@@ -325,7 +339,6 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
 extern "C" {
 
 int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flags, cb_decoder** out) {
-    (void)flags;
     if (!m || !out || !m->layer) return fail(CB_ERROR_INVALID, "cb_decoder_create: null argument");
     *out = nullptr;
     if (m->layers == 0 || m->hidden == 0 || m->hidden % 32 != 0 || m->hidden > 4096)
@@ -405,6 +418,14 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
     if (int rc = dalloc(d, &d->sampled, 4)) return bail(rc);
     if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
+    if (flags & CB_DECODER_TENSOR_PREFILL) {
+        const uint32_t widest = std::max<uint32_t>(std::max<uint32_t>(H, static_cast<uint32_t>(qd)), m->ffn);
+        d->tensor_scratch_bytes = cb_matmul_scratch_bytes(CB_MATMUL_TENSOR, T, widest);
+        uint8_t* p = nullptr;
+        if (int rc = dalloc(d, &p, d->tensor_scratch_bytes)) return bail(rc);
+        d->tensor_scratch = p;
+        d->tensor_prefill = true;
+    }
     e = cudaMemset(d->tickets, 0, tickets * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->sel_ticket, 0, cb_select_tickets(m->vocab) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->state, 0, 2 * sizeof(uint32_t));

@@ -338,6 +338,14 @@ typedef struct cb_sampling {
 
 typedef struct cb_decoder cb_decoder;
 
+enum {
+    /* Steps of 128 tokens or more run their products in the tensor-core
+     * form (CB_MATMUL_TENSOR, tolerance tier) instead of the exact forms;
+     * shorter steps (decode) and the head's last-token product stay exact.
+     * No counterpart in the reference. */
+    CB_DECODER_TENSOR_PREFILL = 1u
+};
+
 /* Uploads the model and allocates its caches and working buffers for steps
  * of up to max_step_tokens (the reference's prefill block is 512). */
 CB_API int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flags, cb_decoder** out);
