@@ -55,7 +55,8 @@ class Rope(ctypes.Structure):
                 ("key_gain", ctypes.c_void_p), ("factors", ctypes.c_void_p), ("turns", ctypes.c_void_p),
                 ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
                 ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
-                ("halves", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("epsilon", ctypes.c_float)]
+                ("halves", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("epsilon", ctypes.c_float),
+                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64)]
 
 
 class Attention(ctypes.Structure):
@@ -64,14 +65,16 @@ class Attention(ctypes.Structure):
                 ("tickets", ctypes.c_void_p), ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32),
                 ("tokens", ctypes.c_uint32), ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32),
                 ("kv_heads", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("window", ctypes.c_uint32),
-                ("max_chunks", ctypes.c_uint32), ("scale_log2e", ctypes.c_float)]
+                ("max_chunks", ctypes.c_uint32), ("scale_log2e", ctypes.c_float),
+                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64)]
 
 
 class Gather(ctypes.Structure):
     _fields_ = [("piece", ctypes.c_void_p), ("format", ctypes.c_uint32), ("blocks", ctypes.c_uint32),
                 ("width", ctypes.c_uint32), ("first_row", ctypes.c_uint32), ("row_count", ctypes.c_uint32),
                 ("ids", ctypes.c_void_p), ("sampled", ctypes.c_void_p), ("fed", ctypes.c_uint32),
-                ("tokens", ctypes.c_uint32), ("scale", ctypes.c_float), ("hidden", ctypes.c_void_p)]
+                ("tokens", ctypes.c_uint32), ("scale", ctypes.c_float), ("hidden", ctypes.c_void_p),
+                ("fed_stride", ctypes.c_uint32)]
 
 
 class Select(ctypes.Structure):
@@ -80,7 +83,7 @@ class Select(ctypes.Structure):
                 ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
                 ("seed0", ctypes.c_uint32), ("seed1", ctypes.c_uint32), ("top_k", ctypes.c_uint32),
                 ("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("min_p", ctypes.c_float),
-                ("log_min_p", ctypes.c_float)]
+                ("log_min_p", ctypes.c_float), ("rows", ctypes.c_uint32), ("logits_stride", ctypes.c_uint32)]
 
 
 RUN_PDL = 1

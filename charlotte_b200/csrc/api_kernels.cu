@@ -52,13 +52,15 @@ int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream) {
     if ((r->query_gain == nullptr) != (r->key_gain == nullptr))
         return fail(CB_ERROR_INVALID, "cb_rope_run: QK-norm on queries or keys alone");
     if (r->slots == 0) return fail(CB_ERROR_INVALID, "cb_rope_run: no cache slots");
+    if (r->rows_are_sequences && r->sequence_stride < static_cast<uint64_t>(r->slots) * r->kv_heads * r->head_dim)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: sequences' caches overlap (stride below one cache)");
     if (r->tokens == 0) return CB_OK;
     return launched(rope_run(*r, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_rope_run");
 }
 
 uint32_t cb_attention_tickets(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads) {
     if (kv_heads == 0) return 0;
-    return attention_row_tiles(tokens, query_heads, kv_heads) * kv_heads;
+    return attention_row_tiles(tokens, query_heads, kv_heads, false) * kv_heads;
 }
 
 int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
@@ -69,7 +71,10 @@ int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
         return fail(CB_ERROR_INVALID, "cb_attention_run: %u query heads over %u kv heads", a->query_heads,
                     a->kv_heads);
     if (a->slots == 0 || a->window == 0) return fail(CB_ERROR_INVALID, "cb_attention_run: no slots or no window");
-    if (!a->position && static_cast<uint64_t>(a->position0) + a->tokens > static_cast<uint64_t>(a->max_chunks) * 64)
+    if (a->rows_are_sequences && a->sequence_stride < static_cast<uint64_t>(a->slots) * a->kv_heads * a->head_dim)
+        return fail(CB_ERROR_INVALID, "cb_attention_run: sequences' caches overlap (stride below one cache)");
+    if (!a->position && static_cast<uint64_t>(a->position0) + (a->rows_are_sequences ? 1u : a->tokens) >
+                            static_cast<uint64_t>(a->max_chunks) * 64)
         return fail(CB_ERROR_INVALID, "cb_attention_run: positions past max_chunks");
     if (a->tokens == 0) return CB_OK;
     return launched(attention_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_attention_run");
@@ -82,7 +87,8 @@ int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream) {
         return fail(CB_ERROR_INVALID, "cb_gather_run: format %u", g->format);
     if (g->width == 0 || g->width % (g->format == CB_Q6_K ? 256 : 32) != 0)
         return fail(CB_ERROR_INVALID, "cb_gather_run: width %u is not whole blocks", g->width);
-    if (g->fed && g->tokens != 1) return fail(CB_ERROR_INVALID, "cb_gather_run: a fed step has one token");
+    if (g->fed && g->tokens != 1 && g->fed_stride == 0)
+        return fail(CB_ERROR_INVALID, "cb_gather_run: a fed step of several rows needs fed_stride");
     if (g->tokens == 0) return CB_OK;
     return launched(gather_run(*g, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_gather_run");
 }

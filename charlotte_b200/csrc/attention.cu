@@ -47,10 +47,11 @@ struct Geometry {
     uint32_t G;               // query heads a kv head
 };
 
-__host__ __device__ inline Geometry geometry_of(uint32_t query_heads, uint32_t kv_heads) {
+// Batched decode (rows are sequences): a row a tile, each over its own cache.
+__host__ __device__ inline Geometry geometry_of(uint32_t query_heads, uint32_t kv_heads, bool sequences) {
     Geometry g;
     g.G = query_heads / kv_heads;
-    g.rows_per_tile = kMaxQueries / g.G > 0 ? kMaxQueries / g.G : 1;
+    g.rows_per_tile = sequences ? 1u : (kMaxQueries / g.G > 0 ? kMaxQueries / g.G : 1);
     return g;
 }
 
@@ -70,16 +71,17 @@ constexpr uint32_t kChunkSlots = 16;   // CTAs a (kv head, row tile) takes, stri
 
 // Stages keys and values j_lo..j_hi-1 (absolute positions) of the chunk at
 // key0 into its shared tiles.
-__device__ __forceinline__ void stage_keys(const AttentionArgs& a, uint16_t* ks, uint16_t* vs, uint32_t key0,
-                                           uint32_t j_lo, uint32_t j_hi, uint32_t kvh, uint32_t d) {
+__device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_t* kc, const uint16_t* vc, uint16_t* ks,
+                                           uint16_t* vs, uint32_t key0, uint32_t j_lo, uint32_t j_hi, uint32_t kvh,
+                                           uint32_t d) {
     const uint32_t words = d / 8u;   // uint4 per key row
     const uint32_t b_lo = j_lo - key0, n = (j_hi - j_lo) * words;
 #pragma unroll 4
     for (uint32_t i = threadIdx.x; i < n; i += kAttnThreads) {
         const uint32_t b = b_lo + i / words, w = i % words;
         const size_t at = (static_cast<size_t>((key0 + b) % a.slots) * a.kv_heads + kvh) * d;
-        reinterpret_cast<uint4*>(ks + b * d)[w] = reinterpret_cast<const uint4*>(a.key_cache + at)[w];
-        reinterpret_cast<uint4*>(vs + b * d)[w] = reinterpret_cast<const uint4*>(a.value_cache + at)[w];
+        reinterpret_cast<uint4*>(ks + b * d)[w] = reinterpret_cast<const uint4*>(kc + at)[w];
+        reinterpret_cast<uint4*>(vs + b * d)[w] = reinterpret_cast<const uint4*>(vc + at)[w];
     }
 }
 
@@ -88,10 +90,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     const uint32_t d = a.head_dim;
     const uint32_t B = 2048u / d;
     const uint32_t tiles = kChunk / B;
-    const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
+    const bool seqs = a.rows_are_sequences != 0;
+    const Geometry geo = geometry_of(a.query_heads, a.kv_heads, seqs);
     const uint32_t G = geo.G;
     const uint32_t kvh = blockIdx.x;
     const uint32_t rt = blockIdx.z;
+    // Batched decode: this tile's one row is its sequence's, over its cache.
+    const size_t cache_at = seqs ? static_cast<size_t>(rt) * a.sequence_stride : 0u;
+    const uint16_t* kc = a.key_cache + cache_at;
+    const uint16_t* vc = a.value_cache + cache_at;
     // The step's position was written before the launches preceding this one
     // (by the host, or by the last step's closing launch), so it is read
     // before the dependency wait, as are the keys of earlier steps.
@@ -109,7 +116,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l
 
     // The tile's live chunks: every chunk some row's keys reach.
-    const uint32_t p_first = pos0 + row0, p_last = pos0 + row0 + rows - 1u;
+    const uint32_t p_first = pos0 + (seqs ? 0u : row0), p_last = p_first + (seqs ? 0u : rows - 1u);
     const uint32_t live_first = earliest_of(p_first, a.window) / kChunk;
     const uint32_t live_chunks = p_last / kChunk - live_first + 1u;
     if (blockIdx.y >= live_chunks) {   // no chunk for this slot: no ticket either
@@ -122,7 +129,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     {
         const uint32_t key0 = c_first * kChunk;
         const uint32_t j_hi = min(key0 + kChunk, max(pos0, key0));
-        if (j_hi > key0) stage_keys(a, ks, vs, key0, key0, j_hi, kvh, d);
+        if (j_hi > key0) stage_keys(a, kc, vc, ks, vs, key0, key0, j_hi, kvh, d);
     }
     grid_dependency_wait();
 
@@ -141,13 +148,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         {
             const uint32_t j_lo = first_chunk ? max(key0, min(pos0, key0 + kChunk)) : key0;
             const uint32_t j_hi = min(key0 + kChunk, p_last + 1u);
-            if (j_hi > j_lo) stage_keys(a, ks, vs, key0, j_lo, j_hi, kvh, d);
+            if (j_hi > j_lo) stage_keys(a, kc, vc, ks, vs, key0, j_lo, j_hi, kvh, d);
         }
         __syncthreads();
         // Scores: s = Σ_w dot(q_w, k_w) in quads, in order.
         for (uint32_t i = threadIdx.x; i < Q * kChunk; i += kAttnThreads) {
             const uint32_t m = i / kChunk, b = i % kChunk;
-            const uint32_t p = pos0 + row0 + m / G;
+            const uint32_t p = p_first + (seqs ? 0u : m / G);
             const uint32_t j = key0 + b;
             float s = 0.0f;
             if (j <= p && j >= earliest_of(p, a.window)) {
@@ -169,7 +176,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         // 2^(s − top) across lanes; the sum of a tile's weights, and the
         // running l and m, by lane 0 in key order.
         for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
-            const uint32_t p = pos0 + row0 + m / G;
+            const uint32_t p = p_first + (seqs ? 0u : m / G);
             const uint32_t early = earliest_of(p, a.window);
             bool chunk_live = false;
             float chunk_m = 0.0f, chunk_l = 0.0f;
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
         const uint32_t m = i / d, e = i % d;
         const uint32_t r = m / G, h = kvh * G + m % G;
-        const uint32_t p = pos0 + row0 + r;
+        const uint32_t p = p_first + (seqs ? 0u : r);
         const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
         bool live = false;
         float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
@@ -292,14 +299,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
 
 }  // namespace
 
-uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads) {
-    const Geometry g = geometry_of(query_heads, kv_heads);
+uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads, bool sequences) {
+    const Geometry g = geometry_of(query_heads, kv_heads, sequences);
     return (tokens + g.rows_per_tile - 1) / g.rows_per_tile;
 }
 
 cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
-    if (a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a)) return attention_prefill_run(a, stream, pdl);
-    const Geometry geo = geometry_of(a.query_heads, a.kv_heads);
+    if (!a.rows_are_sequences && a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a))
+        return attention_prefill_run(a, stream, pdl);
+    const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
     size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
                   kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
     const size_t fold = static_cast<size_t>(a.max_chunks) * kMaxQueries * 2u * sizeof(float);   // the fold's stats

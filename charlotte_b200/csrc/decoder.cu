@@ -16,6 +16,14 @@
 // the last draw's (gather's fed form), so a decode step is captured once as
 // a CUDA graph and replayed; a closing launch records the drawn token and
 // advances the position.
+//
+// Batched decode (no counterpart in the reference, which runs one sequence):
+// a decoder may hold S sequences, each with its own caches (sequence s's at
+// s·stride in each layer's cache allocation). A prompt step runs one
+// sequence's tokens; a batched step runs one token of every sequence, all at
+// the same position, as S rows — the products take the S rows in one pass of
+// the weights (a row's bits are those it has alone), rope, attention and the
+// selection treat each row as its own sequence.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -48,22 +56,29 @@ struct DevLayer {
     float* ffn_norm = nullptr;
     float* post_ffn_norm = nullptr;
     float* turns = nullptr;
-    uint16_t* key_cache = nullptr;
+    uint16_t* key_cache = nullptr;    // [sequences][slots][kv_heads][head_dim]
     uint16_t* value_cache = nullptr;
     uint32_t window = 0, slots = 0;
+    uint64_t sequence_stride = 0;      // elements between sequences' caches
 };
 
-// Records the drawn token and advances the step's position (decode graph).
+// Records each row's drawn token and advances the step's position (decode
+// graph): step i's tokens at [i·rows, (i+1)·rows).
 __global__ void advance_kernel(uint32_t* state, const uint32_t* sampled, uint32_t* tokens_out, uint32_t* failed_out,
-                               uint32_t capacity) {
+                               uint32_t capacity, uint32_t rows) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t step = state[1];
-    if (step < capacity) {
-        tokens_out[step] = sampled[0];
-        failed_out[step] = sampled[1];
+    for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) {
+        if (step < capacity) {
+            tokens_out[static_cast<size_t>(step) * rows + r] = sampled[4u * r];
+            failed_out[static_cast<size_t>(step) * rows + r] = sampled[4u * r + 1u];
+        }
     }
-    state[0] += 1u;   // position
-    state[1] = step + 1u;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        state[0] += 1u;   // position
+        state[1] = step + 1u;
+    }
 }
 
 }  // namespace
@@ -100,6 +115,10 @@ struct cb_decoder {
     cb_sampling step_sampling{};
     bool has_step = false;
     uint32_t next_position = 0;   // the position after the last step's tokens
+    uint32_t sequences = 1;
+    uint32_t rows = 0;            // working-set rows: max(step tokens, sequences)
+    std::vector<uint32_t> seq_next;   // each sequence's position after its last step
+    std::vector<uint8_t> seq_drawn;   // whether a sequence's last step drew a token
     bool tensor_prefill = false;  // CB_DECODER_TENSOR_PREFILL
     void* tensor_scratch = nullptr;
     uint64_t tensor_scratch_bytes = 0;
@@ -179,8 +198,12 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
     return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, flags, d->stream);
 }
 
-// The step's launches (graph.cpp's order). `fed`: the token is the last draw.
-int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb_sampling& s) {
+// The step's launches (graph.cpp's order). `fed`: the token is the last
+// draw. `seq` >= 0: `tokens` consecutive positions of sequence `seq`; -1:
+// a batched step, row r the token of sequence r (tokens == sequences).
+int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb_sampling& s, int seq = 0) {
+    const bool batch = seq < 0;
+    const uint32_t row0 = batch ? 0u : static_cast<uint32_t>(seq);   // this step's record / logits row
     const cb_model& m = d->model;
     const uint32_t H = m.hidden, dh = m.head_dim, qd = m.query_heads * dh, kvd = m.kv_heads * dh;
     const uint32_t* pos = d->state;
@@ -194,8 +217,9 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         g.first_row = 0;
         g.row_count = d->token_embd.rows;
         g.ids = d->ids;
-        g.sampled = d->sampled;
+        g.sampled = d->sampled + 4u * row0;
         g.fed = fed ? 1u : 0u;
+        g.fed_stride = batch ? 4u : 0u;
         g.tokens = tokens;
         g.scale = m.embed_scale;
         g.hidden = d->hidden;
@@ -218,8 +242,11 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         r.query = d->q;
         r.key = d->k;
         r.value = d->v;
-        r.key_cache = L.key_cache;
-        r.value_cache = L.value_cache;
+        const size_t cache_at = batch ? 0u : static_cast<size_t>(seq) * L.sequence_stride;
+        r.key_cache = L.key_cache + cache_at;
+        r.value_cache = L.value_cache + cache_at;
+        r.rows_are_sequences = batch ? 1u : 0u;
+        r.sequence_stride = L.sequence_stride;
         r.query_gain = L.q_norm;
         r.key_gain = L.k_norm;
         r.factors = d->factors;
@@ -235,8 +262,10 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         if (int rc = launched(rope_run(r, d->stream, true), "step: rope")) return rc;
         cb_attention at{};
         at.query = d->q;
-        at.key_cache = L.key_cache;
-        at.value_cache = L.value_cache;
+        at.key_cache = L.key_cache + cache_at;
+        at.value_cache = L.value_cache + cache_at;
+        at.rows_are_sequences = batch ? 1u : 0u;
+        at.sequence_stride = L.sequence_stride;
         at.out = d->att;
         at.partials = d->partials;
         at.stats = d->stats;
@@ -273,23 +302,27 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         pending_post = L.post_ffn_norm;
     }
     if (!logits) return CB_OK;
-    cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, 1u, m.epsilon};
+    // The output: a sequence step's last row, or every row of a batched step.
+    const uint32_t heads = batch ? tokens : 1u;
+    cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, batch ? 0u : 1u,
+               m.epsilon};
     if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
     {
         const DevWeight& head = d->output.piece ? d->output : d->token_embd;
-        float* outs[3] = {d->logits, nullptr, nullptr};
+        float* outs[3] = {d->logits + static_cast<size_t>(row0) * m.vocab, nullptr, nullptr};
         const uint32_t strides[3] = {m.vocab, 0, 0};
-        if (int rc = product(d, {&head}, CB_EPILOGUE_WRITE, d->normed + static_cast<size_t>(tokens - 1) * H, H, 1,
-                             outs, strides))
-            return rc;
+        const float* x = batch ? d->normed : d->normed + static_cast<size_t>(tokens - 1) * H;
+        if (int rc = product(d, {&head}, CB_EPILOGUE_WRITE, x, H, heads, outs, strides)) return rc;
     }
     cb_select sel{};
-    sel.logits = d->logits;
+    sel.logits = d->logits + static_cast<size_t>(row0) * m.vocab;
     sel.count = m.vocab;
     sel.partials = d->sel_partials;
     sel.ticket = d->sel_ticket;
-    sel.candidates = d->candidates;
-    sel.sampled = d->sampled;
+    sel.candidates = d->candidates + 128u * row0;
+    sel.sampled = d->sampled + 4u * row0;
+    sel.rows = heads;
+    sel.logits_stride = m.vocab;
     sel.position = pos;
     sel.tokens = tokens;
     sel.seed0 = s.seed0;
@@ -311,11 +344,13 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return fail_cuda(e, "decoder: capture");
-    int rc = enqueue_step(d, 1, fed, true, smp);
+    // One token of the one sequence, or (several sequences) a batched step.
+    const bool batch = d->sequences > 1;
+    int rc = enqueue_step(d, batch ? d->sequences : 1u, fed, true, smp, batch ? -1 : 0);
     if (rc == CB_OK && fed) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1);
-        cfg.blockDim = dim3(1);
+        cfg.blockDim = dim3(d->sequences < 1024 ? (d->sequences + 31u) / 32u * 32u : 1024u);
         cfg.stream = d->stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -323,7 +358,7 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, advance_kernel, d->state, static_cast<const uint32_t*>(d->sampled),
-                               d->gen_tokens, d->gen_failed, d->gen_capacity);
+                               d->gen_tokens, d->gen_failed, d->gen_capacity, d->sequences);
         if (e != cudaSuccess) rc = fail_cuda(e, "decoder: advance");
     }
     const cudaError_t end = cudaStreamEndCapture(d->stream, &g);
@@ -339,7 +374,13 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
 extern "C" {
 
 int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flags, cb_decoder** out) {
+    return cb_decoder_create_batch(m, max_step_tokens, 1u, flags, out);
+}
+
+int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_t sequences, uint32_t flags,
+                            cb_decoder** out) {
     if (!m || !out || !m->layer) return fail(CB_ERROR_INVALID, "cb_decoder_create: null argument");
+    if (sequences == 0 || sequences > 1024) return fail(CB_ERROR_INVALID, "cb_decoder_create: %u sequences", sequences);
     *out = nullptr;
     if (m->layers == 0 || m->hidden == 0 || m->hidden % 32 != 0 || m->hidden > 4096)
         return fail(CB_ERROR_BUILD, "cb_decoder_create: hidden width %u", m->hidden);
@@ -355,12 +396,16 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
     if (!d) return fail(CB_ERROR_BUILD, "cb_decoder_create: out of host memory");
     d->model = *m;
     d->max_tokens = max_step_tokens;
+    d->sequences = sequences;
+    d->rows = std::max(max_step_tokens, sequences);
+    d->seq_next.assign(sequences, 0u);
+    d->seq_drawn.assign(sequences, 0u);
     d->sms = sm_count();
     auto bail = [&](int rc) { cb_decoder_destroy(d); return rc; };
     if (d->sms <= 0) return bail(fail(CB_ERROR_BUILD, "cb_decoder_create: no CUDA device"));
     cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return bail(fail_cuda(e, "cb_decoder_create: stream"));
-    const uint32_t H = m->hidden, dh = m->head_dim, T = max_step_tokens;
+    const uint32_t H = m->hidden, dh = m->head_dim, T = d->rows, S = sequences;
     if (int rc = upload_weight(d, &d->token_embd, m->token_embd, "token_embd")) return bail(rc);
     if (int rc = upload_weight(d, &d->output, m->output, "output")) return bail(rc);
     if (int rc = upload_f32(d, &d->output_norm, m->output_norm, H)) return bail(rc);
@@ -393,7 +438,8 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
         // (kv.h:13-34); a global layer the whole context.
         const uint64_t ring = static_cast<uint64_t>(L.window) + T;
         L.slots = static_cast<uint32_t>(L.window < m->context && ring < m->context ? ring : m->context);
-        const size_t cache = static_cast<size_t>(L.slots) * m->kv_heads * dh;
+        L.sequence_stride = static_cast<uint64_t>(L.slots) * m->kv_heads * dh;
+        const size_t cache = static_cast<size_t>(L.sequence_stride) * S;
         if (int rc = dalloc(d, &L.key_cache, cache)) return bail(rc);
         if (int rc = dalloc(d, &L.value_cache, cache)) return bail(rc);
     }
@@ -407,15 +453,15 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
     if (int rc = dalloc(d, &d->att, T * qd)) return bail(rc);
     if (int rc = dalloc(d, &d->out, static_cast<size_t>(T) * H)) return bail(rc);
     if (int rc = dalloc(d, &d->act, static_cast<size_t>(T) * m->ffn)) return bail(rc);
-    if (int rc = dalloc(d, &d->logits, m->vocab)) return bail(rc);
+    if (int rc = dalloc(d, &d->logits, static_cast<size_t>(S) * m->vocab)) return bail(rc);
     if (int rc = dalloc(d, &d->partials, static_cast<size_t>(d->max_chunks) * T * qd)) return bail(rc);
     if (int rc = dalloc(d, &d->stats, static_cast<size_t>(d->max_chunks) * T * m->query_heads * 2)) return bail(rc);
-    const uint32_t tickets = cb_attention_tickets(T, m->query_heads, m->kv_heads);
+    const uint32_t tickets = std::max(cb_attention_tickets(T, m->query_heads, m->kv_heads), S * m->kv_heads);
     if (int rc = dalloc(d, &d->tickets, tickets)) return bail(rc);
-    if (int rc = dalloc(d, &d->sel_partials, static_cast<size_t>(select_tiles(m->vocab)) * 128)) return bail(rc);
-    if (int rc = dalloc(d, &d->sel_ticket, cb_select_tickets(m->vocab))) return bail(rc);
-    if (int rc = dalloc(d, &d->candidates, 128)) return bail(rc);
-    if (int rc = dalloc(d, &d->sampled, 4)) return bail(rc);
+    if (int rc = dalloc(d, &d->sel_partials, static_cast<size_t>(S) * select_tiles(m->vocab) * 128)) return bail(rc);
+    if (int rc = dalloc(d, &d->sel_ticket, static_cast<size_t>(S) * cb_select_tickets(m->vocab))) return bail(rc);
+    if (int rc = dalloc(d, &d->candidates, static_cast<size_t>(S) * 128)) return bail(rc);
+    if (int rc = dalloc(d, &d->sampled, static_cast<size_t>(S) * 4)) return bail(rc);
     if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
     if (flags & CB_DECODER_TENSOR_PREFILL) {
@@ -427,9 +473,10 @@ int cb_decoder_create(const cb_model* m, uint32_t max_step_tokens, uint32_t flag
         d->tensor_prefill = true;
     }
     e = cudaMemset(d->tickets, 0, tickets * sizeof(unsigned int));
-    if (e == cudaSuccess) e = cudaMemset(d->sel_ticket, 0, cb_select_tickets(m->vocab) * sizeof(unsigned int));
+    if (e == cudaSuccess)
+        e = cudaMemset(d->sel_ticket, 0, static_cast<size_t>(S) * cb_select_tickets(m->vocab) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->state, 0, 2 * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(d->sampled, 0, 4 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(d->sampled, 0, static_cast<size_t>(S) * 4 * sizeof(uint32_t));
     if (e != cudaSuccess) return bail(fail_cuda(e, "cb_decoder_create: memset"));
     *out = d;
     return CB_OK;
@@ -447,7 +494,13 @@ void cb_decoder_destroy(cb_decoder* d) {
 
 int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, uint32_t position, uint32_t logits,
                     const cb_sampling* s, uint32_t* record_host) {
+    return cb_decoder_step_sequence(d, 0, ids_host, tokens, position, logits, s, record_host);
+}
+
+int cb_decoder_step_sequence(cb_decoder* d, uint32_t seq, const uint32_t* ids_host, uint32_t tokens, uint32_t position,
+                             uint32_t logits, const cb_sampling* s, uint32_t* record_host) {
     if (!d || !ids_host || tokens == 0) return fail(CB_ERROR_INVALID, "cb_decoder_step: null argument or no tokens");
+    if (seq >= d->sequences) return fail(CB_ERROR_INVALID, "cb_decoder_step: sequence %u of %u", seq, d->sequences);
     if (tokens > d->max_tokens)
         return fail(CB_ERROR_INVALID, "cb_decoder_step: %u tokens over the step's %u", tokens, d->max_tokens);
     if (static_cast<uint64_t>(position) + tokens > d->model.context)
@@ -460,7 +513,7 @@ int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, ui
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: upload");
     const cb_sampling smp = s ? *s : greedy;
-    if (tokens == 1 && logits) {
+    if (tokens == 1 && logits && d->sequences == 1) {
         // A decode step: the captured graph, replayed.
         if (d->step_graph && !same_sampling(smp, d->step_sampling)) {
             cudaGraphExecDestroy(d->step_graph);
@@ -472,17 +525,49 @@ int cb_decoder_step(cb_decoder* d, const uint32_t* ids_host, uint32_t tokens, ui
         }
         e = cudaGraphLaunch(d->step_graph, d->stream);
         if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: launch");
-    } else if (int rc = enqueue_step(d, tokens, false, logits != 0, smp)) {
+    } else if (int rc = enqueue_step(d, tokens, false, logits != 0, smp, static_cast<int>(seq))) {
         return rc;
     }
     if (logits && record_host) {
-        e = cudaMemcpyAsync(record_host, d->sampled, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+        e = cudaMemcpyAsync(record_host, d->sampled + 4u * seq, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                            d->stream);
         if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step: readback");
     }
     e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step");
+    d->seq_drawn[seq] = logits != 0;
+    d->seq_next[seq] = position + tokens;
     d->has_step = logits != 0;
     d->next_position = position + tokens;
+    return cb_fault_check(nullptr);
+}
+
+int cb_decoder_step_batch(cb_decoder* d, const uint32_t* ids_host, uint32_t position, const cb_sampling* s,
+                          uint32_t* records_host) {
+    if (!d || !ids_host) return fail(CB_ERROR_INVALID, "cb_decoder_step_batch: null argument");
+    const uint32_t S = d->sequences;
+    if (static_cast<uint64_t>(position) + 1 > d->model.context)
+        return fail(CB_ERROR_STEP, "cb_decoder_step_batch: position past the context of %u", d->model.context);
+    for (uint32_t i = 0; i < S; ++i)
+        if (ids_host[i] >= d->model.vocab) return fail(CB_ERROR_INVALID, "cb_decoder_step_batch: token %u", ids_host[i]);
+    const cb_sampling greedy{0, 0, 1, 0.0f, 1.0f, 0.0f};
+    const uint32_t st[2] = {position, 0};
+    cudaError_t e = cudaMemcpyAsync(d->ids, ids_host, S * sizeof(uint32_t), cudaMemcpyHostToDevice, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step_batch: upload");
+    if (int rc = enqueue_step(d, S, false, true, s ? *s : greedy, S > 1 ? -1 : 0)) return rc;
+    if (records_host) {
+        e = cudaMemcpyAsync(records_host, d->sampled, 4ull * S * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+        if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step_batch: readback");
+    }
+    e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step_batch");
+    for (uint32_t i = 0; i < S; ++i) {
+        d->seq_drawn[i] = 1;
+        d->seq_next[i] = position + 1;
+    }
+    d->has_step = true;
+    d->next_position = position + 1;
     return cb_fault_check(nullptr);
 }
 
@@ -490,14 +575,21 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
                         uint32_t* failed_host, float* device_ms) {
     if (!d || !tokens_host) return fail(CB_ERROR_INVALID, "cb_decoder_generate: null argument");
     if (!d->has_step) return fail(CB_ERROR_INVALID, "cb_decoder_generate: no drawn token to feed");
+    if (d->sequences > 1) {
+        for (uint32_t i = 0; i < d->sequences; ++i)
+            if (!d->seq_drawn[i] || d->seq_next[i] != d->seq_next[0])
+                return fail(CB_ERROR_INVALID,
+                            "cb_decoder_generate: every sequence needs a drawn token at one common position");
+        d->next_position = d->seq_next[0];
+    }
     if (steps == 0) return CB_OK;
     const cb_sampling greedy{0, 0, 1, 0.0f, 1.0f, 0.0f};
     const cb_sampling smp = s ? *s : greedy;
     cudaError_t e;
     if (steps > d->gen_capacity) {
         const uint32_t cap = steps < 4096 ? 4096 : steps;
-        if (int rc = dalloc(d, &d->gen_tokens, cap)) return rc;
-        if (int rc = dalloc(d, &d->gen_failed, cap)) return rc;
+        if (int rc = dalloc(d, &d->gen_tokens, static_cast<size_t>(cap) * d->sequences)) return rc;
+        if (int rc = dalloc(d, &d->gen_failed, static_cast<size_t>(cap) * d->sequences)) return rc;
         d->gen_capacity = cap;
         if (d->decode_graph) { cudaGraphExecDestroy(d->decode_graph); d->decode_graph = nullptr; }
     }
@@ -527,9 +619,10 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
         if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate: launch");
     }
     if (device_ms) cudaEventRecord(ev[1], d->stream);
-    e = cudaMemcpyAsync(tokens_host, d->gen_tokens, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+    const size_t n = static_cast<size_t>(steps) * d->sequences;
+    e = cudaMemcpyAsync(tokens_host, d->gen_tokens, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess && failed_host)
-        e = cudaMemcpyAsync(failed_host, d->gen_failed, steps * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
+        e = cudaMemcpyAsync(failed_host, d->gen_failed, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     if (device_ms) {
         if (e == cudaSuccess) e = cudaEventElapsedTime(device_ms, ev[0], ev[1]);
@@ -538,7 +631,15 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
     }
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate");
     d->next_position += steps;
+    for (auto& p : d->seq_next) p = d->next_position;
     return cb_fault_check(nullptr);
+}
+
+int cb_decoder_logits_row(cb_decoder* d, uint32_t row, float* logits_host) {
+    if (!d || !logits_host || row >= d->sequences) return fail(CB_ERROR_INVALID, "cb_decoder_logits_row: argument");
+    const cudaError_t e = cudaMemcpy(logits_host, d->logits + static_cast<size_t>(row) * d->model.vocab,
+                                     d->model.vocab * sizeof(float), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? CB_OK : fail_cuda(e, "cb_decoder_logits_row");
 }
 
 int cb_decoder_logits(cb_decoder* d, float* logits_host) {

@@ -35,7 +35,7 @@ __global__ void gather_kernel(GatherArgs a) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t row = i / groups, g = i % groups;
     if (row >= a.tokens) return;
-    const uint32_t token = a.fed ? a.sampled[0] : a.ids[row];
+    const uint32_t token = a.fed ? a.sampled[static_cast<size_t>(row) * a.fed_stride] : a.ids[row];
     if (token < a.first_row || token - a.first_row >= a.row_count) return;
     const uint32_t r = token - a.first_row;
     const uint8_t* s[F::kStreams];

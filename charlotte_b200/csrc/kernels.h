@@ -21,7 +21,7 @@ using SelectArgs = cb_select;
 cudaError_t norm_run(const NormArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t rope_run(const RopeArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
-uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads);
+uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads, bool sequences);
 // The many-query form (attention_prefill.cu): same bits, a CTA per query tile.
 bool attention_prefill_fits(const AttentionArgs& a);
 cudaError_t attention_prefill_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);

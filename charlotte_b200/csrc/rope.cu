@@ -37,7 +37,9 @@ __global__ void rope_kernel(RopeArgs a) {
     const uint32_t d = a.head_dim;
     const uint32_t lanes = d / 8u;
     const uint32_t row = blockIdx.x;
-    const uint32_t p = (a.position ? *a.position : a.position0) + row;
+    // Rows are consecutive positions of one sequence, or (batched decode)
+    // one token each of `tokens` sequences at the step's position.
+    const uint32_t p = (a.position ? *a.position : a.position0) + (a.rows_are_sequences ? 0u : row);
     float* cosines = angles;
     float* sines = angles + d / 2u;
     for (uint32_t k = threadIdx.x; k < d / 2u; k += blockDim.x) {
@@ -113,7 +115,8 @@ __global__ void rope_kernel(RopeArgs a) {
         dst[lane] = x0;
         dst[lane + lanes] = x1;
     } else {
-        uint16_t* cache = is_value ? a.value_cache : a.key_cache;
+        uint16_t* cache = (is_value ? a.value_cache : a.key_cache) +
+                          (a.rows_are_sequences ? static_cast<size_t>(row) * a.sequence_stride : 0u);
         uint16_t* dst = cache + (static_cast<size_t>(p % a.slots) * hkv + kvh) * d;
         store_f16x4(dst + 4u * lane, x0);
         store_f16x4(dst + 4u * (lane + lanes), x1);

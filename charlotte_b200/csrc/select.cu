@@ -145,6 +145,16 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
     grid_dependency_wait();
     const uint32_t t = threadIdx.x;
     const uint32_t tile = blockIdx.x;
+    // Row blockIdx.y of a batched selection: its own logits, scratch,
+    // candidates and record.
+    const uint32_t row = blockIdx.y;
+    if (row) {
+        a.logits += static_cast<size_t>(row) * a.logits_stride;
+        a.partials += static_cast<size_t>(row) * gridDim.x * kKeep * 2u;
+        a.ticket += static_cast<size_t>(row) * (1u + (gridDim.x + kGroup - 1u) / kGroup);
+        a.candidates += static_cast<size_t>(row) * kKeep * 2u;
+        a.sampled += static_cast<size_t>(row) * 4u;
+    }
     {
         const uint32_t e = tile * kTile + t;
         uint64_t k = 0;
@@ -207,7 +217,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
     __syncthreads();
     if (t == 0) {
         const uint32_t pos = a.position ? *a.position : a.position0;
-        const uint32_t w0 = philox_word0(pos + a.tokens, a.seed0, a.seed1);
+        const uint32_t w0 = philox_word0(pos + a.tokens, a.seed0, a.seed1 + row);
         const float u = static_cast<float>(w0 >> 9) * (1.0f / 8388608.0f) + (1.0f / 16777216.0f);
         if (top_p) {
             float sum = 0.0f;
@@ -257,7 +267,7 @@ cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl) {
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles);
+    cfg.gridDim = dim3(tiles, a.rows > 1 ? a.rows : 1u);
     cfg.blockDim = dim3(kSelThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

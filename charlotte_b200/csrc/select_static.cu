@@ -71,6 +71,8 @@ int cb_select_run_static(const cb_select* s, uint32_t flags, void* stream) {
     if (s->partials || s->ticket)
         return cb::fail(CB_ERROR_INVALID,
                         "cb_select_run_static: partials and ticket must be NULL (this entry point uses its own scratch)");
+    if (s->rows > 1)
+        return cb::fail(CB_ERROR_INVALID, "cb_select_run_static: one row a call (its fixed scratch holds one selection)");
     if (s->count == 0 || s->count > kStaticCount)
         return cb::fail(CB_ERROR_INVALID, "cb_select_run_static: %u logits; its fixed scratch holds 1 to %u",
                         s->count, kStaticCount);

@@ -305,3 +305,82 @@ class Decoder:
         out = np.empty(self.model.arch.vocab, np.float32)
         _check(self.lib.cb_decoder_logits(self.handle, out.ctypes.data))
         return out
+
+
+class BatchDecoder(Decoder):
+    """`sequences` independent sequences in one decoder (cb_decoder_create_batch):
+    prompts go in per sequence, then every sequence steps together, one token
+    each at a common position — the products read the weights once for all
+    rows. Each row's bits are those of its sequence decoded alone."""
+
+    def __init__(self, model: Model, sequences: int, max_step_tokens: int = 512, tensor_prefill: bool = False):
+        L = _lib()
+        L.cb_decoder_create_batch.restype = ctypes.c_int
+        L.cb_decoder_create_batch.argtypes = [ctypes.POINTER(CModel), ctypes.c_uint32, ctypes.c_uint32,
+                                              ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p)]
+        L.cb_decoder_step_sequence.restype = ctypes.c_int
+        L.cb_decoder_step_sequence.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32,
+                                               ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(CSampling),
+                                               ctypes.c_void_p]
+        L.cb_decoder_step_batch.restype = ctypes.c_int
+        L.cb_decoder_step_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                            ctypes.POINTER(CSampling), ctypes.c_void_p]
+        L.cb_decoder_logits_row.restype = ctypes.c_int
+        L.cb_decoder_logits_row.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+        # the one-sequence bindings (destroy, generate, logits) come from Decoder
+        L.cb_decoder_create.restype = ctypes.c_int
+        L.cb_decoder_destroy.argtypes = [ctypes.c_void_p]
+        L.cb_decoder_generate.restype = ctypes.c_int
+        L.cb_decoder_generate.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(CSampling),
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)]
+        self.lib = L
+        self.model = model
+        self.sequences = sequences
+        self.max_step_tokens = max_step_tokens
+        cm, self._layers = to_c(model)
+        self._cm = cm
+        h = ctypes.c_void_p()
+        flags = 1 if tensor_prefill else 0
+        _check(L.cb_decoder_create_batch(ctypes.byref(cm), max_step_tokens, sequences, flags, ctypes.byref(h)))
+        self.handle = h
+
+    def step_sequence(self, seq: int, ids, position: int, logits: bool = True,
+                      sampling: CSampling | None = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rec = np.zeros(4, np.uint32)
+        s = sampling or self.sampling()
+        _check(self.lib.cb_decoder_step_sequence(self.handle, seq, ids.ctypes.data, ids.size, position, int(logits),
+                                                 ctypes.byref(s), rec.ctypes.data))
+        return rec
+
+    def prefill_sequence(self, seq: int, ids, position: int = 0, sampling: CSampling | None = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rec = None
+        for at in range(0, ids.size, self.max_step_tokens):
+            part = ids[at: at + self.max_step_tokens]
+            rec = self.step_sequence(seq, part, position + at, logits=at + part.size >= ids.size, sampling=sampling)
+        return rec
+
+    def step_batch(self, ids, position: int, sampling: CSampling | None = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        assert ids.size == self.sequences
+        recs = np.zeros((self.sequences, 4), np.uint32)
+        s = sampling or self.sampling()
+        _check(self.lib.cb_decoder_step_batch(self.handle, ids.ctypes.data, position, ctypes.byref(s),
+                                              recs.ctypes.data))
+        return recs
+
+    def generate(self, steps: int, sampling: CSampling | None = None, timed: bool = False):
+        """Fed batched steps as one replayed CUDA graph: tokens [steps, sequences]."""
+        toks = np.zeros((steps, self.sequences), np.uint32)
+        failed = np.zeros((steps, self.sequences), np.uint32)
+        s = sampling or self.sampling()
+        ms = ctypes.c_float(0.0)
+        _check(self.lib.cb_decoder_generate(self.handle, steps, ctypes.byref(s), toks.ctypes.data,
+                                            failed.ctypes.data, ctypes.byref(ms) if timed else None))
+        return (toks, failed, ms.value) if timed else (toks, failed)
+
+    def logits_row(self, row: int) -> np.ndarray:
+        out = np.empty(self.model.arch.vocab, np.float32)
+        _check(self.lib.cb_decoder_logits_row(self.handle, row, out.ctypes.data))
+        return out

@@ -177,6 +177,12 @@ typedef struct cb_rope {
     uint32_t halves;
     uint32_t slots;
     float epsilon;
+    /* Batched decode (no counterpart in the reference, which decodes one
+     * sequence): nonzero makes row t the one token of sequence t, every row
+     * at the step's position, its cache at key_cache/value_cache +
+     * t·sequence_stride elements. Zero: rows are consecutive positions. */
+    uint32_t rows_are_sequences;
+    uint64_t sequence_stride;
 } cb_rope;
 CB_API int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream);
 /* θ_k / 2π for k < d/2, base^(−2k/d) in f64 rounded once to f32 (host). */
@@ -209,6 +215,11 @@ typedef struct cb_attention {
     uint32_t window;
     uint32_t max_chunks;
     float scale_log2e;
+    /* Batched decode, as in cb_rope: row t is sequence t's query at the
+     * step's position over its own cache (+ t·sequence_stride); `tickets`
+     * then holds tokens·kv_heads zeroed words. */
+    uint32_t rows_are_sequences;
+    uint64_t sequence_stride;
 } cb_attention;
 CB_API int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream);
 /* Ticket words cb_attention needs for `tokens` rows. */
@@ -231,6 +242,9 @@ typedef struct cb_gather {
     uint32_t tokens;
     float scale;
     float* hidden;
+    /* A fed step of several rows (batched decode): row t reads its token
+     * from sampled[t·fed_stride]. Zero: one fed row, sampled[0]. */
+    uint32_t fed_stride;
 } cb_gather;
 CB_API int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream);
 
@@ -256,6 +270,12 @@ typedef struct cb_select {
     uint32_t seed0, seed1;
     uint32_t top_k;
     float temperature, top_p, min_p, log_min_p;
+    /* Batched decode: `rows` independent selections (0 or 1: one), row r's
+     * logits at logits + r·logits_stride, its partials, ticket words,
+     * candidates and record at r times their one-row sizes; row r draws with
+     * seed1 + r. */
+    uint32_t rows;
+    uint32_t logits_stride;
 } cb_select;
 CB_API int cb_select_run(const cb_select* s, uint32_t flags, void* stream);
 CB_API uint32_t cb_select_tiles(uint32_t count);
@@ -366,6 +386,26 @@ CB_API int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling*
 
 /* The last step's logits [vocab] to host memory. */
 CB_API int cb_decoder_logits(cb_decoder* d, float* logits_host);
+
+/* ---- batched decode (no counterpart in the reference, which runs one
+ * sequence): a decoder holding `sequences` independent sequences, each with
+ * its own KV caches. A prompt goes in per sequence (cb_decoder_step_sequence:
+ * consecutive positions of sequence `seq`, its draw in record row `seq`);
+ * then every sequence steps together, one token each at one common position
+ * — cb_decoder_step_batch from host ids, or cb_decoder_generate (fed from
+ * each row's last draw; tokens_host then holds steps × sequences ids, step
+ * by step). A row's arithmetic is that of its sequence decoded alone, so
+ * its tokens and logits are bit-identical to a one-sequence decoder's. */
+CB_API int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_t sequences, uint32_t flags,
+                                   cb_decoder** out);
+CB_API int cb_decoder_step_sequence(cb_decoder* d, uint32_t seq, const uint32_t* ids_host, uint32_t tokens,
+                                    uint32_t position, uint32_t logits, const cb_sampling* s, uint32_t* record_host);
+/* One token of every sequence (ids_host[sequences]) at `position`; the
+ * records [sequences][4] to records_host. Synchronous. */
+CB_API int cb_decoder_step_batch(cb_decoder* d, const uint32_t* ids_host, uint32_t position, const cb_sampling* s,
+                                 uint32_t* records_host);
+/* Row `row`'s logits of the last step [vocab] to host memory. */
+CB_API int cb_decoder_logits_row(cb_decoder* d, uint32_t row, float* logits_host);
 
 /* Device pointers of the decoder's working buffers, for callers that feed
  * it from their own kernels: the logits [vocab] and the sampled record [4]. */
