@@ -296,6 +296,8 @@ def run_ours(args):
     }
     if not args.no_decode:
         result["qwen3_decode"] = decode_bench(args.decode_steps, 512, SEED + 7 + rank, world)
+    if not args.no_batch:
+        result["gemma_batched_decode"] = gemma_batch_bench(args.batch_steps, world, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         if "qwen3_decode" in result:
@@ -423,6 +425,40 @@ def llama_bench(decode_steps, seed):
                              "ms_per_token": round(dev_ms / decode_steps, 4), "failed_steps": int(failed.sum())}
         dec.close()
     return out
+
+
+def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024):
+    """Gemma-3-1B shapes, random-init weights; 64 independent
+    sequences with random 1,024-token prompts, sharded over the ranks (64/N
+    each, no collective on the data path: strong scaling of a fixed batch);
+    each rank prefills its sequences, then all step together, one token per
+    sequence a step, as one replayed CUDA graph. tok/s = all sequences'
+    tokens / the max over ranks of the device time."""
+    from charlotte_b200 import model as M
+    assert sequences % world == 0
+    S = sequences // world
+    arch = M.gemma_3_1b(context=prompt_len + steps + 64)
+    m = M.synthesize(arch, seed=SEED + 21)   # the same weights on every rank
+    bd = M.BatchDecoder(m, S, max_step_tokens=512)
+    for s in range(S):
+        g = rank * S + s   # global sequence id
+        prompt = np.random.default_rng(SEED + 1000 + g).integers(0, arch.vocab, prompt_len).astype(np.uint32)
+        bd.prefill_sequence(s, prompt)
+    bd.generate(3)   # capture and warm the batched graph
+    for s in range(S):   # restart every sequence from its prompt
+        g = rank * S + s
+        prompt = np.random.default_rng(SEED + 1000 + g).integers(0, arch.vocab, prompt_len).astype(np.uint32)
+        bd.prefill_sequence(s, prompt)
+    barrier(world)
+    toks, failed, dev_ms = bd.generate(steps, timed=True)
+    dev_ms = max_over_ranks(dev_ms, world)
+    bd.close()
+    return {"workload": "gemma-3-1b shapes (configs[4]): %d sequences x %d-token prompts, %d batched steps" % (
+                sequences, prompt_len, steps),
+            "sequences_per_gpu": S, "tok_s": round(sequences * steps / (dev_ms * 1e-3), 1),
+            "ms_per_step": round(dev_ms / steps, 4), "scaling": "strong (64 sequences in all, split over ranks)",
+            "failed_steps": int(failed.sum()),
+            "head": "tied Q8_0 262,144 x 1,152 (Q6_K needs widths of whole 256-weight super-blocks)"}
 
 
 def cpu_decode_baseline(seed):
@@ -636,6 +672,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--no-batch", action="store_true", help="skip the Gemma batched decode (configs[4])")
+    ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--batch-prompt", type=int, default=1024)
     ap.add_argument("--case", default=None, help="profile one product (format:rows:K) or 'decode'")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -645,6 +684,14 @@ def main():
         ms = [16, 128, 256, 512, 2048]
         for f in (4, 8):
             print(json.dumps(sweep_bench(flags=f, ms=ms, formats=(2,), head=False)))
+    elif args.case == "gemma":
+        rank, world, local = dist_setup(args.gpus)
+        r = gemma_batch_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt)
+        if rank == 0:
+            print(json.dumps(r))
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
     elif args.case == "llama":
         import torch
         torch.cuda.set_device(0)

@@ -404,8 +404,8 @@ __device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const flo
     }
 }
 
-template <typename F, int MT>
-__global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a) {
+template <typename F, int MT, int W>
+__global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     constexpr int R = 2;
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t G = a.columns / 32u;
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a)
     const uint32_t tok_floats = 32u * lane_stride;   // one token's staged x
     const uint32_t stage_bytes = RowStreams<F>::row_stage(G) * R;
     const uint32_t batches = batch_count<R>(a);
-    const uint32_t stride = gridDim.x * kWarps;
+    const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
 
     float* xs = reinterpret_cast<float*>(smem);
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a)
         fence_barrier_init();
     }
     __syncwarp();
-    const uint32_t first = blockIdx.x * kWarps + warp;
+    const uint32_t first = blockIdx.x * W + warp;
     if (first < batches) issue_batch<F, R>(a, first, stages, &bars[0], G, lane);
     if (first + stride < batches) issue_batch<F, R>(a, first + stride, stages + stage_bytes, &bars[1], G, lane);
 
@@ -444,11 +444,11 @@ __global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a)
         float4* dst = reinterpret_cast<float4*>(xs + i * tok_floats + lane * lane_stride);
         if (i < nt) {
             const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i) * a.x_stride);
-            for (uint32_t g = lo + warp; g < hi; g += kWarps)
+            for (uint32_t g = lo + warp; g < hi; g += W)
 #pragma unroll
                 for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = xg[g * 8u + v];
         } else {
-            for (uint32_t g = lo + warp; g < hi; g += kWarps)
+            for (uint32_t g = lo + warp; g < hi; g += W)
 #pragma unroll
                 for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -555,20 +555,20 @@ __global__ void __launch_bounds__(kThreads) decode_mt_kernel(const MatmulArgs a)
     }
 }
 
-template <typename F, int MT>
+template <typename F, int MT, int W = kWarps>
 size_t decode_mt_smem(uint32_t G) {
     return static_cast<size_t>(MT) * 32u * x_lane_stride(G) * 4u +
-           kWarps * (16u + 2u * MT * kRedStride * 4u + 2ull * 2u * RowStreams<F>::row_stage(G));
+           W * (16u + 2u * MT * kRedStride * 4u + 2ull * 2u * RowStreams<F>::row_stage(G));
 }
 
-template <typename F, int MT>
+template <typename F, int MT, int W>
 cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    const size_t smem = decode_mt_smem<F, MT>(G);
+    const size_t smem = decode_mt_smem<F, MT, W>(G);
     if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
     const uint32_t batches = a.epilogue == kGated ? a.member[0].rows
                                                   : [&] { uint32_t n = 0; for (uint32_t m = 0; m < a.members; ++m) n += (a.member[m].rows + 1) / 2; return n; }();
-    auto kernel = decode_mt_kernel<F, MT>;
+    auto kernel = decode_mt_kernel<F, MT, W>;
     static bool configured = false;   // per instantiation
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDecodeSmem);
@@ -578,7 +578,7 @@ cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t str
         configured = true;
     }
     const uint32_t groups = (a.tokens + MT - 1) / MT;
-    uint32_t ctas = (batches + kWarps - 1) / kWarps;
+    uint32_t ctas = (batches + W - 1) / W;
     uint32_t per_sm = static_cast<uint32_t>((227u * 1024u) / (smem + 1024u));
     if (per_sm < 1) per_sm = 1;
     if (per_sm > 16) per_sm = 16;
@@ -588,7 +588,7 @@ cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t str
     if (ctas == 0) ctas = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ctas, groups);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(W * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -602,15 +602,25 @@ cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t str
 // Tokens a weight pass: 2, 4, 8 or 16 — the fewest that cover a short step,
 // 16 for longer ones — stepping down while x of that many tokens and the
 // stages do not fit shared memory (wide rows).
+// Eight warps a CTA where they fit (x is staged once a CTA, so more warps
+// share it), else four.
+template <typename F, int MT>
+cudaError_t launch_mt_warps(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    const uint32_t G = a.columns / 32u;
+    if (decode_mt_smem<F, MT, 8>(G) <= static_cast<size_t>(kMaxDecodeSmem))
+        return launch_decode_mt<F, MT, 8>(a, sm_count, stream, pdl);
+    return launch_decode_mt<F, MT, 4>(a, sm_count, stream, pdl);
+}
+
 template <typename F>
 cudaError_t dispatch_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
     const size_t budget = static_cast<size_t>(kMaxDecodeSmem);
     const uint32_t want = a.tokens > 8 ? 16u : (a.tokens > 4 ? 8u : (a.tokens > 2 ? 4u : 2u));
-    if (want >= 16 && decode_mt_smem<F, 16>(G) <= budget) return launch_decode_mt<F, 16>(a, sm_count, stream, pdl);
-    if (want >= 8 && decode_mt_smem<F, 8>(G) <= budget) return launch_decode_mt<F, 8>(a, sm_count, stream, pdl);
-    if (want >= 4 && decode_mt_smem<F, 4>(G) <= budget) return launch_decode_mt<F, 4>(a, sm_count, stream, pdl);
-    if (decode_mt_smem<F, 2>(G) <= budget) return launch_decode_mt<F, 2>(a, sm_count, stream, pdl);
+    if (want >= 16 && decode_mt_smem<F, 16>(G) <= budget) return launch_mt_warps<F, 16>(a, sm_count, stream, pdl);
+    if (want >= 8 && decode_mt_smem<F, 8>(G) <= budget) return launch_mt_warps<F, 8>(a, sm_count, stream, pdl);
+    if (want >= 4 && decode_mt_smem<F, 4>(G) <= budget) return launch_mt_warps<F, 4>(a, sm_count, stream, pdl);
+    if (decode_mt_smem<F, 2>(G) <= budget) return launch_mt_warps<F, 2>(a, sm_count, stream, pdl);
     return cudaErrorInvalidValue;
 }
 

@@ -10,7 +10,7 @@
 //  1. x is rounded to f16 once, into the caller's scratch ([tokens][K]);
 //  2. one CTA a 128-token × 128-slot tile:
 //     - a TMA warp loads each 128 × 64 block of x16 with a tiled bulk tensor
-//       copy (128-byte swizzle, no multicast) straight into the K-major
+//       copy (128-byte swizzle, this CTA only) straight into the K-major
 //       layout the MMA reads;
 //     - eight producer warps decode the tile's weight blocks (four blocks of
 //       codes in flight in registers a thread) to f16 and store them in the
@@ -85,7 +85,7 @@ __global__ void to_f16_kernel(const float* x, uint32_t x_stride, uint32_t K, uin
 }
 
 // Tiled TMA load of box {64, 128} at (k0, row0) of the x16 map into `dst`,
-// completing on `bar`. No cluster multicast.
+// completing on `bar`, into this CTA's shared memory only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t k0, int32_t row0,
                                             uint64_t* bar) {
     asm volatile(
