@@ -461,6 +461,53 @@ def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024):
             "head": "tied Q8_0 262,144 x 1,152 (Q6_K needs widths of whole 256-weight super-blocks)"}
 
 
+def gemma_split_bench(steps, world, rank, sequences=64, prompt_len=1024):
+    """configs[4] with the head split by vocabulary: sequences sharded as in
+    gemma_batch_bench for the layers; per step the normed rows are
+    all-gathered (NCCL), each rank computes its vocabulary shard of the head
+    for all 64 rows and its top 64 (global ids), the candidate lists are
+    all-gathered, and every rank merges and draws (charlotte_b200.shard).
+    Timed with CUDA events on the decoder's stream around the steps (host
+    orchestration between launches included)."""
+    import torch
+    from charlotte_b200 import model as M
+    from charlotte_b200 import shard
+    assert sequences % world == 0
+    S = sequences // world
+    arch = M.gemma_3_1b(context=prompt_len + steps + 64)
+    m = M.synthesize(arch, seed=SEED + 21)
+    bd = M.BatchDecoder(m, S, max_step_tokens=512)
+
+    def prefill():
+        for s in range(S):
+            g = rank * S + s
+            prompt = np.random.default_rng(SEED + 1000 + g).integers(0, arch.vocab, prompt_len).astype(np.uint32)
+            bd.prefill_sequence(s, prompt)
+    sh = shard.SplitHead(bd, sequences, world, rank)
+    prefill()
+    for i in range(3):   # warm
+        sh.step(prompt_len + i)
+    prefill()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(sh.stream)
+    toks = []
+    for i in range(steps):
+        sh.step(prompt_len + i)
+        toks.append(sh.sampled_all[:, 0])
+    e1.record(sh.stream)
+    torch.cuda.synchronize()
+    dev_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    bd.close()
+    return {"workload": "gemma-3-1b shapes (configs[4]) with a vocabulary-split head: %d sequences x %d-token "
+                        "prompts, %d steps" % (sequences, prompt_len, steps),
+            "sequences_per_gpu": S, "vocab_rows_per_gpu": arch.vocab // world,
+            "tok_s": round(sequences * steps / (dev_ms * 1e-3), 1), "ms_per_step": round(dev_ms / steps, 4),
+            "collectives_per_step": "all-gather of normed rows (%d B) + all-gather of candidates (%d B) a rank" % (
+                S * arch.hidden * 4, sequences * 128 * 4)}
+
+
 def cpu_decode_baseline(seed):
     """The oracle's pass (the reference's order of operations) on all host
     cores: a 16-token prompt then 4 decode steps of Qwen3-0.6B."""
@@ -687,6 +734,14 @@ def main():
     elif args.case == "gemma":
         rank, world, local = dist_setup(args.gpus)
         r = gemma_batch_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt)
+        if rank == 0:
+            print(json.dumps(r))
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    elif args.case == "gemma-split":
+        rank, world, local = dist_setup(args.gpus)
+        r = gemma_split_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt)
         if rank == 0:
             print(json.dumps(r))
         if world > 1:

@@ -83,7 +83,16 @@ class Select(ctypes.Structure):
                 ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
                 ("seed0", ctypes.c_uint32), ("seed1", ctypes.c_uint32), ("top_k", ctypes.c_uint32),
                 ("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("min_p", ctypes.c_float),
-                ("log_min_p", ctypes.c_float), ("rows", ctypes.c_uint32), ("logits_stride", ctypes.c_uint32)]
+                ("log_min_p", ctypes.c_float), ("rows", ctypes.c_uint32), ("logits_stride", ctypes.c_uint32),
+                ("id_offset", ctypes.c_uint32), ("candidates_only", ctypes.c_uint32)]
+
+
+class SelectMerge(ctypes.Structure):
+    _fields_ = [("lists_data", ctypes.c_void_p), ("lists", ctypes.c_uint32), ("rows", ctypes.c_uint32),
+                ("candidates", ctypes.c_void_p), ("sampled", ctypes.c_void_p), ("position", ctypes.c_void_p),
+                ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32), ("seed0", ctypes.c_uint32),
+                ("seed1", ctypes.c_uint32), ("top_k", ctypes.c_uint32), ("temperature", ctypes.c_float),
+                ("top_p", ctypes.c_float), ("min_p", ctypes.c_float), ("log_min_p", ctypes.c_float)]
 
 
 RUN_PDL = 1
@@ -114,7 +123,7 @@ def lib() -> ctypes.CDLL:
                                     ctypes.c_uint32, ctypes.c_void_p]
         for name, struct in (("cb_norm_run", Norm), ("cb_rope_run", Rope), ("cb_attention_run", Attention),
                              ("cb_gather_run", Gather), ("cb_select_run", Select),
-                             ("cb_select_run_static", Select)):
+                             ("cb_select_run_static", Select), ("cb_select_merge_run", SelectMerge)):
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(struct), ctypes.c_uint32, ctypes.c_void_p]
@@ -196,7 +205,7 @@ def run(kind: str, **fields) -> None:
     select, select_static; fields are the C struct's (tensors become device
     pointers)."""
     struct = {"norm": Norm, "rope": Rope, "attention": Attention, "gather": Gather, "select": Select,
-              "select_static": Select}[kind]
+              "select_static": Select, "select_merge": SelectMerge}[kind]
     fn = {"select_static": "cb_select_run_static"}.get(kind, f"cb_{kind}_run")
     stream = fields.pop("stream", None)
     flags = fields.pop("flags", 0)

@@ -98,11 +98,23 @@ uint32_t cb_select_tiles(uint32_t count) { return select_tiles(count); }
 uint32_t cb_select_tickets(uint32_t count) { return 1u + (select_tiles(count) + 15u) / 16u; }
 
 int cb_select_run(const cb_select* s, uint32_t flags, void* stream) {
-    if (!s || !s->logits || !s->partials || !s->ticket || !s->candidates || !s->sampled)
+    if (!s || !s->logits || !s->partials || !s->ticket || !s->candidates || (!s->sampled && !s->candidates_only))
         return fail(CB_ERROR_INVALID, "cb_select_run: null argument");
+    if (s->rows > 1 && s->logits_stride < s->count)
+        return fail(CB_ERROR_INVALID, "cb_select_run: rows overlap (logits_stride below count)");
+    if (static_cast<uint64_t>(s->id_offset) + s->count > 0xFFFFFFFFull)
+        return fail(CB_ERROR_INVALID, "cb_select_run: ids past 2^32 - 1");
     if (s->count == 0 || s->count > 262144)
         return fail(CB_ERROR_INVALID, "cb_select_run: %u entries (1 to 262,144)", s->count);
     return launched(select_run(*s, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_select_run");
+}
+
+int cb_select_merge_run(const cb_select_merge* m, uint32_t flags, void* stream) {
+    if (!m || !m->lists_data || !m->candidates || !m->sampled)
+        return fail(CB_ERROR_INVALID, "cb_select_merge_run: null argument");
+    if (m->lists == 0 || m->lists > 64) return fail(CB_ERROR_INVALID, "cb_select_merge_run: %u lists (1 to 64)", m->lists);
+    if (m->rows == 0) return CB_OK;
+    return launched(select_merge_run(*m, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_select_merge_run");
 }
 
 }  // extern "C"

@@ -201,7 +201,8 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
 // The step's launches (graph.cpp's order). `fed`: the token is the last
 // draw. `seq` >= 0: `tokens` consecutive positions of sequence `seq`; -1:
 // a batched step, row r the token of sequence r (tokens == sequences).
-int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb_sampling& s, int seq = 0) {
+int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb_sampling& s, int seq = 0,
+                 bool head_and_draw = true) {
     const bool batch = seq < 0;
     const uint32_t row0 = batch ? 0u : static_cast<uint32_t>(seq);   // this step's record / logits row
     const cb_model& m = d->model;
@@ -307,6 +308,7 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
     cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, batch ? 0u : 1u,
                m.epsilon};
     if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
+    if (!head_and_draw) return CB_OK;   // the caller runs the head (a vocabulary split)
     {
         const DevWeight& head = d->output.piece ? d->output : d->token_embd;
         float* outs[3] = {d->logits + static_cast<size_t>(row0) * m.vocab, nullptr, nullptr};
@@ -633,6 +635,43 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
     d->next_position += steps;
     for (auto& p : d->seq_next) p = d->next_position;
     return cb_fault_check(nullptr);
+}
+
+int cb_decoder_step_body(cb_decoder* d, const uint32_t* ids_host, uint32_t position) {
+    if (!d) return fail(CB_ERROR_INVALID, "cb_decoder_step_body: null decoder");
+    const uint32_t S = d->sequences;
+    if (static_cast<uint64_t>(position) + 1 > d->model.context)
+        return fail(CB_ERROR_STEP, "cb_decoder_step_body: position past the context of %u", d->model.context);
+    const uint32_t st[2] = {position, 0};
+    cudaError_t e = cudaSuccess;
+    if (ids_host) {
+        for (uint32_t i = 0; i < S; ++i)
+            if (ids_host[i] >= d->model.vocab) return fail(CB_ERROR_INVALID, "cb_decoder_step_body: token %u", ids_host[i]);
+        e = cudaMemcpyAsync(d->ids, ids_host, S * sizeof(uint32_t), cudaMemcpyHostToDevice, d->stream);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->state, st, sizeof st, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step_body: upload");
+    const cb_sampling greedy{0, 0, 1, 0.0f, 1.0f, 0.0f};
+    if (int rc = enqueue_step(d, S, ids_host == nullptr, true, greedy, S > 1 ? -1 : 0, false)) return rc;
+    // the state copy's host array must outlive the copy
+    e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_step_body");
+    for (uint32_t i = 0; i < S; ++i) d->seq_next[i] = position + 1;
+    d->next_position = position + 1;
+    return CB_OK;
+}
+
+void* cb_decoder_stream(cb_decoder* d) { return d ? static_cast<void*>(d->stream) : nullptr; }
+const float* cb_decoder_device_normed(cb_decoder* d) { return d ? d->normed : nullptr; }
+uint32_t* cb_decoder_device_sampled(cb_decoder* d) { return d ? d->sampled : nullptr; }
+
+int cb_decoder_head(cb_decoder* d, cb_member* head, uint32_t* format, uint32_t* columns) {
+    if (!d || !head || !format || !columns) return fail(CB_ERROR_INVALID, "cb_decoder_head: null argument");
+    const DevWeight& w = d->output.piece ? d->output : d->token_embd;
+    *head = {w.piece, w.blocks, 0, w.rows, 0};
+    *format = w.format;
+    *columns = w.cols;
+    return CB_OK;
 }
 
 int cb_decoder_logits_row(cb_decoder* d, uint32_t row, float* logits_host) {

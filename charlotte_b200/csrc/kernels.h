@@ -28,6 +28,7 @@ cudaError_t attention_prefill_run(const AttentionArgs& a, cudaStream_t stream, b
 // Steps of at least this many rows take the many-query form.
 constexpr uint32_t kPrefillAttentionRows = 32;
 cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t select_merge_run(const cb_select_merge& a, cudaStream_t stream, bool pdl);
 cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl);
 uint32_t select_tiles(uint32_t count);
 

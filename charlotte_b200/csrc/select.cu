@@ -139,53 +139,14 @@ __device__ __forceinline__ uint32_t philox_word0(uint32_t c0, uint32_t k0, uint3
     return c[0];
 }
 
-__global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
-    extern __shared__ __align__(16) uint64_t buf[];   // a tile of keys
-    __shared__ unsigned int last;
-    grid_dependency_wait();
+// The 64 candidates src[0..63] (descending keys) as (bits, token) pairs to
+// `candidates`, then the draw (draw.wgsl:71-163; temperature 0 keeps
+// candidate 0, greedy) into the 16-byte record `sampled`. The block's
+// threads all call it; row r draws with seed1 + r.
+template <typename Args>
+__device__ void draw_candidates(const uint64_t* src, const Args& a, uint32_t* candidates, uint32_t* sampled,
+                                uint32_t row) {
     const uint32_t t = threadIdx.x;
-    const uint32_t tile = blockIdx.x;
-    // Row blockIdx.y of a batched selection: its own logits, scratch,
-    // candidates and record.
-    const uint32_t row = blockIdx.y;
-    if (row) {
-        a.logits += static_cast<size_t>(row) * a.logits_stride;
-        a.partials += static_cast<size_t>(row) * gridDim.x * kKeep * 2u;
-        a.ticket += static_cast<size_t>(row) * (1u + (gridDim.x + kGroup - 1u) / kGroup);
-        a.candidates += static_cast<size_t>(row) * kKeep * 2u;
-        a.sampled += static_cast<size_t>(row) * 4u;
-    }
-    {
-        const uint32_t e = tile * kTile + t;
-        uint64_t k = 0;
-        if (e < a.count) k = entry_key(__float_as_uint(a.logits[e]), e);
-        buf[t] = k;
-    }
-    __syncthreads();
-    sort_tile(buf);
-    if (t < kKeep) entry_pair(buf[t], a.partials + 2u * (tile * kKeep + t));
-    grid_dependents_launch();
-
-    // Level 1: the last tile of each group of kGroup merges the group's
-    // lists into the group's first slot. Level 2: the last group merges the
-    // groups' lists. Both merge pairwise by rank (merge_lists).
-    __shared__ unsigned int flag;
-    const uint32_t group = tile / kGroup;
-    const uint32_t groups = (gridDim.x + kGroup - 1u) / kGroup;
-    const uint32_t in_group = min(kGroup, gridDim.x - group * kGroup);
-    if (!last_to_arrive(a.ticket + 1u + group, in_group, &flag)) return;
-    uint64_t* work = buf;                   // kGroup lists
-    uint64_t* tmp = buf + kGroup * kKeep;   // half as many
-    for (uint32_t i = t; i < in_group * kKeep; i += kSelThreads) work[i] = load_key(a.partials, group * kGroup * kKeep + i);
-    __syncthreads();
-    merge_lists(work, tmp, in_group);
-    if (t < kKeep) entry_pair(work[t], a.partials + 2u * (group * kGroup * kKeep + t));
-    if (!last_to_arrive(a.ticket, groups, &flag)) return;
-    for (uint32_t i = t; i < groups * kKeep; i += kSelThreads)
-        work[i] = load_key(a.partials, (i / kKeep) * kGroup * kKeep + i % kKeep);
-    __syncthreads();
-    merge_lists(work, tmp, groups);
-    uint64_t* src = work;
     // src[0..63]: the candidates, in the reference's order.
     __shared__ uint32_t cand[2 * kKeep];
     __shared__ float weight[kKeep], tempered[kKeep], running[kKeep];
@@ -193,8 +154,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
     __shared__ float total_s;
     if (t < kKeep) {
         entry_pair(src[t], cand + 2u * t);
-        a.candidates[2u * t] = cand[2u * t];
-        a.candidates[2u * t + 1u] = cand[2u * t + 1u];
+        candidates[2u * t] = cand[2u * t];
+        candidates[2u * t + 1u] = cand[2u * t + 1u];
     }
     __syncthreads();
     // The draw (draw.wgsl:71-163); temperature 0 keeps candidate 0 (greedy).
@@ -244,14 +205,101 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
             for (uint32_t i = 0; i < survivors; ++i)
                 if (running[i] > goal) { chosen = i; break; }
         }
-        a.sampled[0] = failed ? 0u : cand[2u * chosen + 1u];
-        a.sampled[1] = failed ? 1u : 0u;
-        a.sampled[2] = __float_as_uint(u);
-        a.sampled[3] = 0u;
+        sampled[0] = failed ? 0u : cand[2u * chosen + 1u];
+        sampled[1] = failed ? 1u : 0u;
+        sampled[2] = __float_as_uint(u);
+        sampled[3] = 0u;
     }
 }
 
+__global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
+    extern __shared__ __align__(16) uint64_t buf[];   // a tile of keys
+    __shared__ unsigned int last;
+    grid_dependency_wait();
+    const uint32_t t = threadIdx.x;
+    const uint32_t tile = blockIdx.x;
+    // Row blockIdx.y of a batched selection: its own logits, scratch,
+    // candidates and record.
+    const uint32_t row = blockIdx.y;
+    if (row) {
+        a.logits += static_cast<size_t>(row) * a.logits_stride;
+        a.partials += static_cast<size_t>(row) * gridDim.x * kKeep * 2u;
+        a.ticket += static_cast<size_t>(row) * (1u + (gridDim.x + kGroup - 1u) / kGroup);
+        a.candidates += static_cast<size_t>(row) * kKeep * 2u;
+        a.sampled += static_cast<size_t>(row) * 4u;
+    }
+    {
+        const uint32_t e = tile * kTile + t;
+        uint64_t k = 0;
+        if (e < a.count) k = entry_key(__float_as_uint(a.logits[e]), e + a.id_offset);
+        buf[t] = k;
+    }
+    __syncthreads();
+    sort_tile(buf);
+    if (t < kKeep) entry_pair(buf[t], a.partials + 2u * (tile * kKeep + t));
+    grid_dependents_launch();
+
+    // Level 1: the last tile of each group of kGroup merges the group's
+    // lists into the group's first slot. Level 2: the last group merges the
+    // groups' lists. Both merge pairwise by rank (merge_lists).
+    __shared__ unsigned int flag;
+    const uint32_t group = tile / kGroup;
+    const uint32_t groups = (gridDim.x + kGroup - 1u) / kGroup;
+    const uint32_t in_group = min(kGroup, gridDim.x - group * kGroup);
+    if (!last_to_arrive(a.ticket + 1u + group, in_group, &flag)) return;
+    uint64_t* work = buf;                   // kGroup lists
+    uint64_t* tmp = buf + kGroup * kKeep;   // half as many
+    for (uint32_t i = t; i < in_group * kKeep; i += kSelThreads) work[i] = load_key(a.partials, group * kGroup * kKeep + i);
+    __syncthreads();
+    merge_lists(work, tmp, in_group);
+    if (t < kKeep) entry_pair(work[t], a.partials + 2u * (group * kGroup * kKeep + t));
+    if (!last_to_arrive(a.ticket, groups, &flag)) return;
+    for (uint32_t i = t; i < groups * kKeep; i += kSelThreads)
+        work[i] = load_key(a.partials, (i / kKeep) * kGroup * kKeep + i % kKeep);
+    __syncthreads();
+    merge_lists(work, tmp, groups);
+    if (a.candidates_only) {   // a vocabulary shard's top 64, for a merge elsewhere
+        if (t < kKeep) entry_pair(work[t], a.candidates + 2u * t);
+        return;
+    }
+    draw_candidates(work, a, a.candidates, a.sampled, row);
+}
+
+// Merges `lists` candidate lists of each row (a vocabulary split over ranks:
+// list l of row r at ((l·rows + r)·64) pairs) into the row's top 64 — the
+// union holds the whole vocabulary's top 64, so these are the candidates of
+// one selection over the whole vocabulary — then draws. One CTA a row.
+__global__ void __launch_bounds__(kSelThreads) merge_kernel(cb_select_merge a) {
+    extern __shared__ __align__(16) uint64_t mbuf[];
+    grid_dependency_wait();
+    const uint32_t row = blockIdx.x, t = threadIdx.x;
+    uint64_t* work = mbuf;
+    uint64_t* tmp = mbuf + a.lists * kKeep;
+    for (uint32_t i = t; i < a.lists * kKeep; i += kSelThreads)
+        work[i] = load_key(a.lists_data, (i / kKeep * a.rows + row) * kKeep + i % kKeep);
+    __syncthreads();
+    grid_dependents_launch();
+    merge_lists(work, tmp, a.lists);
+    draw_candidates(work, a, a.candidates + static_cast<size_t>(row) * kKeep * 2u, a.sampled + 4u * row, row);
+}
+
 }  // namespace
+
+cudaError_t select_merge_run(const cb_select_merge& a, cudaStream_t stream, bool pdl) {
+    if (a.lists == 0 || a.lists > 64 || a.rows == 0) return cudaErrorInvalidValue;
+    const size_t smem = (a.lists + a.lists / 2u + 1u) * kKeep * sizeof(uint64_t);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.rows);
+    cfg.blockDim = dim3(kSelThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, merge_kernel, a);
+}
 
 uint32_t select_tiles(uint32_t count) { return (count + kTile - 1u) / kTile; }
 

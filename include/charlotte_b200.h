@@ -276,6 +276,12 @@ typedef struct cb_select {
      * seed1 + r. */
     uint32_t rows;
     uint32_t logits_stride;
+    /* A vocabulary split over ranks (no counterpart in the reference): the
+     * logits are entries id_offset.. of the vocabulary (candidates carry
+     * global ids); with candidates_only, the top 64 are written and no draw
+     * is made (sampled may be NULL) — cb_select_merge_run finishes. */
+    uint32_t id_offset;
+    uint32_t candidates_only;
 } cb_select;
 CB_API int cb_select_run(const cb_select* s, uint32_t flags, void* stream);
 CB_API uint32_t cb_select_tiles(uint32_t count);
@@ -293,6 +299,28 @@ CB_API uint32_t cb_select_tickets(uint32_t count);
  * before any stream capture). All calls share the array: calls that overlap
  * on the GPU race — order them on one stream. */
 CB_API int cb_select_run_static(const cb_select* s, uint32_t flags, void* stream);
+
+/* The merge of a vocabulary split (no counterpart in the reference): each
+ * row's `lists` candidate lists, list l of row r at pairs
+ * ((l·rows + r)·64 ...) of lists_data — what an all-gather of every rank's
+ * candidates_only output gives — merged into the row's top 64 under the
+ * same total order (the union holds the whole vocabulary's top 64, so the
+ * result is one selection's over the whole vocabulary), then the draw,
+ * rows' records at sampled + 4·r and candidates at candidates + 128·r. */
+typedef struct cb_select_merge {
+    const uint32_t* lists_data;
+    uint32_t lists;             /* 1 to 64 (ranks)                           */
+    uint32_t rows;
+    uint32_t* candidates;       /* [rows][64][2]                             */
+    uint32_t* sampled;          /* [rows][4]                                 */
+    const uint32_t* position;
+    uint32_t position0;
+    uint32_t tokens;
+    uint32_t seed0, seed1;
+    uint32_t top_k;
+    float temperature, top_p, min_p, log_min_p;
+} cb_select_merge;
+CB_API int cb_select_merge_run(const cb_select_merge* m, uint32_t flags, void* stream);
 
 /* Flags of the kernel entry points above. */
 enum { CB_RUN_PDL = 1u };
@@ -406,6 +434,21 @@ CB_API int cb_decoder_step_batch(cb_decoder* d, const uint32_t* ids_host, uint32
                                  uint32_t* records_host);
 /* Row `row`'s logits of the last step [vocab] to host memory. */
 CB_API int cb_decoder_logits_row(cb_decoder* d, uint32_t row, float* logits_host);
+
+/* A vocabulary split over ranks (no counterpart in the reference): a
+ * batched step up to the final norm (ids_host NULL: each row fed from its
+ * record in cb_decoder_device_sampled), leaving the normed rows
+ * [sequences][hidden] at cb_decoder_device_normed on cb_decoder_stream;
+ * the caller runs its head shard (cb_decoder_head gives the weight; its
+ * member's first_row and rows select the shard), cb_select_run with
+ * candidates_only, the exchange, and cb_select_merge_run, and writes each
+ * of its rows' record back into cb_decoder_device_sampled for the next
+ * step. Returns after the enqueued work completes. */
+CB_API int cb_decoder_step_body(cb_decoder* d, const uint32_t* ids_host, uint32_t position);
+CB_API void* cb_decoder_stream(cb_decoder* d);
+CB_API const float* cb_decoder_device_normed(cb_decoder* d);
+CB_API uint32_t* cb_decoder_device_sampled(cb_decoder* d);
+CB_API int cb_decoder_head(cb_decoder* d, cb_member* head, uint32_t* format, uint32_t* columns);
 
 /* Device pointers of the decoder's working buffers, for callers that feed
  * it from their own kernels: the logits [vocab] and the sampled record [4]. */
