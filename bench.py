@@ -265,6 +265,11 @@ def run_ours(args):
         achieved = head["gbs"]
         per_launch_bytes = gs.items[-1]["bytes"]
     peak = peaks.get("hbm_gbs", 6650.0)
+    # DRAM traffic per launch: the ncu capture's DRAM bytes over the same
+    # product's algorithmic bytes (profiles/gemv_q4_0_qkv_4096x1024.md:
+    # 2,397,440 / 2,379,776; profiles/gemv_q6k_head_151936x1024.md:
+    # 132,133,120 / 128,238,080), scaled to this launch's algorithmic bytes.
+    traffic_ratio = 2397440 / 2379776 if share_q4 >= 0.5 else 132133120 / 128238080
 
     # e2e: the same products through the C ABI with host buffers.
     e2e = None if args.no_e2e else run_e2e(gs, stream, max(args.steps // 20, 5), world)
@@ -287,7 +292,9 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (375 MB weights a step vs 126 MB L2)",
                    "parallelism": f"replicas x{world}", "graph": "CUDA graph of PDL launches"},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": round(per_launch_bytes * traffic_ratio),
+                     "traffic_source": "ncu DRAM bytes of the committed capture, scaled to this launch",
                      "bytes_per_launch": round(per_launch_bytes), "peak_source": "measured" if peaks else "fallback"},
         "per_product": {k: {kk: round(vv, 4) for kk, vv in v.items()} for k, v in per_kind.items()},
         "e2e": e2e,

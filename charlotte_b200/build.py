@@ -57,6 +57,11 @@ def build(verbose: bool = False) -> str:
     srcs = sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, digest), srcs))
+    # objects of earlier header or flag states are never linked again
+    keep = {os.path.basename(o) for o in objs}
+    for f in os.listdir(OBJ):
+        if f.endswith(".o") and f not in keep:
+            os.remove(os.path.join(OBJ, f))
     newest = max(os.path.getmtime(o) for o in objs)
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
         cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
