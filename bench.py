@@ -238,24 +238,39 @@ def run_ours(args):
     ms_per_step = ms_total / args.steps
     value = gs.bytes * world / (ms_per_step * 1e-3) / 1e9
 
-    # Roofline of the dominant kernel: per-launch CUDA events around the Q4_0
-    # and Q6_K launches over a further timed pass (same stream, eager).
-    events = {"qkv": ([], []), "o": ([], []), "gate_up": ([], []), "down": ([], []), "head": ([], [])}
-    with torch.cuda.stream(stream):
-        for _ in range(20):
-            gs.step(stream, events)
-    torch.cuda.synchronize()
+    # Roofline of the dominant kernel: each kind of product (the 28 QKV, O,
+    # gate|up, down launches; the head) captured alone as a CUDA graph of its
+    # PDL launches and replayed, timed with CUDA events on the replay stream:
+    # a launch's average duration inside a dependent chain, without the host.
     per_kind = {}
-    for kind, (s, e) in events.items():
-        ms = [a.elapsed_time(b) for a, b in zip(s, e)]
-        by = [it["bytes"] for it in gs.items if it["kind"] == kind]
-        per_kind[kind] = dict(launches=len(ms), ms=float(np.mean(ms)),
-                              gbs=float(np.mean(by)) / (float(np.mean(ms)) * 1e-3) / 1e9)
-    q4_ms = sum(per_kind[k]["ms"] * per_kind[k]["launches"] for k in ("qkv", "o", "gate_up", "down"))
-    q4_bytes = sum(it["bytes"] for it in gs.items if it["fmt"] == Q4_0) * 20
-    q4_launches = sum(per_kind[k]["launches"] for k in ("qkv", "o", "gate_up", "down"))
+    for kind in ("qkv", "o", "gate_up", "down", "head"):
+        items = [it for it in gs.items if it["kind"] == kind]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for it in items:
+                gs.launch(it, stream)
+        reps = 20
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream()
+        a.record(cur)
+        for _ in range(reps):
+            g.replay()
+        b.record(cur)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / (reps * len(items))
+        by = float(np.mean([it["bytes"] for it in items]))
+        per_kind[kind] = dict(launches=len(items) * reps, ms=ms, gbs=by / (ms * 1e-3) / 1e9)
+        del g
+    q4_kinds = ("qkv", "o", "gate_up", "down")
+    q4_ms = sum(per_kind[k]["ms"] * per_kind[k]["launches"] for k in q4_kinds)
+    q4_launches = sum(per_kind[k]["launches"] for k in q4_kinds)
+    q4_bytes = sum(it["bytes"] for it in gs.items if it["fmt"] == Q4_0) * (q4_launches // 112)
     head = per_kind["head"]
-    share_q4 = q4_ms / (q4_ms + head["ms"] * head["launches"])
+    q4_step = sum(per_kind[k]["ms"] * len([it for it in gs.items if it["kind"] == k]) for k in q4_kinds)
+    share_q4 = q4_step / (q4_step + head["ms"])
     peaks = read_peaks()
     dom = "decode_kernel<Q4_0>" if share_q4 >= 0.5 else "decode_kernel<Q6_K>"
     if share_q4 >= 0.5:
