@@ -71,6 +71,8 @@ int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
         return fail(CB_ERROR_INVALID, "cb_attention_run: %u query heads over %u kv heads", a->query_heads,
                     a->kv_heads);
     if (a->slots == 0 || a->window == 0) return fail(CB_ERROR_INVALID, "cb_attention_run: no slots or no window");
+    if (!aligned16(a->key_cache) || !aligned16(a->value_cache) || !aligned16(a->query))
+        return fail(CB_ERROR_INVALID, "cb_attention_run: caches and queries must be 16-byte aligned");
     if (a->rows_are_sequences && a->sequence_stride < static_cast<uint64_t>(a->slots) * a->kv_heads * a->head_dim)
         return fail(CB_ERROR_INVALID, "cb_attention_run: sequences' caches overlap (stride below one cache)");
     if (!a->position && static_cast<uint64_t>(a->position0) + (a->rows_are_sequences ? 1u : a->tokens) >

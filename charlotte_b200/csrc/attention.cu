@@ -30,6 +30,7 @@
 
 #include <cstdint>
 
+#include "api_common.h"
 #include "kernels.h"
 #include "numerics.cuh"
 #include "tma.cuh"
@@ -70,22 +71,30 @@ __device__ __forceinline__ uint32_t earliest_of(uint32_t p, uint32_t window) {
 constexpr uint32_t kChunkSlots = 16;   // CTAs a (kv head, row tile) takes, striding over its live chunks
 
 // Stages keys and values j_lo..j_hi-1 (absolute positions) of the chunk at
-// key0 into its shared tiles.
+// key0
+// into its shared tiles: one bulk asynchronous copy (TMA, untiled) a key
+// row and a value row, issued by warp 0's lanes, completing on `bar`. With
+// `arrive`, lane 0 arrives with the copies' bytes; without, it only raises
+// the phase's expected bytes (the arrival comes with a later batch).
 __device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_t* kc, const uint16_t* vc, uint16_t* ks,
                                            uint16_t* vs, uint32_t key0, uint32_t j_lo, uint32_t j_hi, uint32_t kvh,
-                                           uint32_t d) {
-    const uint32_t words = d / 8u;   // uint4 per key row
-    const uint32_t b_lo = j_lo - key0, n = (j_hi - j_lo) * words;
-#pragma unroll 4
-    for (uint32_t i = threadIdx.x; i < n; i += kAttnThreads) {
-        const uint32_t b = b_lo + i / words, w = i % words;
+                                           uint32_t d, uint64_t* bar, bool arrive) {
+    if (threadIdx.x >= 32u) return;
+    const uint32_t lane = threadIdx.x;
+    const uint32_t n = j_hi > j_lo ? j_hi - j_lo : 0u, row_bytes = d * 2u;
+    if (lane == 0) {
+        if (arrive) mbar_arrive_expect_tx(bar, 2u * n * row_bytes);
+        else if (n) mbar_expect_tx(bar, 2u * n * row_bytes);
+    }
+    __syncwarp();
+    for (uint32_t b = j_lo - key0 + lane; b < j_hi - key0; b += 32u) {
         const size_t at = (static_cast<size_t>((key0 + b) % a.slots) * a.kv_heads + kvh) * d;
-        reinterpret_cast<uint4*>(ks + b * d)[w] = reinterpret_cast<const uint4*>(kc + at)[w];
-        reinterpret_cast<uint4*>(vs + b * d)[w] = reinterpret_cast<const uint4*>(vc + at)[w];
+        bulk_g2s(ks + b * d, kc + at, row_bytes, bar);
+        bulk_g2s(vs + b * d, vc + at, row_bytes, bar);
     }
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a, unsigned int* fault) {
     extern __shared__ __align__(16) uint8_t smem[];
     const uint32_t d = a.head_dim;
     const uint32_t B = 2048u / d;
@@ -123,13 +132,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         grid_dependency_wait();
         return;
     }
-    // This slot's first chunk's keys of earlier steps (below pos0), staged
+    // One mbarrier phase a chunk for its keys and values.
+    __shared__ uint64_t kv_bar;
+    uint32_t kv_phase = 0;
+    if (threadIdx.x == 0) {
+        mbar_init(&kv_bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // This slot's first chunk's keys of earlier steps (below pos0), in flight
     // while the launch before this one (rope) finishes.
     const uint32_t c_first = live_first + blockIdx.y;
     {
         const uint32_t key0 = c_first * kChunk;
         const uint32_t j_hi = min(key0 + kChunk, max(pos0, key0));
-        if (j_hi > key0) stage_keys(a, kc, vc, ks, vs, key0, key0, j_hi, kvh, d);
+        stage_keys(a, kc, vc, ks, vs, key0, key0, j_hi, kvh, d, &kv_bar, false);
     }
     grid_dependency_wait();
 
@@ -142,14 +159,25 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     for (uint32_t c = c_first; c <= p_last / kChunk; c += gridDim.y) {
         const uint32_t key0 = c * kChunk;
         const bool first_chunk = c == c_first;
-        if (!first_chunk) __syncthreads();   // the last chunk's reads of ks, vs, ps are done
+        if (!first_chunk) {
+            __syncthreads();      // the last chunk's reads of ks, vs, ps are done
+            fence_proxy_async();  // and ordered before the copy engine's writes
+        }
         // The chunk's keys this step wrote (for later chunks, all of them);
         // positions past p_last are never live and are not staged.
         {
             const uint32_t j_lo = first_chunk ? max(key0, min(pos0, key0 + kChunk)) : key0;
             const uint32_t j_hi = min(key0 + kChunk, p_last + 1u);
-            if (j_hi > j_lo) stage_keys(a, kc, vc, ks, vs, key0, j_lo, j_hi, kvh, d);
+            stage_keys(a, kc, vc, ks, vs, key0, j_lo, j_hi, kvh, d, &kv_bar, true);
         }
+        if (!mbar_wait(&kv_bar, kv_phase, fault)) {
+            // A copy did not land in time (the fault word is set): wait once
+            // more, bounded, so none is left writing this CTA's shared
+            // memory, and leave without a ticket (the step reports failure).
+            mbar_wait(&kv_bar, kv_phase, nullptr);
+            return;
+        }
+        kv_phase ^= 1u;
         __syncthreads();
         // Scores: s = Σ_w dot(q_w, k_w) in quads, in order.
         for (uint32_t i = threadIdx.x; i < Q * kChunk; i += kAttnThreads) {
@@ -269,16 +297,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
         bool live = false;
         float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
-        for (uint32_t cc = c0; cc <= c1; cc += 4u) {
-            // four chunks' partials in flight at once, then folded in order
-            float co[4];
+        for (uint32_t cc = c0; cc <= c1; cc += 8u) {
+            // eight chunks' partials in flight at once, then folded in order
+            float co[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < 8; ++k) {
                 const size_t at = (static_cast<size_t>(cc + k) * a.tokens + row0 + r) * a.query_heads + h;
                 co[k] = cc + k <= c1 ? __ldcg(a.partials + at * d + e) : 0.0f;
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < 8; ++k) {
                 if (cc + k > c1) break;
                 const uint32_t si = (cc + k - live_first) * Q + m;
                 const float cm = fstat[2u * si], cl = fstat[2u * si + 1u];
@@ -330,7 +358,7 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attention_kernel, a);
+    return cudaLaunchKernelEx(&cfg, attention_kernel, a, fault_word());
 }
 
 }  // namespace cb

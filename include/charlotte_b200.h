@@ -391,7 +391,13 @@ enum {
      * form (CB_MATMUL_TENSOR, tolerance tier) instead of the exact forms;
      * shorter steps (decode) and the head's last-token product stay exact.
      * No counterpart in the reference. */
-    CB_DECODER_TENSOR_PREFILL = 1u
+    CB_DECODER_TENSOR_PREFILL = 1u,
+    /* One-token steps of a one-sequence decoder run as one persistent
+     * cooperative launch (the gather and every layer, stages separated by
+     * grid-wide barriers; the same bits as the separate launches) unless
+     * this flag keeps the separate launches. No counterpart in the
+     * reference. */
+    CB_DECODER_UNFUSED = 2u
 };
 
 /* Uploads the model and allocates its caches and working buffers for steps

@@ -65,3 +65,28 @@ def test_qwen3_0_6b_greedy_decode_token_for_token(cuda):
     """configs[2]'s architecture at full size (28 layers, 151,936 vocab),
     a shorter run: 64-token prompt in two steps, 16 greedy steps."""
     run_both(M.qwen3_0_6b(), 64, 16, [40, 24], seed=7)
+
+
+@pytest.mark.parametrize("kind", ["qwen3", "llama", "gemma3"])
+def test_fused_step_matches_separate_launches(cuda, kind):
+    """The fused one-token step (one persistent launch, grid-wide barriers)
+    gives the same tokens and logits, bit for bit, as the separate launches
+    (CB_DECODER_UNFUSED), fed from the device and from host ids."""
+    arch = M.tiny(kind)
+    m = M.synthesize(arch, seed=17)
+    rng = np.random.default_rng(2)
+    prompt = rng.integers(0, arch.vocab, 30).astype(np.uint32)
+    out = {}
+    for fused in (True, False):
+        dec = M.Decoder(m, max_step_tokens=32, fused=fused)
+        dec.prefill(prompt)
+        toks, failed = dec.generate(20)
+        assert not failed.any()
+        lg = dec.logits()
+        rec = dec.step(np.array([7], np.uint32), 50)
+        out[fused] = (toks, lg, rec, dec.logits())
+        dec.close()
+    np.testing.assert_array_equal(out[True][0], out[False][0])
+    np.testing.assert_array_equal(out[True][1], out[False][1])
+    np.testing.assert_array_equal(out[True][2], out[False][2])
+    np.testing.assert_array_equal(out[True][3], out[False][3])
