@@ -618,7 +618,7 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
     if (int rc = dalloc(d, &d->sampled, static_cast<size_t>(S) * 4)) return bail(rc);
     if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
-    if (S == 1 && !(flags & CB_DECODER_UNFUSED))
+    if (S == 1 && (flags & CB_DECODER_FUSED))
         if (int rc = setup_fused(d)) return bail(rc);
     if (flags & CB_DECODER_TENSOR_PREFILL) {
         const uint32_t widest = std::max<uint32_t>(std::max<uint32_t>(H, static_cast<uint32_t>(qd)), m->ffn);

@@ -237,7 +237,7 @@ def to_c(model: Model):
 class Decoder:
     """A model uploaded through the C ABI; steps run on the GPU."""
 
-    def __init__(self, model: Model, max_step_tokens: int = 512, tensor_prefill: bool = False, fused: bool = True):
+    def __init__(self, model: Model, max_step_tokens: int = 512, tensor_prefill: bool = False, fused: bool = False):
         L = _lib()
         L.cb_decoder_create.restype = ctypes.c_int
         L.cb_decoder_create.argtypes = [ctypes.POINTER(CModel), ctypes.c_uint32, ctypes.c_uint32,
@@ -257,7 +257,7 @@ class Decoder:
         cm, self._layers = to_c(model)
         self._cm = cm
         h = ctypes.c_void_p()
-        flags = (1 if tensor_prefill else 0) | (0 if fused else 2)   # CB_DECODER_TENSOR_PREFILL, CB_DECODER_UNFUSED
+        flags = (1 if tensor_prefill else 0) | (2 if fused else 0)   # CB_DECODER_TENSOR_PREFILL, CB_DECODER_FUSED
         _check(L.cb_decoder_create(ctypes.byref(cm), max_step_tokens, flags, ctypes.byref(h)))
         self.handle = h
 

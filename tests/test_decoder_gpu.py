@@ -69,9 +69,9 @@ def test_qwen3_0_6b_greedy_decode_token_for_token(cuda):
 
 @pytest.mark.parametrize("kind", ["qwen3", "llama", "gemma3"])
 def test_fused_step_matches_separate_launches(cuda, kind):
-    """The fused one-token step (one persistent launch, grid-wide barriers)
-    gives the same tokens and logits, bit for bit, as the separate launches
-    (CB_DECODER_UNFUSED), fed from the device and from host ids."""
+    """The fused one-token step (CB_DECODER_FUSED: one persistent launch,
+    grid-wide barriers) gives the same tokens and logits, bit for bit, as the
+    separate launches, fed from the device and from host ids."""
     arch = M.tiny(kind)
     m = M.synthesize(arch, seed=17)
     rng = np.random.default_rng(2)
