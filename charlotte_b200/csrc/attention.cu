@@ -40,7 +40,7 @@ namespace cb {
 namespace {
 
 constexpr uint32_t kChunk = 64;
-constexpr uint32_t kAttnThreads = 128;
+constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kMaxQueries = 16;   // queries (rows × G) a CTA works
 
 struct Geometry {
@@ -280,16 +280,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Stage every live chunk's (m, l) for the tile's queries in shared memory.
-    float* fstat = reinterpret_cast<float*>(smem);   // [chunks][Q][2], over ks/vs
-    for (uint32_t i = threadIdx.x; i < live_chunks * Q; i += kAttnThreads) {
-        const uint32_t cc = live_first + i / Q, m = i % Q;
-        const uint32_t r = m / G, h = kvh * G + m % G;
-        const size_t at = (static_cast<size_t>(cc) * a.tokens + row0 + r) * a.query_heads + h;
-        fstat[2u * i] = __ldcg(a.stats + at * 2u);
-        fstat[2u * i + 1u] = __ldcg(a.stats + at * 2u + 1u);
-    }
-    __syncthreads();
+    // Each (query, dimension) loads its chunks' partials and (m, l) together,
+    // eight chunks in flight at once, and folds them in chunk order.
     for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
         const uint32_t m = i / d, e = i % d;
         const uint32_t r = m / G, h = kvh * G + m % G;
@@ -298,18 +290,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         bool live = false;
         float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
         for (uint32_t cc = c0; cc <= c1; cc += 8u) {
-            // eight chunks' partials in flight at once, then folded in order
-            float co[8];
+            float co[8], cms[8], cls[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const size_t at = (static_cast<size_t>(cc + k) * a.tokens + row0 + r) * a.query_heads + h;
-                co[k] = cc + k <= c1 ? __ldcg(a.partials + at * d + e) : 0.0f;
+                const bool in = cc + k <= c1;
+                co[k] = in ? __ldcg(a.partials + at * d + e) : 0.0f;
+                cms[k] = in ? __ldcg(a.stats + at * 2u) : 0.0f;
+                cls[k] = in ? __ldcg(a.stats + at * 2u + 1u) : 0.0f;
             }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 if (cc + k > c1) break;
-                const uint32_t si = (cc + k - live_first) * Q + m;
-                const float cm = fstat[2u * si], cl = fstat[2u * si + 1u];
+                const float cm = cms[k], cl = cls[k];
                 float fa, fb, fm;
                 if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
                 else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
@@ -338,8 +331,6 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
     size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
                   kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
-    const size_t fold = static_cast<size_t>(a.max_chunks) * kMaxQueries * 2u * sizeof(float);   // the fold's stats
-    if (fold > smem) smem = fold;
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
