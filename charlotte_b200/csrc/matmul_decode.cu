@@ -296,17 +296,17 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     const uint32_t t0 = blockIdx.y * MT;
     const uint32_t nt = min(static_cast<uint32_t>(MT), a.tokens - t0);
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
-    for (uint32_t i = 0; i < MT; ++i) {
-        float4* dst = reinterpret_cast<float4*>(xs + i * tok_floats + lane * lane_stride);
-        if (i < nt) {
-            const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i) * a.x_stride);
-            for (uint32_t g = lo + warp; g < hi; g += W)
-#pragma unroll
-                for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = xg[g * 8u + v];
-        } else {
-            for (uint32_t g = lo + warp; g < hi; g += W)
-#pragma unroll
-                for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Every warp takes part: lane r's (token, group, float4) triples are
+    // dealt over the warps (a range may hold a single group).
+    {
+        const uint32_t per_token = (hi - lo) * 8u;
+        for (uint32_t idx = warp; idx < MT * per_token; idx += W) {
+            const uint32_t i = idx / per_token, rem = idx % per_token;
+            const uint32_t g = lo + rem / 8u, v = rem % 8u;
+            float4* dst = reinterpret_cast<float4*>(xs + i * tok_floats + lane * lane_stride);
+            dst[(g - lo) * 8u + v] =
+                i < nt ? reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i) * a.x_stride)[g * 8u + v]
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     __syncthreads();

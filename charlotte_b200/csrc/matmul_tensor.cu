@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) tensor_kernel(const MatmulArgs a
                 sp[s] = piece + RowStreams<F>::base(s, blocks) +
                         static_cast<uint64_t>(live ? row : 0u) * RowStreams<F>::row_bytes(s, G);
         }
-        // Four blocks' codes in flight in registers: block kb+4 is read from
+        // Eight blocks' codes in flight in registers: block kb+8 is read from
         // global memory while block kb is decoded and stored.
         auto fetch = [&](uint32_t kb, F& f) {
             const uint32_t g = 2u * kb + h;   // this thread's 32-wide group of the block
@@ -193,20 +193,16 @@ __global__ void __launch_bounds__(kThreadsT, 1) tensor_kernel(const MatmulArgs a
             mbar_arrive(&full[s]);
             return true;
         };
-        F f0, f1, f2, f3;
-        fetch(0u, f0);
-        fetch(1u, f1);
-        fetch(2u, f2);
-        fetch(3u, f3);
-        for (uint32_t kb = 0; kb < kblocks; kb += 4u) {
-            if (!put(kb, f0)) break;
-            fetch(kb + 4u, f0);
-            if (kb + 1u >= kblocks || !put(kb + 1u, f1)) break;
-            fetch(kb + 5u, f1);
-            if (kb + 2u >= kblocks || !put(kb + 2u, f2)) break;
-            fetch(kb + 6u, f2);
-            if (kb + 3u >= kblocks || !put(kb + 3u, f3)) break;
-            fetch(kb + 7u, f3);
+        F f[8];
+#pragma unroll
+        for (uint32_t j = 0; j < 8u; ++j) fetch(j, f[j]);
+        bool running = true;
+        for (uint32_t kb = 0; kb < kblocks && running; kb += 8u) {
+#pragma unroll
+            for (uint32_t j = 0; j < 8u; ++j) {
+                if (kb + j >= kblocks || !put(kb + j, f[j])) { running = false; break; }
+                fetch(kb + j + 8u, f[j]);
+            }
         }
     } else if (warp == kTmaWarp) {
         // ---- the TMA warp: x16 blocks ------------------------------------------
