@@ -206,6 +206,37 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
     return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, flags, d->stream);
 }
 
+// A one-token product with the RMSNorm before it folded into its prologue
+// (matmul_decode.cu): every CTA computes the normed row of hidden (+ y,
+// post-normed first when post_gain); CTA 0 writes hidden + y to hidden_out.
+int product_normed(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, float* const outs[3],
+                   const float* hidden, const float* y, const float* post_gain, const float* gain, float* hidden_out) {
+    MatmulArgs a{};
+    const DevWeight* first = *ws.begin();
+    a.format = first->format;
+    a.columns = first->cols;
+    a.members = static_cast<uint32_t>(ws.size());
+    a.epilogue = epilogue;
+    a.activation = d->model.activation;
+    a.tokens = 1;
+    uint32_t i = 0, total = 0;
+    for (const DevWeight* w : ws) {
+        a.member[i++] = {w->piece, w->blocks, 0, w->rows, 0};
+        total += w->rows;
+    }
+    a.total_rows = epilogue == CB_EPILOGUE_GATED ? first->rows : total;
+    for (uint32_t k = 0; k < 3; ++k) a.out[k] = outs[k];
+    a.x_stride = a.columns;
+    a.fault = fault_word();
+    a.norm_hidden = hidden;
+    a.norm_y = y;
+    a.norm_post_gain = post_gain;
+    a.norm_gain = gain;
+    a.norm_hidden_out = hidden_out;
+    a.norm_epsilon = d->model.epsilon;
+    return launched(matmul_decode(a, d->sms, d->stream, true), "step: normed product");
+}
+
 // The step's launches (graph.cpp's order). `fed`: the token is the last
 // draw. `seq` >= 0: `tokens` consecutive positions of sequence `seq`; -1:
 // a batched step, row r the token of sequence r (tokens == sequences).
@@ -236,12 +267,24 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
     }
     const float* pending_post = nullptr;
     bool pending_add = false;
+    // A one-token step of one sequence folds each norm into the product after
+    // it; the residual stream then alternates between two buffers.
+    const bool fold = tokens == 1 && !batch;
+    float* stream_buf[2] = {d->hidden, d->hidden2};
+    uint32_t cur = 0;
     for (uint32_t l = 0; l < m.layers; ++l) {
         const DevLayer& L = d->layers[l];
-        cb_norm n{d->hidden, d->out, L.attn_norm, pending_post, d->normed, H, tokens, pending_add ? 1u : 0u, 0u,
-                  m.epsilon};
-        if (int rc = launched(norm_run(n, d->stream, true), "step: attention norm")) return rc;
-        {
+        if (fold) {
+            float* outs[3] = {d->q, d->k, d->v};
+            if (int rc = product_normed(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, outs, stream_buf[cur],
+                                        pending_add ? d->out : nullptr, pending_post, L.attn_norm,
+                                        pending_add ? stream_buf[cur ^ 1u] : nullptr))
+                return rc;
+            if (pending_add) cur ^= 1u;
+        } else {
+            cb_norm n{d->hidden, d->out, L.attn_norm, pending_post, d->normed, H, tokens, pending_add ? 1u : 0u, 0u,
+                      m.epsilon};
+            if (int rc = launched(norm_run(n, d->stream, true), "step: attention norm")) return rc;
             float* outs[3] = {d->q, d->k, d->v};
             const uint32_t strides[3] = {qd, kvd, kvd};
             if (int rc = product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, d->normed, H, tokens, outs, strides))
@@ -294,9 +337,15 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
             const uint32_t strides[3] = {H, 0, 0};
             if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides)) return rc;
         }
-        cb_norm n2{d->hidden, d->out, L.ffn_norm, L.post_attn_norm, d->normed, H, tokens, 1u, 0u, m.epsilon};
-        if (int rc = launched(norm_run(n2, d->stream, true), "step: feed-forward norm")) return rc;
-        {
+        if (fold) {
+            float* outs[3] = {d->act, nullptr, nullptr};
+            if (int rc = product_normed(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, outs, stream_buf[cur], d->out,
+                                        L.post_attn_norm, L.ffn_norm, stream_buf[cur ^ 1u]))
+                return rc;
+            cur ^= 1u;
+        } else {
+            cb_norm n2{d->hidden, d->out, L.ffn_norm, L.post_attn_norm, d->normed, H, tokens, 1u, 0u, m.epsilon};
+            if (int rc = launched(norm_run(n2, d->stream, true), "step: feed-forward norm")) return rc;
             float* outs[3] = {d->act, nullptr, nullptr};
             const uint32_t strides[3] = {m.ffn, 0, 0};
             if (int rc = product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, d->normed, H, tokens, outs, strides))
@@ -310,12 +359,25 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         pending_add = true;
         pending_post = L.post_ffn_norm;
     }
-    if (!logits) return CB_OK;
+    if (!logits) return CB_OK;   // the residual stream is not carried to the next step
     // The output: a sequence step's last row, or every row of a batched step.
     const uint32_t heads = batch ? tokens : 1u;
-    cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, batch ? 0u : 1u,
-               m.epsilon};
-    if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
+    if (fold && head_and_draw) {
+        const DevWeight& head = d->output.piece ? d->output : d->token_embd;
+        float* outs[3] = {d->logits + static_cast<size_t>(row0) * m.vocab, nullptr, nullptr};
+        if (int rc = product_normed(d, {&head}, CB_EPILOGUE_WRITE, outs, stream_buf[cur], d->out, pending_post,
+                                    d->output_norm, nullptr))
+            return rc;
+    } else {
+    if (fold) {
+        // the caller wants the normed row (a vocabulary split): the norm kernel over the stream's buffer
+        cb_norm fn{stream_buf[cur], d->out, d->output_norm, pending_post, d->normed, H, 1u, 1u, 1u, m.epsilon};
+        if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
+    } else {
+        cb_norm fn{d->hidden, d->out, d->output_norm, pending_post, d->normed, H, tokens, 1u, batch ? 0u : 1u,
+                   m.epsilon};
+        if (int rc = launched(norm_run(fn, d->stream, true), "step: output norm")) return rc;
+    }
     if (!head_and_draw) return CB_OK;   // the caller runs the head (a vocabulary split)
     {
         const DevWeight& head = d->output.piece ? d->output : d->token_embd;
@@ -323,6 +385,7 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         const uint32_t strides[3] = {m.vocab, 0, 0};
         const float* x = batch ? d->normed : d->normed + static_cast<size_t>(tokens - 1) * H;
         if (int rc = product(d, {&head}, CB_EPILOGUE_WRITE, x, H, heads, outs, strides)) return rc;
+    }
     }
     cb_select sel{};
     sel.logits = d->logits + static_cast<size_t>(row0) * m.vocab;
@@ -480,7 +543,6 @@ int setup_fused(cb_decoder* d) {
     d->fplan = fused_plan(max_cols, row_stage, gated_stage, m.head_dim, d->sms, dev);
     if (d->fplan.warps == 0) return CB_OK;   // the separate kernels serve
     if (int rc = dalloc(d, &d->flayers, m.layers)) return rc;
-    if (int rc = dalloc(d, &d->hidden2, H)) return rc;
     if (int rc = dalloc(d, &d->fbar, 2)) return rc;
     cudaError_t e = cudaMemcpy(d->flayers, host.data(), m.layers * sizeof(FusedLayer), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(d->fbar, 0, 2 * sizeof(unsigned int));
@@ -601,6 +663,7 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
     const size_t qd = static_cast<size_t>(m->query_heads) * dh, kvd = static_cast<size_t>(m->kv_heads) * dh;
     if (int rc = dalloc(d, &d->hidden, static_cast<size_t>(T) * H)) return bail(rc);
     if (int rc = dalloc(d, &d->normed, static_cast<size_t>(T) * H)) return bail(rc);
+    if (int rc = dalloc(d, &d->hidden2, static_cast<size_t>(T) * H)) return bail(rc);
     if (int rc = dalloc(d, &d->q, T * qd)) return bail(rc);
     if (int rc = dalloc(d, &d->k, T * kvd)) return bail(rc);
     if (int rc = dalloc(d, &d->v, T * kvd)) return bail(rc);

@@ -40,6 +40,17 @@ struct MatmulArgs {
     uint32_t gate_input_column;
     unsigned int* fault;    // device word: a bounded wait that ran out sets a bit
     void* scratch;          // tensor form: x rounded to f16, [tokens][columns]
+    // One-token decode with the RMSNorm before the product folded in (the
+    // decoder's own path; norm_gain NULL: x is read as given). Every CTA
+    // computes norm_kernel's row — hidden (+ y, post-normed first when
+    // norm_post_gain) — into its x stage; CTA 0 writes hidden + y to
+    // norm_hidden_out (the residual stream's other buffer).
+    const float* norm_hidden;
+    const float* norm_y;
+    const float* norm_post_gain;
+    const float* norm_gain;
+    float* norm_hidden_out;
+    float norm_epsilon;
 };
 
 // Decode form over `tokens` rows of x (each token its own grid row): the

@@ -49,6 +49,111 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxDecodeSmem = 220 * 1024;
 
+// The reference's 256-way halving tree (norm.wgsl:67-78) on a 128-thread
+// CTA: thread t holds partials t and t+128 (the tree's first level adds
+// exactly those two), then the levels 64 and 32 in shared memory and the
+// shuffles of the last warp, as norm_kernel does.
+__device__ __forceinline__ float tree_sum_pairs(float lo, float hi, float* scratch) {
+    const uint32_t t = threadIdx.x;
+    scratch[t] = lo + hi;
+    __syncthreads();
+    if (t < 64u) scratch[t] = scratch[t] + scratch[t + 64u];
+    __syncthreads();
+    if (t < 32u) scratch[t] = scratch[t] + scratch[t + 32u];
+    __syncthreads();
+    if (t < 32u) {
+        float w = scratch[t];
+#pragma unroll
+        for (int stride = 16; stride > 0; stride >>= 1) w = w + __shfl_down_sync(0xFFFFFFFFu, w, stride);
+        if (t == 0) scratch[0] = w;
+    }
+    __syncthreads();
+    const float total = scratch[0];
+    __syncthreads();
+    return total;
+}
+
+// norm_kernel's row (norm.cu) for one token on a 128-thread CTA: thread t
+// does the work of norm_kernel's threads t and t+128 (vec4s t + 128h + 256k);
+// the normed row goes to the x stage, range-major; CTA 0 writes the add.
+__device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint32_t G, uint32_t lane_stride) {
+    __shared__ float scratch[kThreads];
+    const uint32_t width = a.columns, vec4s = width / 4u, t = threadIdx.x;
+    const float n = static_cast<float>(width);
+    float4 x[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = t + 128u * h + 256u * k;
+            x[h][k] = i < vec4s ? __ldcg(reinterpret_cast<const float4*>(a.norm_hidden) + i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    if (a.norm_y) {
+        float4 y[2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = t + 128u * h + 256u * k;
+                y[h][k] = i < vec4s ? __ldcg(reinterpret_cast<const float4*>(a.norm_y) + i)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        if (a.norm_post_gain) {
+            float sq[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (t + 128u * h + 256u * k < vec4s) sq[h] = sq[h] + dot4(y[h][k], y[h][k]);
+            const float r = 1.0f / sqrtf(tree_sum_pairs(sq[0], sq[1], scratch) / n + a.norm_epsilon);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t i = t + 128u * h + 256u * k;
+                    if (i < vec4s) {
+                        const float4 g = reinterpret_cast<const float4*>(a.norm_post_gain)[i];
+                        y[h][k] = make_float4(((y[h][k].x * r) * g.x) * 1.0f, ((y[h][k].y * r) * g.y) * 1.0f,
+                                              ((y[h][k].z * r) * g.z) * 1.0f, ((y[h][k].w * r) * g.w) * 1.0f);
+                    }
+                }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = t + 128u * h + 256u * k;
+                if (i < vec4s) {
+                    x[h][k] = make_float4(x[h][k].x + y[h][k].x, x[h][k].y + y[h][k].y, x[h][k].z + y[h][k].z,
+                                          x[h][k].w + y[h][k].w);
+                    if (blockIdx.x == 0 && a.norm_hidden_out)
+                        reinterpret_cast<float4*>(a.norm_hidden_out)[i] = x[h][k];
+                }
+            }
+    }
+    float sq[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (t + 128u * h + 256u * k < vec4s) sq[h] = sq[h] + dot4(x[h][k], x[h][k]);
+    const float r = 1.0f / sqrtf(tree_sum_pairs(sq[0], sq[1], scratch) / n + a.norm_epsilon);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = t + 128u * h + 256u * k;
+            if (i < vec4s) {
+                const float4 g = reinterpret_cast<const float4*>(a.norm_gain)[i];
+                const float4 v = make_float4((x[h][k].x * r) * g.x, (x[h][k].y * r) * g.y, (x[h][k].z * r) * g.z,
+                                             (x[h][k].w * r) * g.w);
+                const uint32_t e = 4u * i, grp = e / 32u, lr = lane_of(grp, G);
+                *reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 32u + e % 32u) = v;
+            }
+        }
+}
+
 template <typename F, int R>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -83,10 +188,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
     grid_dependency_wait();
 
     // x, range-major: lane r's groups at r·lane_stride, a 16-byte skew a
-    // range; warp w copies the lane's groups w, w+4, ... (no division).
+    // range; warp w copies the lane's groups w, w+4, ... (no division). Or,
+    // with the norm folded in, the normed row computed here.
     const uint32_t t = blockIdx.y;
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
-    {
+    if (a.norm_gain) {
+        norm_row128(a, xs, G, lane_stride);
+    } else {
         const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t) * a.x_stride);
         float4* dst = reinterpret_cast<float4*>(xs + lane * lane_stride);
         for (uint32_t g = lo + warp; g < hi; g += kWarps)
