@@ -16,7 +16,10 @@
 // zero point; S and C are exact in binary32 (j is chosen so that C's
 // significand fits), so the single rounding of the fma is the rounding of
 // the reference's (q − z)·s. For Q4_0 and Q8_0 that product is exact; for
-// Q6_K it is the reference's one rounding of (d·sc)·(q − 32).
+// Q6_K it is the reference's one rounding of (d·sc)·(q − 32). Two rows'
+// weights may be decoded by one paired fma (__ffma2_rn: two independent
+// fmas, each rounded once) from their constants as pairs (consts2): the
+// same bits as two scalar fmas.
 #pragma once
 
 #include <cstdint>
@@ -31,6 +34,8 @@ enum Format : uint32_t { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ8_0 = 8, kQ6_K = 14 };
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return __byte_perm(a, b, sel);
 }
+
+__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
 
 // ---- Q4_0 -------------------------------------------------------------------
 // Weight k of a block: byte k % 16 of its codes, low nibble for k < 16, high
@@ -91,6 +96,31 @@ struct Q4_0 {
         constexpr int j = jpos<k>();
         return j == 8 ? c.c8 : (j == 12 ? c.c12 : c.c16);
     }
+    // Two rows' constants as pairs (row A, row B): consts() of each, the same
+    // operations elementwise.
+    struct Consts2 { float2 s8, s12, s16, c8, c12, c16; };
+    __device__ __forceinline__ static Consts2 consts2(const Q4_0& A, const Q4_0& B) {
+        const float2 d = make_float2(A.d, B.d);
+        Consts2 c;
+        c.s8 = __fmul2_rn(d, make_float2(32768.0f, 32768.0f));
+        c.s12 = __fmul2_rn(d, make_float2(2048.0f, 2048.0f));
+        c.s16 = __fmul2_rn(d, make_float2(128.0f, 128.0f));
+        const float2 z = __fmul2_rn(d, make_float2(8.0f, 8.0f));
+        c.c8 = neg2(__fadd2_rn(c.s8, z));
+        c.c12 = neg2(__fadd2_rn(c.s12, z));
+        c.c16 = neg2(__fadd2_rn(c.s16, z));
+        return c;
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 S2(const Consts2& c) {
+        constexpr int j = jpos<k>();
+        return j == 8 ? c.s8 : (j == 12 ? c.s12 : c.s16);
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 C2(const Consts2& c) {
+        constexpr int j = jpos<k>();
+        return j == 8 ? c.c8 : (j == 12 ? c.c12 : c.c16);
+    }
 };
 
 // ---- Q8_0 -------------------------------------------------------------------
@@ -138,6 +168,18 @@ struct Q8_0 {
     __device__ __forceinline__ static float S(const Consts& c) { return c.s; }
     template <int k>
     __device__ __forceinline__ static float C(const Consts& c) { return c.c; }
+    struct Consts2 { float2 s, c; };
+    __device__ __forceinline__ static Consts2 consts2(const Q8_0& A, const Q8_0& B) {
+        const float2 d = make_float2(A.d, B.d);
+        Consts2 c;
+        c.s = __fmul2_rn(d, make_float2(32768.0f, 32768.0f));
+        c.c = neg2(__fadd2_rn(c.s, __fmul2_rn(d, make_float2(128.0f, 128.0f))));
+        return c;
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 S2(const Consts2& c) { return c.s; }
+    template <int k>
+    __device__ __forceinline__ static float2 C2(const Consts2& c) { return c.c; }
 };
 
 // ---- Q6_K (repacked) ----------------------------------------------------------
@@ -196,6 +238,20 @@ struct Q6_K {
     __device__ __forceinline__ static float S(const Consts& c) { return k < 16 ? c.S1 : c.S2; }
     template <int k>
     __device__ __forceinline__ static float C(const Consts& c) { return k < 16 ? c.C1 : c.C2; }
+    struct Consts2 { float2 S1, S2, C1, C2; };
+    __device__ __forceinline__ static Consts2 consts2(const Q6_K& A, const Q6_K& B) {
+        const float2 s1 = make_float2(A.s1, B.s1), s2 = make_float2(A.s2, B.s2);
+        Consts2 c;
+        c.S1 = __fmul2_rn(s1, make_float2(128.0f, 128.0f));
+        c.S2 = __fmul2_rn(s2, make_float2(128.0f, 128.0f));
+        c.C1 = __fmul2_rn(s1, make_float2(-160.0f, -160.0f));
+        c.C2 = __fmul2_rn(s2, make_float2(-160.0f, -160.0f));
+        return c;
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 S2(const Consts2& c) { return k < 16 ? c.S1 : c.S2; }
+    template <int k>
+    __device__ __forceinline__ static float2 C2(const Consts2& c) { return k < 16 ? c.C1 : c.C2; }
 };
 
 // A row's streams: stream s of row r of a piece of `nb` blocks starts at

@@ -26,6 +26,11 @@ __device__ __forceinline__ uint32_t lane_of(uint32_t g, uint32_t G) { return (32
 // Floats of x a range holds in shared memory: its most groups, and a 16-byte skew.
 __host__ __device__ __forceinline__ uint32_t x_lane_stride(uint32_t G) { return (G + 31u) / 32u * 32u + 4u; }
 
+// The same with every float of x held twice ((x_k, x_k), the paired FMA's
+// operand for two rows): a group takes 64 floats; the 16-byte skew keeps a
+// quarter-warp's 16-byte reads on distinct banks.
+__host__ __device__ __forceinline__ uint32_t x2_lane_stride(uint32_t G) { return (G + 31u) / 32u * 64u + 4u; }
+
 // A batch: up to R consecutive rows of one member (non-gated), or R/2
 // outputs' gate rows then the same up rows (gated). Batches never straddle
 // members, so a batch's rows of each stream are one contiguous run.
@@ -146,6 +151,40 @@ __device__ __forceinline__ void chain_group(const F& A, const F& B, const float4
                                             std::integer_sequence<int, ks...>) {
     const typename F::Consts ca = A.consts(), cbb = B.consts();
     (chain_step<F, ks>(A, B, ca, cbb, x4, acc_a, acc_b), ...);
+}
+
+// Two rows' chains as one: each step's decode and multiply-add run as paired
+// FMAs (fma.rn.f32x2: two independent fused multiply-adds, each rounded
+// once, so each row's bits are those of chain_step). x2 holds x doubled.
+template <typename F, int k>
+__device__ __forceinline__ void chain_step2(const F& A, const F& B, const typename F::Consts2& c, const float4* x2,
+                                            float2& acc) {
+    const float4 xq = x2[k / 2];
+    const float2 xk = (k % 2 == 0) ? make_float2(xq.x, xq.y) : make_float2(xq.z, xq.w);
+    const float2 m = make_float2(__uint_as_float(A.template magic<k>()), __uint_as_float(B.template magic<k>()));
+    acc = __ffma2_rn(__ffma2_rn(m, F::template S2<k>(c), F::template C2<k>(c)), xk, acc);
+}
+
+template <typename F, int... ks>
+__device__ __forceinline__ void chain_group2(const F& A, const F& B, const float4* x2, float2& acc,
+                                             std::integer_sequence<int, ks...>) {
+    const typename F::Consts2 c = F::consts2(A, B);
+    (chain_step2<F, ks>(A, B, c, x2, acc), ...);
+}
+
+// One row's chain reading x doubled (x2).
+template <typename F, int k>
+__device__ __forceinline__ void chain_step1d(const F& A, const typename F::Consts& ca, const float4* x2, float& acc) {
+    const float4 xq = x2[k / 2];
+    const float xk = (k % 2 == 0) ? xq.x : xq.z;
+    acc = fmaf(fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca)), xk, acc);
+}
+
+template <typename F, int... ks>
+__device__ __forceinline__ void chain_group1d(const F& A, const float4* x2, float& acc,
+                                              std::integer_sequence<int, ks...>) {
+    const typename F::Consts ca = A.consts();
+    (chain_step1d<F, ks>(A, ca, x2, acc), ...);
 }
 
 template <typename F, int k>

@@ -12,22 +12,30 @@
 // oracle's and to the reference's prefill form of the same token.
 //
 // B200 mapping.
-//  - A warp owns batches of R rows (R = 1, 2, 4 or 8, chosen by the product's
-//    size so that small products still spread over every SM). Each batch's
-//    row streams (codes, scales, ...) are brought into the warp's shared
-//    memory by bulk asynchronous copies (cp.async.bulk, the untiled TMA),
-//    completing on an mbarrier, through a two-stage ring: the copy of batch
-//    i+2 is in flight while batch i is worked.
+//  - A warp owns batches of R rows. Small products (most of a decode step)
+//    take the latency shape: R from 2 and W warps a CTA chosen so that every
+//    warp has one batch and the grid is at most one CTA an SM — all copies
+//    are issued before the wait on the launch before, every CTA is resident
+//    beside that launch's (none starts late, after it has exited), and x is
+//    read once an SM. Larger products stream: several batches a warp through
+//    a two-stage ring, the copy of batch i+2 in flight while batch i is
+//    worked.
+//  - Each batch's row streams (codes, scales, ...) are brought into the
+//    warp's shared memory by bulk asynchronous copies (cp.async.bulk, the
+//    untiled TMA), completing on an mbarrier.
 //  - The first two batches' copies are issued before griddepcontrol.wait:
 //    weights are never written on the device, so under programmatic
 //    dependent launch a product's weight stream overlaps the launch before it;
 //    only x, the previous launch's output, waits.
-//  - Rows are worked two at a time sharing each x read: one fma decodes a
-//    weight exactly (formats.cuh), one fma accumulates it.
+//  - Rows are worked two at a time: one paired fma (fma.rn.f32x2, two fmas
+//    each rounded once) decodes a weight of each row exactly (formats.cuh),
+//    one accumulates both, with x held doubled ((x_k, x_k)) in shared memory
+//    as the pair's operand.
 //  - Batches never straddle members, so a batch's rows come in one bulk copy
 //    per stream (two for a gated batch: its gate rows and its up rows).
 //  - x is staged once per CTA in shared memory range-major, a 16-byte skew
-//    per range, so the lanes' 128-bit reads fall in distinct banks.
+//    per range, so the lanes' 128-bit reads fall in distinct banks; the row
+//    is read from global memory in order (each warp one contiguous span).
 //  - Every mbarrier wait is bounded (tma.cuh): a copy that never lands sets
 //    the launch's fault word, which the host reports as a failed step.
 #include <cuda_runtime.h>
@@ -46,16 +54,16 @@ namespace cb {
 namespace {
 
 constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
 constexpr int kMaxDecodeSmem = 220 * 1024;
 
-// The reference's 256-way halving tree (norm.wgsl:67-78) on a 128-thread
-// CTA: thread t holds partials t and t+128 (the tree's first level adds
-// exactly those two), then the levels 64 and 32 in shared memory and the
-// shuffles of the last warp, as norm_kernel does.
+// The reference's 256-way halving tree (norm.wgsl:67-78) on the first 128
+// threads of a CTA (the rest only meet its barriers): thread t holds partials
+// t and t+128 (the tree's first level adds exactly those two), then the
+// levels 64 and 32 in shared memory and the shuffles of the last warp, as
+// norm_kernel does.
 __device__ __forceinline__ float tree_sum_pairs(float lo, float hi, float* scratch) {
     const uint32_t t = threadIdx.x;
-    scratch[t] = lo + hi;
+    if (t < 128u) scratch[t] = lo + hi;
     __syncthreads();
     if (t < 64u) scratch[t] = scratch[t] + scratch[t + 64u];
     __syncthreads();
@@ -73,39 +81,44 @@ __device__ __forceinline__ float tree_sum_pairs(float lo, float hi, float* scrat
     return total;
 }
 
-// norm_kernel's row (norm.cu) for one token on a 128-thread CTA: thread t
-// does the work of norm_kernel's threads t and t+128 (vec4s t + 128h + 256k);
-// the normed row goes to the x stage, range-major; CTA 0 writes the add.
-__device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint32_t G, uint32_t lane_stride) {
-    __shared__ float scratch[kThreads];
-    const uint32_t width = a.columns, vec4s = width / 4u, t = threadIdx.x;
+// norm_kernel's row (norm.cu) for one token on the first 128 threads of a
+// CTA: thread t does the work of norm_kernel's threads t and t+128 (vec4s
+// t + 128h + 256k), the same operations in the same order. The hidden row
+// (and y) come into `tmp` by asynchronous copies, each thread's own
+// elements, so no registers wait on the loads; the normed row goes to the x
+// stage, range-major with every float doubled; CTA 0 writes the add.
+// Threads from 128 up hold no elements and only meet the tree's barriers.
+__device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, float* tmp, uint32_t G,
+                                            uint32_t lane_stride) {
+    __shared__ float scratch[128];
+    const uint32_t width = a.columns, t = threadIdx.x;
+    const uint32_t vec4s = t < 128u ? width / 4u : 0u;
     const float n = static_cast<float>(width);
-    float4 x[2][4];
+    float4* th = reinterpret_cast<float4*>(tmp);
+    float4* ty = th + width / 4u;
+    const float4* hg = reinterpret_cast<const float4*>(a.norm_hidden);
+    const float4* yg = reinterpret_cast<const float4*>(a.norm_y);
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const uint32_t i = t + 128u * h + 256u * k;
-            x[h][k] = i < vec4s ? __ldcg(reinterpret_cast<const float4*>(a.norm_hidden) + i)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    if (a.norm_y) {
-        float4 y[2][4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t i = t + 128u * h + 256u * k;
-                y[h][k] = i < vec4s ? __ldcg(reinterpret_cast<const float4*>(a.norm_y) + i)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < vec4s) {
+                cp_async16(th + i, hg + i);
+                if (yg) cp_async16(ty + i, yg + i);
             }
+        }
+    cp_async_wait_all();
+    if (yg) {
         if (a.norm_post_gain) {
             float sq[2] = {0.0f, 0.0f};
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (t + 128u * h + 256u * k < vec4s) sq[h] = sq[h] + dot4(y[h][k], y[h][k]);
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t i = t + 128u * h + 256u * k;
+                    if (i < vec4s) sq[h] = sq[h] + dot4(ty[i], ty[i]);
+                }
             const float r = 1.0f / sqrtf(tree_sum_pairs(sq[0], sq[1], scratch) / n + a.norm_epsilon);
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -114,8 +127,9 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint
                     const uint32_t i = t + 128u * h + 256u * k;
                     if (i < vec4s) {
                         const float4 g = reinterpret_cast<const float4*>(a.norm_post_gain)[i];
-                        y[h][k] = make_float4(((y[h][k].x * r) * g.x) * 1.0f, ((y[h][k].y * r) * g.y) * 1.0f,
-                                              ((y[h][k].z * r) * g.z) * 1.0f, ((y[h][k].w * r) * g.w) * 1.0f);
+                        const float4 y = ty[i];
+                        ty[i] = make_float4(((y.x * r) * g.x) * 1.0f, ((y.y * r) * g.y) * 1.0f,
+                                            ((y.z * r) * g.z) * 1.0f, ((y.w * r) * g.w) * 1.0f);
                     }
                 }
         }
@@ -125,10 +139,10 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint
             for (int k = 0; k < 4; ++k) {
                 const uint32_t i = t + 128u * h + 256u * k;
                 if (i < vec4s) {
-                    x[h][k] = make_float4(x[h][k].x + y[h][k].x, x[h][k].y + y[h][k].y, x[h][k].z + y[h][k].z,
-                                          x[h][k].w + y[h][k].w);
-                    if (blockIdx.x == 0 && a.norm_hidden_out)
-                        reinterpret_cast<float4*>(a.norm_hidden_out)[i] = x[h][k];
+                    const float4 x = th[i], y = ty[i];
+                    const float4 v = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+                    th[i] = v;
+                    if (blockIdx.x == 0 && a.norm_hidden_out) reinterpret_cast<float4*>(a.norm_hidden_out)[i] = v;
                 }
             }
     }
@@ -136,8 +150,10 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (t + 128u * h + 256u * k < vec4s) sq[h] = sq[h] + dot4(x[h][k], x[h][k]);
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = t + 128u * h + 256u * k;
+            if (i < vec4s) sq[h] = sq[h] + dot4(th[i], th[i]);
+        }
     const float r = 1.0f / sqrtf(tree_sum_pairs(sq[0], sq[1], scratch) / n + a.norm_epsilon);
 #pragma unroll
     for (int h = 0; h < 2; ++h)
@@ -146,31 +162,38 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint
             const uint32_t i = t + 128u * h + 256u * k;
             if (i < vec4s) {
                 const float4 g = reinterpret_cast<const float4*>(a.norm_gain)[i];
-                const float4 v = make_float4((x[h][k].x * r) * g.x, (x[h][k].y * r) * g.y, (x[h][k].z * r) * g.z,
-                                             (x[h][k].w * r) * g.w);
+                const float4 x = th[i];
+                const float4 v = make_float4((x.x * r) * g.x, (x.y * r) * g.y, (x.z * r) * g.z, (x.w * r) * g.w);
                 const uint32_t e = 4u * i, grp = e / 32u, lr = lane_of(grp, G);
-                *reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 32u + e % 32u) = v;
+                float4* d = reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 64u + 2u * (e % 32u));
+                d[0] = make_float4(v.x, v.x, v.y, v.y);
+                d[1] = make_float4(v.z, v.z, v.w, v.w);
             }
         }
 }
 
-template <typename F, int R>
-__global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
+// Bytes of the folded norm's row buffers (the hidden row, and y when added).
+__host__ __device__ __forceinline__ uint32_t norm_tmp_bytes(const MatmulArgs& a) {
+    return a.norm_gain ? (a.norm_y ? 2u : 1u) * a.columns * 4u : 0u;
+}
+
+template <typename F, int R, int W>
+__global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t G = a.columns / 32u;
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t lane_stride = x_lane_stride(G);
+    const uint32_t lane_stride = x2_lane_stride(G);
     const uint32_t stage_bytes = RowStreams<F>::row_stage(G) * R;
     const uint32_t batches = batch_count<R>(a);
-    const uint32_t stride = gridDim.x * kWarps;
+    const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
 
-    // Shared memory: x (range-major floats), then per warp: 2 barriers,
-    // range sums, 2 stages.
+    // Shared memory: x (range-major, each float doubled), the folded norm's
+    // row buffers, then per warp: 2 barriers, range sums, 2 stages.
     float* xs = reinterpret_cast<float*>(smem);
     const uint32_t x_bytes = 32u * lane_stride * 4u;
     const uint32_t warp_bytes = 16u + R * kRedStride * 4u + 2u * stage_bytes;
-    uint8_t* wbase = smem + x_bytes + warp * warp_bytes;
+    uint8_t* wbase = smem + x_bytes + norm_tmp_bytes(a) + warp * warp_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
     float* red = reinterpret_cast<float*>(wbase + 16);
     uint8_t* stages = wbase + 16u + R * kRedStride * 4u;
@@ -181,25 +204,30 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
         fence_barrier_init();
     }
     __syncwarp();
-    const uint32_t first = blockIdx.x * kWarps + warp;
+    const uint32_t first = blockIdx.x * W + warp;
     if (first < batches) issue_batch<F, R>(a, first, stages, &bars[0], G, lane);
     if (first + stride < batches) issue_batch<F, R>(a, first + stride, stages + stage_bytes, &bars[1], G, lane);
 
     grid_dependency_wait();
 
-    // x, range-major: lane r's groups at r·lane_stride, a 16-byte skew a
-    // range; warp w copies the lane's groups w, w+4, ... (no division). Or,
-    // with the norm folded in, the normed row computed here.
+    // x, range-major: lane r's groups at r·lane_stride (64 floats a group,
+    // each float doubled), a 16-byte skew a range. The row's 16-byte chunks
+    // are dealt to all threads in row order (each warp reads one contiguous
+    // span). Or, with the norm folded in, the normed row computed here.
     const uint32_t t = blockIdx.y;
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
     if (a.norm_gain) {
-        norm_row128(a, xs, G, lane_stride);
+        norm_row128(a, xs, reinterpret_cast<float*>(smem + x_bytes), G, lane_stride);
     } else {
         const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t) * a.x_stride);
-        float4* dst = reinterpret_cast<float4*>(xs + lane * lane_stride);
-        for (uint32_t g = lo + warp; g < hi; g += kWarps)
-#pragma unroll
-            for (int v = 0; v < 8; ++v) dst[(g - lo) * 8u + v] = xg[g * 8u + v];
+#pragma unroll 2
+        for (uint32_t c = threadIdx.x; c < G * 8u; c += W * 32u) {
+            const float4 v = __ldcg(xg + c);
+            const uint32_t grp = c / 8u, lr = lane_of(grp, G);
+            float4* d = reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 64u + (c % 8u) * 8u);
+            d[0] = make_float4(v.x, v.x, v.y, v.y);
+            d[1] = make_float4(v.z, v.z, v.w, v.w);
+        }
     }
     __syncthreads();
     grid_dependents_launch();
@@ -254,7 +282,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
             for (uint32_t g = lo; g < hi; ++g) {
                 F A;
                 A.load(seg[0], g);
-                chain_group1<F>(A, xl + (g - lo) * 8u, acc, std::make_integer_sequence<int, 32>{});
+                chain_group1d<F>(A, xl + (g - lo) * 16u, acc, std::make_integer_sequence<int, 32>{});
             }
             red[lane] = acc;
         } else {
@@ -274,21 +302,23 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const MatmulArgs a) {
                 pa[q] = (upper ? seg[1][q] : seg[0][q]) + ia * rb[q];
                 pb[q] = (gated && R == 2) ? seg[1][q] : pa[q] + rb[q];
             }
-            float aa = 0.0f, ab = 0.0f;
+            float2 acc = make_float2(0.0f, 0.0f);   // rows a, b
             for (uint32_t g = lo; g < hi; ++g) {
                 F A, B;
                 if (la) A.load(pa, g); else A.zero();
                 if (lb) B.load(pb, g); else B.zero();
-                chain_group<F>(A, B, xl + (g - lo) * 8u, aa, ab, std::make_integer_sequence<int, 32>{});
+                chain_group2<F>(A, B, xl + (g - lo) * 16u, acc, std::make_integer_sequence<int, 32>{});
             }
-            red[(2 * p) * kRedStride + lane] = aa;
-            red[(2 * p + 1) * kRedStride + lane] = ab;
+            red[(2 * p) * kRedStride + lane] = acc.x;
+            red[(2 * p + 1) * kRedStride + lane] = acc.y;
         }
         }
-        // The stage is read: let the copy engine refill it with batch i+2.
-        fence_proxy_async();
+        // The stage is read: let the copy engine refill it with batch i+2
+        // (the fence orders these reads before the copy's writes).
+        const bool refill = b + 2u * stride < batches;
+        if (refill) fence_proxy_async();
         __syncwarp();
-        if (b + 2u * stride < batches) issue_batch<F, R>(a, b + 2u * stride, stage, &bars[s], G, lane);
+        if (refill) issue_batch<F, R>(a, b + 2u * stride, stage, &bars[s], G, lane);
         // Slot `lane`'s total: its 32 range sums added in order (slot_total, :237).
         float total = 0.0f;
         if (lane < static_cast<uint32_t>(R)) {
@@ -404,18 +434,19 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     const uint32_t t0 = blockIdx.y * MT;
     const uint32_t nt = min(static_cast<uint32_t>(MT), a.tokens - t0);
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
-    // Every warp takes part: lane r's (token, group, float4) triples are
-    // dealt over the warps (a range may hold a single group).
+    // The tokens' 16-byte chunks dealt to all threads in row order (each
+    // warp reads one contiguous span), copied asynchronously to their
+    // range's run; tokens past the step's last are zeros.
     {
-        const uint32_t per_token = (hi - lo) * 8u;
-        for (uint32_t idx = warp; idx < MT * per_token; idx += W) {
-            const uint32_t i = idx / per_token, rem = idx % per_token;
-            const uint32_t g = lo + rem / 8u, v = rem % 8u;
-            float4* dst = reinterpret_cast<float4*>(xs + i * tok_floats + lane * lane_stride);
-            dst[(g - lo) * 8u + v] =
-                i < nt ? reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i) * a.x_stride)[g * 8u + v]
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t chunks = G * 8u;
+        for (uint32_t idx = threadIdx.x; idx < MT * chunks; idx += W * 32u) {
+            const uint32_t i = idx / chunks, c = idx % chunks;
+            const uint32_t grp = c / 8u, lr = lane_of(grp, G);
+            float* dst = xs + i * tok_floats + lr * lane_stride + (grp - range_lo(lr, G)) * 32u + (c % 8u) * 4u;
+            if (i < nt) cp_async16(dst, a.x + static_cast<size_t>(t0 + i) * a.x_stride + 4u * c);
+            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        cp_async_wait_all();
     }
     __syncthreads();
     grid_dependents_launch();
@@ -588,20 +619,22 @@ cudaError_t dispatch_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, 
     return cudaErrorInvalidValue;
 }
 
-template <typename F, int R>
-size_t decode_smem(uint32_t G) {
-    return 32ull * x_lane_stride(G) * 4u + kWarps * (16u + R * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
+// `extra`: the folded norm's row buffers (norm_tmp_bytes).
+template <typename F, int R, int W = kWarps>
+size_t decode_smem(uint32_t G, uint32_t extra = 0) {
+    return 32ull * x2_lane_stride(G) * 4u + extra +
+           W * (16u + R * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
 }
 
-template <typename F, int R>
+template <typename F, int R, int W = kWarps>
 cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    const size_t smem = decode_smem<F, R>(G);
+    const size_t smem = decode_smem<F, R, W>(G, norm_tmp_bytes(a));
     if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
     uint32_t batches = 0;
     if (a.epilogue == kGated) batches = (a.member[0].rows + (R > 1 ? R / 2 : 1) - 1) / (R > 1 ? R / 2 : 1);
     else for (uint32_t m = 0; m < a.members; ++m) batches += (a.member[m].rows + R - 1) / R;
-    auto kernel = decode_kernel<F, R>;
+    auto kernel = decode_kernel<F, R, W>;
     static bool configured = false;   // per instantiation
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDecodeSmem);
@@ -612,7 +645,7 @@ cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    uint32_t ctas = (batches + kWarps - 1) / kWarps;
+    uint32_t ctas = (batches + W - 1) / W;
     // Resident CTAs an SM holds at this shared-memory size, times the SMs:
     // beyond that the warps stride over batches with their copies in flight.
     uint32_t per_sm = static_cast<uint32_t>((227u * 1024u) / (smem + 1024u));
@@ -623,7 +656,7 @@ cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
     if (ctas == 0) ctas = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ctas, a.tokens ? a.tokens : 1u);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(W * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -634,18 +667,55 @@ cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
     return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
-// Rows a batch takes: enough batches that every SM has several warps, more
-// rows a warp when the product is large (fewer, longer copies); fewer rows
-// when a wide row's stages would not fit shared memory.
+// Latency shape, for products small enough that one batch a warp and at
+// most one CTA an SM hold all of their rows: every copy is issued before the
+// wait on the grid before, every CTA fits beside that grid's (none starts
+// late, when the one before has exited), and x is read once an SM. The
+// fewest rows a batch that fit, from two (rows in pairs take the paired
+// FMAs), then the fewest warps a CTA (the most SMs).
+constexpr size_t kLatencySmem = 100u * 1024u;
+
+template <typename F, int R>
+bool latency_shape(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl, cudaError_t& err) {
+    const uint32_t G = a.columns / 32u;
+    uint64_t batches = 0;
+    constexpr uint32_t H = R > 1 ? R / 2 : 1;   // a gated batch's outputs (gated products take R >= 2)
+    if (a.epilogue == kGated) batches = (a.member[0].rows + H - 1) / H;
+    else for (uint32_t m = 0; m < a.members; ++m) batches += (a.member[m].rows + R - 1) / R;
+    const uint64_t sms = static_cast<uint64_t>(sm_count);
+    if ((batches + 3) / 4 <= sms && decode_smem<F, R, 4>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+        err = launch_decode<F, R, 4>(a, sm_count, stream, pdl);
+        return true;
+    }
+    if ((batches + 7) / 8 <= sms && decode_smem<F, R, 8>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+        err = launch_decode<F, R, 8>(a, sm_count, stream, pdl);
+        return true;
+    }
+    if ((batches + 15) / 16 <= sms && decode_smem<F, R, 16>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+        err = launch_decode<F, R, 16>(a, sm_count, stream, pdl);
+        return true;
+    }
+    return false;
+}
+
+// Rows a batch takes: the latency shape where it fits; otherwise enough
+// batches that every SM has several warps, more rows a warp when the
+// product is large (fewer, longer copies), fewer rows when a wide row's
+// stages would not fit shared memory.
 template <typename F>
 cudaError_t dispatch(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
     const bool gated = a.epilogue == kGated;
+    cudaError_t err = cudaSuccess;
+    if (latency_shape<F, 2>(a, sm_count, stream, pdl, err)) return err;
+    if (latency_shape<F, 4>(a, sm_count, stream, pdl, err)) return err;
+    if (latency_shape<F, 8>(a, sm_count, stream, pdl, err)) return err;
     const uint64_t slots = gated ? 2ull * a.member[0].rows : a.total_rows;
     const uint64_t warps_wanted = static_cast<uint64_t>(sm_count) * 16u;
     const size_t budget = 110u * 1024u;   // two CTAs an SM at least
-    if (slots >= warps_wanted * 8u && decode_smem<F, 8>(G) <= budget) return launch_decode<F, 8>(a, sm_count, stream, pdl);
-    if (slots >= warps_wanted * 4u && decode_smem<F, 4>(G) <= budget) return launch_decode<F, 4>(a, sm_count, stream, pdl);
+    const uint32_t extra = norm_tmp_bytes(a);
+    if (slots >= warps_wanted * 8u && decode_smem<F, 8>(G, extra) <= budget) return launch_decode<F, 8>(a, sm_count, stream, pdl);
+    if (slots >= warps_wanted * 4u && decode_smem<F, 4>(G, extra) <= budget) return launch_decode<F, 4>(a, sm_count, stream, pdl);
     if (slots >= warps_wanted * 2u || gated) return launch_decode<F, 2>(a, sm_count, stream, pdl);
     return launch_decode<F, 1>(a, sm_count, stream, pdl);
 }
