@@ -84,17 +84,18 @@ __device__ __forceinline__ float tree_sum_pairs(float lo, float hi, float* scrat
 // norm_kernel's row (norm.cu) for one token on the first 128 threads of a
 // CTA: thread t does the work of norm_kernel's threads t and t+128 (vec4s
 // t + 128h + 256k), the same operations in the same order. The hidden row
-// (and y) come into `tmp` by asynchronous copies, each thread's own
-// elements, so no registers wait on the loads; the normed row goes to the x
-// stage, range-major with every float doubled; CTA 0 writes the add.
-// Threads from 128 up hold no elements and only meet the tree's barriers.
-__device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, float* tmp, uint32_t G,
-                                            uint32_t lane_stride) {
+// and y come by asynchronous copies, each thread's own elements, into the x
+// stage's space (twice the row: room for both), so no registers wait on the
+// loads; the normed row then goes to the x stage, range-major with every
+// float doubled, once every thread holds its own normed elements; CTA 0
+// writes the add. Threads from 128 up hold no elements and only meet the
+// barriers.
+__device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint32_t G, uint32_t lane_stride) {
     __shared__ float scratch[128];
     const uint32_t width = a.columns, t = threadIdx.x;
     const uint32_t vec4s = t < 128u ? width / 4u : 0u;
     const float n = static_cast<float>(width);
-    float4* th = reinterpret_cast<float4*>(tmp);
+    float4* th = reinterpret_cast<float4*>(xs);
     float4* ty = th + width / 4u;
     const float4* hg = reinterpret_cast<const float4*>(a.norm_hidden);
     const float4* yg = reinterpret_cast<const float4*>(a.norm_y);
@@ -155,6 +156,10 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, floa
             if (i < vec4s) sq[h] = sq[h] + dot4(th[i], th[i]);
         }
     const float r = 1.0f / sqrtf(tree_sum_pairs(sq[0], sq[1], scratch) / n + a.norm_epsilon);
+    // The normed elements into y's half (read by their own thread only, dead
+    // after the add), then, every thread past the barrier, into registers
+    // and the stage's doubled layout (which spans both halves).
+    float4* tv = th + width / 4u;
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -163,18 +168,30 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, floa
             if (i < vec4s) {
                 const float4 g = reinterpret_cast<const float4*>(a.norm_gain)[i];
                 const float4 x = th[i];
-                const float4 v = make_float4((x.x * r) * g.x, (x.y * r) * g.y, (x.z * r) * g.z, (x.w * r) * g.w);
-                const uint32_t e = 4u * i, grp = e / 32u, lr = lane_of(grp, G);
-                float4* d = reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 64u + 2u * (e % 32u));
-                d[0] = make_float4(v.x, v.x, v.y, v.y);
-                d[1] = make_float4(v.z, v.z, v.w, v.w);
+                tv[i] = make_float4((x.x * r) * g.x, (x.y * r) * g.y, (x.z * r) * g.z, (x.w * r) * g.w);
             }
         }
-}
-
-// Bytes of the folded norm's row buffers (the hidden row, and y when added).
-__host__ __device__ __forceinline__ uint32_t norm_tmp_bytes(const MatmulArgs& a) {
-    return a.norm_gain ? (a.norm_y ? 2u : 1u) * a.columns * 4u : 0u;
+    float4 v[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = t + 128u * h + 256u * k;
+            v[h][k] = i < vec4s ? tv[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    __syncthreads();   // every thread holds its elements: the stage may overwrite the rows
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = t + 128u * h + 256u * k;
+            if (i < vec4s) {
+                const uint32_t e = 4u * i, grp = e / 32u, lr = lane_of(grp, G);
+                float4* d = reinterpret_cast<float4*>(xs + lr * lane_stride + (grp - range_lo(lr, G)) * 64u + 2u * (e % 32u));
+                d[0] = make_float4(v[h][k].x, v[h][k].x, v[h][k].y, v[h][k].y);
+                d[1] = make_float4(v[h][k].z, v[h][k].z, v[h][k].w, v[h][k].w);
+            }
+        }
 }
 
 template <typename F, int R, int W>
@@ -188,12 +205,12 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
 
-    // Shared memory: x (range-major, each float doubled), the folded norm's
-    // row buffers, then per warp: 2 barriers, range sums, 2 stages.
+    // Shared memory: x (range-major, each float doubled), then per warp: 2
+    // barriers, range sums, 2 stages.
     float* xs = reinterpret_cast<float*>(smem);
     const uint32_t x_bytes = 32u * lane_stride * 4u;
     const uint32_t warp_bytes = 16u + R * kRedStride * 4u + 2u * stage_bytes;
-    uint8_t* wbase = smem + x_bytes + norm_tmp_bytes(a) + warp * warp_bytes;
+    uint8_t* wbase = smem + x_bytes + warp * warp_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
     float* red = reinterpret_cast<float*>(wbase + 16);
     uint8_t* stages = wbase + 16u + R * kRedStride * 4u;
@@ -217,7 +234,7 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     const uint32_t t = blockIdx.y;
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
     if (a.norm_gain) {
-        norm_row128(a, xs, reinterpret_cast<float*>(smem + x_bytes), G, lane_stride);
+        norm_row128(a, xs, G, lane_stride);
     } else {
         const float4* xg = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t) * a.x_stride);
 #pragma unroll 2
@@ -619,17 +636,15 @@ cudaError_t dispatch_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, 
     return cudaErrorInvalidValue;
 }
 
-// `extra`: the folded norm's row buffers (norm_tmp_bytes).
 template <typename F, int R, int W = kWarps>
-size_t decode_smem(uint32_t G, uint32_t extra = 0) {
-    return 32ull * x2_lane_stride(G) * 4u + extra +
-           W * (16u + R * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
+size_t decode_smem(uint32_t G) {
+    return 32ull * x2_lane_stride(G) * 4u + W * (16u + R * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
 }
 
 template <typename F, int R, int W = kWarps>
 cudaError_t launch_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    const size_t smem = decode_smem<F, R, W>(G, norm_tmp_bytes(a));
+    const size_t smem = decode_smem<F, R, W>(G);
     if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
     uint32_t batches = 0;
     if (a.epilogue == kGated) batches = (a.member[0].rows + (R > 1 ? R / 2 : 1) - 1) / (R > 1 ? R / 2 : 1);
@@ -683,15 +698,15 @@ bool latency_shape(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool 
     if (a.epilogue == kGated) batches = (a.member[0].rows + H - 1) / H;
     else for (uint32_t m = 0; m < a.members; ++m) batches += (a.member[m].rows + R - 1) / R;
     const uint64_t sms = static_cast<uint64_t>(sm_count);
-    if ((batches + 3) / 4 <= sms && decode_smem<F, R, 4>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+    if ((batches + 3) / 4 <= sms && decode_smem<F, R, 4>(G) <= kLatencySmem) {
         err = launch_decode<F, R, 4>(a, sm_count, stream, pdl);
         return true;
     }
-    if ((batches + 7) / 8 <= sms && decode_smem<F, R, 8>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+    if ((batches + 7) / 8 <= sms && decode_smem<F, R, 8>(G) <= kLatencySmem) {
         err = launch_decode<F, R, 8>(a, sm_count, stream, pdl);
         return true;
     }
-    if ((batches + 15) / 16 <= sms && decode_smem<F, R, 16>(G, norm_tmp_bytes(a)) <= kLatencySmem) {
+    if ((batches + 15) / 16 <= sms && decode_smem<F, R, 16>(G) <= kLatencySmem) {
         err = launch_decode<F, R, 16>(a, sm_count, stream, pdl);
         return true;
     }
@@ -713,9 +728,8 @@ cudaError_t dispatch(const MatmulArgs& a, int sm_count, cudaStream_t stream, boo
     const uint64_t slots = gated ? 2ull * a.member[0].rows : a.total_rows;
     const uint64_t warps_wanted = static_cast<uint64_t>(sm_count) * 16u;
     const size_t budget = 110u * 1024u;   // two CTAs an SM at least
-    const uint32_t extra = norm_tmp_bytes(a);
-    if (slots >= warps_wanted * 8u && decode_smem<F, 8>(G, extra) <= budget) return launch_decode<F, 8>(a, sm_count, stream, pdl);
-    if (slots >= warps_wanted * 4u && decode_smem<F, 4>(G, extra) <= budget) return launch_decode<F, 4>(a, sm_count, stream, pdl);
+    if (slots >= warps_wanted * 8u && decode_smem<F, 8>(G) <= budget) return launch_decode<F, 8>(a, sm_count, stream, pdl);
+    if (slots >= warps_wanted * 4u && decode_smem<F, 4>(G) <= budget) return launch_decode<F, 4>(a, sm_count, stream, pdl);
     if (slots >= warps_wanted * 2u || gated) return launch_decode<F, 2>(a, sm_count, stream, pdl);
     return launch_decode<F, 1>(a, sm_count, stream, pdl);
 }
