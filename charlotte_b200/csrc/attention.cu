@@ -42,6 +42,10 @@ namespace {
 constexpr uint32_t kChunk = 64;
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kMaxQueries = 16;   // queries (rows × G) a CTA works
+// Halves past a staged key or value row's d: a 16-byte pad, so the rows of
+// consecutive keys (read by consecutive lanes) start on different banks.
+constexpr uint32_t kRowPad = 8;
+constexpr uint32_t kChunkSlots = 16;   // CTAs a (kv head, row tile) takes, striding over its live chunks
 
 struct Geometry {
     uint32_t rows_per_tile;   // query rows a CTA takes
@@ -57,18 +61,24 @@ __host__ __device__ inline Geometry geometry_of(uint32_t query_heads, uint32_t k
 }
 
 __host__ __device__ inline size_t attention_smem(uint32_t d, uint32_t queries) {
-    return 2ull * kChunk * d * 2u            // K and V, f16
+    return 2ull * kChunk * (d + kRowPad) * 2u   // K and V, f16, padded rows
            + static_cast<size_t>(queries) * d * 4u   // q·scale·log2e
            + static_cast<size_t>(queries) * kChunk * 4u   // scores, then weights
            + static_cast<size_t>(queries) * 8u * 4u       // a tile's alpha (≤ 8 tiles)
            + static_cast<size_t>(queries) * 4u * 4u;      // m, l, live, spare
 }
 
+// Cluster fold (decode shapes: a row a tile, Q = G queries): the floats of
+// rank 0's shared memory that take every chunk's partial and (m, l), after
+// the layout above.
+__host__ __device__ inline size_t cluster_fold_floats(uint32_t d, uint32_t G) {
+    return static_cast<size_t>(kChunkSlots) * G * (d + 2u);
+}
+
 __device__ __forceinline__ uint32_t earliest_of(uint32_t p, uint32_t window) {
     return p + 1u > window ? p + 1u - window : 0u;
 }
 
-constexpr uint32_t kChunkSlots = 16;   // CTAs a (kv head, row tile) takes, striding over its live chunks
 
 // Stages keys and values j_lo..j_hi-1 (absolute positions) of the chunk at
 // key0
@@ -89,8 +99,100 @@ __device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_
     __syncwarp();
     for (uint32_t b = j_lo - key0 + lane; b < j_hi - key0; b += 32u) {
         const size_t at = (static_cast<size_t>((key0 + b) % a.slots) * a.kv_heads + kvh) * d;
-        bulk_g2s(ks + b * d, kc + at, row_bytes, bar);
-        bulk_g2s(vs + b * d, vc + at, row_bytes, bar);
+        bulk_g2s(ks + b * (d + kRowPad), kc + at, row_bytes, bar);
+        bulk_g2s(vs + b * (d + kRowPad), vc + at, row_bytes, bar);
+    }
+}
+
+// One step of the chunks' fold in chunk order (fold_factors/fold_sum/fold,
+// attention.wgsl:101-127): chunk (co, cm, cl) into the running (o, m, l).
+__device__ __forceinline__ void fold_step(float co, float cm, float cl, bool& live, float& run_m, float& run_l,
+                                          float& o) {
+    float fa, fb, fm;
+    if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
+    else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
+    else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
+    else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
+    run_l = fmaf(run_l, fa, cl * fb);
+    o = fmaf(o, fa, co * fb);
+    run_m = fm;
+    live = true;
+}
+
+// One query's softmax over a staged chunk (its scores in ps[0..63]), tiles
+// of B keys (8, 16 or 32), for the warp calling it: writes each key's weight
+// over its score, the tiles' alphas, and the chunk's (m, l) — the
+// operations of the tile-by-tile loop, in its order: the tile's top, then
+// old, top = max(old, tile top), a = 2^(old − top) (1 when equal), each live
+// key's 2^(s − top), the tile's sum from zero in key order, l = fma(l, a, sum).
+__device__ __forceinline__ void softmax_chunk(float* ps, float* alpha, float* stat, uint32_t key0, uint32_t p,
+                                              uint32_t window, uint32_t B, uint32_t lane) {
+    const uint32_t early = earliest_of(p, window);
+    const uint32_t tiles = kChunk / B, half = 32u / B;   // tiles in a half of the chunk
+    const uint32_t j0 = key0 + lane, j1 = key0 + lane + 32u;
+    const bool live0 = j0 <= p && j0 >= early, live1 = j1 <= p && j1 >= early;
+    const float s0 = ps[lane], s1 = ps[lane + 32u];
+    float t0 = live0 ? s0 : -INFINITY, t1 = live1 ? s1 : -INFINITY;
+    for (uint32_t o = B / 2u; o > 0u; o >>= 1) {
+        t0 = fmaxf(t0, __shfl_xor_sync(0xFFFFFFFFu, t0, o));
+        t1 = fmaxf(t1, __shfl_xor_sync(0xFFFFFFFFu, t1, o));
+    }
+    const uint32_t seen0 = __ballot_sync(0xFFFFFFFFu, live0), seen1 = __ballot_sync(0xFFFFFFFFu, live1);
+    const uint32_t group = B == 32u ? 0xFFFFFFFFu : (1u << B) - 1u;
+    // The running top and alpha, tile by tile (every lane alike); each lane
+    // keeps the tops of its own two keys' tiles.
+    bool chunk_live = false;
+    float chunk_m = 0.0f, top0 = 0.0f, top1 = 0.0f, al[8];
+#pragma unroll
+    for (uint32_t t = 0; t < 8u; ++t) {
+        al[t] = 1.0f;
+        if (t >= tiles) continue;
+        const bool lower = t < half;
+        const uint32_t src = (lower ? t : t - half) * B;
+        const float tt = __shfl_sync(0xFFFFFFFFu, lower ? t0 : t1, src);
+        const bool seen = (((lower ? seen0 : seen1) >> src) & group) != 0u;
+        if (seen) {
+            const float old = chunk_live ? chunk_m : tt;
+            chunk_live = true;
+            const float top = fmaxf(old, tt);
+            al[t] = old == top ? 1.0f : exp2_np(old - top);
+            chunk_m = top;
+        }
+        if (lane / B == t) top0 = chunk_m;
+        if (lane / B + half == t) top1 = chunk_m;
+    }
+    ps[lane] = live0 ? exp2_np(s0 - top0) : 0.0f;
+    ps[lane + 32u] = live1 ? exp2_np(s1 - top1) : 0.0f;
+    __syncwarp();
+    // Tile t's sum by lane t, in key order from zero.
+    float sum = 0.0f;
+    if (lane < tiles) {
+        const float4* e4 = reinterpret_cast<const float4*>(ps + lane * B);
+        for (uint32_t q = 0; q < B / 4u; ++q) {
+            const float4 v = e4[q];
+            sum = sum + v.x;
+            sum = sum + v.y;
+            sum = sum + v.z;
+            sum = sum + v.w;
+        }
+    }
+    float chunk_l = 0.0f;
+    bool any = false;
+#pragma unroll
+    for (uint32_t t = 0; t < 8u; ++t) {
+        if (t >= tiles) continue;
+        const float st = __shfl_sync(0xFFFFFFFFu, sum, t);
+        const bool lower = t < half;
+        const uint32_t src = (lower ? t : t - half) * B;
+        if ((((lower ? seen0 : seen1) >> src) & group) != 0u) {
+            chunk_l = fmaf(chunk_l, al[t], st);
+            any = true;
+        }
+        if (lane == 0) alpha[t] = al[t];
+    }
+    if (lane == 0) {
+        stat[0] = chunk_m;
+        stat[1] = any ? chunk_l : 0.0f;
     }
 }
 
@@ -117,18 +219,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     const uint32_t Q = rows * G;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
 
+    const uint32_t pitch = d + kRowPad;   // halves a staged key or value row takes
     uint16_t* ks = reinterpret_cast<uint16_t*>(smem);
-    uint16_t* vs = ks + kChunk * d;
-    float* qs = reinterpret_cast<float*>(vs + kChunk * d);
+    uint16_t* vs = ks + kChunk * pitch;
+    float* qs = reinterpret_cast<float*>(vs + kChunk * pitch);
     float* ps = qs + kMaxQueries * d;                 // [Q][64]
     float* alpha = ps + kMaxQueries * kChunk;         // [Q][8]
     float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l
+    float* fold_part = stat + kMaxQueries * 4u;       // cluster fold, rank 0: [slot][Q][d], then [slot][Q][2]
+    float* fold_stat = fold_part + kChunkSlots * G * d;
 
     // The tile's live chunks: every chunk some row's keys reach.
     const uint32_t p_first = pos0 + (seqs ? 0u : row0), p_last = p_first + (seqs ? 0u : rows - 1u);
     const uint32_t live_first = earliest_of(p_first, a.window) / kChunk;
     const uint32_t live_chunks = p_last / kChunk - live_first + 1u;
-    if (blockIdx.y >= live_chunks) {   // no chunk for this slot: no ticket either
+    // Cluster fold: the tile's chunk CTAs are one cluster (the launch makes
+    // them one for decode shapes when it fits) and each has at most one
+    // live chunk. Each CTA then stores its partial and (m, l) into rank 0's
+    // shared memory; after one cluster barrier, which every CTA of the
+    // cluster meets, chunk or not, rank 0 folds them. Otherwise partials go
+    // through global memory and the last CTA to take a ticket folds them.
+    const bool cluster_fold = cluster_size() > 1u && live_chunks <= gridDim.y;
+    if (blockIdx.y >= live_chunks && !cluster_fold) {   // no chunk for this slot: no ticket either
         grid_dependency_wait();
         return;
     }
@@ -151,11 +263,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     grid_dependency_wait();
 
     // Queries m = r·G + g: row r, head kvh·G + g, scaled into log2 units.
-    for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+    for (uint32_t i = threadIdx.x; i < (blockIdx.y < live_chunks ? Q * d : 0u); i += kAttnThreads) {
         const uint32_t m = i / d, e = i % d;
         const uint32_t r = m / G, h = kvh * G + m % G;
         qs[m * d + e] = a.query[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] * a.scale_log2e;
     }
+    bool failed = false;
     for (uint32_t c = c_first; c <= p_last / kChunk; c += gridDim.y) {
         const uint32_t key0 = c * kChunk;
         const bool first_chunk = c == c_first;
@@ -170,15 +283,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             const uint32_t j_hi = min(key0 + kChunk, p_last + 1u);
             stage_keys(a, kc, vc, ks, vs, key0, j_lo, j_hi, kvh, d, &kv_bar, true);
         }
-        if (!mbar_wait(&kv_bar, kv_phase, fault)) {
-            // A copy did not land in time (the fault word is set): wait once
-            // more, bounded, so none is left writing this CTA's shared
-            // memory, and leave without a ticket (the step reports failure).
+        if (!__syncthreads_and(mbar_wait(&kv_bar, kv_phase, fault))) {
+            // A copy did not land in time (the fault word is set; the whole
+            // CTA agrees): wait once more, bounded, so none is left writing
+            // this CTA's shared memory, and stop (the step reports failure).
             mbar_wait(&kv_bar, kv_phase, nullptr);
-            return;
+            failed = true;
+            break;
         }
         kv_phase ^= 1u;
-        __syncthreads();
         // Scores: s = Σ_w dot(q_w, k_w) in quads, in order.
         for (uint32_t i = threadIdx.x; i < Q * kChunk; i += kAttnThreads) {
             const uint32_t m = i / kChunk, b = i % kChunk;
@@ -186,23 +299,37 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             const uint32_t j = key0 + b;
             float s = 0.0f;
             if (j <= p && j >= earliest_of(p, a.window)) {
+                // Two quads a 16-byte read of the key row (padded rows:
+                // consecutive lanes' keys on distinct banks).
                 const float4* q4 = reinterpret_cast<const float4*>(qs + m * d);
-                const uint2* k4 = reinterpret_cast<const uint2*>(ks + b * d);
-#pragma unroll 8
-                for (uint32_t w = 0; w < d / 4u; ++w) {
-                    const uint2 kw = k4[w];
-                    const float4 kk = make_float4(fp16_bits_to_f32(kw.x & 0xFFFF), fp16_bits_to_f32(kw.x >> 16),
+                const uint4* k8 = reinterpret_cast<const uint4*>(ks + b * pitch);
+#pragma unroll 4
+                for (uint32_t w = 0; w < d / 8u; ++w) {
+                    const uint4 kw = k8[w];
+                    const float4 ka = make_float4(fp16_bits_to_f32(kw.x & 0xFFFF), fp16_bits_to_f32(kw.x >> 16),
                                                   fp16_bits_to_f32(kw.y & 0xFFFF), fp16_bits_to_f32(kw.y >> 16));
-                    s = s + dot4(q4[w], kk);
+                    const float4 kb = make_float4(fp16_bits_to_f32(kw.z & 0xFFFF), fp16_bits_to_f32(kw.z >> 16),
+                                                  fp16_bits_to_f32(kw.w & 0xFFFF), fp16_bits_to_f32(kw.w >> 16));
+                    s = s + dot4(q4[2u * w], ka);
+                    s = s + dot4(q4[2u * w + 1u], kb);
                 }
             }
             ps[m * kChunk + b] = s;
         }
         __syncthreads();
-    // The online softmax, a warp a query, tile by tile in key order: the
+        // The online softmax, a warp a query, tile by tile in key order: the
         // tile's top (a max: any order gives its bits) and each live key's
-        // 2^(s − top) across lanes; the sum of a tile's weights, and the
-        // running l and m, by lane 0 in key order.
+        // 2^(s − top); the sum of a tile's weights in key order, and the
+        // running l and m. Tiles of 8, 16 or 32 keys (d = 256, 128, 64): a
+        // lane holds keys lane and lane+32, every tile's top comes from one
+        // butterfly over its lanes at once, and each tile's sum is read back
+        // from shared memory by a lane of its own.
+        if (B >= 8u && B <= 32u && (B & (B - 1u)) == 0u) {
+            for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
+                softmax_chunk(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p_first + (seqs ? 0u : m / G),
+                              a.window, B, lane);
+            }
+        } else
         for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
             const uint32_t p = p_first + (seqs ? 0u : m / G);
             const uint32_t early = earliest_of(p, a.window);
@@ -252,20 +379,64 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             for (uint32_t t = 0; t < tiles; ++t) {
                 o = o * alpha[m * 8u + t];
                 const uint32_t b_end = min((t + 1u) * B, valid);
-#pragma unroll 8
-                for (uint32_t b = t * B; b < b_end; ++b)
-                    o = fmaf(ps[m * kChunk + b], fp16_bits_to_f32(vs[b * d + e]), o);
+                // Eight keys' weights and values into registers, then their
+                // fmas in key order (keys from b_end on are skipped).
+                for (uint32_t b0 = t * B; b0 < b_end; b0 += 8u) {
+                    float pw[8], vv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t b = b0 + k < b_end ? b0 + k : b0;
+                        pw[k] = ps[m * kChunk + b];
+                        vv[k] = fp16_bits_to_f32(vs[b * pitch + e]);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (b0 + k < b_end) o = fmaf(pw[k], vv[k], o);
+                }
             }
-            const uint32_t r = m / G, h = kvh * G + m % G;
-            const size_t at = (static_cast<size_t>(c) * a.tokens + row0 + r) * a.query_heads + h;
-            a.partials[at * d + e] = o;
-            if (e == 0) {
-                a.stats[at * 2u] = stat[m * 4u];
-                a.stats[at * 2u + 1u] = stat[m * 4u + 1u];
+            if (cluster_fold) {
+                // Into rank 0's slot for this CTA's chunk (slot = rank).
+                const uint32_t slot = blockIdx.y;
+                st_cluster_f32(cluster_map(fold_part + (slot * G + m) * d + e, 0u), o);
+                if (e == 0) {
+                    st_cluster_f32(cluster_map(fold_stat + (slot * G + m) * 2u, 0u), stat[m * 4u]);
+                    st_cluster_f32(cluster_map(fold_stat + (slot * G + m) * 2u + 1u, 0u), stat[m * 4u + 1u]);
+                }
+            } else {
+                const uint32_t r = m / G, h = kvh * G + m % G;
+                const size_t at = (static_cast<size_t>(c) * a.tokens + row0 + r) * a.query_heads + h;
+                a.partials[at * d + e] = o;
+                if (e == 0) {
+                    a.stats[at * 2u] = stat[m * 4u];
+                    a.stats[at * 2u + 1u] = stat[m * 4u + 1u];
+                }
             }
         }
     }
     grid_dependents_launch();
+
+    if (cluster_fold) {
+        cluster_sync();   // every chunk's partial and (m, l) is in rank 0's shared memory
+        if (cluster_rank() != 0u) return;
+        // Each (query, dimension) folds its chunks (slot = chunk − the
+        // tile's first live chunk) in chunk order.
+        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
+            const uint32_t m = i / d, e = i % d;
+            const uint32_t r = m / G, h = kvh * G + m % G;
+            const uint32_t p = p_first + (seqs ? 0u : r);
+            const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
+            bool live = false;
+            float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
+            for (uint32_t c = c0; c <= c1; ++c) {
+                const uint32_t slot = c - live_first;
+                fold_step(fold_part[(slot * G + m) * d + e], fold_stat[(slot * G + m) * 2u],
+                          fold_stat[(slot * G + m) * 2u + 1u], live, run_m, run_l, o);
+            }
+            a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
+        }
+        return;
+    }
+    if (failed) return;   // without a ticket: the step reports failure
 
     // The last of the tile's chunk CTAs to finish folds the chunks in order.
     __shared__ unsigned int last;
@@ -302,16 +473,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 if (cc + k > c1) break;
-                const float cm = cms[k], cl = cls[k];
-                float fa, fb, fm;
-                if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
-                else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
-                else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
-                else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
-                run_l = fmaf(run_l, fa, cl * fb);
-                o = fmaf(o, fa, co[k] * fb);
-                run_m = fm;
-                live = true;
+                fold_step(co[k], cms[k], cls[k], live, run_m, run_l, o);
             }
         }
         a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
@@ -329,26 +491,49 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     if (!a.rows_are_sequences && a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a))
         return attention_prefill_run(a, stream, pdl);
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
-    size_t smem = 2ull * kChunk * a.head_dim * 2u + kMaxQueries * a.head_dim * 4u + kMaxQueries * kChunk * 4u +
-                  kMaxQueries * 8u * 4u + kMaxQueries * 4u * 4u;
-    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
+    if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
+    // Decode shapes (a row a tile) may fold over a cluster, with room in
+    // rank 0 for every chunk's partial.
+    const bool decode_shape = a.tokens == 1u || a.rows_are_sequences;
+    const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
         configured = true;
     }
+    const uint32_t slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads, a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots,
-                       (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
+    cfg.gridDim = dim3(a.kv_heads, slots, (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    // A (kv head, row tile)'s chunk CTAs as one cluster, when a cluster of
+    // that many CTAs can be resident at this shared-memory size (asked of
+    // the occupancy calculator once a size).
+    static int cluster_fits[kChunkSlots + 1] = {};   // 0 unknown, 1 yes, -1 no
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = slots;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    const bool can_cluster = decode_shape && slots > 1 && cluster_smem <= 200u * 1024u;
+    if (can_cluster && cluster_fits[slots] == 0) {
+        cfg.numAttrs = 2;
+        cfg.dynamicSmemBytes = cluster_smem;
+        int clusters = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel, &cfg);
+        if (e != cudaSuccess) cudaGetLastError();
+        cluster_fits[slots] = e == cudaSuccess && clusters >= 1 ? 1 : -1;
+    }
+    const bool cluster = can_cluster && cluster_fits[slots] > 0;
+    cfg.numAttrs = cluster ? 2 : 1;
+    cfg.dynamicSmemBytes = cluster ? cluster_smem : base_smem;
     return cudaLaunchKernelEx(&cfg, attention_kernel, a, fault_word());
 }
 
