@@ -66,7 +66,8 @@ class Attention(ctypes.Structure):
                 ("tokens", ctypes.c_uint32), ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32),
                 ("kv_heads", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("window", ctypes.c_uint32),
                 ("max_chunks", ctypes.c_uint32), ("scale_log2e", ctypes.c_float),
-                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64)]
+                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64),
+                ("rope", ctypes.c_void_p)]
 
 
 class Gather(ctypes.Structure):
@@ -210,7 +211,14 @@ def run(kind: str, **fields) -> None:
     stream = fields.pop("stream", None)
     flags = fields.pop("flags", 0)
     v = struct()
+    keep = []   # nested structs, alive through the call
     for name, value in fields.items():
+        if isinstance(value, dict):   # attention's fused rope: a cb_rope passed by pointer
+            sub = Rope()
+            for n2, v2 in value.items():
+                setattr(sub, n2, v2.data_ptr() if hasattr(v2, "data_ptr") else v2)
+            keep.append(sub)
+            value = ctypes.addressof(sub)
         if hasattr(value, "data_ptr"):
             value = value.data_ptr()
         setattr(v, name, value)

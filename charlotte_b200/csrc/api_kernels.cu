@@ -78,6 +78,22 @@ int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
     if (!a->position && static_cast<uint64_t>(a->position0) + (a->rows_are_sequences ? 1u : a->tokens) >
                             static_cast<uint64_t>(a->max_chunks) * 64)
         return fail(CB_ERROR_INVALID, "cb_attention_run: positions past max_chunks");
+    if (const cb_rope* r = a->rope) {
+        if (!(a->tokens == 1 || a->rows_are_sequences))
+            return fail(CB_ERROR_INVALID, "cb_attention_run: a fused rope needs a decode shape (one token, or sequences)");
+        if (!r->query || !r->key || !r->value || !r->turns || !aligned16(r->query) || !aligned16(r->key) ||
+            !aligned16(r->value))
+            return fail(CB_ERROR_INVALID, "cb_attention_run: fused rope: null or unaligned rows");
+        if (r->tokens != a->tokens || r->head_dim != a->head_dim || r->query_heads != a->query_heads ||
+            r->kv_heads != a->kv_heads || r->slots != a->slots || r->key_cache != a->key_cache ||
+            r->value_cache != a->value_cache || r->position != a->position ||
+            (!a->position && r->position0 != a->position0) ||
+            (r->rows_are_sequences != 0) != (a->rows_are_sequences != 0) ||
+            (a->rows_are_sequences && r->sequence_stride != a->sequence_stride))
+            return fail(CB_ERROR_INVALID, "cb_attention_run: the fused rope describes other rows, heads or caches");
+        if ((r->query_gain == nullptr) != (r->key_gain == nullptr))
+            return fail(CB_ERROR_INVALID, "cb_attention_run: fused rope: both norm gains or neither");
+    }
     if (a->tokens == 0) return CB_OK;
     return launched(attention_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_attention_run");
 }

@@ -33,6 +33,7 @@
 #include "api_common.h"
 #include "kernels.h"
 #include "numerics.cuh"
+#include "rope_math.cuh"
 #include "tma.cuh"
 
 namespace cb {
@@ -196,7 +197,10 @@ __device__ __forceinline__ void softmax_chunk(float* ps, float* alpha, float* st
     }
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a, unsigned int* fault) {
+// The step's rope done in the prologue (decode shapes, `fused`): r is that
+// rope step's arguments.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a, RopeArgs r, uint32_t fused,
+                                                                 unsigned int* fault) {
     extern __shared__ __align__(16) uint8_t smem[];
     const uint32_t d = a.head_dim;
     const uint32_t B = 2048u / d;
@@ -253,17 +257,68 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     }
     __syncthreads();
     // This slot's first chunk's keys of earlier steps (below pos0), in flight
-    // while the launch before this one (rope) finishes.
+    // while the launch before this one finishes.
     const uint32_t c_first = live_first + blockIdx.y;
     {
         const uint32_t key0 = c_first * kChunk;
         const uint32_t j_hi = min(key0 + kChunk, max(pos0, key0));
         stage_keys(a, kc, vc, ks, vs, key0, key0, j_hi, kvh, d, &kv_bar, false);
     }
+    const bool working = blockIdx.y < live_chunks;
+    // The fused rope's angle table for the rows' position (decode shapes: one
+    // position a tile), into the score buffer, free until the scores.
+    float* cosines = ps;
+    float* sines = ps + d / 2u;
+    if (fused && working) rope_angles(p_first, r.turns, r.factors, d, cosines, sines, threadIdx.x, kAttnThreads);
     grid_dependency_wait();
 
+    // The fused rope: G query heads (and, in the CTA whose chunks hold the
+    // newest key, that key and its value), d/8 threads a head as in the rope
+    // launch. Queries go to the q stage scaled as below; the key and value,
+    // packed f16, to the caches and — when the newest key's chunk is this
+    // CTA's first — straight into the chunk's stage.
+    if (fused && working) {
+        __syncthreads();   // the angle table
+        const uint32_t lanes = d / 8u;
+        const uint32_t newest_chunk = p_first / kChunk;
+        const bool newest = (newest_chunk - live_first) % gridDim.y == blockIdx.y;
+        const uint32_t heads = G + (newest ? 2u : 0u);
+        if (threadIdx.x < (heads * lanes + 31u) / 32u * 32u) {
+            const uint32_t head = threadIdx.x / lanes, lane = threadIdx.x % lanes;
+            const bool valid = head < heads, is_query = head < G, is_value = head == G + 1u;
+            const size_t row = row0;
+            const float* src = is_query ? r.query + (row * a.query_heads + kvh * G + head) * d
+                                        : (is_value ? r.value : r.key) + (row * a.kv_heads + kvh) * d;
+            float4 x0 = valid ? reinterpret_cast<const float4*>(src)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 x1 = valid ? reinterpret_cast<const float4*>(src)[lane + lanes] : make_float4(0.f, 0.f, 0.f, 0.f);
+            rope_head(x0, x1, lane, lanes, d, r.query_gain != nullptr, r.epsilon, is_query ? r.query_gain : r.key_gain,
+                      !is_value, r.halves != 0, cosines, sines);
+            if (valid && is_query) {
+                float4* q4 = reinterpret_cast<float4*>(qs + head * d);
+                q4[lane] = make_float4(x0.x * a.scale_log2e, x0.y * a.scale_log2e, x0.z * a.scale_log2e,
+                                       x0.w * a.scale_log2e);
+                q4[lane + lanes] = make_float4(x1.x * a.scale_log2e, x1.y * a.scale_log2e, x1.z * a.scale_log2e,
+                                               x1.w * a.scale_log2e);
+            } else if (valid) {
+                uint16_t* cache = (is_value ? r.value_cache : r.key_cache) + (seqs ? row * r.sequence_stride : 0u);
+                uint16_t* dst = cache + (static_cast<size_t>(p_first % a.slots) * a.kv_heads + kvh) * d;
+                store_f16x4(dst + 4u * lane, x0);
+                store_f16x4(dst + 4u * (lane + lanes), x1);
+                if (newest_chunk == c_first) {
+                    uint16_t* st = (is_value ? vs : ks) + (p_first - c_first * kChunk) * pitch;
+                    store_f16x4(st + 4u * lane, x0);
+                    store_f16x4(st + 4u * (lane + lanes), x1);
+                }
+            }
+        }
+        // The new rows' global stores before a bulk copy that reads them (a
+        // later chunk of this CTA's), and the angle table's last reads.
+        fence_proxy_async_global();
+        __syncthreads();
+    }
+
     // Queries m = r·G + g: row r, head kvh·G + g, scaled into log2 units.
-    for (uint32_t i = threadIdx.x; i < (blockIdx.y < live_chunks ? Q * d : 0u); i += kAttnThreads) {
+    for (uint32_t i = threadIdx.x; i < (working && !fused ? Q * d : 0u); i += kAttnThreads) {
         const uint32_t m = i / d, e = i % d;
         const uint32_t r = m / G, h = kvh * G + m % G;
         qs[m * d + e] = a.query[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] * a.scale_log2e;
@@ -277,11 +332,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             fence_proxy_async();  // and ordered before the copy engine's writes
         }
         // The chunk's keys this step wrote (for later chunks, all of them);
-        // positions past p_last are never live and are not staged.
+        // positions past p_last are never live and are not staged. A fused
+        // rope's newest key, when this is its chunk and the CTA's first, is
+        // staged already.
         {
             const uint32_t j_lo = first_chunk ? max(key0, min(pos0, key0 + kChunk)) : key0;
-            const uint32_t j_hi = min(key0 + kChunk, p_last + 1u);
-            stage_keys(a, kc, vc, ks, vs, key0, j_lo, j_hi, kvh, d, &kv_bar, true);
+            const bool staged_new = fused && first_chunk && p_last / kChunk == c;
+            const uint32_t j_hi = min(key0 + kChunk, staged_new ? p_last : p_last + 1u);
+            stage_keys(a, kc, vc, ks, vs, key0, j_lo, max(j_lo, j_hi), kvh, d, &kv_bar, true);
         }
         if (!__syncthreads_and(mbar_wait(&kv_bar, kv_phase, fault))) {
             // A copy did not land in time (the fault word is set; the whole
@@ -491,6 +549,15 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     if (!a.rows_are_sequences && a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a))
         return attention_prefill_run(a, stream, pdl);
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
+    if (a.rope && (geo.G + 2u) * (a.head_dim / 8u) > kAttnThreads) {
+        // More heads than one CTA's threads hold: the rope launch first, then
+        // the attention over its output, as without the fused form.
+        if (cudaError_t e = rope_run(*a.rope, stream, pdl); e != cudaSuccess) return e;
+        AttentionArgs b = a;
+        b.query = a.rope->query;
+        b.rope = nullptr;
+        return attention_run(b, stream, pdl);
+    }
     const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
     if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
     // Decode shapes (a row a tile) may fold over a cluster, with room in
@@ -527,14 +594,16 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
         cfg.numAttrs = 2;
         cfg.dynamicSmemBytes = cluster_smem;
         int clusters = 0;
-        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel, &cfg);
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel, &cfg);   // any arguments
         if (e != cudaSuccess) cudaGetLastError();
         cluster_fits[slots] = e == cudaSuccess && clusters >= 1 ? 1 : -1;
     }
     const bool cluster = can_cluster && cluster_fits[slots] > 0;
     cfg.numAttrs = cluster ? 2 : 1;
     cfg.dynamicSmemBytes = cluster ? cluster_smem : base_smem;
-    return cudaLaunchKernelEx(&cfg, attention_kernel, a, fault_word());
+    RopeArgs r{};
+    if (a.rope) r = *a.rope;
+    return cudaLaunchKernelEx(&cfg, attention_kernel, a, r, a.rope ? 1u : 0u, fault_word());
 }
 
 }  // namespace cb

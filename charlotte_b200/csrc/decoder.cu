@@ -311,8 +311,13 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         r.halves = m.halves;
         r.slots = L.slots;
         r.epsilon = m.epsilon;
-        if (int rc = launched(rope_run(r, d->stream, true), "step: rope")) return rc;
+        // Decode shapes fold the rope into the attention's prologue (one
+        // launch fewer a layer); steps of several positions launch it.
+        const bool fuse_rope = tokens == 1u || batch;
+        if (!fuse_rope)
+            if (int rc = launched(rope_run(r, d->stream, true), "step: rope")) return rc;
         cb_attention at{};
+        at.rope = fuse_rope ? &r : nullptr;
         at.query = d->q;
         at.key_cache = L.key_cache + cache_at;
         at.value_cache = L.value_cache + cache_at;

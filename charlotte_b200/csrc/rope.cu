@@ -19,17 +19,12 @@
 
 #include "kernels.h"
 #include "numerics.cuh"
+#include "rope_math.cuh"
 #include "tma.cuh"
 
 namespace cb {
 
 namespace {
-
-__device__ __forceinline__ void store_f16x4(uint16_t* dst, float4 v) {
-    const uint32_t lo = static_cast<uint32_t>(f32_to_f16_sat(v.x)) | (static_cast<uint32_t>(f32_to_f16_sat(v.y)) << 16);
-    const uint32_t hi = static_cast<uint32_t>(f32_to_f16_sat(v.z)) | (static_cast<uint32_t>(f32_to_f16_sat(v.w)) << 16);
-    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-}
 
 __global__ void rope_kernel(RopeArgs a) {
     extern __shared__ float angles[];   // cos then sin, d/2 each
@@ -42,12 +37,7 @@ __global__ void rope_kernel(RopeArgs a) {
     const uint32_t p = (a.position ? *a.position : a.position0) + (a.rows_are_sequences ? 0u : row);
     float* cosines = angles;
     float* sines = angles + d / 2u;
-    for (uint32_t k = threadIdx.x; k < d / 2u; k += blockDim.x) {
-        float t = static_cast<float>(p) * a.turns[k];
-        if (a.factors) t = t / a.factors[k];
-        const float angle = 6.283185307179586f * (t - rintf(t));
-        sincos_turn(angle, &sines[k], &cosines[k]);
-    }
+    rope_angles(p, a.turns, a.factors, d, cosines, sines, threadIdx.x, blockDim.x);
     __syncthreads();
     grid_dependents_launch();
 
@@ -68,48 +58,8 @@ __global__ void rope_kernel(RopeArgs a) {
     // QK-norm (uniform over the CTA: both gains or neither). Every lane takes
     // part in the shuffles — a warp may hold a key head and a value head —
     // and value heads discard the result.
-    float r = 1.0f;
-    if (a.query_gain) {
-        float v = dot4(x0, x0) + dot4(x1, x1);
-        for (uint32_t stride = lanes / 2u; stride > 0; stride >>= 1)
-            v = v + __shfl_down_sync(0xFFFFFFFFu, v, stride, lanes);
-        const float total = __shfl_sync(0xFFFFFFFFu, v, 0, lanes);
-        r = 1.0f / sqrtf(total / static_cast<float>(d) + a.epsilon);
-    }
-    if (!is_value) {
-        const float* gain = is_query ? a.query_gain : a.key_gain;
-        if (gain) {
-            const float4 g0 = reinterpret_cast<const float4*>(gain)[lane];
-            const float4 g1 = reinterpret_cast<const float4*>(gain)[lane + lanes];
-            x0 = make_float4((x0.x * r) * g0.x, (x0.y * r) * g0.y, (x0.z * r) * g0.z, (x0.w * r) * g0.w);
-            x1 = make_float4((x1.x * r) * g1.x, (x1.y * r) * g1.y, (x1.z * r) * g1.z, (x1.w * r) * g1.w);
-        }
-        if (a.halves) {
-            // pairs k = 4·lane + c: (x0.c, x1.c) turned by angle k
-            float* e0 = &x0.x;
-            float* e1 = &x1.x;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t k = 4u * lane + c;
-                const float u = e0[c], w = e1[c];
-                e0[c] = fmaf(u, cosines[k], -(w * sines[k]));
-                e1[c] = fmaf(u, sines[k], w * cosines[k]);
-            }
-        } else {
-            // adjacent pairs: x0 holds pairs 2·lane, 2·lane+1; x1 pairs d/4 + 2·lane, +1
-            float* e[2] = {&x0.x, &x1.x};
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const uint32_t k = (h ? d / 4u : 0u) + 2u * lane + c;
-                    const float u = e[h][2 * c], w = e[h][2 * c + 1];
-                    e[h][2 * c] = fmaf(u, cosines[k], (-w) * sines[k]);
-                    e[h][2 * c + 1] = fmaf(w, cosines[k], u * sines[k]);
-                }
-            }
-        }
-    }
+    rope_head(x0, x1, lane, lanes, d, a.query_gain != nullptr, a.epsilon, is_query ? a.query_gain : a.key_gain,
+              !is_value, a.halves != 0, cosines, sines);
     if (is_query) {
         float4* dst = reinterpret_cast<float4*>(a.query + (static_cast<size_t>(row) * hq + head) * d);
         dst[lane] = x0;

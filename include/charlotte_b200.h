@@ -220,6 +220,16 @@ typedef struct cb_attention {
      * then holds tokens·kv_heads zeroed words. */
     uint32_t rows_are_sequences;
     uint64_t sequence_stride;
+    /* Decode shapes only (tokens == 1, or rows_are_sequences): when not NULL
+     * (a host pointer, read at launch), this launch also does that rope step
+     * for its rows, and no rope launch comes before it (no counterpart in the
+     * reference, which launches rope then attention). `query` is then not
+     * read: each CTA norms and turns its rows' raw queries from rope->query
+     * in its prologue (they are not written back), and the CTA holding each
+     * row's newest key turns that key, appends it and the value to the
+     * caches, and stages both itself. Its fields must describe the same
+     * rows, heads, caches and position as this struct's. */
+    const cb_rope* rope;
 } cb_attention;
 CB_API int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream);
 /* Ticket words cb_attention needs for `tokens` rows. */

@@ -195,6 +195,65 @@ def test_attention_bit_exact(cuda, case, position, tokens):
             assert np.max(np.abs(got[t, h * d:(h + 1) * d] - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
 
 
+# ---- attention with the step's rope in its prologue --------------------------------
+
+FUSED = [
+    # name, d, Hq, Hkv, NEOX halves, QK-norm, base, llama3 factors, window
+    ("qwen3", 128, 16, 8, True, True, 1e6, False, 1 << 30),
+    ("llama3", 64, 32, 8, False, False, 5e5, True, 1 << 30),
+    ("gemma3", 256, 4, 1, True, True, 1e4, False, 512),
+]
+
+
+@pytest.mark.parametrize("case", FUSED, ids=[c[0] for c in FUSED])
+# 1500 with a full window: 24 live chunks, more than the 16 chunk CTAs (the
+# newest key's chunk is then a later chunk of its CTA, copied from the cache)
+@pytest.mark.parametrize("position", [0, 63, 64, 700, 1500])
+@pytest.mark.parametrize("sequences", [0, 3])
+def test_attention_fused_rope_matches_separate(cuda, case, position, sequences):
+    """Decode attention with the step's rope folded into its prologue gives
+    the bits of the rope launch followed by the attention launch: the
+    outputs and both caches (the step's key and value appended)."""
+    name, d, hq, hkv, halves, qk, base, factors, window = case
+    rng = np.random.default_rng(position * 3 + sequences + d)
+    rows, slots = max(sequences, 1), 2048
+    stride = slots * hkv * d
+    kc = f16_cache(rng, rows * slots, hkv, d, 2.0)
+    vc = f16_cache(rng, rows * slots, hkv, d)
+    q = (rng.standard_normal((rows, hq * d)) * 2).astype(np.float32)
+    k = (rng.standard_normal((rows, hkv * d)) * 2).astype(np.float32)
+    v = rng.standard_normal((rows, hkv * d)).astype(np.float32)
+    qg = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32) if qk else None
+    kg = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32) if qk else None
+    turns = dev(cb.rope_turns(base, d))
+    fac = dev(llama3_factors(d, base)) if factors else 0
+    gains = dict(query_gain=dev(qg) if qk else 0, key_gain=dev(kg) if qk else 0)
+    scale_log2e = float(np.float32((1.0 / math.sqrt(d)) * 1.4426950408889634))
+    max_chunks = min(slots // 64, (position + 64) // 64 + 5)   # idle chunk CTAs too
+    tickets_n = rows * hkv if sequences else cb.lib().cb_attention_tickets(1, hq, hkv)
+    shape = dict(position=0, position0=position, tokens=rows, head_dim=d, query_heads=hq, kv_heads=hkv, slots=slots)
+    seq = dict(rows_are_sequences=1, sequence_stride=stride) if sequences else {}
+    outs = []
+    for fused in (False, True):
+        kcd, vcd, qd = dev(kc), dev(vc), dev(q)
+        out = torch.zeros((rows, hq * d), dtype=torch.float32, device="cuda")
+        partials = torch.zeros(max_chunks * rows * hq * d, dtype=torch.float32, device="cuda")
+        stats = torch.zeros(max_chunks * rows * hq * 2, dtype=torch.float32, device="cuda")
+        tickets = torch.zeros(tickets_n, dtype=torch.int32, device="cuda")
+        rope = dict(query=qd, key=dev(k), value=dev(v), key_cache=kcd, value_cache=vcd, factors=fac, turns=turns,
+                    halves=int(halves), epsilon=1e-6, **gains, **shape, **seq)
+        if not fused:
+            cb.run("rope", **rope)
+        cb.run("attention", query=qd, key_cache=kcd, value_cache=vcd, out=out, partials=partials, stats=stats,
+               tickets=tickets, window=min(window, 0xFFFFFFFF), max_chunks=max_chunks, scale_log2e=scale_log2e,
+               rope=rope if fused else 0, **shape, **seq)
+        done()
+        assert not tickets.any()
+        outs.append((out.cpu().numpy(), kcd.cpu().numpy(), vcd.cpu().numpy()))
+    for a, b in zip(*outs):
+        same(b, a)
+
+
 # ---- gather ------------------------------------------------------------------------
 
 @pytest.mark.parametrize("fmt,width,scale", [(O.Q6_K, 1024, 1.0), (O.Q4_0, 2048, 1.0),
