@@ -412,7 +412,10 @@ def decode_bench(steps, prompt_len, seed, world):
         "workload": "qwen3-0.6b greedy decode (configs[2]): 512-token prompt, %d steps, f16 KV, context 4096" % steps,
         "tok_s": round(steps * world / (dev_ms * 1e-3), 1),
         "ms_per_token": round(dev_ms / steps, 4),
-        "launches_per_token": 4 + 8 * arch.layers + 1,
+        # gather, then a layer's QKV (its norm folded in), attention (its rope
+        # folded in), O, gate|up (norm folded in), down; the head (final norm
+        # folded in), top-k + draw, the position advance
+        "launches_per_token": 4 + 5 * arch.layers,
         "prefill_512_ms_wall": round(prefill_warm_s * 1e3, 1),
         "prefill_512_ms_wall_first": round(prefill_s * 1e3, 1),
         "host_driven_matches_graph": bool(host_toks == toks.tolist()),

@@ -126,74 +126,76 @@ __device__ __forceinline__ void fold_step(float co, float cm, float cl, bool& li
 // operations of the tile-by-tile loop, in its order: the tile's top, then
 // old, top = max(old, tile top), a = 2^(old − top) (1 when equal), each live
 // key's 2^(s − top), the tile's sum from zero in key order, l = fma(l, a, sum).
+// The chunk's live keys are one run [lo, hi); every lane reads the scores and
+// then the weights of all tiles from shared memory (the same addresses on
+// every lane), so no shuffle stands between the phases.
+template <uint32_t B>
 __device__ __forceinline__ void softmax_chunk(float* ps, float* alpha, float* stat, uint32_t key0, uint32_t p,
-                                              uint32_t window, uint32_t B, uint32_t lane) {
+                                              uint32_t window, uint32_t lane) {
     const uint32_t early = earliest_of(p, window);
-    const uint32_t tiles = kChunk / B, half = 32u / B;   // tiles in a half of the chunk
-    const uint32_t j0 = key0 + lane, j1 = key0 + lane + 32u;
-    const bool live0 = j0 <= p && j0 >= early, live1 = j1 <= p && j1 >= early;
-    const float s0 = ps[lane], s1 = ps[lane + 32u];
-    float t0 = live0 ? s0 : -INFINITY, t1 = live1 ? s1 : -INFINITY;
-    for (uint32_t o = B / 2u; o > 0u; o >>= 1) {
-        t0 = fmaxf(t0, __shfl_xor_sync(0xFFFFFFFFu, t0, o));
-        t1 = fmaxf(t1, __shfl_xor_sync(0xFFFFFFFFu, t1, o));
+    constexpr uint32_t tiles = kChunk / B;
+    const uint32_t lo = early > key0 ? min(early - key0, kChunk) : 0u;
+    const uint32_t hi = p >= key0 ? min(p - key0 + 1u, kChunk) : 0u;
+    const float4* s4 = reinterpret_cast<const float4*>(ps);
+    // Each tile's top over its live scores (-inf when none is live).
+    float tt[tiles];
+#pragma unroll
+    for (uint32_t t = 0; t < tiles; ++t) {
+        tt[t] = -INFINITY;
+#pragma unroll
+        for (uint32_t q = t * B / 4u; q < (t + 1u) * B / 4u; ++q) {
+            const float4 v = s4[q];
+            const uint32_t b = 4u * q;
+            if (b >= lo && b < hi) tt[t] = fmaxf(tt[t], v.x);
+            if (b + 1u >= lo && b + 1u < hi) tt[t] = fmaxf(tt[t], v.y);
+            if (b + 2u >= lo && b + 2u < hi) tt[t] = fmaxf(tt[t], v.z);
+            if (b + 3u >= lo && b + 3u < hi) tt[t] = fmaxf(tt[t], v.w);
+        }
     }
-    const uint32_t seen0 = __ballot_sync(0xFFFFFFFFu, live0), seen1 = __ballot_sync(0xFFFFFFFFu, live1);
-    const uint32_t group = B == 32u ? 0xFFFFFFFFu : (1u << B) - 1u;
     // The running top and alpha, tile by tile (every lane alike); each lane
     // keeps the tops of its own two keys' tiles.
     bool chunk_live = false;
-    float chunk_m = 0.0f, top0 = 0.0f, top1 = 0.0f, al[8];
+    float chunk_m = 0.0f, top0 = 0.0f, top1 = 0.0f, al[tiles];
+    uint32_t seen_tiles = 0;
 #pragma unroll
-    for (uint32_t t = 0; t < 8u; ++t) {
+    for (uint32_t t = 0; t < tiles; ++t) {
         al[t] = 1.0f;
-        if (t >= tiles) continue;
-        const bool lower = t < half;
-        const uint32_t src = (lower ? t : t - half) * B;
-        const float tt = __shfl_sync(0xFFFFFFFFu, lower ? t0 : t1, src);
-        const bool seen = (((lower ? seen0 : seen1) >> src) & group) != 0u;
-        if (seen) {
-            const float old = chunk_live ? chunk_m : tt;
+        if (t * B < hi && (t + 1u) * B > lo && lo < hi) {
+            seen_tiles |= 1u << t;
+            const float old = chunk_live ? chunk_m : tt[t];
             chunk_live = true;
-            const float top = fmaxf(old, tt);
+            const float top = fmaxf(old, tt[t]);
             al[t] = old == top ? 1.0f : exp2_np(old - top);
             chunk_m = top;
         }
         if (lane / B == t) top0 = chunk_m;
-        if (lane / B + half == t) top1 = chunk_m;
+        if ((lane + 32u) / B == t) top1 = chunk_m;
     }
+    const float s0 = ps[lane], s1 = ps[lane + 32u];
+    const bool live0 = lane >= lo && lane < hi, live1 = lane + 32u >= lo && lane + 32u < hi;
+    __syncwarp();   // every lane has read the scores
     ps[lane] = live0 ? exp2_np(s0 - top0) : 0.0f;
     ps[lane + 32u] = live1 ? exp2_np(s1 - top1) : 0.0f;
     __syncwarp();
-    // Tile t's sum by lane t, in key order from zero.
-    float sum = 0.0f;
-    if (lane < tiles) {
-        const float4* e4 = reinterpret_cast<const float4*>(ps + lane * B);
-        for (uint32_t q = 0; q < B / 4u; ++q) {
-            const float4 v = e4[q];
+    // Each seen tile's sum in key order from zero, then l.
+    float chunk_l = 0.0f;
+#pragma unroll
+    for (uint32_t t = 0; t < tiles; ++t) {
+        float sum = 0.0f;
+#pragma unroll
+        for (uint32_t q = t * B / 4u; q < (t + 1u) * B / 4u; ++q) {
+            const float4 v = s4[q];
             sum = sum + v.x;
             sum = sum + v.y;
             sum = sum + v.z;
             sum = sum + v.w;
         }
-    }
-    float chunk_l = 0.0f;
-    bool any = false;
-#pragma unroll
-    for (uint32_t t = 0; t < 8u; ++t) {
-        if (t >= tiles) continue;
-        const float st = __shfl_sync(0xFFFFFFFFu, sum, t);
-        const bool lower = t < half;
-        const uint32_t src = (lower ? t : t - half) * B;
-        if ((((lower ? seen0 : seen1) >> src) & group) != 0u) {
-            chunk_l = fmaf(chunk_l, al[t], st);
-            any = true;
-        }
+        if ((seen_tiles >> t) & 1u) chunk_l = fmaf(chunk_l, al[t], sum);
         if (lane == 0) alpha[t] = al[t];
     }
     if (lane == 0) {
         stat[0] = chunk_m;
-        stat[1] = any ? chunk_l : 0.0f;
+        stat[1] = chunk_live ? chunk_l : 0.0f;
     }
 }
 
@@ -384,8 +386,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         // from shared memory by a lane of its own.
         if (B >= 8u && B <= 32u && (B & (B - 1u)) == 0u) {
             for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
-                softmax_chunk(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p_first + (seqs ? 0u : m / G),
-                              a.window, B, lane);
+                const uint32_t p = p_first + (seqs ? 0u : m / G);
+                if (B == 16u) softmax_chunk<16>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
+                else if (B == 32u) softmax_chunk<32>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
+                else softmax_chunk<8>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
             }
         } else
         for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
@@ -436,20 +440,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             const uint32_t valid = min(kChunk, p_last + 1u - key0);
             for (uint32_t t = 0; t < tiles; ++t) {
                 o = o * alpha[m * 8u + t];
-                const uint32_t b_end = min((t + 1u) * B, valid);
-                // Eight keys' weights and values into registers, then their
-                // fmas in key order (keys from b_end on are skipped).
-                for (uint32_t b0 = t * B; b0 < b_end; b0 += 8u) {
-                    float pw[8], vv[8];
+                // Eight keys at a time: their weights (two 16-byte reads) and
+                // values into registers, unconditionally (every row of the
+                // stage is in bounds), then their fmas in key order, keys from
+                // `valid` on (never staged) skipped.
+                for (uint32_t b0 = t * B; b0 < (t + 1u) * B; b0 += 8u) {
+                    const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
+                    const float4 pa = p4[0], pb = p4[1];
+                    const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                    float vv[8];
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const uint32_t b = b0 + k < b_end ? b0 + k : b0;
-                        pw[k] = ps[m * kChunk + b];
-                        vv[k] = fp16_bits_to_f32(vs[b * pitch + e]);
-                    }
+                    for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
-                        if (b0 + k < b_end) o = fmaf(pw[k], vv[k], o);
+                        if (b0 + k < valid) o = fmaf(pw[k], vv[k], o);
                 }
             }
             if (cluster_fold) {

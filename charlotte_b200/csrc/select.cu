@@ -45,23 +45,42 @@ __device__ __forceinline__ void entry_pair(uint64_t k, uint32_t* out) {
     out[1] = 0xFFFFFFFFu - static_cast<uint32_t>(k);
 }
 
-// Bitonic sort of 1,024 keys in shared memory, descending.
+// Bitonic sort of 1,024 keys, descending, thread t holding position t: the
+// stages whose partner (t ^ j, j < 32) is in the same warp run in registers
+// with shuffles; the wider stages compare and swap in shared memory, one
+// barrier a stage. The sorted keys are left in `keys`.
 __device__ void sort_tile(uint64_t* keys) {
     const uint32_t t = threadIdx.x;
+    uint64_t v = keys[t];
     for (uint32_t k = 2; k <= kTile; k <<= 1) {
-        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-            const uint32_t ixj = t ^ j;
-            if (ixj > t) {
-                const uint64_t a = keys[t], b = keys[ixj];
-                const bool descending = (t & k) == 0;
-                if (descending ? a < b : a > b) {
-                    keys[t] = b;
-                    keys[ixj] = a;
-                }
-            }
+        if (k > 32u) {
+            keys[t] = v;
             __syncthreads();
+            for (uint32_t j = k >> 1; j >= 32u; j >>= 1) {
+                const uint32_t ixj = t ^ j;
+                if (ixj > t) {
+                    const uint64_t a = keys[t], b = keys[ixj];
+                    const bool descending = (t & k) == 0;
+                    if (descending ? a < b : a > b) {
+                        keys[t] = b;
+                        keys[ixj] = a;
+                    }
+                }
+                __syncthreads();
+            }
+            v = keys[t];
+        }
+        for (uint32_t j = min(k >> 1, 16u); j > 0; j >>= 1) {
+            const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, j);
+            // The lower position of a pair keeps the larger key in a
+            // descending run, the smaller in an ascending one.
+            const bool keep_larger = ((t & k) == 0) == ((t & j) == 0);
+            v = keep_larger ? (v > w ? v : w) : (v < w ? v : w);
         }
     }
+    __syncthreads();   // every thread's reads of `keys` are done
+    keys[t] = v;
+    __syncthreads();
 }
 
 // How many of a descending 64-key list come before v (ties: list first
