@@ -564,9 +564,10 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     }
     const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
     if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
-    // Decode shapes (a row a tile) may fold over a cluster, with room in
-    // rank 0 for every chunk's partial.
-    const bool decode_shape = a.tokens == 1u || a.rows_are_sequences;
+    // A one-token decode step may fold over a cluster, with room in rank 0
+    // for every chunk's partial. Batched sequences keep the global fold: the
+    // fold room would halve the CTAs an SM holds across their many row tiles.
+    const bool decode_shape = a.tokens == 1u;
     const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
     static bool configured = false;
     if (!configured) {
