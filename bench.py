@@ -291,9 +291,9 @@ def run_ours(args):
     peak = peaks.get("hbm_gbs", 6650.0)
     # DRAM traffic per launch: the ncu capture's DRAM bytes over the same
     # product's algorithmic bytes (profiles/gemv_q4_0_qkv_4096x1024.md:
-    # 2,397,440 / 2,379,776; profiles/gemv_q6k_head_151936x1024.md:
-    # 132,133,120 / 128,238,080), scaled to this launch's algorithmic bytes.
-    traffic_ratio = 2397440 / 2379776 if share_q4 >= 0.5 else 132133120 / 128238080
+    # 2,420,992 / 2,379,776; profiles/gemv_q6k_head_151936x1024.md:
+    # 132,129,024 / 128,238,080), scaled to this launch's algorithmic bytes.
+    traffic_ratio = 2420992 / 2379776 if share_q4 >= 0.5 else 132129024 / 128238080
 
     # e2e: the same products through the C ABI with host buffers.
     e2e = None if args.no_e2e else run_e2e(gs, stream, max(args.steps // 20, 5), world)
