@@ -305,8 +305,9 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
         } else {
         // Pairs of slots: non-gated rows (2p, 2p+1) of the segment. Gated:
         // with R = 2 the pair is the output's gate row and up row; otherwise
-        // pairs p < R/4 are gate rows (2p, 2p+1), then the same up rows.
-#pragma unroll 1
+        // pairs p < R/4 are gate rows (2p, 2p+1), then the same up rows. The
+        // pairs unrolled, so a warp has R/2 independent chains in flight.
+#pragma unroll
         for (int p = 0; p < R / 2; ++p) {
             const bool upper = gated && R > 2 && p >= R / 4;
             const uint32_t ia = upper ? 2u * p - R / 2 : 2u * p;
