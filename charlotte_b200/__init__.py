@@ -16,7 +16,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libcharlotte_b200.so")
 
-F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
+F32, F16, Q4_0, Q4_1, Q8_0, Q6_K, BF16 = 0, 1, 2, 3, 8, 14, 30
 WRITE, QKV, GATED, GATED_BY_INPUT = 0, 1, 2, 3
 SILU, GELU_TANH, SIGMOID = 0, 1, 2
 MATMUL_PDL, MATMUL_TENSOR, MATMUL_STREAMED, MATMUL_TILED = 1, 2, 4, 8

@@ -108,7 +108,8 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
                   const uint32_t out_stride[3], uint32_t flags, void* stream) {
     using namespace cb;
     if (!m || !x || !out) return fail(CB_ERROR_INVALID, "cb_matmul_run: null argument");
-    if (m->format != CB_Q4_0 && m->format != CB_Q8_0 && m->format != CB_Q6_K)
+    if (m->format != CB_Q4_0 && m->format != CB_Q4_1 && m->format != CB_Q8_0 && m->format != CB_Q6_K &&
+        m->format != CB_BF16)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: format %u has no matmul kernel", m->format);
     if (m->columns == 0 || m->columns % 32 != 0)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: columns %u is not a whole number of 32-weight groups",
@@ -151,7 +152,8 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
             return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u's piece is null or not 16-byte aligned", i);
         if (s.rows == 0) return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u has no rows", i);
         const uint64_t groups = static_cast<uint64_t>(s.first_row + s.rows) * (m->columns / 32);
-        const uint64_t needed_blocks = m->format == CB_Q6_K ? groups / 8 : groups;
+        // stored blocks: a Q6_K super-block holds 8 groups, a BF16 block one value
+        const uint64_t needed_blocks = m->format == CB_Q6_K ? groups / 8 : (m->format == CB_BF16 ? groups * 32 : groups);
         if (needed_blocks > s.blocks)
             return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u reads rows past its piece (%llu of %u blocks)", i,
                         static_cast<unsigned long long>(needed_blocks), s.blocks);

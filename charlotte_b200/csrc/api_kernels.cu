@@ -101,7 +101,8 @@ int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
 int cb_gather_run(const cb_gather* g, uint32_t flags, void* stream) {
     if (!g || !g->piece || !g->hidden || (!g->fed && !g->ids) || (g->fed && !g->sampled))
         return fail(CB_ERROR_INVALID, "cb_gather_run: null argument");
-    if (g->format != CB_Q4_0 && g->format != CB_Q8_0 && g->format != CB_Q6_K)
+    if (g->format != CB_Q4_0 && g->format != CB_Q4_1 && g->format != CB_Q8_0 && g->format != CB_Q6_K &&
+        g->format != CB_BF16)
         return fail(CB_ERROR_INVALID, "cb_gather_run: format %u", g->format);
     if (g->width == 0 || g->width % (g->format == CB_Q6_K ? 256 : 32) != 0)
         return fail(CB_ERROR_INVALID, "cb_gather_run: width %u is not whole blocks", g->width);

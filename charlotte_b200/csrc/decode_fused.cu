@@ -585,7 +585,7 @@ __device__ void fold_one(const FusedArgs& a, const FusedLayer& L, uint32_t hq, u
 // gather_kernel's arithmetic (gather.cu) for group g of the token's row.
 template <typename F, int k>
 __device__ __forceinline__ void gather_put(const F& f, const typename F::Consts& c, float scale, float* out) {
-    out[k] = fmaf(__uint_as_float(f.template magic<k>()), F::template S<k>(c), F::template C<k>(c)) * scale;
+    out[k] = F::template weight<k>(f, c) * scale;
 }
 template <typename F, int... ks>
 __device__ __forceinline__ void gather_all(const F& f, float scale, float* out, std::integer_sequence<int, ks...>) {

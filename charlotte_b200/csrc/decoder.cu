@@ -153,11 +153,14 @@ int upload_f32(cb_decoder* d, float** dst, const float* host, size_t n) {
     return e == cudaSuccess ? CB_OK : fail_cuda(e, "cb_decoder_create: upload");
 }
 
-uint32_t weights_per_block(uint32_t f) { return f == CB_Q6_K ? 256u : (f == CB_Q4_0 || f == CB_Q8_0 ? 32u : 1u); }
+uint32_t weights_per_block(uint32_t f) {
+    return f == CB_Q6_K ? 256u : (f == CB_Q4_0 || f == CB_Q4_1 || f == CB_Q8_0 ? 32u : 1u);
+}
 
 int upload_weight(cb_decoder* d, DevWeight* w, const cb_weight& src, const char* name) {
     if (src.rows == 0) return CB_OK;
-    if (src.format != CB_Q4_0 && src.format != CB_Q8_0 && src.format != CB_Q6_K)
+    if (src.format != CB_Q4_0 && src.format != CB_Q4_1 && src.format != CB_Q8_0 && src.format != CB_Q6_K &&
+        src.format != CB_BF16)
         return fail(CB_ERROR_BUILD, "cb_decoder_create: %s's format %u has no matmul kernel", name, src.format);
     if (src.cols % weights_per_block(src.format) != 0)
         return fail(CB_ERROR_BUILD, "cb_decoder_create: %s's rows of %u are not whole blocks", name, src.cols);
@@ -488,6 +491,8 @@ uint32_t row_stage_of(uint32_t format, uint32_t columns) {
     switch (format) {
         case CB_Q4_0: return RowStreams<Q4_0>::row_stage(G);
         case CB_Q8_0: return RowStreams<Q8_0>::row_stage(G);
+        case CB_Q4_1: return RowStreams<Q4_1>::row_stage(G);
+        case CB_BF16: return RowStreams<BF16>::row_stage(G);
         default: return RowStreams<Q6_K>::row_stage(G);
     }
 }

@@ -29,7 +29,7 @@
 
 namespace cb {
 
-enum Format : uint32_t { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ8_0 = 8, kQ6_K = 14 };
+enum Format : uint32_t { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ4_1 = 3, kQ8_0 = 8, kQ6_K = 14, kBF16 = 30 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return __byte_perm(a, b, sel);
@@ -37,10 +37,46 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 
 __device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
 
+// Every format gives weight k of a group as weight<k>(f, consts) and the
+// same weight of two rows at once as weight2<k>(a, b, consts2) (a paired
+// fma rounds each half once: the bits of weight<k> on each row). The
+// magic-float formats decode with one fma: w = fma(m, S, C).
+template <typename F>
+struct MagicDecode {
+    template <int k, typename C>
+    __device__ __forceinline__ static float weight(const F& f, const C& c) {
+        return fmaf(__uint_as_float(f.template magic<k>()), F::template S<k>(c), F::template C<k>(c));
+    }
+    template <int k, typename C2>
+    __device__ __forceinline__ static float2 weight2(const F& a, const F& b, const C2& c) {
+        const float2 m = make_float2(__uint_as_float(a.template magic<k>()), __uint_as_float(b.template magic<k>()));
+        return __ffma2_rn(m, F::template S2<k>(c), F::template C2<k>(c));
+    }
+};
+
+// A 32-weight block of 4-bit codes (Q4_0, Q4_1): weight k is byte k % 16's
+// low nibble for k < 16, its high nibble after. nibble_magic<k> moves the
+// nibble into the mantissa of 1.0 at bit j = nibble_j<k>() (8, 12 or 16):
+// the float 1 + q·2^(j−23), exactly.
+template <int k>
+__device__ __forceinline__ uint32_t nibble_magic(const uint4& codes) {
+    constexpr int i = k % 4, w = (k % 16) / 4, h = k / 16;
+    constexpr int pos = 8 * i + 4 * h;
+    const uint32_t c = w == 0 ? codes.x : (w == 1 ? codes.y : (w == 2 ? codes.z : codes.w));
+    if constexpr (pos >= 8 && pos <= 16) return (c & (0xFu << pos)) | 0x3F800000u;
+    else if constexpr (pos >= 20) return ((c >> 12) & (0xFu << (pos - 12))) | 0x3F800000u;
+    else return ((c << 8) & (0xFu << (pos + 8))) | 0x3F800000u;
+}
+template <int k>
+__host__ __device__ static constexpr int nibble_j() {
+    constexpr int pos = 8 * (k % 4) + 4 * (k / 16);
+    return pos >= 8 && pos <= 16 ? pos : (pos >= 20 ? pos - 12 : pos + 8);
+}
+
 // ---- Q4_0 -------------------------------------------------------------------
 // Weight k of a block: byte k % 16 of its codes, low nibble for k < 16, high
 // nibble after (q4_0.wgsl:11-16); value (q − 8)·d.
-struct Q4_0 {
+struct Q4_0 : MagicDecode<Q4_0> {
     static constexpr uint32_t kGroupsPerBlock = 1;
     static constexpr int kStreams = 2;
     __host__ __device__ static constexpr uint32_t block_stream(int s) { return s == 0 ? 16u : 2u; }   // codes, d
@@ -73,19 +109,9 @@ struct Q4_0 {
     // The magic float of weight k (k a compile-time constant once unrolled),
     // and which constants (j) it takes.
     template <int k>
-    __device__ __forceinline__ uint32_t magic() const {
-        constexpr int i = k % 4, w = (k % 16) / 4, h = k / 16;
-        constexpr int pos = 8 * i + 4 * h;
-        const uint32_t c = word(w);
-        if constexpr (pos >= 8 && pos <= 16) return (c & (0xFu << pos)) | 0x3F800000u;
-        else if constexpr (pos >= 20) return ((c >> 12) & (0xFu << (pos - 12))) | 0x3F800000u;
-        else return ((c << 8) & (0xFu << (pos + 8))) | 0x3F800000u;
-    }
+    __device__ __forceinline__ uint32_t magic() const { return nibble_magic<k>(codes); }
     template <int k>
-    __host__ __device__ static constexpr int jpos() {
-        constexpr int pos = 8 * (k % 4) + 4 * (k / 16);
-        return pos >= 8 && pos <= 16 ? pos : (pos >= 20 ? pos - 12 : pos + 8);
-    }
+    __host__ __device__ static constexpr int jpos() { return nibble_j<k>(); }
     template <int k>
     __device__ __forceinline__ static float S(const Consts& c) {
         constexpr int j = jpos<k>();
@@ -126,7 +152,7 @@ struct Q4_0 {
 // ---- Q8_0 -------------------------------------------------------------------
 // Weight k: signed byte k of the codes; value q·d (q8_0.wgsl:11-15). The
 // byte, offset by 128, lies at mantissa bits 8..15 (j = 8).
-struct Q8_0 {
+struct Q8_0 : MagicDecode<Q8_0> {
     static constexpr uint32_t kGroupsPerBlock = 1;
     static constexpr int kStreams = 2;
     __host__ __device__ static constexpr uint32_t block_stream(int s) { return s == 0 ? 32u : 2u; }   // codes, d
@@ -188,7 +214,7 @@ struct Q8_0 {
 // from bit 0 up), scales 2k and 2k+1 for weights 0..15 and 16..31, and the
 // block's d; value (d·sc)·(q − 32) (q6_k.wgsl:13-42). q's six bits sit at
 // mantissa bits 16..21 (j = 16).
-struct Q6_K {
+struct Q6_K : MagicDecode<Q6_K> {
     static constexpr uint32_t kGroupsPerBlock = 8;
     static constexpr int kStreams = 4;
     __host__ __device__ static constexpr uint32_t block_stream(int s) {   // lo, hi, scales, d
@@ -254,6 +280,92 @@ struct Q6_K {
     __device__ __forceinline__ static float2 C2(const Consts2& c) { return k < 16 ? c.C1 : c.C2; }
 };
 
+// ---- Q4_1 -------------------------------------------------------------------
+// Weight k: the nibble of Q4_0's place, value q·d + m (q4_1.wgsl:6-20), the
+// multiply and add fused, rounded once — one of the two evaluations the
+// reference accepts (tests/support/q4_1_reference.h:13-21). The device
+// layout holds every block's 16 code bytes, then every block's (d, m) word,
+// d in its low half. q comes out of the magic float exactly (one fma by
+// ±2^(23−j)), then w = fma(q, d, m).
+struct Q4_1 {
+    static constexpr uint32_t kGroupsPerBlock = 1;
+    static constexpr int kStreams = 2;
+    __host__ __device__ static constexpr uint32_t block_stream(int s) { return s == 0 ? 16u : 4u; }   // codes, (d, m)
+    uint4 codes;
+    float d, m;
+
+    __device__ __forceinline__ void load(const uint8_t* const* s, uint32_t g) {
+        codes = *reinterpret_cast<const uint4*>(s[0] + 16u * g);
+        const uint32_t dm = *reinterpret_cast<const uint32_t*>(s[1] + 4u * g);
+        d = fp16_bits_to_f32(static_cast<uint16_t>(dm & 0xFFFFu));
+        m = fp16_bits_to_f32(static_cast<uint16_t>(dm >> 16));
+    }
+    __device__ __forceinline__ void zero() { codes = make_uint4(0, 0, 0, 0); d = 0.0f; m = 0.0f; }
+    struct Consts { float d, m; };
+    __device__ __forceinline__ Consts consts() const { return Consts{d, m}; }
+    struct Consts2 { float2 d, m; };
+    __device__ __forceinline__ static Consts2 consts2(const Q4_1& A, const Q4_1& B) {
+        return Consts2{make_float2(A.d, B.d), make_float2(A.m, B.m)};
+    }
+    // 2^(23−j) for weight k (k < 32; larger k, instantiated but never run
+    // by kernels that decode half a group at a time, take 1).
+    template <int k>
+    __host__ __device__ static constexpr float unit() {
+        return nibble_j<k>() <= 23 ? static_cast<float>(1u << (nibble_j<k>() <= 23 ? 23 - nibble_j<k>() : 0)) : 1.0f;
+    }
+    template <int k>
+    __device__ __forceinline__ static float code(const Q4_1& f) {
+        constexpr float P = unit<k>();
+        return fmaf(__uint_as_float(nibble_magic<k>(f.codes)), P, -P);
+    }
+    template <int k>
+    __device__ __forceinline__ static float weight(const Q4_1& f, const Consts& c) {
+        return fmaf(code<k>(f), c.d, c.m);
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 weight2(const Q4_1& a, const Q4_1& b, const Consts2& c) {
+        constexpr float P = unit<k>();
+        const float2 mg = make_float2(__uint_as_float(nibble_magic<k>(a.codes)), __uint_as_float(nibble_magic<k>(b.codes)));
+        const float2 q = __ffma2_rn(mg, make_float2(P, P), make_float2(-P, -P));
+        return __ffma2_rn(q, c.d, c.m);
+    }
+};
+
+// ---- BF16 -------------------------------------------------------------------
+// Each value is the top half of an f32 (bf16.wgsl:1-20): nothing computed.
+// Groups of 32 values, 64 bytes (the bandwidth and stream accounting counts
+// such a group as a block); value k is half k % 2 of word k / 2, the lower
+// half first.
+struct BF16 {
+    static constexpr uint32_t kGroupsPerBlock = 1;
+    static constexpr int kStreams = 1;
+    __host__ __device__ static constexpr uint32_t block_stream(int) { return 64u; }
+    uint4 v[4];
+
+    __device__ __forceinline__ void load(const uint8_t* const* s, uint32_t g) {
+        const uint4* p = reinterpret_cast<const uint4*>(s[0] + 64u * g);
+        v[0] = p[0]; v[1] = p[1]; v[2] = p[2]; v[3] = p[3];
+    }
+    __device__ __forceinline__ void zero() {
+        v[0] = v[1] = v[2] = v[3] = make_uint4(0, 0, 0, 0);
+    }
+    struct Consts {};
+    __device__ __forceinline__ Consts consts() const { return Consts{}; }
+    struct Consts2 {};
+    __device__ __forceinline__ static Consts2 consts2(const BF16&, const BF16&) { return Consts2{}; }
+    template <int k>
+    __device__ __forceinline__ static float weight(const BF16& f, const Consts&) {
+        const uint4& q = f.v[k / 8];
+        constexpr int w = (k % 8) / 2;
+        const uint32_t word = w == 0 ? q.x : (w == 1 ? q.y : (w == 2 ? q.z : q.w));
+        return __uint_as_float(k % 2 == 0 ? word << 16 : word & 0xFFFF0000u);
+    }
+    template <int k>
+    __device__ __forceinline__ static float2 weight2(const BF16& a, const BF16& b, const Consts2&) {
+        return make_float2(weight<k>(a, Consts{}), weight<k>(b, Consts{}));
+    }
+};
+
 // A row's streams: stream s of row r of a piece of `nb` blocks starts at
 // base(s) + r·row_bytes(s) and is row_bytes(s) long (device_layout.h's
 // streams, each over every block in order).
@@ -282,7 +394,11 @@ struct RowStreams {
 
 // Bytes of weight data a 32-weight group occupies, for bandwidth accounting.
 __host__ __device__ constexpr double group_bytes(uint32_t format) {
-    return format == kQ4_0 ? 18.0 : (format == kQ8_0 ? 34.0 : (format == kQ6_K ? 210.0 / 8.0 : 0.0));
+    return format == kQ4_0 ? 18.0
+         : format == kQ4_1 ? 20.0
+         : format == kQ8_0 ? 34.0
+         : format == kQ6_K ? 210.0 / 8.0
+         : format == kBF16 ? 64.0 : 0.0;
 }
 
 }  // namespace cb

@@ -19,7 +19,7 @@ namespace {
 
 template <typename F, int k>
 __device__ __forceinline__ void put(const F& f, const typename F::Consts& c, float scale, float* out) {
-    out[k] = fmaf(__uint_as_float(f.template magic<k>()), F::template S<k>(c), F::template C<k>(c)) * scale;
+    out[k] = F::template weight<k>(f, c) * scale;
 }
 
 template <typename F, int... ks>
@@ -73,6 +73,8 @@ cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl) {
         case kQ4_0: return launch<Q4_0>(a, stream, pdl);
         case kQ8_0: return launch<Q8_0>(a, stream, pdl);
         case kQ6_K: return launch<Q6_K>(a, stream, pdl);
+        case kQ4_1: return launch<Q4_1>(a, stream, pdl);
+        case kBF16: return launch<BF16>(a, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

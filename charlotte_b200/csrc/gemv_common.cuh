@@ -140,8 +140,8 @@ __device__ __forceinline__ void chain_step(const F& A, const F& B, const typenam
                                            float& acc_b) {
     const float4 xq = x4[k / 4];
     const float xk = (k % 4 == 0) ? xq.x : ((k % 4 == 1) ? xq.y : ((k % 4 == 2) ? xq.z : xq.w));
-    const float wa = fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca));
-    const float wb = fmaf(__uint_as_float(B.template magic<k>()), F::template S<k>(cbb), F::template C<k>(cbb));
+    const float wa = F::template weight<k>(A, ca);
+    const float wb = F::template weight<k>(B, cbb);
     acc_a = fmaf(wa, xk, acc_a);
     acc_b = fmaf(wb, xk, acc_b);
 }
@@ -161,8 +161,7 @@ __device__ __forceinline__ void chain_step2(const F& A, const F& B, const typena
                                             float2& acc) {
     const float4 xq = x2[k / 2];
     const float2 xk = (k % 2 == 0) ? make_float2(xq.x, xq.y) : make_float2(xq.z, xq.w);
-    const float2 m = make_float2(__uint_as_float(A.template magic<k>()), __uint_as_float(B.template magic<k>()));
-    acc = __ffma2_rn(__ffma2_rn(m, F::template S2<k>(c), F::template C2<k>(c)), xk, acc);
+    acc = __ffma2_rn(F::template weight2<k>(A, B, c), xk, acc);
 }
 
 template <typename F, int... ks>
@@ -177,7 +176,7 @@ template <typename F, int k>
 __device__ __forceinline__ void chain_step1d(const F& A, const typename F::Consts& ca, const float4* x2, float& acc) {
     const float4 xq = x2[k / 2];
     const float xk = (k % 2 == 0) ? xq.x : xq.z;
-    acc = fmaf(fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca)), xk, acc);
+    acc = fmaf(F::template weight<k>(A, ca), xk, acc);
 }
 
 template <typename F, int... ks>
@@ -191,7 +190,7 @@ template <typename F, int k>
 __device__ __forceinline__ void chain_step1(const F& A, const typename F::Consts& ca, const float4* x4, float& acc) {
     const float4 xq = x4[k / 4];
     const float xk = (k % 4 == 0) ? xq.x : ((k % 4 == 1) ? xq.y : ((k % 4 == 2) ? xq.z : xq.w));
-    acc = fmaf(fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca)), xk, acc);
+    acc = fmaf(F::template weight<k>(A, ca), xk, acc);
 }
 
 template <typename F, int... ks>

@@ -23,6 +23,8 @@ uint32_t block_bytes(uint32_t format) {
         case CB_F32: return 4;
         case CB_F16: return 2;
         case CB_Q4_0: return 18;
+        case CB_Q4_1: return 20;
+        case CB_BF16: return 2;
         case CB_Q8_0: return 34;
         case CB_Q6_K: return 210;
         default: return 0;
@@ -73,6 +75,12 @@ int cb_piece_from_stored(uint32_t format, const void* stored_host, uint64_t bloc
             }
             return CB_OK;
         }
+        case CB_Q4_1:   // codes, then each block's (d, m) word (device_layout.h:122)
+            for (uint64_t b = 0; b < blocks; ++b) {
+                std::memcpy(out + 16 * b, st + 20 * b + 4, 16);
+                std::memcpy(out + 16 * blocks + 4 * b, st + 20 * b, 4);
+            }
+            return CB_OK;
         case CB_Q6_K:
             for (uint64_t b = 0; b < blocks; ++b) {
                 const uint8_t* blk = st + 210 * b;

@@ -389,8 +389,8 @@ __device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const flo
         float wa[4], wb[4];
         auto dec = [&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            wa[k % 4] = fmaf(__uint_as_float(A.template magic<k>()), F::template S<k>(ca), F::template C<k>(ca));
-            wb[k % 4] = fmaf(__uint_as_float(B.template magic<k>()), F::template S<k>(cbb), F::template C<k>(cbb));
+            wa[k % 4] = F::template weight<k>(A, ca);
+            wb[k % 4] = F::template weight<k>(B, cbb);
         };
         // k = 4q .. 4q+3 as compile-time constants
         if (q == 0) { dec(std::integral_constant<int, 0>{}); dec(std::integral_constant<int, 1>{}); dec(std::integral_constant<int, 2>{}); dec(std::integral_constant<int, 3>{}); }
@@ -743,6 +743,8 @@ size_t matmul_decode_smem_bytes(uint32_t format, uint32_t columns) {
         case kQ4_0: return decode_smem<Q4_0, 1>(G);
         case kQ8_0: return decode_smem<Q8_0, 1>(G);
         case kQ6_K: return decode_smem<Q6_K, 1>(G);
+        case kQ4_1: return decode_smem<Q4_1, 1>(G);
+        case kBF16: return decode_smem<BF16, 1>(G);
         default: return 0;
     }
 }
@@ -753,6 +755,8 @@ cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
             case kQ4_0: return dispatch_mt<Q4_0>(a, sm_count, stream, pdl);
             case kQ8_0: return dispatch_mt<Q8_0>(a, sm_count, stream, pdl);
             case kQ6_K: return dispatch_mt<Q6_K>(a, sm_count, stream, pdl);
+            case kQ4_1: return dispatch_mt<Q4_1>(a, sm_count, stream, pdl);
+            case kBF16: return dispatch_mt<BF16>(a, sm_count, stream, pdl);
             default: return cudaErrorInvalidValue;
         }
     }
@@ -760,6 +764,8 @@ cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
         case kQ4_0: return dispatch<Q4_0>(a, sm_count, stream, pdl);
         case kQ8_0: return dispatch<Q8_0>(a, sm_count, stream, pdl);
         case kQ6_K: return dispatch<Q6_K>(a, sm_count, stream, pdl);
+        case kQ4_1: return dispatch<Q4_1>(a, sm_count, stream, pdl);
+        case kBF16: return dispatch<BF16>(a, sm_count, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -64,9 +64,7 @@ template <typename F, int K0, int... ks>
 __device__ __forceinline__ void decode16(const F& f, const typename F::Consts& c, uint32_t (&h)[8],
                                          std::integer_sequence<int, ks...>) {
     float w[16];
-    ((w[ks] = fmaf(__uint_as_float(f.template magic<K0 + ks>()), F::template S<K0 + ks>(c),
-                   F::template C<K0 + ks>(c))),
-     ...);
+    ((w[ks] = F::template weight<K0 + ks>(f, c)), ...);
 #pragma unroll
     for (int i = 0; i < 8; ++i) h[i] = pack_half2(w[2 * i], w[2 * i + 1]);
 }
@@ -401,6 +399,8 @@ cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
         case kQ4_0: return launch_tensor<Q4_0>(a, map, stream, pdl);
         case kQ8_0: return launch_tensor<Q8_0>(a, map, stream, pdl);
         case kQ6_K: return launch_tensor<Q6_K>(a, map, stream, pdl);
+        case kQ4_1: return launch_tensor<Q4_1>(a, map, stream, pdl);
+        case kBF16: return launch_tensor<BF16>(a, map, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

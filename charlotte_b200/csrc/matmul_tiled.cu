@@ -74,9 +74,7 @@ __device__ __forceinline__ uint32_t xs_index(uint32_t k, uint32_t t) {
 template <typename F, int BN, int K0, int... ks>
 __device__ __forceinline__ void decode_part(const F& f, float* ws_col, std::integer_sequence<int, ks...>) {
     const typename F::Consts c = f.consts();
-    ((ws_col[(K0 + ks) * BN] =
-          fmaf(__uint_as_float(f.template magic<K0 + ks>()), F::template S<K0 + ks>(c), F::template C<K0 + ks>(c))),
-     ...);
+    ((ws_col[(K0 + ks) * BN] = F::template weight<K0 + ks>(f, c)), ...);
 }
 
 template <typename F, typename T>
@@ -348,6 +346,8 @@ cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream,
         case kQ4_0: return dispatch_tiled<Q4_0>(a, sm_count, stream, pdl);
         case kQ8_0: return dispatch_tiled<Q8_0>(a, sm_count, stream, pdl);
         case kQ6_K: return dispatch_tiled<Q6_K>(a, sm_count, stream, pdl);
+        case kQ4_1: return dispatch_tiled<Q4_1>(a, sm_count, stream, pdl);
+        case kBF16: return dispatch_tiled<BF16>(a, sm_count, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

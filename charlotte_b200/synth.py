@@ -3,16 +3,17 @@ benchmark configurations name (random-init weights; there are no real model
 files on these machines).
 
 Blocks are generated in the stored (file) order of ggml's block structs —
-Q4_0 {d: f16, qs[16]}, Q8_0 {d: f16, qs[32]}, Q6_K {ql[128], qh[64],
-scales[16]: i8, d: f16} — and turned into the device layout by `to_piece`.
+Q4_0 {d: f16, qs[16]}, Q4_1 {d: f16, m: f16, qs[16]}, Q8_0 {d: f16,
+qs[32]}, Q6_K {ql[128], qh[64], scales[16]: i8, d: f16}, BF16 values — and
+turned into the device layout by `to_piece`.
 """
 from __future__ import annotations
 
 import numpy as np
 
-F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
-BLOCK_BYTES = {F32: 4, F16: 2, Q4_0: 18, Q8_0: 34, Q6_K: 210}
-BLOCK_WEIGHTS = {F32: 1, F16: 1, Q4_0: 32, Q8_0: 32, Q6_K: 256}
+F32, F16, Q4_0, Q4_1, Q8_0, Q6_K, BF16 = 0, 1, 2, 3, 8, 14, 30
+BLOCK_BYTES = {F32: 4, F16: 2, Q4_0: 18, Q4_1: 20, Q8_0: 34, Q6_K: 210, BF16: 2}
+BLOCK_WEIGHTS = {F32: 1, F16: 1, Q4_0: 32, Q4_1: 32, Q8_0: 32, Q6_K: 256, BF16: 1}
 
 
 def _fp16_bits(values: np.ndarray) -> np.ndarray:
@@ -26,6 +27,25 @@ def q4_0_blocks(rng: np.random.Generator, n_blocks: int, sigma: float = 0.02) ->
     out[:, 0:2] = d.view(np.uint8).reshape(n_blocks, 2)
     out[:, 2:] = rng.integers(0, 256, (n_blocks, 16), dtype=np.uint8)
     return out.reshape(-1)
+
+
+def q4_1_blocks(rng: np.random.Generator, n_blocks: int, sigma: float = 0.02) -> np.ndarray:
+    """d = |N(0, sigma)|/8 and m = -7.5*d*(1 + N(0, 0.05)) as f16, 16 bytes of
+    uniform codes (value q*d + m)."""
+    out = np.empty((n_blocks, 20), np.uint8)
+    d = np.abs(rng.normal(0.0, sigma, n_blocks)) / 8.0
+    m = -7.5 * d * (1.0 + rng.normal(0.0, 0.05, n_blocks))
+    out[:, 0:2] = _fp16_bits(d).view(np.uint8).reshape(n_blocks, 2)
+    out[:, 2:4] = _fp16_bits(m).view(np.uint8).reshape(n_blocks, 2)
+    out[:, 4:] = rng.integers(0, 256, (n_blocks, 16), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+def bf16_values(rng: np.random.Generator, n: int, sigma: float = 0.02) -> np.ndarray:
+    """N(0, sigma) rounded to bfloat16 (nearest, ties to even), 2 bytes each."""
+    bits = rng.normal(0.0, sigma, n).astype(np.float32).view(np.uint32)
+    rounded = (bits + 0x7FFF + ((bits >> 16) & 1)) >> 16
+    return rounded.astype(np.uint16).view(np.uint8)
 
 
 def q8_0_blocks(rng: np.random.Generator, n_blocks: int, sigma: float = 0.02) -> np.ndarray:
@@ -52,11 +72,16 @@ def random_bytes_blocks(rng: np.random.Generator, fmt: int, n_blocks: int) -> np
     every scale class (subnormal, zero, negative) — the unpack edge cases."""
     bb = BLOCK_BYTES[fmt]
     out = rng.integers(0, 256, (n_blocks, bb), dtype=np.uint8)
-    at = 208 if fmt == Q6_K else 0
-    # clear exponent bit 14 of the f16 scale when the exponent would be 31
-    hi = out[:, at + 1]
-    exp_all_ones = (hi & 0x7C) == 0x7C
-    out[exp_all_ones, at + 1] = hi[exp_all_ones] & 0xFB
+    if fmt == BF16:
+        # clear the exponent's lowest bit where all eight are ones
+        exp_all_ones = ((out[:, 1] & 0x7F) == 0x7F) & ((out[:, 0] & 0x80) != 0)
+        out[exp_all_ones, 0] &= 0x7F
+        return out.reshape(-1)
+    for at in ((208,) if fmt == Q6_K else ((0, 2) if fmt == Q4_1 else (0,))):
+        # clear exponent bit 14 of an f16 field when the exponent would be 31
+        hi = out[:, at + 1]
+        exp_all_ones = (hi & 0x7C) == 0x7C
+        out[exp_all_ones, at + 1] = hi[exp_all_ones] & 0xFB
     return out.reshape(-1)
 
 
@@ -64,6 +89,10 @@ def blocks(rng: np.random.Generator, fmt: int, rows: int, cols: int) -> np.ndarr
     n = rows * cols // BLOCK_WEIGHTS[fmt]
     if fmt == Q4_0:
         return q4_0_blocks(rng, n)
+    if fmt == Q4_1:
+        return q4_1_blocks(rng, n)
+    if fmt == BF16:
+        return bf16_values(rng, n)
     if fmt == Q8_0:
         return q8_0_blocks(rng, n)
     if fmt == Q6_K:
@@ -106,7 +135,11 @@ def to_piece(fmt: int, stored: np.ndarray) -> np.ndarray:
         out[192 * n: 208 * n] = st[:, 192:208].reshape(-1)
         out[208 * n: 210 * n] = st[:, 208:210].reshape(-1)
         return out
-    if fmt in (F32, F16):
+    if fmt == Q4_1:   # codes, then each block's (d, m) word
+        out[: 16 * n] = st[:, 4:].reshape(-1)
+        out[16 * n: 20 * n] = st[:, :4].reshape(-1)
+        return out
+    if fmt in (F32, F16, BF16):
         out[: bb * n] = st.reshape(-1)
         return out
     raise ValueError(f"format {fmt}")

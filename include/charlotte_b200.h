@@ -45,7 +45,7 @@ typedef enum cb_status {
 } cb_status;
 
 /* GGUF tensor types a weight may take (src/core/gguf/types.h:41-43). */
-enum { CB_F32 = 0, CB_F16 = 1, CB_Q4_0 = 2, CB_Q8_0 = 8, CB_Q6_K = 14 };
+enum { CB_F32 = 0, CB_F16 = 1, CB_Q4_0 = 2, CB_Q4_1 = 3, CB_Q8_0 = 8, CB_Q6_K = 14, CB_BF16 = 30 };
 
 /* Copies the calling thread's last error message (NUL-terminated, truncated
  * to `capacity`); returns its full length. Replaces the message the
@@ -100,7 +100,7 @@ typedef struct cb_member {
 } cb_member;
 
 typedef struct cb_matmul {
-    uint32_t format;               /* CB_Q4_0, CB_Q8_0 or CB_Q6_K                        */
+    uint32_t format;               /* CB_Q4_0, CB_Q4_1, CB_Q8_0, CB_Q6_K or CB_BF16      */
     uint32_t columns;              /* K, a multiple of 32                                */
     uint32_t members;              /* 1 to 3                                             */
     uint32_t epilogue;             /* CB_EPILOGUE_*                                      */
@@ -356,7 +356,7 @@ CB_API int cb_piece_from_stored(uint32_t format, const void* stored_host, uint64
  * (src/core/kernels/program.h:262-331, residency/upload.h) for a caller that
  * brings its weights as host memory. */
 typedef struct cb_weight {
-    uint32_t format;             /* CB_Q4_0, CB_Q8_0, CB_Q6_K (matmuls); rows=0: absent */
+    uint32_t format;             /* CB_Q4_0, Q4_1, Q8_0, Q6_K, BF16 (matmuls); rows=0: absent */
     uint32_t rows, cols;         /* rows of cols weights (cols a multiple of the block) */
     const void* stored_host;     /* the file's stored blocks                        */
 } cb_weight;

@@ -16,10 +16,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libcharlotte_ref.so")
 
-F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
+F32, F16, Q4_0, Q4_1, Q8_0, Q6_K, BF16 = 0, 1, 2, 3, 8, 14, 30
 SILU, GELU_TANH, SIGMOID = 0, 1, 2
-BLOCK_BYTES = {F32: 4, F16: 2, Q4_0: 18, Q8_0: 34, Q6_K: 210}
-BLOCK_WEIGHTS = {F32: 1, F16: 1, Q4_0: 32, Q8_0: 32, Q6_K: 256}
+BLOCK_BYTES = {F32: 4, F16: 2, Q4_0: 18, Q4_1: 20, Q8_0: 34, Q6_K: 210, BF16: 2}
+BLOCK_WEIGHTS = {F32: 1, F16: 1, Q4_0: 32, Q4_1: 32, Q8_0: 32, Q6_K: 256, BF16: 1}
 
 _lib = None
 _ref = None
@@ -82,7 +82,8 @@ def ref():
     global _ref
     if _ref is None and os.path.exists(REF_PATH):
         R = ctypes.CDLL(REF_PATH)
-        for name in ("ref_dequant_q4_0", "ref_dequant_q8_0", "ref_dequant_q6_k"):
+        for name in ("ref_dequant_q4_0", "ref_dequant_q8_0", "ref_dequant_q6_k", "ref_dequant_q4_1_fused",
+                     "ref_dequant_q4_1_rounded"):
             getattr(R, name).restype = ctypes.c_int
             getattr(R, name).argtypes = [c_u8p, ctypes.c_size_t, c_f32p]
         R.ref_fp16_to_fp32.restype = ctypes.c_float

@@ -160,6 +160,8 @@ uint32_t or_block_bytes(int type) {
         case OR_F32: return 4;
         case OR_F16: return 2;
         case OR_Q4_0: return 18;
+        case OR_Q4_1: return 20;
+        case OR_BF16: return 2;
         case OR_Q8_0: return 34;
         case OR_Q6_K: return 210;
         default: return 0;
@@ -168,8 +170,8 @@ uint32_t or_block_bytes(int type) {
 
 uint32_t or_block_weights(int type) {
     switch (type) {
-        case OR_F32: case OR_F16: return 1;
-        case OR_Q4_0: case OR_Q8_0: return 32;
+        case OR_F32: case OR_F16: case OR_BF16: return 1;
+        case OR_Q4_0: case OR_Q4_1: case OR_Q8_0: return 32;
         case OR_Q6_K: return 256;
         default: return 0;
     }
@@ -197,6 +199,22 @@ int or_dequant_stored(int type, const uint8_t* data, size_t blocks, float* out) 
                 const uint8_t* blk = data + b * 34;
                 float d = or_fp16_to_fp32(rd16(blk));
                 for (int j = 0; j < 32; ++j) out[b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+            }
+            return 0;
+        case OR_Q4_1:   /* q4_1_reference.h:44-50, the fused evaluation: fma(q, d, m) */
+            for (b = 0; b < blocks; ++b) {
+                const uint8_t* blk = data + b * 20;
+                float d = or_fp16_to_fp32(rd16(blk)), m = or_fp16_to_fp32(rd16(blk + 2));
+                for (int j = 0; j < 16; ++j) {
+                    out[b * 32 + j] = fmaf((float)(blk[4 + j] & 0x0F), d, m);
+                    out[b * 32 + j + 16] = fmaf((float)(blk[4 + j] >> 4), d, m);
+                }
+            }
+            return 0;
+        case OR_BF16:   /* the top half of an f32 (bf16.wgsl) */
+            for (b = 0; b < blocks; ++b) {
+                uint32_t bits = (uint32_t)rd16(data + 2 * b) << 16;
+                memcpy(out + b, &bits, 4);
             }
             return 0;
         case OR_Q6_K:
@@ -270,7 +288,13 @@ int or_to_piece(int type, const uint8_t* stored, size_t blocks, uint8_t* piece) 
                 memcpy(piece + 208 * blocks + 2 * b, blk + 208, 2);
             }
             return 0;
-        case OR_F32: case OR_F16:
+        case OR_Q4_1:   /* codes, then each block's (d, m) word (device_layout.h:122) */
+            for (b = 0; b < blocks; ++b) {
+                memcpy(piece + 16 * b, stored + 20 * b + 4, 16);
+                memcpy(piece + 16 * blocks + 4 * b, stored + 20 * b, 4);
+            }
+            return 0;
+        case OR_F32: case OR_F16: case OR_BF16:
             memcpy(piece, stored, blocks * or_block_bytes(type));
             return 0;
         default:
@@ -316,6 +340,22 @@ int or_unpack(int type, const uint8_t* piece, uint32_t n, uint32_t group, float*
             return 0;
         case OR_F16:
             for (int j = 0; j < 32; ++j) out[j] = or_fp16_to_fp32(rd16(piece + (size_t)64 * group + 2 * j));
+            return 0;
+        case OR_Q4_1: {   /* q4_1.wgsl:6-20, fused: fma(q, d, m) */
+            const uint8_t* dm = piece + (size_t)16 * n + 4 * (size_t)group;
+            float d = or_fp16_to_fp32(rd16(dm)), m = or_fp16_to_fp32(rd16(dm + 2));
+            const uint8_t* qs = piece + (size_t)16 * group;
+            for (int j = 0; j < 16; ++j) {
+                out[j] = fmaf((float)(qs[j] & 0xF), d, m);
+                out[j + 16] = fmaf((float)(qs[j] >> 4), d, m);
+            }
+            return 0;
+        }
+        case OR_BF16:   /* bf16.wgsl:9-20 */
+            for (int j = 0; j < 32; ++j) {
+                uint32_t bits = (uint32_t)rd16(piece + (size_t)64 * group + 2 * j) << 16;
+                memcpy(out + j, &bits, 4);
+            }
             return 0;
         default:
             return -1;

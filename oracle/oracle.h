@@ -39,7 +39,7 @@ extern "C" {
 #endif
 
 /* GGUF tensor types (src/core/gguf/types.h:41-43). */
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q6_K = 14 };
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q8_0 = 8, OR_Q6_K = 14, OR_BF16 = 30 };
 
 /* Activations (matmul.wgsl:189-205 `activation` override). */
 enum { OR_SILU = 0, OR_GELU_TANH = 1, OR_SIGMOID = 2 };

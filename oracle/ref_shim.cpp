@@ -15,6 +15,7 @@
 #include "core/quant/q4_0.h"
 #include "support/f16_reference.h"
 #include "support/q4_0_reference.h"
+#include "support/q4_1_reference.h"
 #include "support/q6_k_reference.h"
 #include "support/q8_0_reference.h"
 #include "support/sampler_reference.h"
@@ -41,6 +42,16 @@ int ref_dequant_q8_0(const std::uint8_t* data, std::size_t bytes, float* out) {
 // tests/support/q6_k_reference.h:17
 int ref_dequant_q6_k(const std::uint8_t* data, std::size_t bytes, float* out) {
     return copy_out(bllm::test::dequantize_q6_k, data, bytes, out);
+}
+// tests/support/q4_1_reference.h:25: both evaluations it accepts, the
+// multiply-add fused (one rounding) and rounded twice.
+int ref_dequant_q4_1_fused(const std::uint8_t* data, std::size_t bytes, float* out) {
+    return copy_out([](std::span<const std::uint8_t> s) { return bllm::test::dequantize_q4_1(s).fused; }, data,
+                    bytes, out);
+}
+int ref_dequant_q4_1_rounded(const std::uint8_t* data, std::size_t bytes, float* out) {
+    return copy_out([](std::span<const std::uint8_t> s) { return bllm::test::dequantize_q4_1(s).rounded; }, data,
+                    bytes, out);
 }
 // src/core/quant/q4_0.h:66
 float ref_fp16_to_fp32(std::uint16_t h) { return bllm::quant::fp16_to_fp32(h); }

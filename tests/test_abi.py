@@ -43,14 +43,34 @@ def test_invalid_arguments_are_a_status_not_a_fault():
     """Argument checks run before any device work: no GPU needed."""
     import ctypes
     m = cb.Matmul()
-    m.format = 3            # Q4_1: no kernel here
+    m.format = 6            # Q5_0: no kernel here
     m.columns = 64
     m.members = 1
     outs = (ctypes.c_void_p * 3)(1, 0, 0)
     st = (ctypes.c_uint32 * 3)(0, 0, 0)
     rc = cb.lib().cb_matmul_run(ctypes.byref(m), 16, 64, 1, ctypes.byref(outs), ctypes.byref(st), 0, None)
-    assert rc == cb.ERROR_INVALID and "format 3" in cb.last_error()
+    assert rc == cb.ERROR_INVALID and "format 6" in cb.last_error()
     m.format = cb.Q4_0
     m.columns = 33
     rc = cb.lib().cb_matmul_run(ctypes.byref(m), 16, 64, 1, ctypes.byref(outs), ctypes.byref(st), 0, None)
     assert rc == cb.ERROR_INVALID and "32-weight" in cb.last_error()
+
+
+@pytest.mark.parametrize("fmt", [2, 3, 8, 14, 30])   # Q4_0, Q4_1, Q8_0, Q6_K, BF16
+def test_piece_from_stored_is_the_device_layout(fmt):
+    """cb_piece_from_stored (host code, no GPU) writes the device layout the
+    kernels read: the same bytes as the oracle's layout of the same blocks."""
+    import ctypes
+    import numpy as np
+    import oracle as O
+    from charlotte_b200 import synth
+    rng = np.random.default_rng(fmt)
+    stored = synth.random_bytes_blocks(rng, fmt, 64 if fmt != 30 else 640)
+    blocks = stored.size // O.BLOCK_BYTES[fmt]
+    L = cb.lib()
+    L.cb_piece_bytes.restype = ctypes.c_size_t
+    L.cb_piece_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint64]
+    out = np.zeros(L.cb_piece_bytes(fmt, blocks), np.uint8)
+    L.cb_piece_from_stored.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    assert L.cb_piece_from_stored(fmt, stored.ctypes.data, blocks, out.ctypes.data) == 0
+    assert np.array_equal(out, O.to_piece(fmt, stored))

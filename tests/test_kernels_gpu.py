@@ -258,7 +258,8 @@ def test_attention_fused_rope_matches_separate(cuda, case, position, sequences):
 
 @pytest.mark.parametrize("fmt,width,scale", [(O.Q6_K, 1024, 1.0), (O.Q4_0, 2048, 1.0),
                                              (O.Q8_0, 1152, float(np.sqrt(np.float32(1152)))),
-                                             (O.Q8_0, 1024, 1.0)])
+                                             (O.Q8_0, 1024, 1.0), (O.Q4_1, 1024, 1.0),
+                                             (O.BF16, 1152, float(np.sqrt(np.float32(1152))))])
 def test_gather_bit_exact(cuda, fmt, width, scale):
     rng = np.random.default_rng(width + fmt)
     vocab = 300

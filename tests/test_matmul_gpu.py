@@ -39,9 +39,12 @@ def run(fmt, K, members, x, outs, **kw):
 
 
 def assert_exact(got, want):
+    """Bit-exact (zeros by value); a NaN must meet a NaN (weights of random
+    bytes reach every exponent, so sums can overflow to inf − inf)."""
     got = np.asarray(got, np.float32)
     want = np.asarray(want, np.float32)
-    bad = np.flatnonzero(got.reshape(-1) != want.reshape(-1))
+    g, w = got.reshape(-1), want.reshape(-1)
+    bad = np.flatnonzero((g != w) & ~(np.isnan(g) & np.isnan(w)))
     assert bad.size == 0, f"{bad.size} outputs differ; first at {bad[:5]}: {got.reshape(-1)[bad[:5]]} vs {want.reshape(-1)[bad[:5]]}"
 
 
@@ -66,6 +69,10 @@ SHAPES = [
     (O.Q6_K, 300, 2048),
     (O.Q6_K, 70, 6912),
     (O.Q6_K, 31, 256),
+    (O.Q4_1, 1024, 3072),    # the Qwen3 file's Q4_1 down projection
+    (O.Q4_1, 100, 1152),
+    (O.BF16, 1024, 1024),
+    (O.BF16, 77, 64),
 ]
 
 
@@ -82,7 +89,7 @@ def test_decode_write_bit_exact(cuda, fmt, rows, K):
     assert_tolerance(got, stored, fmt, rows, K, x)
 
 
-@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q4_1, O.Q8_0, O.Q6_K, O.BF16])
 def test_dequant_through_one_hot_inputs_is_bit_exact(cuda, fmt):
     """x = e_k gives y[o] = w[o][k] exactly (one fma of w by 1 onto +0), so
     K one-hot tokens read the whole decoded matrix back: every weight must
@@ -98,7 +105,7 @@ def test_dequant_through_one_hot_inputs_is_bit_exact(cuda, fmt):
     assert_exact(y.cpu().numpy().T, W)
 
 
-@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q6_K])
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q4_1, O.Q6_K, O.BF16])
 def test_random_bytes_weights_bit_exact(cuda, fmt):
     rng = np.random.default_rng(77 + fmt)
     rows, K = 257, 2048

@@ -49,6 +49,8 @@ CASES = [
     (O.Q8_0, 333, 1024, 40),     # several token groups
     (O.Q6_K, 4096, 1024, 7),
     (O.Q6_K, 300, 2048, 64),
+    (O.Q4_1, 1024, 3072, 5),
+    (O.BF16, 333, 1024, 40),
 ]
 
 

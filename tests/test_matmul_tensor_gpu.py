@@ -57,6 +57,8 @@ CASES = [
     (O.Q8_0, 1024, 2048, 384),
     (O.Q6_K, 2048, 1024, 256),
     (O.Q6_K, 1000, 2048, 1),
+    (O.Q4_1, 1024, 3072, 256),
+    (O.BF16, 1024, 1024, 128),
 ]
 
 

@@ -59,6 +59,8 @@ CASES = [
     (O.Q6_K, 4096, 1024, 64),
     (O.Q6_K, 300, 2048, 129),
     (O.Q6_K, 70, 256, 16),
+    (O.Q4_1, 1024, 3072, 130),
+    (O.BF16, 300, 1152, 77),
 ]
 
 

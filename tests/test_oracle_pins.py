@@ -18,13 +18,14 @@ needs_ref = pytest.mark.skipif(REF is None, reason="oracle/_ref not built (the r
 
 def _ref_dequant(fmt, stored):
     out = np.empty(stored.size // O.BLOCK_BYTES[fmt] * O.BLOCK_WEIGHTS[fmt], np.float32)
-    fn = {O.Q4_0: REF.ref_dequant_q4_0, O.Q8_0: REF.ref_dequant_q8_0, O.Q6_K: REF.ref_dequant_q6_k}[fmt]
+    fn = {O.Q4_0: REF.ref_dequant_q4_0, O.Q8_0: REF.ref_dequant_q8_0, O.Q6_K: REF.ref_dequant_q6_k,
+          O.Q4_1: REF.ref_dequant_q4_1_fused}[fmt]
     fn(O.ptr(stored, ctypes.c_uint8), stored.size, O.ptr(out, ctypes.c_float))
     return out
 
 
 @needs_ref
-@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q4_1, O.Q8_0, O.Q6_K])
 @pytest.mark.parametrize("gen", ["random_bytes", "config"])
 def test_dequant_matches_reference_bit_for_bit(fmt, gen):
     rng = np.random.default_rng(fmt * 7 + len(gen))
@@ -37,7 +38,7 @@ def test_dequant_matches_reference_bit_for_bit(fmt, gen):
 
 
 @needs_ref
-@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q4_1, O.Q8_0, O.Q6_K])
 def test_unpack_from_device_layout_equals_reference_dequant(fmt):
     rng = np.random.default_rng(100 + fmt)
     n = 64
@@ -61,7 +62,34 @@ def test_q6_k_repack_matches_reference_repack():
     assert np.array_equal(synth.to_piece(O.Q6_K, stored), piece)
 
 
-@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q8_0, O.Q6_K])
+@needs_ref
+def test_q4_1_is_one_of_the_reference_evaluations():
+    """The reference accepts a Q4_1 weight rounded once (fused) or twice
+    (tests/support/q4_1_reference.h:13-21); this build takes the fused one:
+    it equals the reference's fused value everywhere, and over typical blocks
+    most weights agree with the twice-rounded value too."""
+    rng = np.random.default_rng(41)
+    stored = synth.blocks(rng, O.Q4_1, 64, 256)
+    n = stored.size // 20
+    fused, rounded = (np.empty(n * 32, np.float32) for _ in range(2))
+    REF.ref_dequant_q4_1_fused(O.ptr(stored, ctypes.c_uint8), stored.size, O.ptr(fused, ctypes.c_float))
+    REF.ref_dequant_q4_1_rounded(O.ptr(stored, ctypes.c_uint8), stored.size, O.ptr(rounded, ctypes.c_float))
+    ours = O.dequant_stored(O.Q4_1, stored)
+    assert np.array_equal(ours, fused)
+    assert np.mean(ours == rounded) > 0.5
+
+
+def test_bf16_is_the_top_half_of_an_f32():
+    rng = np.random.default_rng(42)
+    stored = synth.random_bytes_blocks(rng, O.BF16, 999)
+    want = (stored.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    assert np.array_equal(O.dequant_stored(O.BF16, stored), want)
+    piece = O.to_piece(O.BF16, stored)
+    got = np.concatenate([O.unpack(O.BF16, piece, 999, g) for g in range(999 // 32)])
+    assert np.array_equal(got, want[: got.size])
+
+
+@pytest.mark.parametrize("fmt", [O.Q4_0, O.Q4_1, O.Q8_0, O.Q6_K, O.BF16])
 def test_synth_device_layout_equals_oracle_layout(fmt):
     rng = np.random.default_rng(9)
     stored = synth.random_bytes_blocks(rng, fmt, 40)
