@@ -524,6 +524,15 @@ MatmulArgs fused_product(const cb_decoder* d, std::initializer_list<const DevWei
 int setup_fused(cb_decoder* d) {
     const cb_model& m = d->model;
     const uint32_t H = m.hidden, qd = m.query_heads * m.head_dim;
+    // The fused step decodes Q4_0, Q8_0 and Q6_K; a model with other weights
+    // (Q4_1, BF16) or another table format keeps the separate kernels.
+    const auto fused_format = [](uint32_t f) { return f == CB_Q4_0 || f == CB_Q8_0 || f == CB_Q6_K; };
+    if (!fused_format(d->token_embd.format)) return CB_OK;
+    for (uint32_t l = 0; l < m.layers; ++l) {
+        const DevLayer& L = d->layers[l];
+        for (const DevWeight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+            if (!fused_format(w->format)) return CB_OK;
+    }
     uint32_t max_cols = std::max(std::max(H, qd), m.ffn), row_stage = 0, gated_stage = 0;
     std::vector<FusedLayer> host(m.layers);
     for (uint32_t l = 0; l < m.layers; ++l) {

@@ -42,6 +42,7 @@ class Arch:
     window_pattern: int = 0             # every n-th layer (n-1 mod n) is global
     llama3_factors: bool = False
     matmul_format: int = Q4_0
+    down_format: int = 0                # the down projections' format (0: matmul_format)
     embed_format: int = Q6_K
     output_format: int = 0              # 0: tied to the embedding
 
@@ -171,7 +172,7 @@ def synthesize(arch: Arch, seed: int = 0) -> Model:
             w(f, H, arch.query_heads * d),
             _gain(rng, d) if arch.qk_norm else None, _gain(rng, d) if arch.qk_norm else None,
             _gain(rng, H) if arch.post_norms else None, _gain(rng, H),
-            w(f, F, H), w(f, F, H), w(f, H, F), _gain(rng, H) if arch.post_norms else None,
+            w(f, F, H), w(f, F, H), w(arch.down_format or f, H, F), _gain(rng, H) if arch.post_norms else None,
             arch.layer_window(l), arch.layer_rope_base(l)))
     factors = llama3_factors(d, arch.rope_base) if arch.llama3_factors else None
     return Model(arch, embd, _gain(rng, H), output, layers, factors)

@@ -55,6 +55,16 @@ def test_tiny_decoder_matches_oracle(cuda, kind):
     run_both(M.tiny(kind), 40, 12, [7, 33 - 7, 7], seed=hash(kind) % 1000)
 
 
+@pytest.mark.parametrize("matmul,down", [(2, 3), (30, 30)], ids=["q4_1_down", "bf16"])
+def test_decoder_with_q4_1_and_bf16_weights(cuda, matmul, down):
+    """Q4_1 down projections (as the real Qwen3 Q4_0 file has) and BF16
+    layer weights through the whole decoder, token for token and logits bit
+    for bit against the oracle."""
+    import dataclasses
+    arch = dataclasses.replace(M.tiny("qwen3"), matmul_format=matmul, down_format=down)
+    run_both(arch, 24, 8, [5, 19], seed=11)
+
+
 def test_gemma_window_ring_wraps(cuda):
     """A sliding-window layer's ring (window 16 + step slots) wraps several
     times over a 120-token prompt and 20 decode steps."""
