@@ -22,7 +22,7 @@ struct MemberArgs {
 };
 
 struct MatmulArgs {
-    uint32_t format;        // GGUF type: 2 Q4_0, 8 Q8_0, 14 Q6_K
+    uint32_t format;        // GGUF type: 2 Q4_0, 3 Q4_1, 8 Q8_0, 14 Q6_K, 30 BF16
     uint32_t columns;       // K, a multiple of 32
     uint32_t members;       // 1 to 3
     uint32_t total_rows;    // the members' rows together

@@ -56,6 +56,9 @@ struct Tile {
     static constexpr int kPartWeights = 32 / kParts;
     static constexpr int kXVec = BM * 8 / kThreads;              // float4 of x a thread stages a step
     static constexpr size_t kSmem = 2ull * 32u * (BM + BN) * 4u;
+    // The 256-thread four-row tile is the occupancy shape: held to 128
+    // registers a thread, two of its CTAs share an SM.
+    static constexpr int kMinBlocks = TM == 4 && kThreads == 256 ? 2 : 1;
     static_assert(kThreads % BN == 0 && (kParts == 1 || kParts == 2), "one or two threads a slot");
     static_assert(BM * 8 % kThreads == 0, "x staging divides evenly");
     static_assert(BM >= 32 && (BM / 4) % 8 == 0, "x swizzle spans eight float4 columns");
@@ -78,7 +81,7 @@ __device__ __forceinline__ void decode_part(const F& f, float* ws_col, std::inte
 }
 
 template <typename F, typename T>
-__global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) {
+__global__ void __launch_bounds__(T::kThreads, T::kMinBlocks) tiled_kernel(const MatmulArgs a) {
     constexpr int BM = T::BM, BN = T::BN, TM = T::TM;
     extern __shared__ __align__(16) float smem_f[];
     float* xs = smem_f;                 // [2][32][BM], swizzled
@@ -169,11 +172,13 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
 
     // ---- compute role: tokens ty·4.. (+BM/2), slots tx·4.. and BN/2 + tx·4.. --
     const uint32_t tx = tid % (BN / 8), ty = tid / (BN / 8);
-    float s[TM][8], total[TM][8];
+    // Outputs (i, 2p) and (i, 2p + 1) as one pair: the paired FMA
+    // (fma.rn.f32x2) rounds each half once, so each output keeps fmaf's bits.
+    float2 s[TM][4], total[TM][4];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) { s[i][c] = 0.0f; total[i][c] = 0.0f; }
+        for (int p = 0; p < 4; ++p) { s[i][p] = make_float2(0.0f, 0.0f); total[i][p] = make_float2(0.0f, 0.0f); }
 
     load_w(0);
     grid_dependency_wait();
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
         const float* wb = ws + buf * 32u * BN;
 #pragma unroll
         for (uint32_t k = 0; k < 32; ++k) {
-            float xv[TM], wv[8];
+            float xv[TM];
             const uint32_t sw = (k >> 2) & 7u;
             const float4 x0 = *reinterpret_cast<const float4*>(xb + k * BM + 4u * (ty ^ sw));
             xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
@@ -203,18 +208,20 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
             }
             const float4 w0 = *reinterpret_cast<const float4*>(wb + k * BN + 4u * tx);
             const float4 w1 = *reinterpret_cast<const float4*>(wb + k * BN + BN / 2 + 4u * tx);
-            wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
-            wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+            const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                                  make_float2(w1.z, w1.w)};
 #pragma unroll
-            for (int i = 0; i < TM; ++i)
+            for (int i = 0; i < TM; ++i) {
+                const float2 xx = make_float2(xv[i], xv[i]);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) s[i][c] = fmaf(wv[c], xv[i], s[i][c]);
+                for (int p = 0; p < 4; ++p) s[i][p] = __ffma2_rn(wp[p], xx, s[i][p]);
+            }
         }
         if (closes_range(g, G)) {
 #pragma unroll
             for (int i = 0; i < TM; ++i)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) { total[i][c] = total[i][c] + s[i][c]; s[i][c] = 0.0f; }
+                for (int p = 0; p < 4; ++p) { total[i][p] = __fadd2_rn(total[i][p], s[i][p]); s[i][p] = make_float2(0.0f, 0.0f); }
         }
         if (more) {
             store_w(ws + (buf ^ 1u) * 32u * BN);
@@ -225,6 +232,7 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
     grid_dependents_launch();
 
     // ---- epilogue -----------------------------------------------------------
+    auto sum = [&](int i, int c) { return (c & 1) ? total[i][c >> 1].y : total[i][c >> 1].x; };
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const uint32_t t = m0 + (i < 4 ? ty * 4u + i : BM / 2 + ty * 4u + (i - 4));
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
                 const uint32_t o = n0 + tx * 4u + c;
                 if (o < a.member[0].rows)
                     a.out[0][static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o] =
-                        activate(a.activation, total[i][c]) * total[i][4 + c];
+                        activate(a.activation, sum(i, c)) * sum(i, 4 + c);
             }
             continue;
         }
@@ -256,13 +264,13 @@ __global__ void __launch_bounds__(T::kThreads) tiled_kernel(const MatmulArgs a) 
             if (a.epilogue == kQKV) {
                 float* out = q == 1 ? a.out[1] : (q == 2 ? a.out[2] : a.out[0]);
                 const uint32_t stride = q == 1 ? a.out_stride[1] : (q == 2 ? a.out_stride[2] : a.out_stride[0]);
-                out[static_cast<size_t>(t) * stride + o] = total[i][c];
+                out[static_cast<size_t>(t) * stride + o] = sum(i, c);
             } else if (a.epilogue == kWrite) {
-                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = total[i][c];
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = sum(i, c);
             } else {   // kGatedByInput (matmul.wgsl:346-350)
                 const float u = a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride +
                                              a.gate_input_column + o];
-                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total[i][c]) * u;
+                a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, sum(i, c)) * u;
             }
         }
     }
