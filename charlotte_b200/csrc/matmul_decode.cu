@@ -377,43 +377,33 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
 // The same warp layout with R = 2 (a pair of rows, or a gated output's gate
 // and up rows) and MT tokens: each weight is decoded once and multiplied
 // into MT chains, one per token, each still the reference's chain for that
-// (row, token). x of the CTA's MT tokens is staged range-major, token after
-// token. The 2·MT range-sum rows meet in shared memory, and lane slot·MT + i
-// adds row `slot`'s range sums for token i in range order.
-template <typename F, int MT>
-__device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const float4* x4, uint32_t tok4,
-                                               float (&aa)[MT], float (&ab)[MT]) {
-    const typename F::Consts ca = A.consts(), cbb = B.consts();
+// (row, token). Tokens go in pairs through the paired FMA (fma.rn.f32x2,
+// each half one fma, so each chain keeps its bits): one paired fma advances
+// tokens 2p and 2p + 1 of a row, with the row's weight as both halves of one
+// operand. x is staged range-major by token pair, the pair's two floats of
+// each k side by side. The 2·MT range-sum rows meet in shared memory, and
+// lane slot·MT + i adds row `slot`'s range sums for token i in range order.
+template <typename F, int MT, int k>
+__device__ __forceinline__ void chain_step_mt(const F& A, const F& B, const typename F::Consts2& c,
+                                              const float4* x2, uint32_t pair4, float2 (&pa)[MT / 2],
+                                              float2 (&pb)[MT / 2]) {
+    const float2 w = F::template weight2<k>(A, B, c);
+    const float2 wa = make_float2(w.x, w.x), wb = make_float2(w.y, w.y);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        float wa[4], wb[4];
-        auto dec = [&](auto kc) {
-            constexpr int k = decltype(kc)::value;
-            wa[k % 4] = F::template weight<k>(A, ca);
-            wb[k % 4] = F::template weight<k>(B, cbb);
-        };
-        // k = 4q .. 4q+3 as compile-time constants
-        if (q == 0) { dec(std::integral_constant<int, 0>{}); dec(std::integral_constant<int, 1>{}); dec(std::integral_constant<int, 2>{}); dec(std::integral_constant<int, 3>{}); }
-        if (q == 1) { dec(std::integral_constant<int, 4>{}); dec(std::integral_constant<int, 5>{}); dec(std::integral_constant<int, 6>{}); dec(std::integral_constant<int, 7>{}); }
-        if (q == 2) { dec(std::integral_constant<int, 8>{}); dec(std::integral_constant<int, 9>{}); dec(std::integral_constant<int, 10>{}); dec(std::integral_constant<int, 11>{}); }
-        if (q == 3) { dec(std::integral_constant<int, 12>{}); dec(std::integral_constant<int, 13>{}); dec(std::integral_constant<int, 14>{}); dec(std::integral_constant<int, 15>{}); }
-        if (q == 4) { dec(std::integral_constant<int, 16>{}); dec(std::integral_constant<int, 17>{}); dec(std::integral_constant<int, 18>{}); dec(std::integral_constant<int, 19>{}); }
-        if (q == 5) { dec(std::integral_constant<int, 20>{}); dec(std::integral_constant<int, 21>{}); dec(std::integral_constant<int, 22>{}); dec(std::integral_constant<int, 23>{}); }
-        if (q == 6) { dec(std::integral_constant<int, 24>{}); dec(std::integral_constant<int, 25>{}); dec(std::integral_constant<int, 26>{}); dec(std::integral_constant<int, 27>{}); }
-        if (q == 7) { dec(std::integral_constant<int, 28>{}); dec(std::integral_constant<int, 29>{}); dec(std::integral_constant<int, 30>{}); dec(std::integral_constant<int, 31>{}); }
-#pragma unroll
-        for (int i = 0; i < MT; ++i) {
-            const float4 xq = x4[i * tok4 + q];
-            aa[i] = fmaf(wa[0], xq.x, aa[i]);
-            ab[i] = fmaf(wb[0], xq.x, ab[i]);
-            aa[i] = fmaf(wa[1], xq.y, aa[i]);
-            ab[i] = fmaf(wb[1], xq.y, ab[i]);
-            aa[i] = fmaf(wa[2], xq.z, aa[i]);
-            ab[i] = fmaf(wb[2], xq.z, ab[i]);
-            aa[i] = fmaf(wa[3], xq.w, aa[i]);
-            ab[i] = fmaf(wb[3], xq.w, ab[i]);
-        }
+    for (int p = 0; p < MT / 2; ++p) {
+        const float4 xq = x2[p * pair4 + k / 2];
+        const float2 xk = (k % 2 == 0) ? make_float2(xq.x, xq.y) : make_float2(xq.z, xq.w);
+        pa[p] = __ffma2_rn(wa, xk, pa[p]);
+        pb[p] = __ffma2_rn(wb, xk, pb[p]);
     }
+}
+
+template <typename F, int MT, int... ks>
+__device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const float4* x2, uint32_t pair4,
+                                               float2 (&pa)[MT / 2], float2 (&pb)[MT / 2],
+                                               std::integer_sequence<int, ks...>) {
+    const typename F::Consts2 c = F::consts2(A, B);
+    (chain_step_mt<F, MT, ks>(A, B, c, x2, pair4, pa, pb), ...);
 }
 
 template <typename F, int MT, int W>
@@ -422,15 +412,15 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t G = a.columns / 32u;
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t lane_stride = x_lane_stride(G);
-    const uint32_t tok_floats = 32u * lane_stride;   // one token's staged x
+    const uint32_t lane_stride = x2_lane_stride(G);
+    const uint32_t pair_floats = 32u * lane_stride;   // one token pair's staged x
     const uint32_t stage_bytes = RowStreams<F>::row_stage(G) * R;
     const uint32_t batches = batch_count<R>(a);
     const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
 
     float* xs = reinterpret_cast<float*>(smem);
-    const uint32_t x_bytes = MT * tok_floats * 4u;
+    const uint32_t x_bytes = MT / 2 * pair_floats * 4u;
     const uint32_t warp_bytes = 16u + R * MT * kRedStride * 4u + 2u * stage_bytes;
     uint8_t* wbase = smem + x_bytes + warp * warp_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(wbase);
@@ -452,24 +442,29 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     const uint32_t t0 = blockIdx.y * MT;
     const uint32_t nt = min(static_cast<uint32_t>(MT), a.tokens - t0);
     const uint32_t lo = range_lo(lane, G), hi = range_lo(lane + 1u, G);
-    // The tokens' 16-byte chunks dealt to all threads in row order (each
-    // warp reads one contiguous span), copied asynchronously to their
-    // range's run; tokens past the step's last are zeros.
+    // A token pair's 16-byte chunks dealt to all threads in row order (each
+    // warp reads one contiguous span of both rows) and interleaved into
+    // their range's run; tokens past the step's last are zeros.
     {
         const uint32_t chunks = G * 8u;
-        for (uint32_t idx = threadIdx.x; idx < MT * chunks; idx += W * 32u) {
-            const uint32_t i = idx / chunks, c = idx % chunks;
+        const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (uint32_t idx = threadIdx.x; idx < MT / 2 * chunks; idx += W * 32u) {
+            const uint32_t p = idx / chunks, c = idx % chunks;
             const uint32_t grp = c / 8u, lr = lane_of(grp, G);
-            float* dst = xs + i * tok_floats + lr * lane_stride + (grp - range_lo(lr, G)) * 32u + (c % 8u) * 4u;
-            if (i < nt) cp_async16(dst, a.x + static_cast<size_t>(t0 + i) * a.x_stride + 4u * c);
-            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+            const uint32_t i0 = 2u * p;
+            const float4 v0 = i0 < nt ? __ldcg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i0) * a.x_stride) + c) : zero;
+            const float4 v1 = i0 + 1u < nt ? __ldcg(reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t0 + i0 + 1u) * a.x_stride) + c) : zero;
+            float4* dst = reinterpret_cast<float4*>(xs + p * pair_floats + lr * lane_stride + (grp - range_lo(lr, G)) * 64u +
+                                                    (c % 8u) * 8u);
+            dst[0] = make_float4(v0.x, v1.x, v0.y, v1.y);
+            dst[1] = make_float4(v0.z, v1.z, v0.w, v1.w);
         }
-        cp_async_wait_all();
     }
     __syncthreads();
     grid_dependents_launch();
     const float4* xl = reinterpret_cast<const float4*>(xs + lane * lane_stride);
-    const uint32_t tok4 = tok_floats / 4u;
+    const uint32_t pair4 = pair_floats / 4u;
 
     uint32_t rb[F::kStreams], sl[F::kStreams], reg[F::kStreams];
 #pragma unroll
@@ -513,19 +508,21 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
         }
         const bool la = bt.live > 0;
         const bool lb = gated ? la : bt.live > 1;
-        float aa[MT], ab[MT];
+        float2 aa[MT / 2], ab[MT / 2];
 #pragma unroll
-        for (int i = 0; i < MT; ++i) { aa[i] = 0.0f; ab[i] = 0.0f; }
+        for (int p = 0; p < MT / 2; ++p) { aa[p] = make_float2(0.0f, 0.0f); ab[p] = make_float2(0.0f, 0.0f); }
         for (uint32_t g = lo; g < hi; ++g) {
             F A, B;
             if (la) A.load(pa, g); else A.zero();
             if (lb) B.load(pb, g); else B.zero();
-            chain_group_mt<F, MT>(A, B, xl + (g - lo) * 8u, tok4, aa, ab);
+            chain_group_mt<F, MT>(A, B, xl + (g - lo) * 16u, pair4, aa, ab, std::make_integer_sequence<int, 32>{});
         }
 #pragma unroll
-        for (int i = 0; i < MT; ++i) {
-            red[i * kRedStride + lane] = aa[i];
-            red[(MT + i) * kRedStride + lane] = ab[i];
+        for (int p = 0; p < MT / 2; ++p) {
+            red[(2 * p) * kRedStride + lane] = aa[p].x;
+            red[(2 * p + 1) * kRedStride + lane] = aa[p].y;
+            red[(MT + 2 * p) * kRedStride + lane] = ab[p].x;
+            red[(MT + 2 * p + 1) * kRedStride + lane] = ab[p].y;
         }
         fence_proxy_async();
         __syncwarp();
@@ -570,7 +567,7 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
 
 template <typename F, int MT, int W = kWarps>
 size_t decode_mt_smem(uint32_t G) {
-    return static_cast<size_t>(MT) * 32u * x_lane_stride(G) * 4u +
+    return static_cast<size_t>(MT / 2) * 32u * x2_lane_stride(G) * 4u +
            W * (16u + 2u * MT * kRedStride * 4u + 2ull * 2u * RowStreams<F>::row_stage(G));
 }
 
