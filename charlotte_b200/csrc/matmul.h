@@ -66,11 +66,12 @@ cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl);
 uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns);
 
 // Which exact form a step takes by default: the streamed (decode-layout)
-// form keeps every SM busy on short steps and narrow products, the tiled
-// GEMM wins once the step has enough tiles (measured on B200: for 1,024-row
-// products from 512 tokens, for 4,096 rows and more from 256).
+// form's time grows with tokens × rows, the tiled GEMM's stays flat while
+// its 128 × 128 tiles fit one wave, so the tiled form wins from a fixed
+// amount of work (measured on B200, Qwen3 shapes: 4,096 rows from ~192
+// tokens, 6,144 from ~128, 1,024 rows from 512–1,024 tokens).
 inline bool tiled_form(uint32_t tokens, uint32_t slots) {
-    return tokens >= 512 || (tokens >= 256 && slots >= 4096);
+    return static_cast<uint64_t>(tokens) * slots >= 786432u;
 }
 
 // Shared memory the decode form needs at its smallest batch, for a width.

@@ -587,13 +587,22 @@ cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t str
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    // CTAs an SM holds at this width (shared memory and registers), per
+    // instantiation for the last width asked.
+    static size_t occupancy_smem = 0;
+    static uint32_t per_sm = 1;
+    if (occupancy_smem != smem) {
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, W * 32, smem);
+        if (e != cudaSuccess) return e;
+        per_sm = n > 0 ? static_cast<uint32_t>(n) : 1u;
+        occupancy_smem = smem;
+    }
     const uint32_t groups = (a.tokens + MT - 1) / MT;
     uint32_t ctas = (batches + W - 1) / W;
-    uint32_t per_sm = static_cast<uint32_t>((227u * 1024u) / (smem + 1024u));
-    if (per_sm < 1) per_sm = 1;
-    if (per_sm > 16) per_sm = 16;
-    // Enough CTAs across the token groups to fill the SMs, no more.
-    const uint32_t cap = (static_cast<uint32_t>(sm_count) * per_sm + groups - 1) / groups;
+    // Enough CTAs across the token groups to fill the SMs in one wave, no
+    // more: a CTA past the wave would start only when one ends.
+    const uint32_t cap = static_cast<uint32_t>(sm_count) * per_sm / groups;
     if (ctas > cap) ctas = cap;
     if (ctas == 0) ctas = 1;
     cudaLaunchConfig_t cfg = {};
