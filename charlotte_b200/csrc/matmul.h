@@ -69,9 +69,11 @@ uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns);
 // form's time grows with tokens × rows, the tiled GEMM's stays flat while
 // its 128 × 128 tiles fit one wave, so the tiled form wins from a fixed
 // amount of work (measured on B200, Qwen3 shapes: 4,096 rows from ~192
-// tokens, 6,144 from ~128, 1,024 rows from 512–1,024 tokens).
+// tokens, 6,144 from ~128, 1,024 rows from 512–1,024 tokens). Its smallest
+// tile is 32 tokens high, so steps of fewer tokens pay for 32: the
+// vocabulary heads (150–260 K rows) stay streamed below ~24 tokens.
 inline bool tiled_form(uint32_t tokens, uint32_t slots) {
-    return static_cast<uint64_t>(tokens) * slots >= 786432u;
+    return tokens >= 24u && static_cast<uint64_t>(tokens) * slots >= 786432u;
 }
 
 // Shared memory the decode form needs at its smallest batch, for a width.
