@@ -12,6 +12,15 @@ so every step streams from HBM). The step is captured once as a CUDA graph
 each step copies every x host->device and every y back inside the timed
 region.
 
+Beside the headline, the same JSON line carries every configuration of the
+path, each with its roofline (and, at one GPU, a CPU baseline: the oracle
+on the host cores): `qwen3_decode`, `gemma_batched_decode`
+(configs[4], 64 sequences sharded over the ranks) and, at N > 1,
+`gemma_split_head_decode` (the vocabulary-split head with its two NCCL
+all-gathers a step, timed); at one GPU also `config1_q4_0_gemv`
+(configs[0]), `sweep_m16_m128` (configs[1] at M = 16 and 128) and
+`llama_prefill_decode` (configs[3]).
+
 `--impl reference` times the reference path's CPU restatement (the oracle:
 the reference's order of operations over its dequantizers, all host
 threads) on a bounded sample of the same step.
@@ -158,7 +167,17 @@ class GemvSet:
         rng = np.random.default_rng(seed)
         self.items = []
         self.bytes = 0.0
-        for name, fmt, rows, K in qwen3_gemv_set():
+        spec = qwen3_gemv_set()
+        # Every product's x in one contiguous buffer and every output in
+        # another (16-byte aligned slices), so that the end-to-end run moves
+        # a step's inputs and results with one copy each way.
+        align = lambda n: (n + 3) // 4 * 4
+        x_floats = sum(align(K) for _, _, _, K in spec)
+        y_floats = sum(align(r) for _, _, rows, _ in spec for r in (rows if len(rows) != 2 else rows[:1]))
+        self.xbuf = torch.empty(x_floats, dtype=torch.float32, device="cuda")
+        self.ybuf = torch.zeros(y_floats, dtype=torch.float32, device="cuda")
+        xo = yo = 0
+        for name, fmt, rows, K in spec:
             members = []
             for r in rows:   # distinct weights for every layer and member
                 stored = synth.blocks(rng, fmt, r, K)
@@ -166,11 +185,13 @@ class GemvSet:
                 members.append((torch.from_numpy(synth.to_piece(fmt, stored)).cuda(), nb, 0, r, 0))
             kind = name.split(".")[0]
             epi = {"qkv": cb.QKV, "gate_up": cb.GATED}.get(kind, cb.WRITE)
-            x = torch.from_numpy(synth.activations(rng, 1, K)).cuda()
-            if epi == cb.QKV:
-                outs = [torch.zeros((1, r), dtype=torch.float32, device="cuda") for r in rows]
-            else:
-                outs = [torch.zeros((1, rows[0]), dtype=torch.float32, device="cuda")]
+            x = self.xbuf[xo: xo + K].view(1, K)
+            x.copy_(torch.from_numpy(synth.activations(rng, 1, K)))
+            xo += align(K)
+            outs = []
+            for r in (rows if epi == cb.QKV else rows[:1]):
+                outs.append(self.ybuf[yo: yo + r].view(1, r))
+                yo += align(r)
             self.items.append(dict(name=name, kind=kind, fmt=fmt, K=K, rows=rows, members=members, epi=epi, x=x,
                                    outs=outs, bytes=algorithmic_bytes(fmt, rows, K)))
             self.bytes += self.items[-1]["bytes"]
@@ -296,7 +317,7 @@ def run_ours(args):
     traffic_ratio = 2420992 / 2379776 if share_q4 >= 0.5 else 132129024 / 128238080
 
     # e2e: the same products through the C ABI with host buffers.
-    e2e = None if args.no_e2e else run_e2e(gs, stream, max(args.steps // 20, 5), world)
+    e2e = None if args.no_e2e else run_e2e(gs, graph, stream, max(args.steps // 4, 20), world)
 
     result = {
         "metric": "Q4_0/Q6_K GEMV HBM GB/s",
@@ -325,11 +346,20 @@ def run_ours(args):
         "gpu_launches": len(gs.items) * args.steps,
         "clocks": clocks.summary(),
     }
+    cpu = not args.no_cpu_baseline
     if not args.no_decode:
         result["qwen3_decode"] = decode_bench(args.decode_steps, 512, SEED + 7 + rank, world)
     if not args.no_batch:
-        result["gemma_batched_decode"] = gemma_batch_bench(args.batch_steps, world, rank)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["gemma_batched_decode"] = gemma_batch_bench(args.batch_steps, world, rank, cpu=cpu)
+        if world > 1:
+            # the vocabulary-split head (the path's one exchange) beside the sequence-sharded run
+            result["gemma_split_head_decode"] = gemma_split_bench(args.batch_steps, world, rank)
+    if world == 1 and not args.no_configs:
+        # the single-GPU configurations: configs[0], configs[1] at M = 16 and 128, configs[3]
+        result["config1_q4_0_gemv"] = config1_bench(cpu=cpu)
+        result["sweep_m16_m128"] = sweep_summary(sweep_bench(iters=20, ms=[16, 128], formats=(2,), head=True))
+        result["llama_prefill_decode"] = llama_bench(128, SEED + 11, cpu=cpu)
+    if rank == 0 and world == 1 and cpu:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         if "qwen3_decode" in result:
             result["qwen3_decode"]["cpu_baseline"] = cpu_decode_baseline(SEED + 7)
@@ -341,23 +371,23 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_e2e(gs, stream, steps, world):
-    """Every x host->device and every y device->host in the timed region,
-    pinned host buffers, one copy a buffer, through the same C ABI calls."""
+def run_e2e(gs, graph, stream, steps, world):
+    """The same products end to end with host buffers: each step copies every
+    product's x from one pinned host buffer to the device (one copy), replays
+    the captured graph of C ABI launches, and copies every output back to one
+    pinned host buffer (one copy); all three inside the timed region, on the
+    replay stream."""
     import torch
-    hx = [it["x"].cpu().pin_memory() for it in gs.items]
-    hy = [[torch.empty_like(o, device="cpu").pin_memory() for o in it["outs"]] for it in gs.items]
-    h2d = sum(x.numel() * 4 for x in hx)
-    d2h = sum(o.numel() * 4 for ys in hy for o in ys)
+    hx = gs.xbuf.cpu().pin_memory()
+    hy = torch.empty_like(gs.ybuf, device="cpu").pin_memory()
+    h2d = hx.numel() * 4
+    d2h = hy.numel() * 4
 
     def one():
         with torch.cuda.stream(stream):
-            for it, x in zip(gs.items, hx):
-                it["x"].copy_(x, non_blocking=True)
-            gs.step(stream)
-            for it, ys in zip(gs.items, hy):
-                for o, y in zip(it["outs"], ys):
-                    y.copy_(o, non_blocking=True)
+            gs.xbuf.copy_(hx, non_blocking=True)
+            graph.replay()
+            hy.copy_(gs.ybuf, non_blocking=True)
     for _ in range(3):
         one()
     torch.cuda.synchronize()
@@ -370,7 +400,9 @@ def run_e2e(gs, stream, steps, world):
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
     return {"value": round(gs.bytes * world / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4)}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
+            "how": "one pinned host->device copy of every x, the captured graph of cb_matmul_run launches, one "
+                   "device->host copy of every output, a step"}
 
 
 def decode_bench(steps, prompt_len, seed, world):
@@ -412,6 +444,7 @@ def decode_bench(steps, prompt_len, seed, world):
         "workload": "qwen3-0.6b greedy decode (configs[2]): 512-token prompt, %d steps, f16 KV, context 4096" % steps,
         "tok_s": round(steps * world / (dev_ms * 1e-3), 1),
         "ms_per_token": round(dev_ms / steps, 4),
+        "roofline": decode_roofline(m, range(prompt_len, prompt_len + steps), dev_ms / steps),
         # gather, then a layer's QKV (its norm folded in), attention (its rope
         # folded in), O, gate|up (norm folded in), down; the head (final norm
         # folded in), top-k + draw, the position advance
@@ -425,43 +458,62 @@ def decode_bench(steps, prompt_len, seed, world):
     }
 
 
-def llama_bench(decode_steps, seed):
+def llama_bench(decode_steps, seed, cpu=True):
     """Llama-3.2-1B shapes, random-init weights, a 2,048-token
     prompt as four 512-token steps on the tcgen05 path
     (CB_DECODER_TENSOR_PREFILL), then `decode_steps` greedy decode steps
     (exact form, one CUDA graph replayed). The same prompt through the exact
-    forms is timed beside it."""
+    forms is timed beside it. Prefill is wall-timed around the four
+    synchronous steps (host calls included); its roofline is the tensor
+    form's FLOPs (every layer product, the causal attention, the last
+    token's head) over that time against the measured sustained bf16 tensor
+    peak; decode's is bytes a token against HBM."""
     import torch
     from charlotte_b200 import model as M
     arch = M.llama_3_2_1b(context=2048 + decode_steps + 64)
     m = M.synthesize(arch, seed=seed)
     rng = np.random.default_rng(seed + 1)
-    prompt = rng.integers(0, arch.vocab, 2048).astype(np.uint32)
+    P = 2048
+    prompt = rng.integers(0, arch.vocab, P).astype(np.uint32)
     out = {"workload": "llama-3.2-1b shapes (configs[3]): 2048-token prompt as 4x512 steps, "
                        "then %d greedy steps" % decode_steps}
-    flops_per_token = 2.0 * sum(w.rows * w.cols for L in m.layers for w in (L.q, L.k, L.v, L.o, L.gate, L.up,
-                                                                           L.down))
+    layer_params = sum(w.rows * w.cols for L in m.layers for w in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down))
+    head = m.output if m.output is not None else m.token_embd
+    attention_flops = 4.0 * arch.head_dim * arch.query_heads * arch.layers * (P * (P + 1) / 2)
+    flops = 2.0 * P * layer_params + attention_flops + 2.0 * head.rows * head.cols
+    peaks = read_peaks()
+    tensor_peak = peaks.get("bf16_tflops_sustained", 1370.0)
     for tensor in (True, False):
         dec = M.Decoder(m, max_step_tokens=512, tensor_prefill=tensor)
         dec.prefill(prompt)   # warm
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         rec = dec.prefill(prompt)
-        s = time.perf_counter() - t0
+        sec = time.perf_counter() - t0
         key = "prefill_tensor" if tensor else "prefill_exact"
-        out[key] = {"ms": round(s * 1e3, 2), "tok_s": round(2048 / s, 1),
-                    "matmul_tflops": round(2048 * flops_per_token / s / 1e12, 1)}
+        tflops = flops / sec / 1e12
+        out[key] = {"ms": round(sec * 1e3, 2), "tok_s": round(P / sec, 1), "tflops": round(tflops, 1),
+                    "flops": flops}
         if tensor:
+            out[key]["roofline"] = {"bound": "tensor", "kernel": "prefill step (all launches)",
+                                    "achieved": round(tflops, 1), "peak": tensor_peak, "unit": "TFLOP/s",
+                                    "frac": round(tflops / tensor_peak, 4), "traffic": None,
+                                    "peak_source": "measured sustained" if peaks else "fallback"}
             dec.generate(4)
             dec.prefill(prompt)
             toks, failed, dev_ms = dec.generate(decode_steps, timed=True)
             out["decode"] = {"tok_s": round(decode_steps / (dev_ms * 1e-3), 1),
-                             "ms_per_token": round(dev_ms / decode_steps, 4), "failed_steps": int(failed.sum())}
+                             "ms_per_token": round(dev_ms / decode_steps, 4), "failed_steps": int(failed.sum()),
+                             "roofline": decode_roofline(m, range(P, P + decode_steps), dev_ms / decode_steps)}
+        else:
+            out[key]["note"] = "exact f32 forms on the CUDA cores (the reference's order of operations)"
         dec.close()
+    if cpu:
+        out["cpu_baseline"] = cpu_model_decode_baseline(M.llama_3_2_1b(context=64), seed)
     return out
 
 
-def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024):
+def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024, cpu=True):
     """Gemma-3-1B shapes, random-init weights; 64 independent
     sequences with random 1,024-token prompts, sharded over the ranks (64/N
     each, no collective on the data path: strong scaling of a fixed batch);
@@ -485,14 +537,22 @@ def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024):
         bd.prefill_sequence(s, prompt)
     barrier(world)
     toks, failed, dev_ms = bd.generate(steps, timed=True)
+    dev_local = dev_ms
     dev_ms = max_over_ranks(dev_ms, world)
     bd.close()
-    return {"workload": "gemma-3-1b shapes (configs[4]): %d sequences x %d-token prompts, %d batched steps" % (
+    out = {"workload": "gemma-3-1b shapes (configs[4]): %d sequences x %d-token prompts, %d batched steps" % (
                 sequences, prompt_len, steps),
-            "sequences_per_gpu": S, "tok_s": round(sequences * steps / (dev_ms * 1e-3), 1),
-            "ms_per_step": round(dev_ms / steps, 4), "scaling": "strong (64 sequences in all, split over ranks)",
-            "failed_steps": int(failed.sum()),
-            "head": "tied Q8_0 262,144 x 1,152 (Q6_K needs widths of whole 256-weight super-blocks)"}
+           "sequences_per_gpu": S, "tok_s": round(sequences * steps / (dev_ms * 1e-3), 1),
+           "ms_per_step": round(dev_ms / steps, 4), "scaling": "strong (64 sequences in all, split over ranks)",
+           "failed_steps": int(failed.sum()),
+           # one rank's step: its sequences' KV reads and the whole weights
+           "roofline": decode_roofline(m, range(prompt_len, prompt_len + steps), dev_local / steps, rows=S,
+                                       kernel="batched decode step on one rank (all launches)"),
+           "head": "tied Q8_0 262,144 x 1,152 (Q6_K needs widths of whole 256-weight super-blocks)"}
+    if rank == 0 and world == 1 and cpu:
+        out["cpu_baseline"] = cpu_model_decode_baseline(M.gemma_3_1b(context=64), SEED + 21, steps=3)
+        out["cpu_baseline"]["sample"] += " (one sequence: the GPU figure steps 64)"
+    return out
 
 
 def gemma_split_bench(steps, world, rank, sequences=64, prompt_len=1024):
@@ -527,22 +587,25 @@ def gemma_split_bench(steps, world, rank, sequences=64, prompt_len=1024):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(sh.stream)
     toks = []
+    timing = []
     for i in range(steps):
-        sh.step(prompt_len + i)
+        sh.step(prompt_len + i, timing=timing)
         toks.append(sh.sampled_all[:, 0])
     e1.record(sh.stream)
     torch.cuda.synchronize()
     dev_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    gather_ms = max_over_ranks(sum(a.elapsed_time(b) + c.elapsed_time(d) for a, b, c, d in timing) / steps, world)
     bd.close()
     return {"workload": "gemma-3-1b shapes (configs[4]) with a vocabulary-split head: %d sequences x %d-token "
                         "prompts, %d steps" % (sequences, prompt_len, steps),
             "sequences_per_gpu": S, "vocab_rows_per_gpu": arch.vocab // world,
             "tok_s": round(sequences * steps / (dev_ms * 1e-3), 1), "ms_per_step": round(dev_ms / steps, 4),
+            "allgather_ms_per_step": round(gather_ms, 4),
             "collectives_per_step": "all-gather of normed rows (%d B) + all-gather of candidates (%d B) a rank" % (
                 S * arch.hidden * 4, sequences * 128 * 4)}
 
 
-def config1_bench(iters=200):
+def config1_bench(iters=200, cpu=True):
     """one Q4_0 GEMV, W [8192, 2048] (Llama-3.2-1B gate_proj),
     d = |N(0,0.02)|/8, x ~ N(0,1): GB/s graph-timed over copies of W that
     together exceed L2, the bits checked against the oracle, and the oracle
@@ -570,20 +633,28 @@ def config1_bench(iters=200):
     torch.cuda.synchronize()
     exact = bool(np.array_equal(y.cpu().numpy(), O.matmul(Q4_0, piece_h, nb, rows, K, xh)))
     nbytes = rows * K * 18 / 32 + 4 * K + 4 * rows
-    threads = os.cpu_count() or 1
-    O.matmul(Q4_0, piece_h, nb, rows, K, xh, threads=threads)
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < 3.0:
-        O.matmul(Q4_0, piece_h, nb, rows, K, xh, threads=threads)
-        n += 1
-    cpu_s = (time.perf_counter() - t0) / n
-    peak = read_peaks().get("hbm_gbs", 6650.0)
+    peaks = read_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
     gbs = nbytes / (ms * 1e-3) / 1e9
-    return {"workload": "configs[0]: Q4_0 GEMV 8192 x 2048", "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
-            "frac_of_measured_hbm": round(gbs / peak, 4), "bit_exact_vs_oracle": exact,
-            "cpu_baseline": {"value": round(nbytes / cpu_s / 1e9, 2), "unit": "GB/s", "cores": threads,
-                             "kind": "port", "sample": "%d runs of the same product, oracle" % n}}
+    out = {"workload": "configs[0]: Q4_0 GEMV 8192 x 2048", "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+           "bit_exact_vs_oracle": exact,
+           "roofline": {"bound": "hbm", "kernel": "decode_kernel<Q4_0>", "achieved": round(gbs, 1), "peak": peak,
+                        "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None,
+                        "bytes_per_launch": round(nbytes), "peak_source": "measured" if peaks else "fallback",
+                        "how": "%d launches in a CUDA graph over copies of W totalling more than L2" % iters}}
+    if cpu:
+        threads = os.cpu_count() or 1
+        O.matmul(Q4_0, piece_h, nb, rows, K, xh, threads=threads)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 3.0:
+            O.matmul(Q4_0, piece_h, nb, rows, K, xh, threads=threads)
+            n += 1
+        cpu_s = (time.perf_counter() - t0) / n
+        out["cpu_baseline"] = {"value": round(nbytes / cpu_s / 1e9, 2), "unit": "GB/s", "cores": threads,
+                               "kind": "port", "sample": "%d runs of the same product, oracle, %.1f s" % (
+                                   n, time.perf_counter() - t0)}
+    return out
 
 
 def cpu_decode_baseline(seed):
@@ -614,6 +685,62 @@ def read_peaks():
         with open(p) as f:
             return json.load(f)
     return {}
+
+
+BYTES_PER_WEIGHT_ALL = {2: 18 / 32, 3: 20 / 32, 8: 34 / 32, 14: 210 / 256, 30: 2.0}
+
+
+def weight_bytes(model):
+    """Algorithmic bytes of a decode token's weights: every layer product and
+    the head (the table itself when tied), each read once."""
+    layers = sum(w.rows * w.cols * BYTES_PER_WEIGHT_ALL[w.format] for L in model.layers
+                 for w in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down))
+    head = model.output if model.output is not None else model.token_embd
+    return layers, head.rows * head.cols * BYTES_PER_WEIGHT_ALL[head.format]
+
+
+def kv_read_bytes(arch, position):
+    """f16 keys and values attention reads for one query at `position`:
+    every layer's live keys (its window, or position + 1)."""
+    per_key = 2 * arch.kv_heads * arch.head_dim * 2
+    return sum(min(arch.layer_window(l), position + 1) for l in range(arch.layers)) * per_key
+
+
+def decode_roofline(model, positions, ms_per_step, rows=1, kernel="decode step (all launches)"):
+    """A decode step's algorithmic bytes (the weights once, each row's KV
+    reads at the steps' mean position) over its measured time, against the
+    measured HBM peak."""
+    layers, head = weight_bytes(model)
+    kv = rows * float(np.mean([kv_read_bytes(model.arch, p) for p in positions]))
+    nbytes = layers + head + kv
+    peak = read_peaks().get("hbm_gbs")
+    achieved = nbytes / (ms_per_step * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak or 6650.0,
+            "unit": "GB/s", "frac": round(achieved / (peak or 6650.0), 4), "traffic": None,
+            "bytes_per_step": round(nbytes), "weight_bytes": round(layers + head), "kv_bytes": round(kv),
+            "peak_source": "measured" if peak else "fallback"}
+
+
+def cpu_model_decode_baseline(arch, seed, prompt=16, steps=4, threads=0):
+    """The oracle's pass (the reference's order of operations) on the host
+    cores: a short prompt, then `steps` greedy decode steps of one sequence."""
+    from charlotte_b200 import model as M
+    from oracle.model import OracleDecoder
+    m = M.synthesize(arch, seed=seed)
+    od = OracleDecoder(m, threads=threads)
+    rng = np.random.default_rng(seed + 1)
+    rec, _ = od.step(rng.integers(0, arch.vocab, prompt).astype(np.uint32), 0, logits=False)
+    rec, _ = od.step([1], prompt)
+    tok = rec[0]
+    t0 = time.perf_counter()
+    for i in range(steps):
+        rec, _ = od.step([tok], prompt + 1 + i)
+        tok = rec[0]
+    el = time.perf_counter() - t0
+    od.close()
+    return {"value": round(steps / el, 2), "unit": "tok/s", "cores": od.threads, "kind": "port",
+            "sample": f"{arch.name} decode of one sequence, {steps} steps after {prompt + 1} positions, oracle, "
+                      f"{od.threads} threads, {el:.1f} s"}
 
 
 def cpu_sample_items(fraction=1.0):
@@ -787,6 +914,21 @@ def sweep_bench(iters=20, flags=0, ms=None, formats=(8, 2, 14), head=True):
     return {"workload": "configs[1]: Qwen3-shape product sweep", "form": form, "results": rows_out}
 
 
+def sweep_summary(sweep):
+    """The sweep's rows with each one's roofline fraction: HBM for M = 16
+    (weights dominate the bytes), the sustained tensor peak for the others
+    (their exact forms run on the CUDA cores, so the fraction says how far
+    the exact order is from the tensor cores)."""
+    peaks = read_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tensor = peaks.get("bf16_tflops_sustained", 1370.0)
+    for r in sweep["results"]:
+        r["frac_hbm"] = round(r["gbs"] / hbm, 4)
+        r["frac_tensor_sustained"] = round(r["tflops"] / tensor, 4)
+    sweep["peak_source"] = "measured" if peaks else "fallback"
+    return sweep
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -798,6 +940,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-batch", action="store_true", help="skip the Gemma batched decode (configs[4])")
+    ap.add_argument("--no-configs", action="store_true", help="skip configs[0], the M=16/128 sweep and configs[3]")
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--batch-prompt", type=int, default=1024)
     ap.add_argument("--case", default=None, help="profile one product (format:rows:K) or 'decode'")

@@ -41,8 +41,13 @@ def _headers_digest() -> str:
 
 
 def _compile(src: str, digest: str) -> str:
-    obj = os.path.join(OBJ, os.path.basename(src) + "." + digest + ".o")
-    if os.path.exists(obj) and os.path.getmtime(obj) >= os.path.getmtime(src):
+    # An object is named by the digest of its own source, every header and
+    # the flags: a name that exists was compiled from exactly these bytes,
+    # whatever the files' times say (a copy of the tree keeps no mtimes).
+    with open(src, "rb") as fh:
+        own = hashlib.sha256(digest.encode() + fh.read()).hexdigest()[:16]
+    obj = os.path.join(OBJ, os.path.basename(src) + "." + own + ".o")
+    if os.path.exists(obj):
         return obj
     cmd = [NVCC, *NVCC_FLAGS, "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -62,13 +67,18 @@ def build(verbose: bool = False) -> str:
     for f in os.listdir(OBJ):
         if f.endswith(".o") and f not in keep:
             os.remove(os.path.join(OBJ, f))
-    newest = max(os.path.getmtime(o) for o in objs)
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
+    # The library is relinked unless its stamp names exactly these objects.
+    stamp = LIB + ".objects"
+    want = "\n".join(sorted(keep))
+    have = open(stamp).read() if os.path.exists(stamp) and os.path.exists(LIB) else None
+    if have != want:
         cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
                *objs, "-o", LIB]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        with open(stamp, "w") as fh:
+            fh.write(want)
     if verbose:
         print(LIB)
     return LIB

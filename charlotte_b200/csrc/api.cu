@@ -10,13 +10,16 @@
 #include "api_common.h"
 #include "charlotte_b200.h"
 #include "matmul.h"
+#include "tma.cuh"
 
 namespace cb {
 
 namespace {
 thread_local std::string g_error;
-// One word a device: set by a kernel whose bounded wait ran out.
-__device__ unsigned int g_fault_word;
+// Two words a device: [0] set by a kernel whose bounded wait ran out; [1]
+// the polls of a first wait on a copy when a test shortened them
+// (cb_debug_spin_limit), else 0.
+__device__ unsigned int g_fault_word[2];
 }
 
 int fail(int status, const char* format, ...) {
@@ -66,6 +69,13 @@ unsigned int* fault_word() {
 }  // namespace cb
 
 extern "C" {
+
+int cb_debug_spin_limit(uint32_t polls) {
+    unsigned int* w = cb::fault_word();
+    if (!w) return cb::fail(CB_ERROR_STEP, "cb_debug_spin_limit: no CUDA device");
+    const cudaError_t e = cudaMemcpy(w + 1, &polls, sizeof polls, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? CB_OK : cb::fail_cuda(e, "cb_debug_spin_limit");
+}
 
 int cb_fault_check(unsigned int* faults) {
     unsigned int* w = cb::fault_word();

@@ -28,6 +28,12 @@ int sm_count();
 // bits in it; cb_fault_check reads and clears it.
 unsigned int* fault_word();
 
+// cb_select's preconditions, shared by cb_select_run and
+// cb_select_run_static: `who` names the entry point in the message; with
+// own_scratch the caller's partials and ticket are not required (the entry
+// point brings its own). CB_OK or CB_ERROR_INVALID.
+int select_arguments(const cb_select* s, const char* who, bool own_scratch);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace cb

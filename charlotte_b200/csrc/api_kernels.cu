@@ -20,6 +20,22 @@ bool head_dim_ok(uint32_t d) { return d == 64 || d == 128 || d == 256; }
 
 }  // namespace
 
+namespace cb {
+
+int select_arguments(const cb_select* s, const char* who, bool own_scratch) {
+    if (!s || !s->logits || !s->candidates || (!s->sampled && !s->candidates_only))
+        return fail(CB_ERROR_INVALID, "%s: null argument", who);
+    if (!own_scratch && (!s->partials || !s->ticket)) return fail(CB_ERROR_INVALID, "%s: null argument", who);
+    if (s->rows > 1 && s->logits_stride < s->count)
+        return fail(CB_ERROR_INVALID, "%s: rows overlap (logits_stride below count)", who);
+    if (static_cast<uint64_t>(s->id_offset) + s->count > 0xFFFFFFFFull)
+        return fail(CB_ERROR_INVALID, "%s: ids past 2^32 - 1", who);
+    if (s->count == 0 || s->count > 262144) return fail(CB_ERROR_INVALID, "%s: %u entries (1 to 262,144)", who, s->count);
+    return CB_OK;
+}
+
+}  // namespace cb
+
 extern "C" {
 
 int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream) {
@@ -117,14 +133,7 @@ uint32_t cb_select_tiles(uint32_t count) { return select_tiles(count); }
 uint32_t cb_select_tickets(uint32_t count) { return 1u + (select_tiles(count) + 15u) / 16u; }
 
 int cb_select_run(const cb_select* s, uint32_t flags, void* stream) {
-    if (!s || !s->logits || !s->partials || !s->ticket || !s->candidates || (!s->sampled && !s->candidates_only))
-        return fail(CB_ERROR_INVALID, "cb_select_run: null argument");
-    if (s->rows > 1 && s->logits_stride < s->count)
-        return fail(CB_ERROR_INVALID, "cb_select_run: rows overlap (logits_stride below count)");
-    if (static_cast<uint64_t>(s->id_offset) + s->count > 0xFFFFFFFFull)
-        return fail(CB_ERROR_INVALID, "cb_select_run: ids past 2^32 - 1");
-    if (s->count == 0 || s->count > 262144)
-        return fail(CB_ERROR_INVALID, "cb_select_run: %u entries (1 to 262,144)", s->count);
+    if (int rc = select_arguments(s, "cb_select_run", false)) return rc;
     return launched(select_run(*s, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_select_run");
 }
 

@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     const uint32_t G = geo.G;
     const uint32_t kvh = blockIdx.x;
     const uint32_t rt = blockIdx.z;
+    const uint32_t spin = spin_limit_of(fault);   // read early: off the first wait's path
     // Batched decode: this tile's one row is its sequence's, over its cache.
     const size_t cache_at = seqs ? static_cast<size_t>(rt) * a.sequence_stride : 0u;
     const uint16_t* kc = a.key_cache + cache_at;
@@ -343,7 +344,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             const uint32_t j_hi = min(key0 + kChunk, staged_new ? p_last : p_last + 1u);
             stage_keys(a, kc, vc, ks, vs, key0, j_lo, max(j_lo, j_hi), kvh, d, &kv_bar, true);
         }
-        if (!__syncthreads_and(mbar_wait(&kv_bar, kv_phase, fault))) {
+        if (!__syncthreads_and(mbar_wait(&kv_bar, kv_phase, fault, spin))) {
             // A copy did not land in time (the fault word is set; the whole
             // CTA agrees): wait once more, bounded, so none is left writing
             // this CTA's shared memory, and stop (the step reports failure).

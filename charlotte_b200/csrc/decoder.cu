@@ -35,7 +35,6 @@
 
 #include "api_common.h"
 #include "charlotte_b200.h"
-#include "decode_fused.h"
 #include "formats.cuh"
 #include "kernels.h"
 #include "matmul.h"
@@ -122,12 +121,7 @@ struct cb_decoder {
     std::vector<uint32_t> seq_next;   // each sequence's position after its last step
     std::vector<uint8_t> seq_drawn;   // whether a sequence's last step drew a token
     bool tensor_prefill = false;  // CB_DECODER_TENSOR_PREFILL
-    // The fused decode step (decode_fused.cu): one sequence, one token.
-    bool fused = false;
-    cb::FusedPlan fplan{};
-    cb::FusedLayer* flayers = nullptr;   // device array
     float* hidden2 = nullptr;
-    unsigned int* fbar = nullptr;
     void* tensor_scratch = nullptr;
     uint64_t tensor_scratch_bytes = 0;
 };
@@ -418,158 +412,6 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
 
 bool same_sampling(const cb_sampling& a, const cb_sampling& b) { return std::memcmp(&a, &b, sizeof a) == 0; }
 
-// One token's step through the fused launch (gather, layers, final norm),
-// then the head, the selection and the draw as in enqueue_step.
-int enqueue_fused(cb_decoder* d, bool fed, const cb_sampling& s) {
-    const cb_model& m = d->model;
-    FusedArgs f{};
-    f.layers = d->flayers;
-    f.n_layers = m.layers;
-    f.H = m.hidden;
-    f.Hq = m.query_heads;
-    f.Hkv = m.kv_heads;
-    f.d = m.head_dim;
-    f.ffn = m.ffn;
-    f.halves = m.halves;
-    f.epsilon = m.epsilon;
-    f.embed_scale = m.embed_scale;
-    f.scale_log2e = static_cast<float>(static_cast<double>(m.attention_scale) * 1.4426950408889634);
-    f.factors = d->factors;
-    f.embed_piece = d->token_embd.piece;
-    f.embed_format = d->token_embd.format;
-    f.embed_blocks = d->token_embd.blocks;
-    f.output_norm = d->output_norm;
-    f.hidden[0] = d->hidden;
-    f.hidden[1] = d->hidden2;
-    f.out = d->out;
-    f.q = d->q;
-    f.k = d->k;
-    f.v = d->v;
-    f.att = d->att;
-    f.act = d->act;
-    f.normed = d->normed;
-    f.partials = d->partials;
-    f.stats = d->stats;
-    f.sampled = d->sampled;
-    f.ids = d->ids;
-    f.fed = fed ? 1u : 0u;
-    f.state = d->state;
-    f.bar = d->fbar;
-    f.fault = fault_word();
-    f.stage_bytes = d->fplan.stage_bytes;
-    f.x_stage_floats = d->fplan.x_stage_floats;
-    if (int rc = launched(fused_step_run(f, d->fplan, d->stream), "step: fused layers")) return rc;
-    {
-        const DevWeight& head = d->output.piece ? d->output : d->token_embd;
-        float* outs[3] = {d->logits, nullptr, nullptr};
-        const uint32_t strides[3] = {m.vocab, 0, 0};
-        if (int rc = product(d, {&head}, CB_EPILOGUE_WRITE, d->normed, m.hidden, 1, outs, strides)) return rc;
-    }
-    cb_select sel{};
-    sel.logits = d->logits;
-    sel.count = m.vocab;
-    sel.partials = d->sel_partials;
-    sel.ticket = d->sel_ticket;
-    sel.candidates = d->candidates;
-    sel.sampled = d->sampled;
-    sel.position = d->state;
-    sel.tokens = 1;
-    sel.seed0 = s.seed0;
-    sel.seed1 = s.seed1;
-    sel.top_k = s.top_k ? s.top_k : 1;
-    sel.temperature = s.temperature;
-    sel.top_p = s.top_p;
-    sel.min_p = s.min_p;
-    sel.log_min_p = s.min_p > 0.0f ? std::log(s.min_p) : 0.0f;
-    sel.rows = 1;
-    sel.logits_stride = m.vocab;
-    return launched(select_run(sel, d->stream, true), "step: select");
-}
-
-uint32_t row_stage_of(uint32_t format, uint32_t columns) {
-    const uint32_t G = columns / 32u;
-    switch (format) {
-        case CB_Q4_0: return RowStreams<Q4_0>::row_stage(G);
-        case CB_Q8_0: return RowStreams<Q8_0>::row_stage(G);
-        case CB_Q4_1: return RowStreams<Q4_1>::row_stage(G);
-        case CB_BF16: return RowStreams<BF16>::row_stage(G);
-        default: return RowStreams<Q6_K>::row_stage(G);
-    }
-}
-
-MatmulArgs fused_product(const cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue,
-                         std::initializer_list<float*> outs) {
-    MatmulArgs a{};
-    const DevWeight* first = *ws.begin();
-    a.format = first->format;
-    a.columns = first->cols;
-    a.members = static_cast<uint32_t>(ws.size());
-    a.epilogue = epilogue;
-    a.activation = d->model.activation;
-    a.tokens = 1;
-    uint32_t i = 0, total = 0;
-    for (const DevWeight* w : ws) {
-        a.member[i++] = {w->piece, w->blocks, 0, w->rows, 0};
-        total += w->rows;
-    }
-    a.total_rows = epilogue == CB_EPILOGUE_GATED ? first->rows : total;
-    i = 0;
-    for (float* o : outs) a.out[i++] = o;
-    a.fault = fault_word();
-    return a;
-}
-
-// The fused step's plan and its per-layer arguments on the device; false
-// (the separate kernels serve) when its shared memory does not fit.
-int setup_fused(cb_decoder* d) {
-    const cb_model& m = d->model;
-    const uint32_t H = m.hidden, qd = m.query_heads * m.head_dim;
-    // The fused step decodes Q4_0, Q8_0 and Q6_K; a model with other weights
-    // (Q4_1, BF16) or another table format keeps the separate kernels.
-    const auto fused_format = [](uint32_t f) { return f == CB_Q4_0 || f == CB_Q8_0 || f == CB_Q6_K; };
-    if (!fused_format(d->token_embd.format)) return CB_OK;
-    for (uint32_t l = 0; l < m.layers; ++l) {
-        const DevLayer& L = d->layers[l];
-        for (const DevWeight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
-            if (!fused_format(w->format)) return CB_OK;
-    }
-    uint32_t max_cols = std::max(std::max(H, qd), m.ffn), row_stage = 0, gated_stage = 0;
-    std::vector<FusedLayer> host(m.layers);
-    for (uint32_t l = 0; l < m.layers; ++l) {
-        const DevLayer& L = d->layers[l];
-        for (const DevWeight* w : {&L.q, &L.k, &L.v, &L.o, &L.down})
-            row_stage = std::max(row_stage, row_stage_of(w->format, w->cols));
-        gated_stage = std::max(gated_stage, row_stage_of(L.gate.format, L.gate.cols));
-        FusedLayer& F = host[l];
-        F.qkv = fused_product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, {d->q, d->k, d->v});
-        F.o = fused_product(d, {&L.o}, CB_EPILOGUE_WRITE, {d->out});
-        F.gate_up = fused_product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, {d->act});
-        F.down = fused_product(d, {&L.down}, CB_EPILOGUE_WRITE, {d->out});
-        F.attn_norm = L.attn_norm;
-        F.ffn_norm = L.ffn_norm;
-        F.post_attn_norm = L.post_attn_norm;
-        F.post_ffn_norm = L.post_ffn_norm;
-        F.q_norm = L.q_norm;
-        F.k_norm = L.k_norm;
-        F.turns = L.turns;
-        F.key_cache = L.key_cache;
-        F.value_cache = L.value_cache;
-        F.window = L.window;
-        F.slots = L.slots;
-    }
-    int dev = 0;
-    cudaGetDevice(&dev);
-    d->fplan = fused_plan(max_cols, row_stage, gated_stage, m.head_dim, d->sms, dev);
-    if (d->fplan.warps == 0) return CB_OK;   // the separate kernels serve
-    if (int rc = dalloc(d, &d->flayers, m.layers)) return rc;
-    if (int rc = dalloc(d, &d->fbar, 2)) return rc;
-    cudaError_t e = cudaMemcpy(d->flayers, host.data(), m.layers * sizeof(FusedLayer), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset(d->fbar, 0, 2 * sizeof(unsigned int));
-    if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_create: fused step");
-    d->fused = true;
-    return CB_OK;
-}
-
 // Captures one decode step (one token, logits and draw) as a graph: fed
 // (the token is the last draw) and closed by `advance` for generate, or
 // reading its token from the ids buffer for a host-driven step.
@@ -577,11 +419,9 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return fail_cuda(e, "decoder: capture");
-    // One token of the one sequence (fused when the plan fits), or (several
-    // sequences) a batched step.
+    // One token of the one sequence, or (several sequences) a batched step.
     const bool batch = d->sequences > 1;
-    int rc = (!batch && d->fused) ? enqueue_fused(d, fed, smp)
-                                  : enqueue_step(d, batch ? d->sequences : 1u, fed, true, smp, batch ? -1 : 0);
+    int rc = enqueue_step(d, batch ? d->sequences : 1u, fed, true, smp, batch ? -1 : 0);
     if (rc == CB_OK && fed) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1);
@@ -602,6 +442,26 @@ int capture_step(cb_decoder* d, bool fed, const cb_sampling& smp, cudaGraphExec_
     e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     return e == cudaSuccess ? CB_OK : fail_cuda(e, "decoder: instantiate");
+}
+
+// The end of a synchronous step: the fault word read and cleared. When a
+// bounded wait ran out during the step, a CTA that gave up may not have
+// taken its ticket, which would leave a ticket word part-counted and let
+// the next step's fold start early; so the ticket words are cleared before
+// the failure is reported, and the next step starts clean.
+int finish_step(cb_decoder* d) {
+    const int rc = cb_fault_check(nullptr);
+    if (rc == CB_OK) return rc;
+    const uint32_t S = d->sequences;
+    const uint32_t tickets = std::max(cb_attention_tickets(d->rows, d->model.query_heads, d->model.kv_heads),
+                                      S * d->model.kv_heads);
+    cudaError_t e = cudaMemsetAsync(d->tickets, 0, tickets * sizeof(unsigned int), d->stream);
+    if (e == cudaSuccess)
+        e = cudaMemsetAsync(d->sel_ticket, 0,
+                            static_cast<size_t>(S) * cb_select_tickets(d->model.vocab) * sizeof(unsigned int),
+                            d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    return e == cudaSuccess ? rc : fail_cuda(e, "decoder: clearing the tickets after a failed step");
 }
 
 }  // namespace
@@ -700,8 +560,8 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
     if (int rc = dalloc(d, &d->sampled, static_cast<size_t>(S) * 4)) return bail(rc);
     if (int rc = dalloc(d, &d->ids, T)) return bail(rc);
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
-    if (S == 1 && (flags & CB_DECODER_FUSED))
-        if (int rc = setup_fused(d)) return bail(rc);
+    if (flags & ~static_cast<uint32_t>(CB_DECODER_TENSOR_PREFILL))
+        return bail(fail(CB_ERROR_INVALID, "cb_decoder_create: unknown flags 0x%x", flags));
     if (flags & CB_DECODER_TENSOR_PREFILL) {
         const uint32_t widest = std::max<uint32_t>(std::max<uint32_t>(H, static_cast<uint32_t>(qd)), m->ffn);
         d->tensor_scratch_bytes = cb_matmul_scratch_bytes(CB_MATMUL_TENSOR, T, widest);
@@ -777,7 +637,7 @@ int cb_decoder_step_sequence(cb_decoder* d, uint32_t seq, const uint32_t* ids_ho
     d->seq_next[seq] = position + tokens;
     d->has_step = logits != 0;
     d->next_position = position + tokens;
-    return cb_fault_check(nullptr);
+    return finish_step(d);
 }
 
 int cb_decoder_step_batch(cb_decoder* d, const uint32_t* ids_host, uint32_t position, const cb_sampling* s,
@@ -806,7 +666,7 @@ int cb_decoder_step_batch(cb_decoder* d, const uint32_t* ids_host, uint32_t posi
     }
     d->has_step = true;
     d->next_position = position + 1;
-    return cb_fault_check(nullptr);
+    return finish_step(d);
 }
 
 int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uint32_t* tokens_host,
@@ -870,7 +730,7 @@ int cb_decoder_generate(cb_decoder* d, uint32_t steps, const cb_sampling* s, uin
     if (e != cudaSuccess) return fail_cuda(e, "cb_decoder_generate");
     d->next_position += steps;
     for (auto& p : d->seq_next) p = d->next_position;
-    return cb_fault_check(nullptr);
+    return finish_step(d);
 }
 
 int cb_decoder_step_body(cb_decoder* d, const uint32_t* ids_host, uint32_t position) {

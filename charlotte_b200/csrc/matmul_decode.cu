@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     const uint32_t batches = batch_count<R>(a);
     const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
+    const uint32_t spin = spin_limit_of(a.fault);   // read early: off the first wait's path
 
     // Shared memory: x (range-major, each float doubled), then per warp: 2
     // barriers, range sums, 2 stages.
@@ -263,10 +264,11 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     for (uint32_t b = first; b < batches; b += stride, ++i) {
         const uint32_t s = i & 1u;
         uint8_t* stage = stages + s * stage_bytes;
-        if (!mbar_wait(&bars[s], (i >> 1) & 1u, a.fault)) {
-            // A copy did not land in time: the fault word is set. Wait (bounded)
-            // for the other stage's copy so none is left writing this CTA's
-            // shared memory, then leave.
+        if (!mbar_wait(&bars[s], (i >> 1) & 1u, a.fault, spin)) {
+            // A copy did not land in time: the fault word is set. Wait (with
+            // the full bound) for this stage's copy and the other stage's so
+            // none is left writing this CTA's shared memory, then leave.
+            mbar_wait(&bars[s], (i >> 1) & 1u, nullptr);
             if (b + stride < batches) mbar_wait(&bars[s ^ 1u], ((i + 1) >> 1) & 1u, nullptr);
             return;
         }
@@ -418,6 +420,7 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     const uint32_t batches = batch_count<R>(a);
     const uint32_t stride = gridDim.x * W;
     const bool gated = a.epilogue == kGated;
+    const uint32_t spin = spin_limit_of(a.fault);   // read early: off the first wait's path
 
     float* xs = reinterpret_cast<float*>(smem);
     const uint32_t x_bytes = MT / 2 * pair_floats * 4u;
@@ -478,7 +481,8 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     for (uint32_t b = first; b < batches; b += stride, ++it) {
         const uint32_t s = it & 1u;
         uint8_t* stage = stages + s * stage_bytes;
-        if (!mbar_wait(&bars[s], (it >> 1) & 1u, a.fault)) {
+        if (!mbar_wait(&bars[s], (it >> 1) & 1u, a.fault, spin)) {
+            mbar_wait(&bars[s], (it >> 1) & 1u, nullptr);
             if (b + stride < batches) mbar_wait(&bars[s ^ 1u], ((it + 1) >> 1) & 1u, nullptr);
             return;
         }

@@ -66,8 +66,7 @@ int scratch_address(uint32_t** out) {
 extern "C" {
 
 int cb_select_run_static(const cb_select* s, uint32_t flags, void* stream) {
-    if (!s || !s->logits || !s->candidates || !s->sampled)
-        return cb::fail(CB_ERROR_INVALID, "cb_select_run_static: null argument");
+    if (int rc = cb::select_arguments(s, "cb_select_run_static", true)) return rc;
     if (s->partials || s->ticket)
         return cb::fail(CB_ERROR_INVALID,
                         "cb_select_run_static: partials and ticket must be NULL (this entry point uses its own scratch)");

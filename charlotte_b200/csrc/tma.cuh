@@ -65,10 +65,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// The polls a kernel's first wait on a copy may take: the word after the
+// device's fault word holds a shorter bound when a test set one
+// (cb_debug_spin_limit, so a wait can be made to run out), else 0 for the
+// full bound. Read at run time, so a captured graph follows it too.
+__device__ __forceinline__ uint32_t spin_limit_of(const unsigned int* fault) {
+    const uint32_t v = fault ? fault[1] : 0u;
+    return v ? v : kSpinLimit;
+}
+
 // Waits for the phase of `parity` to complete; false (and the fault word
-// set) if it did not within the bound.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* fault) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+// set) if it did not within `limit` polls. The wait that drains a CTA's
+// copies before it leaves always takes the full bound.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* fault,
+                                          uint32_t limit = kSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (fault) atomicOr(fault, kFaultTimeout);
     return false;

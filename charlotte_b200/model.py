@@ -238,7 +238,7 @@ def to_c(model: Model):
 class Decoder:
     """A model uploaded through the C ABI; steps run on the GPU."""
 
-    def __init__(self, model: Model, max_step_tokens: int = 512, tensor_prefill: bool = False, fused: bool = False):
+    def __init__(self, model: Model, max_step_tokens: int = 512, tensor_prefill: bool = False):
         L = _lib()
         L.cb_decoder_create.restype = ctypes.c_int
         L.cb_decoder_create.argtypes = [ctypes.POINTER(CModel), ctypes.c_uint32, ctypes.c_uint32,
@@ -258,7 +258,7 @@ class Decoder:
         cm, self._layers = to_c(model)
         self._cm = cm
         h = ctypes.c_void_p()
-        flags = (1 if tensor_prefill else 0) | (2 if fused else 0)   # CB_DECODER_TENSOR_PREFILL, CB_DECODER_FUSED
+        flags = 1 if tensor_prefill else 0   # CB_DECODER_TENSOR_PREFILL
         _check(L.cb_decoder_create(ctypes.byref(cm), max_step_tokens, flags, ctypes.byref(h)))
         self.handle = h
 

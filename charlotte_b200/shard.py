@@ -138,14 +138,28 @@ class SplitHead:
             mine = self.sampled_all[self.rank * self.local:(self.rank + 1) * self.local]
             self.local_sampled().copy_(mine)
 
-    def step(self, position: int, ids=None, sampling=None):
-        """One batched step across ranks through torch.distributed."""
+    def step(self, position: int, ids=None, sampling=None, timing=None):
+        """One batched step across ranks through torch.distributed. With
+        `timing` (a list), CUDA events around the two all-gathers on the
+        decoder's stream are appended to it: (before rows, after rows,
+        before candidates, after candidates)."""
         import torch
         import torch.distributed as dist
         self.body(position, ids)
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timing is not None else None
         with torch.cuda.stream(self.stream):
+            if events:
+                events[0].record(self.stream)
             dist.all_gather_into_tensor(self.normed_all, self.local_normed().contiguous())
+            if events:
+                events[1].record(self.stream)
             self.shard_candidates()
+            if events:
+                events[2].record(self.stream)
             dist.all_gather_into_tensor(self.cand_all, self.cand)
+            if events:
+                events[3].record(self.stream)
             self.merge(position, sampling)
+        if events:
+            timing.append(events)
         return self.sampled_all

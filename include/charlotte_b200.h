@@ -65,6 +65,16 @@ CB_API int cb_device_sm_count(void);
  * otherwise CB_ERROR_STEP, with the bits in *faults (may be NULL). */
 CB_API int cb_fault_check(unsigned int* faults);
 
+/* A test hook for failure detection (no counterpart in the reference): on
+ * the current device, the first wait of each kernel on a bulk copy (the
+ * decode products and decode attention) gives up after `polls` polls
+ * instead of the full bound, so a test can make a wait run out — the kernel
+ * records the timeout in the fault word, drains its copies (with the full
+ * bound) and returns — without any fault. 0 restores the full bound. Read
+ * by the kernels when they run (captured graphs included); set it only
+ * between steps. Synchronous. */
+CB_API int cb_debug_spin_limit(uint32_t polls);
+
 /* ---- matrix products --------------------------------------------------------
  * Replaces the matmul kernel's entry points decode_write, decode_qkv,
  * decode_gated, decode_gated_input (src/core/kernels/matmul/matmul.wgsl
@@ -401,14 +411,7 @@ enum {
      * form (CB_MATMUL_TENSOR, tolerance tier) instead of the exact forms;
      * shorter steps (decode) and the head's last-token product stay exact.
      * No counterpart in the reference. */
-    CB_DECODER_TENSOR_PREFILL = 1u,
-    /* One-token steps of a one-sequence decoder run as one persistent
-     * cooperative launch: the gather and every layer, stages separated by
-     * grid-wide barriers, the same bits as the separate launches. Off by
-     * default: on B200 it measures slower (1.76 ms a Qwen3-0.6B token
-     * against 1.31 ms for the separate launches under programmatic
-     * dependent launch). No counterpart in the reference. */
-    CB_DECODER_FUSED = 2u
+    CB_DECODER_TENSOR_PREFILL = 1u
 };
 
 /* Uploads the model and allocates its caches and working buffers for steps

@@ -30,12 +30,27 @@ c_u16p = ctypes.POINTER(ctypes.c_uint16)
 c_u32p = ctypes.POINTER(ctypes.c_uint32)
 
 
+def reference_root() -> str | None:
+    """The reference project's root: $CHARLOTTE_REFERENCE, else the
+    `reference_path` BASELINE.json records; None where neither names an
+    existing directory (a GPU box, which carries the prebuilt oracle/_ref)."""
+    root = os.environ.get("CHARLOTTE_REFERENCE")
+    if not root:
+        import json
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as fh:
+                root = json.load(fh).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(root) else None
+
+
 def build() -> None:
     """Compile liboracle.so (and oracle/_ref when the reference is present)."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
-    if os.path.isdir(os.environ.get("CHARLOTTE_REFERENCE", "/root/reference")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref",
-                        "REF=" + os.environ.get("CHARLOTTE_REFERENCE", "/root/reference")], check=True)
+    root = reference_root()
+    if root:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + root], check=True)
 
 
 def ptr(a: np.ndarray, ctype):

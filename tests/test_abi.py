@@ -74,3 +74,26 @@ def test_piece_from_stored_is_the_device_layout(fmt):
     L.cb_piece_from_stored.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
     assert L.cb_piece_from_stored(fmt, stored.ctypes.data, blocks, out.ctypes.data) == 0
     assert np.array_equal(out, O.to_piece(fmt, stored))
+
+
+@pytest.mark.parametrize("fn", ["cb_select_run", "cb_select_run_static"])
+def test_select_refuses_ids_past_32_bits(fn):
+    """Both selection entry points share one argument check: ids of a
+    vocabulary shard (id_offset + count) past 2^32 - 1 would wrap into the
+    padding id, so they are refused before anything runs (no GPU)."""
+    import ctypes
+    s = cb.Select()
+    s.logits, s.candidates, s.sampled = 16, 16, 16
+    if fn == "cb_select_run":
+        s.partials, s.ticket = 16, 16
+    s.count = 1024
+    s.id_offset = 0xFFFFFFFF - 1000
+    rc = getattr(cb.lib(), fn)(ctypes.byref(s), 0, None)
+    assert rc == cb.ERROR_INVALID and "2^32" in cb.last_error()
+    # candidates_only with no record is accepted by the checks of both
+    s.id_offset = 0
+    s.count = 0
+    s.sampled = 0
+    s.candidates_only = 1
+    rc = getattr(cb.lib(), fn)(ctypes.byref(s), 0, None)
+    assert rc == cb.ERROR_INVALID and "entries" in cb.last_error()

@@ -71,3 +71,31 @@ def test_batch_step_from_host_ids(cuda):
         np.testing.assert_array_equal(rows[s], dec.logits())
         assert int(recs[s, 0]) == int(rec[0])
         dec.close()
+
+
+def test_gemma_3_1b_batch_of_64_rows_match_sequences_alone(cuda):
+    """configs[4]'s shape at full size: 64 sequences batched (each with its
+    own caches, a windowed layer's ring of 512 + 64 slots wrapping over the
+    620 positions), 8 batched greedy steps; rows 0, 21, 42 and 63 give the
+    tokens and logits of their sequences decoded alone (themselves bit-exact
+    with the oracle at full size)."""
+    m = M.synthesize(M.gemma_3_1b(context=1024), seed=23)
+    rng = np.random.default_rng(9)
+    S, P, steps = 64, 612, 8
+    prompts = [rng.integers(0, m.arch.vocab, P).astype(np.uint32) for _ in range(S)]
+    bd = M.BatchDecoder(m, S, max_step_tokens=64)
+    firsts = [int(bd.prefill_sequence(s, p)[0]) for s, p in enumerate(prompts)]
+    toks, failed = bd.generate(steps)
+    assert not failed.any()
+    rows = (0, 21, 42, 63)
+    last = {r: bd.logits_row(r) for r in rows}
+    bd.close()
+    for r in rows:
+        dec = M.Decoder(m, max_step_tokens=64)
+        rec = dec.prefill(prompts[r])
+        assert firsts[r] == int(rec[0])
+        want, wf = dec.generate(steps)
+        assert not wf.any()
+        assert toks[:, r].tolist() == want.tolist(), r
+        np.testing.assert_array_equal(last[r], dec.logits())
+        dec.close()

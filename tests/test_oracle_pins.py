@@ -210,3 +210,126 @@ def test_exp2_and_exp_against_libm():
         e = math.exp(float(x))
         worst = max(worst, abs(b - e) / e)
     assert worst2 < 4e-7 and worst < 4e-7
+
+
+# ---- the rope turns and the draw, against the reference's own code ----------
+
+@needs_ref
+@pytest.mark.parametrize("base", [1e6, 5e5, 1e4])
+@pytest.mark.parametrize("d", [64, 128, 256, 512])
+def test_rope_turns_equal_the_reference_launchers(base, d):
+    """src/core/kernels/rope/rope.cpp:76-87 (constants_of), read back from the
+    reference's rope_launch as tests/kernels_rope_test.cpp:48 reads it: the
+    oracle's turns and the library's (cb_rope_turns, a host function) are
+    the same bits, and the unused slots are zero."""
+    import charlotte_b200 as cb
+    ref = np.zeros(256, np.float32)
+    REF.ref_rope_turns.argtypes = [ctypes.c_float, ctypes.c_uint32, ctypes.POINTER(ctypes.c_float)]
+    assert REF.ref_rope_turns(base, d, O.ptr(ref, ctypes.c_float)) == 0
+    assert not ref[d // 2:].any()
+    assert np.array_equal(O.rope_turns(base, d).view(np.uint32), ref[: d // 2].view(np.uint32))
+    assert np.array_equal(cb.rope_turns(base, d).view(np.uint32), ref[: d // 2].view(np.uint32))
+
+
+def _candidates(seed):
+    """64 candidates, best first, as the reference's draw test makes them
+    (tests/gpu/draw_test.cpp:90-101): logits falling by up to 0.25 a step
+    from 5, tokens below Qwen3's vocabulary."""
+    state = np.uint32(seed)
+    logit = np.float32(5.0)
+    logits, tokens = [], []
+    for _ in range(64):
+        state = np.uint32((int(state) * 1664525 + 1013904223) & 0xFFFFFFFF)
+        logit = np.float32(logit - np.float32(((int(state) >> 8) % 1000) / np.float32(4000.0)))
+        logits.append(logit)
+        tokens.append(((int(state) >> 4) % 151936))
+    return np.array(logits, np.float32), np.array(tokens, np.uint32)
+
+
+def _pairs(logits, tokens):
+    pairs = np.empty(128, np.uint32)
+    pairs[0::2] = logits.view(np.uint32)
+    pairs[1::2] = tokens
+    return pairs
+
+
+def _ref_draw(logits, tokens, s, u):
+    chosen = ctypes.c_uint32()
+    margin = ctypes.c_double()
+    REF.ref_reference_draw.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_uint32),
+                                       ctypes.c_uint32, ctypes.c_float, ctypes.c_uint32, ctypes.c_float,
+                                       ctypes.c_float, ctypes.c_double, ctypes.POINTER(ctypes.c_uint32),
+                                       ctypes.POINTER(ctypes.c_double)]
+    REF.ref_reference_draw(O.ptr(logits, ctypes.c_float), O.ptr(tokens, ctypes.c_uint32), 64, s[0], s[1], s[2],
+                           s[3], u, ctypes.byref(chosen), ctypes.byref(margin))
+    return chosen.value, margin.value
+
+
+def _ref_uniform(seed, position):
+    REF.ref_uniform.restype = ctypes.c_float
+    REF.ref_uniform.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
+    return np.float32(REF.ref_uniform(seed & 0xFFFFFFFF, seed >> 32, position))
+
+
+# (temperature, top_k, top_p, min_p): the reference's draw test's settings
+DRAW_SETTINGS = [(0.8, 40, 0.95, 0.05), (0.6, 20, 0.95, 0.0), (1.0, 64, 0.95, 0.0), (1.5, 64, 1.0, 0.01),
+                 (0.3, 8, 0.5, 0.2)]
+
+
+@needs_ref
+def test_draw_uniform_is_the_reference_philox_bit_for_bit():
+    """tests/gpu/draw_test.cpp:104-125 on the oracle: a step of `tokens`
+    from `position` draws with uniform(seed, position + tokens)."""
+    logits, tokens = _candidates(1)
+    pairs = _pairs(logits, tokens)
+    for seed in (0, 1, 0x0123456789ABCDEF):
+        for position in (0, 1, 2, 1000, 40959, 16777215):
+            rec = O.draw(pairs, position, 1, seed=(seed & 0xFFFFFFFF, seed >> 32), top_k=40, temperature=0.8)
+            assert rec[2] == _ref_uniform(seed, position + 1).view(np.uint32)
+    for n in (2, 17, 512):
+        rec = O.draw(pairs, 100, n, seed=(7, 0), top_k=40, temperature=0.8)
+        assert rec[2] == _ref_uniform(7, 100 + n).view(np.uint32)
+
+
+@needs_ref
+def test_draw_equals_the_reference_f64_draw_given_its_uniform():
+    """tests/gpu/draw_test.cpp:127-152 on the oracle: over five settings and
+    200 positions each, the token drawn is the f64 reference's choice for the
+    same uniform, except where the reference says the decision lies within
+    f32 rounding (margin < 1e-5); those are at most 1% of the draws."""
+    logits, tokens = _candidates(2)
+    pairs = _pairs(logits, tokens)
+    compared = near = 0
+    for s in DRAW_SETTINGS:
+        for position in range(200):
+            rec = O.draw(pairs, position, 1, seed=(42, 0), temperature=s[0], top_k=s[1], top_p=s[2], min_p=s[3])
+            assert rec[1] == 0
+            chosen, margin = _ref_draw(logits, tokens, s, float(rec[2:3].view(np.float32)[0]))
+            if margin < 1e-5:
+                near += 1
+                continue
+            compared += 1
+            assert rec[0] == tokens[chosen], (s, position)
+    assert near * 100 <= compared
+
+
+def test_draw_settings_at_their_edges():
+    """tests/gpu/draw_test.cpp:154-175 on the oracle."""
+    logits, tokens = _candidates(3)
+    pairs = _pairs(logits, tokens)
+    for position in range(20):
+        for s in ((0.0, 40, 0.95, 0.05), (1.0, 1, 1.0, 0.0), (1.0, 64, 0.01, 0.0), (1.0, 64, 1.0, 0.99)):
+            rec = O.draw(pairs, position, 1, seed=(9, 0), temperature=s[0], top_k=s[1], top_p=s[2], min_p=s[3])
+            assert rec[0] == tokens[0]
+    for position in range(50):
+        rec = O.draw(pairs, position, 1, seed=(9, 0), temperature=100.0, top_k=2)
+        assert rec[0] in (tokens[0], tokens[1])
+
+
+def test_non_finite_top_candidate_fails_the_draw():
+    """tests/gpu/draw_test.cpp:177-190 on the oracle: failed = 1, token 0."""
+    for bad in (np.float32("nan"), np.float32("inf")):
+        logits, tokens = _candidates(4)
+        logits[0] = bad
+        rec = O.draw(_pairs(logits, tokens), 0, 1, seed=(1, 0), temperature=0.8, top_k=40, top_p=0.95, min_p=0.05)
+        assert rec[1] == 1 and rec[0] == 0
