@@ -119,7 +119,7 @@ def lib() -> ctypes.CDLL:
         L.cb_fault_check.restype = ctypes.c_int
         L.cb_fault_check.argtypes = [ctypes.POINTER(ctypes.c_uint)]
         L.cb_debug_spin_limit.restype = ctypes.c_int
-        L.cb_debug_spin_limit.argtypes = [ctypes.c_uint32]
+        L.cb_debug_spin_limit.argtypes = [ctypes.c_int32]
         L.cb_matmul_run.restype = ctypes.c_int
         L.cb_matmul_run.argtypes = [ctypes.POINTER(Matmul), ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                     ctypes.POINTER(ctypes.c_void_p * 3), ctypes.POINTER(ctypes.c_uint32 * 3),

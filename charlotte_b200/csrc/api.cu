@@ -17,7 +17,7 @@ namespace cb {
 namespace {
 thread_local std::string g_error;
 // Two words a device: [0] set by a kernel whose bounded wait ran out; [1]
-// the polls of a first wait on a copy when a test shortened them
+// 1 + the polls of a first wait on a copy when a test shortened them
 // (cb_debug_spin_limit), else 0.
 __device__ unsigned int g_fault_word[2];
 }
@@ -70,10 +70,12 @@ unsigned int* fault_word() {
 
 extern "C" {
 
-int cb_debug_spin_limit(uint32_t polls) {
+int cb_debug_spin_limit(int32_t polls) {
     unsigned int* w = cb::fault_word();
     if (!w) return cb::fail(CB_ERROR_STEP, "cb_debug_spin_limit: no CUDA device");
-    const cudaError_t e = cudaMemcpy(w + 1, &polls, sizeof polls, cudaMemcpyHostToDevice);
+    if (polls >= static_cast<int32_t>(cb::kSpinLimit)) polls = -1;
+    const uint32_t word = polls < 0 ? 0u : static_cast<uint32_t>(polls) + 1u;
+    const cudaError_t e = cudaMemcpy(w + 1, &word, sizeof word, cudaMemcpyHostToDevice);
     return e == cudaSuccess ? CB_OK : cb::fail_cuda(e, "cb_debug_spin_limit");
 }
 

@@ -66,12 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // The polls a kernel's first wait on a copy may take: the word after the
-// device's fault word holds a shorter bound when a test set one
+// device's fault word holds 1 + a shorter bound when a test set one
 // (cb_debug_spin_limit, so a wait can be made to run out), else 0 for the
 // full bound. Read at run time, so a captured graph follows it too.
 __device__ __forceinline__ uint32_t spin_limit_of(const unsigned int* fault) {
     const uint32_t v = fault ? fault[1] : 0u;
-    return v ? v : kSpinLimit;
+    return v ? v - 1u : kSpinLimit;
 }
 
 // Waits for the phase of `parity` to complete; false (and the fault word

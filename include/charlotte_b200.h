@@ -67,13 +67,13 @@ CB_API int cb_fault_check(unsigned int* faults);
 
 /* A test hook for failure detection (no counterpart in the reference): on
  * the current device, the first wait of each kernel on a bulk copy (the
- * decode products and decode attention) gives up after `polls` polls
- * instead of the full bound, so a test can make a wait run out — the kernel
- * records the timeout in the fault word, drains its copies (with the full
- * bound) and returns — without any fault. 0 restores the full bound. Read
- * by the kernels when they run (captured graphs included); set it only
- * between steps. Synchronous. */
-CB_API int cb_debug_spin_limit(uint32_t polls);
+ * decode products and decode attention) gives up after `polls` polls (0:
+ * at once, without polling) instead of the full bound, so a test can make a
+ * wait run out — the kernel records the timeout in the fault word, drains
+ * its copies (with the full bound) and returns — without any fault. A
+ * negative value restores the full bound. Read by the kernels when they run
+ * (captured graphs included); set it only between steps. Synchronous. */
+CB_API int cb_debug_spin_limit(int32_t polls);
 
 /* ---- matrix products --------------------------------------------------------
  * Replaces the matmul kernel's entry points decode_write, decode_qkv,
@@ -473,6 +473,132 @@ CB_API int cb_decoder_head(cb_decoder* d, cb_member* head, uint32_t* format, uin
 /* Device pointers of the decoder's working buffers, for callers that feed
  * it from their own kernels: the logits [vocab] and the sampled record [4]. */
 CB_API const float* cb_decoder_device_logits(cb_decoder* d);
+
+/* ---- buffers and programs: the reference's Upload and Program over CUDA ----------
+ * The reference's kernel launchers describe every launch of a graph as a
+ * kernels::Launch (src/core/kernels/interface.h:318-365) over the buffers a
+ * residency plan names; kernels::Program (src/core/kernels/program.h:262-331)
+ * builds them once at load and runs them a step at a time. These entry points
+ * are that Program over CUDA: cb_buffers holds the plan's buffers (what
+ * residency::Upload holds, src/core/residency/upload.h:245-332), cb_launch
+ * is a Launch in plain C, cb_step is the reference's Step byte for byte, and
+ * cb_program builds the launches onto this library's kernels and runs steps
+ * without blocking — at most two outstanding, each one's readback delivered
+ * to its callback in the order the steps were run (program.h:62-70,
+ * src/core/kernels/order.h:30). */
+
+typedef struct cb_buffers cb_buffers;
+/* `count` zeroed device buffers of `sizes` bytes (each 256-byte aligned). */
+CB_API int cb_buffers_create(const uint64_t* sizes, uint32_t count, cb_buffers** out);
+CB_API void cb_buffers_destroy(cb_buffers* b);
+/* Host bytes into / out of buffer `buffer` at `offset` (synchronous). */
+CB_API int cb_buffers_write(cb_buffers* b, uint32_t buffer, uint64_t offset, const void* host, uint64_t bytes);
+CB_API int cb_buffers_read(cb_buffers* b, uint32_t buffer, uint64_t offset, void* host, uint64_t bytes);
+/* The device address of a buffer, or NULL. */
+CB_API void* cb_buffers_device(const cb_buffers* b, uint32_t buffer);
+
+/* The kernels a launch names (the reference's WGSL modules, by the shaders
+ * its launchers embed: shaders::matmul, norm, rope + rope_cache, attention,
+ * gather, topk, draw). */
+enum {
+    CB_KERNEL_UNKNOWN = 0,
+    CB_KERNEL_MATMUL = 1,
+    CB_KERNEL_NORM = 2,
+    CB_KERNEL_ROPE_CACHE = 3,
+    CB_KERNEL_ATTENTION = 4,
+    CB_KERNEL_GATHER = 5,
+    CB_KERNEL_TOPK = 6,
+    CB_KERNEL_DRAW = 7
+};
+enum { CB_ROWS_EVERY_TOKEN = 0, CB_ROWS_LAST_TOKEN = 1 };            /* interface.h Rows      */
+enum { CB_KEY_SPLIT_NONE = 0, CB_KEY_SPLIT_PER_CHUNK = 1, CB_KEY_SPLIT_WHEN_SPLIT = 2 };   /* KeySplit */
+enum { CB_NO_FORMAT = 0xFFFFFFFFu };
+
+/* interface.h Binding: a range of a planned buffer. */
+typedef struct cb_binding {
+    uint32_t buffer;
+    uint32_t reserved;
+    uint64_t offset;
+    uint64_t size;
+} cb_binding;
+
+/* interface.h Override. */
+typedef struct cb_override {
+    const char* name;   /* NUL-terminated */
+    double value;
+} cb_override;
+
+/* interface.h Launch, field for field. */
+typedef struct cb_launch {
+    uint32_t kernel;               /* CB_KERNEL_*                                      */
+    const char* entry_point;       /* NUL-terminated                                   */
+    uint32_t format;               /* GGUF type of the format it unpacks, or CB_NO_FORMAT */
+    uint32_t pack_format;          /* GGUF type of the format it packs, or CB_NO_FORMAT */
+    const uint8_t* constants;      /* binding 1's bytes                                */
+    uint32_t constants_bytes;
+    const cb_binding* bindings;    /* bindings 2 onward                                */
+    uint32_t binding_count;
+    uint32_t invocations_per_row;
+    uint32_t workgroup_size;
+    uint32_t rows;                 /* CB_ROWS_*                                        */
+    const cb_override* overrides;
+    uint32_t override_count;
+    uint32_t rows_per_tile;
+    uint32_t key_split;            /* CB_KEY_SPLIT_*                                   */
+    uint32_t window;
+    uint32_t partial_rows;
+    uint32_t tokens_least, tokens_most;   /* TokenRange                                */
+    uint32_t row_divisor;
+} cb_launch;
+
+/* interface.h Step (64-byte head, then the identifiers), byte for byte. */
+typedef struct cb_step {
+    uint32_t position, tokens, logits, fed;
+    uint32_t seed[2];
+    uint32_t top_k;
+    float temperature, top_p, min_p, log_min_p;
+    uint32_t columns, media, media_token, padding1, padding2;
+    uint32_t ids[512];
+} cb_step;
+
+/* A step's end (program.h StepCallback): its status and message (empty on
+ * success), and its copy of the readback range (NULL for a step that read
+ * none or failed); valid during the call only. */
+typedef void (*cb_step_callback)(int status, const char* message, const void* readback, uint64_t readback_bytes,
+                                 void* userdata);
+/* A profiled step's end (program.h ProfileCallback): as cb_step_callback,
+ * plus the step's device time: its begin and end, and the end of each launch
+ * it ran, in nanoseconds from its begin, by the launch's index in the graph. */
+typedef void (*cb_profile_callback)(int status, const char* message, const void* readback, uint64_t readback_bytes,
+                                    uint64_t begin_ns, uint64_t end_ns, const uint32_t* launch_index,
+                                    const uint64_t* launch_end_ns, uint32_t launches_timed, void* userdata);
+
+typedef struct cb_program cb_program;
+/* Program::build: the launches in the graph's order over `buffers`
+ * (borrowed: they outlive the program), reading back `readback` (NULL: none)
+ * from each step that asks for logits. A launch of a kernel, entry point,
+ * format or variant this backend has no form for is refused, CB_ERROR_BUILD,
+ * with its index and what it names. */
+CB_API int cb_program_build(cb_buffers* buffers, const cb_launch* launches, uint32_t count, const cb_binding* readback,
+                            cb_program** out);
+/* Program::run: enqueues one step and returns; `done` fires from
+ * cb_program_poll once it has finished, in run order. A step past position
+ * 2^24 fails unrun (CB_ERROR_STEP); a third while two are outstanding is
+ * refused at once, its callback fired before this returns. */
+CB_API int cb_program_run(cb_program* p, const cb_step* step, cb_step_callback done, void* userdata);
+/* Program::run_profiled: the first `launches` launches of the step, each
+ * timed by CUDA events on the program's stream; not beside unprofiled steps. */
+CB_API int cb_program_run_profiled(cb_program* p, const cb_step* step, uint32_t launches, cb_profile_callback done,
+                                   void* userdata);
+/* Fires the callbacks of finished steps, oldest first; with `wait`, blocks
+ * until every outstanding step has finished. Returns the callbacks fired. */
+CB_API int cb_program_poll(cb_program* p, uint32_t wait);
+CB_API uint32_t cb_program_outstanding(const cb_program* p);
+CB_API uint32_t cb_program_launch_count(const cb_program* p);
+/* The CUDA stream the program's steps run on. */
+CB_API void* cb_program_stream(const cb_program* p);
+/* Destroys the program: steps still outstanding fire CB_ERROR_CANCELLED. */
+CB_API void cb_program_destroy(cb_program* p);
 
 #ifdef __cplusplus
 }

@@ -97,3 +97,17 @@ def test_select_refuses_ids_past_32_bits(fn):
     s.candidates_only = 1
     rc = getattr(cb.lib(), fn)(ctypes.byref(s), 0, None)
     assert rc == cb.ERROR_INVALID and "entries" in cb.last_error()
+
+
+def test_integration_library_exports_the_boundary():
+    """integration/libcharlotte_program.so (the CUDA Upload and Program built
+    with the reference's loader, plan and launchers) loads beside the
+    library and exports its harness (no GPU: nothing runs)."""
+    import ctypes
+    lib = os.path.join(ROOT, "integration", "libcharlotte_program.so")
+    if not os.path.exists(lib):
+        pytest.skip("the reference sources were absent when it would have been built")
+    cb.lib()
+    L = ctypes.CDLL(lib)
+    for name in ("cbh_open", "cbh_run", "cbh_poll", "cbh_logits", "cbh_profile", "cbh_close"):
+        assert hasattr(L, name)

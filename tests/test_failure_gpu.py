@@ -3,9 +3,9 @@ bounded, and one that runs out sets the device's fault word, drains the
 CTA's copies and returns; the host reads the word (cb_fault_check) and
 reports a failed step (CB_ERROR_STEP), and the context stays usable.
 
-The waits are made to run out on purpose with cb_debug_spin_limit: the
-first wait on each copy then gives up after one poll, long before a copy
-from HBM can land. Nothing faults, traps or hangs; the copies are real and
+The waits are made to run out on purpose with cb_debug_spin_limit(0): the
+first wait on each copy then gives up at once, without polling, before a
+copy from HBM can land. Nothing faults, traps or hangs; the copies are real and
 land (the drain takes the full bound). Afterwards the limit is restored and
 the same work gives the oracle's bits again."""
 import numpy as np
@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def short_waits():
     yield lambda polls: cb.check(cb.lib().cb_debug_spin_limit(polls))
-    cb.lib().cb_debug_spin_limit(0)
+    cb.lib().cb_debug_spin_limit(-1)
 
 
 def test_product_whose_wait_runs_out_reports_a_failed_step(cuda, short_waits):
@@ -37,7 +37,7 @@ def test_product_whose_wait_runs_out_reports_a_failed_step(cuda, short_waits):
     x = torch.from_numpy(xh).cuda()
     y = torch.zeros((1, rows), dtype=torch.float32, device="cuda")
     assert cb.lib().cb_fault_check(None) == cb.OK
-    short_waits(1)
+    short_waits(0)
     cb.matmul(O.Q4_0, K, [(piece, nb, 0, rows, 0)], x, [y])
     torch.cuda.synchronize()
     import ctypes
@@ -46,7 +46,7 @@ def test_product_whose_wait_runs_out_reports_a_failed_step(cuda, short_waits):
     assert bits.value & 1, bits.value
     assert "bounded wait" in cb.last_error()
     # the word was cleared by the read; the full bound again gives the bits
-    short_waits(0)
+    short_waits(-1)
     cb.matmul(O.Q4_0, K, [(piece, nb, 0, rows, 0)], x, [y])
     torch.cuda.synchronize()
     assert cb.lib().cb_fault_check(None) == cb.OK
@@ -64,11 +64,11 @@ def test_decoder_step_after_a_timed_out_step_gives_the_oracle_bits(cuda, short_w
     prompt = rng.integers(0, m.arch.vocab, 12).astype(np.uint32)
     dec = M.Decoder(m, max_step_tokens=16)
     dec.prefill(prompt[:11])
-    short_waits(1)
+    short_waits(0)
     with pytest.raises(cb.CharlotteError) as e:
         dec.step(prompt[11:12], 11)
     assert e.value.status == cb.ERROR_STEP
-    short_waits(0)
+    short_waits(-1)
     rec = dec.step(prompt[11:12], 11)
     got = dec.logits()
     toks, failed = dec.generate(2)
