@@ -27,6 +27,7 @@
 // (kernels/order.h:30).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -960,7 +961,7 @@ int cb_program_poll(cb_program* p, uint32_t wait) {
     if (!p) return fail(CB_ERROR_INVALID, "cb_program_poll: null program");
     int fired = 0;
     while (!p->pending.empty()) {
-        if (!wait) {
+        if (!(wait && fired == 0)) {
             const cudaError_t q = cudaEventQuery(p->slots[p->pending.front().slot].done);
             if (q == cudaErrorNotReady) break;
         }

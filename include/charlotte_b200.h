@@ -590,8 +590,10 @@ CB_API int cb_program_run(cb_program* p, const cb_step* step, cb_step_callback d
  * timed by CUDA events on the program's stream; not beside unprofiled steps. */
 CB_API int cb_program_run_profiled(cb_program* p, const cb_step* step, uint32_t launches, cb_profile_callback done,
                                    void* userdata);
-/* Fires the callbacks of finished steps, oldest first; with `wait`, blocks
- * until every outstanding step has finished. Returns the callbacks fired. */
+/* Fires the callbacks of finished steps, oldest first; with `wait`, first
+ * blocks until the oldest outstanding step has finished (so a caller that
+ * keeps two steps in flight waits for one, runs the next, and so on).
+ * Returns the callbacks fired. */
 CB_API int cb_program_poll(cb_program* p, uint32_t wait);
 CB_API uint32_t cb_program_outstanding(const cb_program* p);
 CB_API uint32_t cb_program_launch_count(const cb_program* p);

@@ -199,8 +199,9 @@ __attribute__((visibility("default"))) int cbh_run(cbh* h, const std::uint32_t* 
     return CB_OK;
 }
 
-// The records of steps finished so far (all outstanding with `wait`), in
-// the order they were run: rows of {tag, status, token, failed, u, 0}.
+// The records of steps finished so far (with `wait`, at least the oldest
+// outstanding one's), in the order they were run: rows of {tag, status,
+// token, failed, u, 0}.
 __attribute__((visibility("default"))) int cbh_poll(cbh* h, std::uint32_t wait, std::uint32_t* out,
                                                     std::uint32_t capacity) {
     h->program->process_events(wait != 0);

@@ -122,8 +122,8 @@ public:
     [[nodiscard]] std::uint32_t launch_count() const noexcept;
     [[nodiscard]] bool can_profile() const noexcept { return true; }
 
-    // Fires the callbacks of finished steps, oldest first (with `wait`, of
-    // every outstanding step). Returns how many fired.
+    // Fires the callbacks of finished steps, oldest first (with `wait`,
+    // after blocking until the oldest has finished). Returns how many fired.
     int process_events(bool wait);
     [[nodiscard]] std::uint32_t outstanding() const noexcept;
 
