@@ -914,6 +914,41 @@ def sweep_bench(iters=20, flags=0, ms=None, formats=(8, 2, 14), head=True):
     return {"workload": "configs[1]: Qwen3-shape product sweep", "form": form, "results": rows_out}
 
 
+def split_forms_bench(iters=10):
+    """The split form beside the streamed and tiled exact forms on the
+    few-tile, wide-K products it is for (Qwen3's O and down, Llama's O and
+    down, Gemma's down), at the token counts a batched decode or a prefill
+    step gives them: device µs a launch, weights rotated over copies larger
+    than L2."""
+    import torch
+    import charlotte_b200 as cb
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(SEED + 5)
+    shapes = [("qwen3.o", 1024, 2048), ("qwen3.down", 1024, 3072), ("llama.o", 2048, 2048),
+              ("llama.down", 2048, 8192), ("gemma.down", 1152, 6912)]
+    rows_out = []
+    for name, rows, K in shapes:
+        stored = synth.blocks(rng, Q4_0, rows, K)
+        nb = stored.size // synth.BLOCK_BYTES[Q4_0]
+        piece = torch.from_numpy(synth.to_piece(Q4_0, stored)).cuda()
+        copies = max(1, min(16, int(np.ceil(256e6 / piece.numel()))))
+        pieces = [piece] + [piece.clone() for _ in range(copies - 1)]
+        for M in (4, 8, 16, 32, 64, 128, 256, 512):
+            x = torch.from_numpy(synth.activations(rng, M, K)).cuda()
+            y = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+            rs = torch.empty(cb.lib().cb_matmul_split_bytes(M, rows) // 4, dtype=torch.float32, device="cuda")
+            row = {"product": name, "N": rows, "K": K, "M": M}
+            for form, flags, scratch in (("streamed", cb.MATMUL_STREAMED, None), ("tiled", cb.MATMUL_TILED, None),
+                                         ("split", cb.MATMUL_SPLIT, rs), ("auto", 0, rs)):
+                def launch(i, flags=flags, scratch=scratch):
+                    cb.matmul(Q4_0, K, [(pieces[i % copies], nb, 0, rows, 0)], x, [y], flags=flags | cb.MATMUL_PDL,
+                              scratch=scratch)
+                row[form] = round(graph_time_ms(launch, iters) * 1e3, 2)
+            cb.check(cb.lib().cb_fault_check(None))
+            rows_out.append(row)
+    return {"workload": "split form vs the exact forms, Q4_0", "unit": "us a launch", "results": rows_out}
+
+
 def sweep_summary(sweep):
     """The sweep's rows with each one's roofline fraction: HBM for M = 16
     (weights dominate the bytes), the sustained tensor peak for the others
@@ -968,6 +1003,8 @@ def main():
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+    elif args.case == "split-forms":
+        print(json.dumps(split_forms_bench()))
     elif args.case == "config1":
         print(json.dumps(config1_bench()))
     elif args.case == "llama":

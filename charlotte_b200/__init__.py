@@ -19,7 +19,7 @@ LIB_PATH = os.path.join(HERE, "libcharlotte_b200.so")
 F32, F16, Q4_0, Q4_1, Q8_0, Q6_K, BF16 = 0, 1, 2, 3, 8, 14, 30
 WRITE, QKV, GATED, GATED_BY_INPUT = 0, 1, 2, 3
 SILU, GELU_TANH, SIGMOID = 0, 1, 2
-MATMUL_PDL, MATMUL_TENSOR, MATMUL_STREAMED, MATMUL_TILED = 1, 2, 4, 8
+MATMUL_PDL, MATMUL_TENSOR, MATMUL_STREAMED, MATMUL_TILED, MATMUL_SPLIT = 1, 2, 4, 8, 16
 OK, ERROR_BUILD, ERROR_STEP, ERROR_DEVICE_LOST, ERROR_CANCELLED, ERROR_INVALID = range(6)
 
 
@@ -139,6 +139,8 @@ def lib() -> ctypes.CDLL:
         L.cb_select_tickets.argtypes = [ctypes.c_uint32]
         L.cb_matmul_scratch_bytes.restype = ctypes.c_uint64
         L.cb_matmul_scratch_bytes.argtypes = [ctypes.c_uint32] * 3
+        L.cb_matmul_split_bytes.restype = ctypes.c_uint64
+        L.cb_matmul_split_bytes.argtypes = [ctypes.c_uint32] * 2
         _lib = L
     return _lib
 
@@ -188,11 +190,11 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
         tokens = x.shape[0] if x.dim() > 1 else 1
     if x_stride is None:
         x_stride = x.shape[-1]
-    if flags & MATMUL_TENSOR:
+    if flags & MATMUL_TENSOR and scratch is None:
         need = lib().cb_matmul_scratch_bytes(flags, tokens, columns)
-        if scratch is None:
-            import torch
-            scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        import torch
+        scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+    if scratch is not None:   # the tensor form's x16, or the split form's range sums
         m.scratch = scratch.data_ptr()
         m.scratch_bytes = scratch.numel() * scratch.element_size()
     outs = (ctypes.c_void_p * 3)(*[_ptr(o) for o in (list(out) + [None, None, None])[:3]])

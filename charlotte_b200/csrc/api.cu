@@ -112,6 +112,10 @@ int cb_device_sm_count(void) {
     return n > 0 ? n : cb::fail(CB_ERROR_STEP, "no CUDA device");
 }
 
+uint64_t cb_matmul_split_bytes(uint32_t tokens, uint32_t rows) {
+    return 32ull * tokens * rows * sizeof(float);
+}
+
 uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t columns) {
     return (flags & CB_MATMUL_TENSOR) ? cb::matmul_tensor_scratch_bytes(tokens, columns) : 0u;
 }
@@ -191,11 +195,26 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
     const int sms = sm_count();
     if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
     const bool pdl = (flags & CB_MATMUL_PDL) != 0;
-    bool tiled = tiled_form(tokens, m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : total);
+    const uint32_t slots = m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : total;
+    bool tiled = tiled_form(tokens, slots);
     if (flags & CB_MATMUL_STREAMED) tiled = false;
     if (flags & CB_MATMUL_TILED) tiled = true;
+    // The split form: asked for, or chosen for a few-tile product when the
+    // caller gave range-sum scratch and no other form.
+    const uint64_t split_need = cb_matmul_split_bytes(tokens, total);
+    const bool split_scratch = m->scratch && aligned16(m->scratch) && m->scratch_bytes >= split_need;
+    bool split = (flags & CB_MATMUL_SPLIT) != 0;
+    if (split && (m->epilogue == CB_EPILOGUE_GATED || !split_scratch || (flags & CB_MATMUL_TENSOR)))
+        return fail(CB_ERROR_INVALID, "cb_matmul_run: the split form takes no gated product and needs %llu bytes of "
+                    "16-byte aligned range-sum scratch", static_cast<unsigned long long>(split_need));
+    if (!split && split_scratch && tokens > 1 &&
+        !(flags & (CB_MATMUL_TENSOR | CB_MATMUL_STREAMED | CB_MATMUL_TILED)) &&
+        split_form(tokens, slots, m->columns, m->epilogue, sms))
+        split = true;
+    if (split) a.range_sums = static_cast<float*>(m->scratch);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = (flags & CB_MATMUL_TENSOR) ? matmul_tensor(a, st, pdl)
+                    : split                    ? matmul_split(a, sms, st, pdl)
                     : tiled                    ? matmul_tiled(a, sms, st, pdl)
                                                : matmul_decode(a, sms, st, pdl);
     if (e != cudaSuccess) return fail_cuda(e, "cb_matmul_run: launch");

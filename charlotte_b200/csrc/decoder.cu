@@ -124,6 +124,8 @@ struct cb_decoder {
     float* hidden2 = nullptr;
     void* tensor_scratch = nullptr;
     uint64_t tensor_scratch_bytes = 0;
+    void* split_scratch = nullptr;   // the split form's range sums (few-tile, wide-K products)
+    uint64_t split_scratch_bytes = 0;
 };
 
 namespace {
@@ -199,6 +201,10 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
         flags |= CB_MATMUL_TENSOR;
         m.scratch = d->tensor_scratch;
         m.scratch_bytes = d->tensor_scratch_bytes;
+    } else if (tokens > 1) {
+        // range-sum scratch: cb_matmul_run takes the split form where it pays
+        m.scratch = d->split_scratch;
+        m.scratch_bytes = d->split_scratch_bytes;
     }
     return cb_matmul_run(&m, x, x_stride, tokens, outs, strides, flags, d->stream);
 }
@@ -562,6 +568,20 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
     if (int rc = dalloc(d, &d->state, 2)) return bail(rc);
     if (flags & ~static_cast<uint32_t>(CB_DECODER_TENSOR_PREFILL))
         return bail(fail(CB_ERROR_INVALID, "cb_decoder_create: unknown flags 0x%x", flags));
+    {
+        // The split form's range sums for the widest product it may take:
+        // non-gated products over K of 64 groups or more (o, down; QKV when
+        // the hidden width is that wide).
+        uint32_t rows = 0;
+        if (qd / 32 >= 64 || m->ffn / 32 >= 64) rows = H;
+        if (H / 32 >= 64) rows = std::max<uint32_t>(rows, static_cast<uint32_t>(qd + 2 * kvd));
+        if (rows) {
+            d->split_scratch_bytes = cb_matmul_split_bytes(T, rows);
+            uint8_t* p = nullptr;
+            if (int rc = dalloc(d, &p, d->split_scratch_bytes)) return bail(rc);
+            d->split_scratch = p;
+        }
+    }
     if (flags & CB_DECODER_TENSOR_PREFILL) {
         const uint32_t widest = std::max<uint32_t>(std::max<uint32_t>(H, static_cast<uint32_t>(qd)), m->ffn);
         d->tensor_scratch_bytes = cb_matmul_scratch_bytes(CB_MATMUL_TENSOR, T, widest);

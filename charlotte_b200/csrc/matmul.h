@@ -40,6 +40,9 @@ struct MatmulArgs {
     uint32_t gate_input_column;
     unsigned int* fault;    // device word: a bounded wait that ran out sets a bit
     void* scratch;          // tensor form: x rounded to f16, [tokens][columns]
+    // Split form (matmul_split): range r's sum of product row p for token t
+    // at range_sums[(r·tokens + t)·total_rows + p] (matmul.wgsl range_sum_at).
+    float* range_sums;
     // One-token decode with the RMSNorm before the product folded in (the
     // decoder's own path; norm_gain NULL: x is read as given). Every CTA
     // computes norm_kernel's row — hidden (+ y, post-normed first when
@@ -60,6 +63,16 @@ cudaError_t matmul_decode(const MatmulArgs& a, int sm_count, cudaStream_t stream
 // Tiled form over a step of `tokens` rows of x: the same sums, bit for bit,
 // as a register-tiled GEMM on the CUDA cores. PDL when `pdl`.
 cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
+
+// Split form (matmul.wgsl split_ranges :609 and combine_* :651-695): the
+// tiled form's tiles once for each of the 32 ranges, each writing its range
+// sums to a.range_sums, then a combine adding each output's 32 in order and
+// applying the epilogue — the same bits as the other exact forms, with 32
+// times the CTAs for products of few output tiles. Not for gated products.
+cudaError_t matmul_split(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl);
+// Whether the split form pays for a product: few output tiles for the SMs
+// and ranges of at least two groups.
+bool split_form(uint32_t tokens, uint32_t slots, uint32_t columns, uint32_t epilogue, int sm_count);
 
 // Tensor-core form (tolerance tier, f16 operands, f32 accumulation in TMEM).
 cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl);

@@ -91,6 +91,9 @@ __global__ void __launch_bounds__(T::kThreads, T::kMinBlocks) tiled_kernel(const
     const uint32_t tid = threadIdx.x;
     const bool gated = a.epilogue == kGated;
     const uint32_t m0 = blockIdx.x * BM;
+    // Split form: this CTA's groups are range blockIdx.z's alone.
+    const bool split = a.range_sums != nullptr;
+    const uint32_t g_lo = split ? blockIdx.z * G / 32u : 0u, g_hi = split ? (blockIdx.z + 1u) * G / 32u : G;
     const uint32_t n0 = blockIdx.y * (gated ? BN / 2 : BN);   // first slot (gated: first output)
 
     // ---- decode role: slot j of the tile, weights of part p --------------
@@ -180,16 +183,18 @@ __global__ void __launch_bounds__(T::kThreads, T::kMinBlocks) tiled_kernel(const
 #pragma unroll
         for (int p = 0; p < 4; ++p) { s[i][p] = make_float2(0.0f, 0.0f); total[i][p] = make_float2(0.0f, 0.0f); }
 
-    load_w(0);
+    if (g_lo < g_hi) load_w(g_lo);
     grid_dependency_wait();
-    load_x(0);
-    store_w(ws);
-    store_x(xs);
+    if (g_lo < g_hi) {
+        load_x(g_lo);
+        store_w(ws);
+        store_x(xs);
+    }
     __syncthreads();
 
-    for (uint32_t g = 0; g < G; ++g) {
-        const uint32_t buf = g & 1u;
-        const bool more = g + 1u < G;
+    for (uint32_t g = g_lo; g < g_hi; ++g) {
+        const uint32_t buf = (g - g_lo) & 1u;
+        const bool more = g + 1u < g_hi;
         if (more) {
             load_w(g + 1u);
             load_x(g + 1u);
@@ -217,7 +222,7 @@ __global__ void __launch_bounds__(T::kThreads, T::kMinBlocks) tiled_kernel(const
                 for (int p = 0; p < 4; ++p) s[i][p] = __ffma2_rn(wp[p], xx, s[i][p]);
             }
         }
-        if (closes_range(g, G)) {
+        if (!split && closes_range(g, G)) {
 #pragma unroll
             for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -232,6 +237,23 @@ __global__ void __launch_bounds__(T::kThreads, T::kMinBlocks) tiled_kernel(const
     grid_dependents_launch();
 
     // ---- epilogue -----------------------------------------------------------
+    if (split) {
+        // The range's sums of every product row of the tile (an empty
+        // range's zeros, which the combine adds as the reference does).
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const uint32_t t = m0 + (i < 4 ? ty * 4u + i : BM / 2 + ty * 4u + (i - 4));
+            if (t >= a.tokens) continue;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t n = n0 + (c < 4 ? tx * 4u + c : BN / 2 + tx * 4u + (c - 4));
+                if (n < a.total_rows)
+                    a.range_sums[(static_cast<size_t>(blockIdx.z) * a.tokens + t) * a.total_rows + n] =
+                        (c & 1) ? s[i][c >> 1].y : s[i][c >> 1].x;
+            }
+        }
+        return;
+    }
     auto sum = [&](int i, int c) { return (c & 1) ? total[i][c >> 1].y : total[i][c >> 1].x; };
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
@@ -292,7 +314,7 @@ cudaError_t launch_tiled(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
     const uint32_t slots = gated ? a.member[0].rows : a.total_rows;
     const uint32_t per_tile = gated ? T::BN / 2 : T::BN;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.tokens + T::BM - 1) / T::BM, (slots + per_tile - 1) / per_tile);
+    cfg.gridDim = dim3((a.tokens + T::BM - 1) / T::BM, (slots + per_tile - 1) / per_tile, a.range_sums ? 32u : 1u);
     cfg.blockDim = dim3(T::kThreads);
     cfg.dynamicSmemBytes = T::kSmem;
     cfg.stream = stream;
@@ -320,7 +342,7 @@ double merit(const MatmulArgs& a, int sm_count) {
     const uint32_t slots = gated ? a.member[0].rows : a.total_rows;
     const uint32_t per_tile = gated ? T::BN / 2 : T::BN;
     const double mt = (a.tokens + T::BM - 1) / T::BM, nt = (slots + per_tile - 1) / per_tile;
-    const double warps = mt * nt * (T::kThreads / 32);
+    const double warps = mt * nt * (T::kThreads / 32) * (a.range_sums ? 32.0 : 1.0);
     const double want = 8.0 * sm_count;
     const double fill = warps >= want ? 1.0 : warps / want;
     const double used = static_cast<double>(a.tokens) / (mt * T::BM);
@@ -347,7 +369,83 @@ cudaError_t dispatch_tiled(const MatmulArgs& a, int sm_count, cudaStream_t strea
     }
 }
 
+// The split form's combine (combine_write, combine_qkv, combine_gated_input,
+// matmul.wgsl:651-695): product row p of token t is the 32 range sums added
+// to a total from zero in range order, then the epilogue.
+__global__ void __launch_bounds__(256) combine_kernel(const MatmulArgs a) {
+    grid_dependency_wait();
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < static_cast<uint64_t>(a.tokens) * a.total_rows) {
+        const uint32_t t = static_cast<uint32_t>(i / a.total_rows), p = static_cast<uint32_t>(i % a.total_rows);
+        const size_t plane = static_cast<size_t>(a.tokens) * a.total_rows;
+        const float* rs = a.range_sums + static_cast<size_t>(t) * a.total_rows + p;
+        float v[32];
+#pragma unroll
+        for (int r = 0; r < 32; ++r) v[r] = __ldcg(rs + r * plane);
+        float total = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 32; ++r) total = total + v[r];
+        uint32_t n = p;
+        int q = 0;
+        if (a.members > 1 && n >= a.member[0].rows) {
+            n -= a.member[0].rows;
+            q = 1;
+            if (a.members > 2 && n >= a.member[1].rows) {
+                n -= a.member[1].rows;
+                q = 2;
+            }
+        }
+        const uint32_t o =
+            (q == 1 ? a.member[1].out_offset : (q == 2 ? a.member[2].out_offset : a.member[0].out_offset)) + n;
+        if (a.epilogue == kQKV) {
+            float* out = q == 1 ? a.out[1] : (q == 2 ? a.out[2] : a.out[0]);
+            const uint32_t stride = q == 1 ? a.out_stride[1] : (q == 2 ? a.out_stride[2] : a.out_stride[0]);
+            out[static_cast<size_t>(t) * stride + o] = total;
+        } else if (a.epilogue == kWrite) {
+            a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = total;
+        } else {
+            const float u =
+                a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride + a.gate_input_column + o];
+            a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * u;
+        }
+    }
+    grid_dependents_launch();
+}
+
+cudaError_t launch_combine(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
+    const uint64_t n = static_cast<uint64_t>(a.tokens) * a.total_rows;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<uint32_t>((n + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, combine_kernel, a);
+}
+
 }  // namespace
+
+// Measured on B200 (bench.py --case split-forms, Q4_0, K of 2,048 to 8,192,
+// 1,024 to 2,048 rows, 4 to 512 tokens): the split form is the fastest exact
+// form from 24–32 tokens while the tiled form's 128 × 128 tiles would fill
+// at most half the SMs (Gemma's down at 64 tokens 28.6 µs against 70.3
+// streamed and 501 tiled; Llama's down at 512 tokens 458 against 592
+// tiled); below ~24 tokens the streamed form wins (4 to 16 tokens: 4–47 µs
+// against 8–38).
+bool split_form(uint32_t tokens, uint32_t slots, uint32_t columns, uint32_t epilogue, int sm_count) {
+    if (epilogue == kGated || columns / 32u < 64u || tokens < 24u) return false;
+    const uint64_t tiles = static_cast<uint64_t>((tokens + 127u) / 128u) * ((slots + 127u) / 128u);
+    return tiles * 2u <= static_cast<uint64_t>(sm_count);
+}
+
+cudaError_t matmul_split(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    if (!a.range_sums || a.epilogue == kGated) return cudaErrorInvalidValue;
+    if (cudaError_t e = matmul_tiled(a, sm_count, stream, pdl); e != cudaSuccess) return e;
+    return launch_combine(a, stream, pdl);
+}
 
 cudaError_t matmul_tiled(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     switch (a.format) {

@@ -9,8 +9,9 @@
 // (cb_matmul_run, cb_norm_run, cb_rope_run, cb_attention_run, cb_gather_run,
 // cb_select_run, cb_select_merge_run), with device pointers resolved from
 // the plan's buffers. A few reference launches have no work of their own
-// here: a split product's range sums and its combine are one product (the
-// exact forms add the 32 ranges in order themselves), attention's combine is
+// here: a split product's range-sum launches and its combine are one
+// product, given the reference's range_sums buffer as the split form's
+// scratch (every exact form adds the 32 ranges in order), attention's combine is
 // part of its main launch, and the top-k passes are one selection, which
 // also makes the draw that follows it. A launch this backend has no form for
 // is refused at build, named.
@@ -318,11 +319,18 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
                         break;
                     }
                 }
-                if (!split || split->binding_count < 2 || l.binding_count < 2)
+                if (!split || split->binding_count < 3 || l.binding_count < 2)
                     return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: a combine without its split", i);
                 if (int rc = build_matmul(p, l, i, epi, false, split->bindings[0], split->bindings[1], l.bindings + 1,
                                           l.binding_count - 1, op))
                     return rc;
+                // The split's range sums (the reference's range_sums buffer,
+                // in its layout) are the split form's scratch; the library
+                // takes the split form where it pays (cb_matmul_run).
+                void* sums = nullptr;
+                if (int rc = resolve(p, split->bindings[2], i, &sums)) return rc;
+                op.mm.scratch = sums;
+                op.mm.scratch_bytes = split->bindings[2].size;
             } else {
                 if (l.binding_count < 3)
                     return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: %u matmul bindings", i, l.binding_count);

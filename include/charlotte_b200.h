@@ -98,7 +98,14 @@ enum {
      * STREAMED decodes each weight once a pass of up to 16 tokens (decode
      * GEMV layout), TILED is the register-tiled GEMM. Default: by size. */
     CB_MATMUL_STREAMED = 4u,
-    CB_MATMUL_TILED = 8u
+    CB_MATMUL_TILED = 8u,
+    /* The split form (split_ranges + combine, matmul.wgsl:609-695): the
+     * tiled form's tiles once for each of the 32 ranges, each writing its
+     * range sums to `scratch`, then a combine adding every output's 32 in
+     * order — the same bits, 32 times the CTAs, for products of few output
+     * tiles over a wide K. Not for gated products. Without the flag it is
+     * chosen by size when `scratch` holds cb_matmul_split_bytes. */
+    CB_MATMUL_SPLIT = 16u
 };
 
 typedef struct cb_member {
@@ -136,6 +143,10 @@ CB_API int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, 
  * (0 for the exact forms). No counterpart in the reference (its prefill is
  * exact f32 only). */
 CB_API uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t columns);
+/* The split form's range-sum scratch for `tokens` rows of a product of
+ * `rows` outputs: 32·tokens·rows floats, laid out as the reference's
+ * range_sums (range_sum_at: (r·tokens + t)·rows + p, matmul.wgsl:600). */
+CB_API uint64_t cb_matmul_split_bytes(uint32_t tokens, uint32_t rows);
 
 
 /* ---- RMSNorm ------------------------------------------------------------------
