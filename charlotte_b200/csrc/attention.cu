@@ -66,7 +66,8 @@ __host__ __device__ inline size_t attention_smem(uint32_t d, uint32_t queries) {
            + static_cast<size_t>(queries) * d * 4u   // q·scale·log2e
            + static_cast<size_t>(queries) * kChunk * 4u   // scores, then weights
            + static_cast<size_t>(queries) * 8u * 4u       // a tile's alpha (≤ 8 tiles)
-           + static_cast<size_t>(queries) * 4u * 4u;      // m, l, live, spare
+           + static_cast<size_t>(queries) * 4u * 4u       // m, l, live, spare
+           + static_cast<size_t>(queries) * 16u * 4u;     // each tile's top and sum
 }
 
 // Cluster fold (decode shapes: a row a tile, Q = G queries): the floats of
@@ -105,97 +106,99 @@ __device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_
     }
 }
 
-// One step of the chunks' fold in chunk order (fold_factors/fold_sum/fold,
-// attention.wgsl:101-127): chunk (co, cm, cl) into the running (o, m, l).
-__device__ __forceinline__ void fold_step(float co, float cm, float cl, bool& live, float& run_m, float& run_l,
-                                          float& o) {
-    float fa, fb, fm;
-    if (!live) { fa = 0.0f; fb = 1.0f; fm = cm; }
-    else if (run_m == cm) { fa = 1.0f; fb = 1.0f; fm = run_m; }
-    else if (run_m > cm) { fa = 1.0f; fb = exp2_np(cm - run_m); fm = run_m; }
-    else { fa = exp2_np(run_m - cm); fb = 1.0f; fm = cm; }
-    run_l = fmaf(run_l, fa, cl * fb);
-    o = fmaf(o, fa, co * fb);
-    run_m = fm;
-    live = true;
-}
-
-// One query's softmax over a staged chunk (its scores in ps[0..63]), tiles
-// of B keys (8, 16 or 32), for the warp calling it: writes each key's weight
-// over its score, the tiles' alphas, and the chunk's (m, l) — the
-// operations of the tile-by-tile loop, in its order: the tile's top, then
-// old, top = max(old, tile top), a = 2^(old − top) (1 when equal), each live
-// key's 2^(s − top), the tile's sum from zero in key order, l = fma(l, a, sum).
-// The chunk's live keys are one run [lo, hi); every lane reads the scores and
-// then the weights of all tiles from shared memory (the same addresses on
-// every lane), so no shuffle stands between the phases.
-template <uint32_t B>
-__device__ __forceinline__ void softmax_chunk(float* ps, float* alpha, float* stat, uint32_t key0, uint32_t p,
-                                              uint32_t window, uint32_t lane) {
-    const uint32_t early = earliest_of(p, window);
-    constexpr uint32_t tiles = kChunk / B;
-    const uint32_t lo = early > key0 ? min(early - key0, kChunk) : 0u;
-    const uint32_t hi = p >= key0 ? min(p - key0 + 1u, kChunk) : 0u;
-    const float4* s4 = reinterpret_cast<const float4*>(ps);
-    // Each tile's top over its live scores (-inf when none is live).
-    float tt[tiles];
-#pragma unroll
-    for (uint32_t t = 0; t < tiles; ++t) {
-        tt[t] = -INFINITY;
-#pragma unroll
-        for (uint32_t q = t * B / 4u; q < (t + 1u) * B / 4u; ++q) {
-            const float4 v = s4[q];
-            const uint32_t b = 4u * q;
-            if (b >= lo && b < hi) tt[t] = fmaxf(tt[t], v.x);
-            if (b + 1u >= lo && b + 1u < hi) tt[t] = fmaxf(tt[t], v.y);
-            if (b + 2u >= lo && b + 2u < hi) tt[t] = fmaxf(tt[t], v.z);
-            if (b + 3u >= lo && b + 3u < hi) tt[t] = fmaxf(tt[t], v.w);
-        }
+// The chunks' fold in chunk order (fold_factors/fold_sum/fold,
+// attention.wgsl:101-127): for each live chunk c of a query, with top the
+// largest of the earlier chunks' tops, (fa, fb) = (0, 1) for the first,
+// (1, 1) when top = m_c, (1, 2^(m_c − top)) when top > m_c, else
+// (2^(top − m_c), 1); then l = fma(l, fa, l_c·fb) and o = fma(o, fa,
+// o_c·fb). The factors depend on the partials only through that running
+// top, a prefix maximum, so here a warp a query finds every chunk's
+// (fa, fb) of a block of 32 chunks at once (a scan of maxima across lanes,
+// then each lane's exp2) and runs the l chain, and then every (query,
+// dimension) runs its o chain in chunk order — the same operations on the
+// same operands as one chunk after the other, so the same bits.
+// `stat_of(c, m, &cm, &cl)` gives chunk c's (m, l) for query m,
+// `part_of(c, m, e)` its partial; queries' chunk ranges from
+// `range_of(m, &c0, &c1)`; `write(m, e, o / l)` takes each output. `fac`
+// holds Q·64 floats of scratch, `carry` Q·4.
+template <typename Range, typename Stat, typename Part, typename Write>
+__device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, float* carry, Range range_of,
+                                            Stat stat_of, Part part_of, Write write, uint32_t lane, uint32_t wid) {
+    uint32_t lo = 0xFFFFFFFFu, hi = 0;
+    for (uint32_t m = 0; m < Q; ++m) {
+        uint32_t c0, c1;
+        range_of(m, &c0, &c1);
+        lo = min(lo, c0);
+        hi = max(hi, c1);
     }
-    // The running top and alpha, tile by tile (every lane alike); each lane
-    // keeps the tops of its own two keys' tiles.
-    bool chunk_live = false;
-    float chunk_m = 0.0f, top0 = 0.0f, top1 = 0.0f, al[tiles];
-    uint32_t seen_tiles = 0;
+    const uint32_t warps = blockDim.x / 32u;
+    // Outputs in groups of the CTA's threads, each one thread's o chain.
+    for (uint32_t i0 = 0; i0 < Q * d; i0 += blockDim.x) {
+        const uint32_t i = i0 + threadIdx.x;
+        const uint32_t me = i / d, e = i % d;
+        uint32_t mc0 = 0, mc1 = 0;
+        if (i < Q * d) range_of(me, &mc0, &mc1);
+        float o = 0.0f;
+        __syncthreads();   // the last group's reads of carry and fac are done
+        for (uint32_t m = wid; m < Q; m += warps)
+            if (lane == 0) { carry[m * 4u] = -INFINITY; carry[m * 4u + 1u] = 0.0f; }
+        __syncthreads();
+        for (uint32_t base = lo; base <= hi; base += 32u) {
+            for (uint32_t m = wid; m < Q; m += warps) {
+                uint32_t c0, c1;
+                range_of(m, &c0, &c1);
+                const uint32_t c = base + lane;
+                const bool in = c >= c0 && c <= c1;
+                float cm = -INFINITY, cl = 0.0f;
+                if (in) stat_of(c, m, &cm, &cl);
+                float incl = cm;
 #pragma unroll
-    for (uint32_t t = 0; t < tiles; ++t) {
-        al[t] = 1.0f;
-        if (t * B < hi && (t + 1u) * B > lo && lo < hi) {
-            seen_tiles |= 1u << t;
-            const float old = chunk_live ? chunk_m : tt[t];
-            chunk_live = true;
-            const float top = fmaxf(old, tt[t]);
-            al[t] = old == top ? 1.0f : exp2_np(old - top);
-            chunk_m = top;
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+                    if (lane >= static_cast<uint32_t>(off)) incl = fmaxf(incl, v);
+                }
+                const float before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                const float top = fmaxf(carry[m * 4u], lane ? before : -INFINITY);   // the running top before c
+                float fa = 1.0f, fb = 1.0f;
+                if (in) {
+                    if (c == c0) { fa = 0.0f; fb = 1.0f; }
+                    else if (top == cm) { fa = 1.0f; fb = 1.0f; }
+                    else if (top > cm) { fa = 1.0f; fb = exp2_np(cm - top); }
+                    else { fa = exp2_np(top - cm); fb = 1.0f; }
+                }
+                fac[(m * 32u + lane) * 2u] = fa;
+                fac[(m * 32u + lane) * 2u + 1u] = fb;
+                // l in chunk order (every lane alike; lane 0 keeps it)
+                float run_l = carry[m * 4u + 1u];
+                for (uint32_t j = 0; j < 32u; ++j) {
+                    const float fa_j = __shfl_sync(0xFFFFFFFFu, fa, j), fb_j = __shfl_sync(0xFFFFFFFFu, fb, j);
+                    const float cl_j = __shfl_sync(0xFFFFFFFFu, cl, j);
+                    if (base + j >= c0 && base + j <= c1) run_l = fmaf(run_l, fa_j, cl_j * fb_j);
+                }
+                const float block_top = __shfl_sync(0xFFFFFFFFu, incl, 31);
+                __syncwarp();
+                if (lane == 0) {
+                    carry[m * 4u] = fmaxf(carry[m * 4u], block_top);
+                    carry[m * 4u + 1u] = run_l;
+                }
+            }
+            __syncthreads();
+            if (i < Q * d) {
+                const uint32_t n = mc1 + 1u > base ? min(32u, mc1 + 1u - base) : 0u;
+                const uint32_t j0 = mc0 > base ? mc0 - base : 0u;
+                float co[8];
+                for (uint32_t j = j0; j < n; j += 8u) {
+#pragma unroll
+                    for (uint32_t k = 0; k < 8u; ++k) co[k] = j + k < n ? part_of(base + j + k, me, e) : 0.0f;
+#pragma unroll
+                    for (uint32_t k = 0; k < 8u; ++k)
+                        if (j + k < n)
+                            o = fmaf(o, fac[(me * 32u + j + k) * 2u], co[k] * fac[(me * 32u + j + k) * 2u + 1u]);
+                }
+            }
+            __syncthreads();
         }
-        if (lane / B == t) top0 = chunk_m;
-        if ((lane + 32u) / B == t) top1 = chunk_m;
-    }
-    const float s0 = ps[lane], s1 = ps[lane + 32u];
-    const bool live0 = lane >= lo && lane < hi, live1 = lane + 32u >= lo && lane + 32u < hi;
-    __syncwarp();   // every lane has read the scores
-    ps[lane] = live0 ? exp2_np(s0 - top0) : 0.0f;
-    ps[lane + 32u] = live1 ? exp2_np(s1 - top1) : 0.0f;
-    __syncwarp();
-    // Each seen tile's sum in key order from zero, then l.
-    float chunk_l = 0.0f;
-#pragma unroll
-    for (uint32_t t = 0; t < tiles; ++t) {
-        float sum = 0.0f;
-#pragma unroll
-        for (uint32_t q = t * B / 4u; q < (t + 1u) * B / 4u; ++q) {
-            const float4 v = s4[q];
-            sum = sum + v.x;
-            sum = sum + v.y;
-            sum = sum + v.z;
-            sum = sum + v.w;
-        }
-        if ((seen_tiles >> t) & 1u) chunk_l = fmaf(chunk_l, al[t], sum);
-        if (lane == 0) alpha[t] = al[t];
-    }
-    if (lane == 0) {
-        stat[0] = chunk_m;
-        stat[1] = chunk_live ? chunk_l : 0.0f;
+        if (i < Q * d) write(me, e, o / carry[me * 4u + 1u]);
     }
 }
 
@@ -233,7 +236,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     float* ps = qs + kMaxQueries * d;                 // [Q][64]
     float* alpha = ps + kMaxQueries * kChunk;         // [Q][8]
     float* stat = alpha + kMaxQueries * 8u;           // [Q][4]: m, l
-    float* fold_part = stat + kMaxQueries * 4u;       // cluster fold, rank 0: [slot][Q][d], then [slot][Q][2]
+    float* tops = stat + kMaxQueries * 4u;            // [Q][8]: each tile's top (-inf: no live key)
+    float* sums = tops + kMaxQueries * 8u;            // [Q][8]: each tile's sum of weights
+    float* fold_part = sums + kMaxQueries * 8u;       // cluster fold, rank 0: [slot][Q][d], then [slot][Q][2]
     float* fold_stat = fold_part + kChunkSlots * G * d;
 
     // The tile's live chunks: every chunk some row's keys reach.
@@ -378,53 +383,64 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             ps[m * kChunk + b] = s;
         }
         __syncthreads();
-        // The online softmax, a warp a query, tile by tile in key order: the
-        // tile's top (a max: any order gives its bits) and each live key's
-        // 2^(s − top); the sum of a tile's weights in key order, and the
-        // running l and m. Tiles of 8, 16 or 32 keys (d = 256, 128, 64): a
-        // lane holds keys lane and lane+32, every tile's top comes from one
-        // butterfly over its lanes at once, and each tile's sum is read back
-        // from shared memory by a lane of its own.
-        if (B >= 8u && B <= 32u && (B & (B - 1u)) == 0u) {
-            for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
+        // The online softmax, tile by tile in key order, a warp a (query,
+        // tile): the tile's top (a max: any order gives its bits); then,
+        // with the running top before the tile (the tops of the earlier
+        // tiles, in order), old, top = max(old, tile top), a = 2^(old − top)
+        // (1 when equal), each live key's 2^(s − top) and the tile's sum
+        // from zero in key order; then, a thread a query, l = fma(l, a,
+        // sum) over the tiles with live keys, in order.
+        {
+            const uint32_t pairs = Q * tiles;
+            for (uint32_t w = wid; w < pairs; w += kAttnThreads / 32u) {
+                const uint32_t m = w / tiles, t = w % tiles;
                 const uint32_t p = p_first + (seqs ? 0u : m / G);
-                if (B == 16u) softmax_chunk<16>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
-                else if (B == 32u) softmax_chunk<32>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
-                else softmax_chunk<8>(ps + m * kChunk, alpha + m * 8u, stat + m * 4u, key0, p, a.window, lane);
-            }
-        } else
-        for (uint32_t m = wid; m < Q; m += kAttnThreads / 32u) {
-            const uint32_t p = p_first + (seqs ? 0u : m / G);
-            const uint32_t early = earliest_of(p, a.window);
-            bool chunk_live = false;
-            float chunk_m = 0.0f, chunk_l = 0.0f;
-            for (uint32_t t = 0; t < tiles; ++t) {
-                const uint32_t b = t * B + lane;
-                const uint32_t j = key0 + b;
-                const bool live = lane < B && j <= p && j >= early;
-                const float s = live ? ps[m * kChunk + b] : 0.0f;
-                float top_tile = live ? s : -INFINITY;
+                const uint32_t j = key0 + t * B + lane;
+                const bool live = lane < B && j <= p && j >= earliest_of(p, a.window);
+                float top = live ? ps[m * kChunk + t * B + lane] : -INFINITY;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) top_tile = fmaxf(top_tile, __shfl_xor_sync(0xFFFFFFFFu, top_tile, o));
-                const bool seen = __any_sync(0xFFFFFFFFu, live);
-                float al = 1.0f;
-                if (seen) {
-                    const float old = chunk_live ? chunk_m : top_tile;
-                    chunk_live = true;
-                    const float top = fmaxf(old, top_tile);
-                    al = old == top ? 1.0f : exp2_np(old - top);
-                    const float e = live ? exp2_np(s - top) : 0.0f;
-                    if (lane < B) ps[m * kChunk + b] = e;
-                    float sum = 0.0f;   // in key order, on every lane alike
-                    for (uint32_t i = 0; i < B; ++i) sum = sum + __shfl_sync(0xFFFFFFFFu, e, i);
-                    chunk_l = fmaf(chunk_l, al, sum);
-                    chunk_m = top;
-                } else if (lane < B) {
-                    ps[m * kChunk + b] = 0.0f;
-                }
-                if (lane == 0) alpha[m * 8u + t] = al;
+                for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+                if (lane == 0) tops[m * 8u + t] = top;
             }
-            if (lane == 0) {
+            __syncthreads();
+            for (uint32_t w = wid; w < pairs; w += kAttnThreads / 32u) {
+                const uint32_t m = w / tiles, t = w % tiles;
+                const uint32_t p = p_first + (seqs ? 0u : m / G);
+                const uint32_t j = key0 + t * B + lane;
+                const bool live = lane < B && j <= p && j >= earliest_of(p, a.window);
+                bool chunk_live = false;
+                float chunk_m = 0.0f, al = 1.0f;
+                for (uint32_t u = 0; u <= t; ++u) {
+                    const float tt = tops[m * 8u + u];
+                    if (tt == -INFINITY) continue;   // no live key in tile u
+                    const float old = chunk_live ? chunk_m : tt;
+                    const float top = fmaxf(old, tt);
+                    if (u == t) al = old == top ? 1.0f : exp2_np(old - top);
+                    chunk_m = top;
+                    chunk_live = true;
+                }
+                const float e = live ? exp2_np(ps[m * kChunk + t * B + lane] - chunk_m) : 0.0f;
+                __syncwarp();
+                if (lane < B) ps[m * kChunk + t * B + lane] = e;
+                float sum = 0.0f;   // in key order
+                for (uint32_t b = 0; b < B; ++b) sum = sum + __shfl_sync(0xFFFFFFFFu, e, b);
+                if (lane == 0) {
+                    alpha[m * 8u + t] = al;
+                    sums[m * 8u + t] = sum;
+                }
+            }
+            __syncthreads();
+            for (uint32_t m = threadIdx.x; m < Q; m += kAttnThreads) {
+                bool chunk_live = false;
+                float chunk_m = 0.0f, chunk_l = 0.0f;
+                for (uint32_t u = 0; u < tiles; ++u) {
+                    const float tt = tops[m * 8u + u];
+                    if (tt == -INFINITY) continue;
+                    const float old = chunk_live ? chunk_m : tt;
+                    chunk_m = fmaxf(old, tt);
+                    chunk_l = fmaf(chunk_l, alpha[m * 8u + u], sums[m * 8u + u]);
+                    chunk_live = true;
+                }
                 stat[m * 4u + 0] = chunk_m;
                 stat[m * 4u + 1] = chunk_live ? chunk_l : 0.0f;
             }
@@ -439,23 +455,24 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             // holds — so the loop needs no test; keys past p_last, never
             // staged, are left out.
             const uint32_t valid = min(kChunk, p_last + 1u - key0);
-            for (uint32_t t = 0; t < tiles; ++t) {
-                o = o * alpha[m * 8u + t];
-                // Eight keys at a time: their weights (two 16-byte reads) and
-                // values into registers, unconditionally (every row of the
-                // stage is in bounds), then their fmas in key order, keys from
-                // `valid` on (never staged) skipped.
-                for (uint32_t b0 = t * B; b0 < (t + 1u) * B; b0 += 8u) {
-                    const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
-                    const float4 pa = p4[0], pb = p4[1];
-                    const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-                    float vv[8];
+            // Eight keys at a time (every tile is a whole number of eights):
+            // at a tile's first key O·a_t, then the keys' fmas in key order
+            // — their weights (two 16-byte reads) and values loaded first,
+            // unconditionally (every row of the stage is in bounds), keys
+            // from `valid` on (never staged) skipped. Fully unrolled, so the
+            // loads of later keys go ahead of the chain.
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
+            for (uint32_t b0 = 0; b0 < kChunk; b0 += 8u) {
+                const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
+                const float4 pa = p4[0], pb = p4[1];
+                const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                float vv[8];
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (b0 + k < valid) o = fmaf(pw[k], vv[k], o);
-                }
+                for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
+                if (b0 % B == 0) o = o * alpha[m * 8u + b0 / B];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (b0 + k < valid) o = fmaf(pw[k], vv[k], o);
             }
             if (cluster_fold) {
                 // Into rank 0's slot for this CTA's chunk (slot = rank).
@@ -481,22 +498,24 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     if (cluster_fold) {
         cluster_sync();   // every chunk's partial and (m, l) is in rank 0's shared memory
         if (cluster_rank() != 0u) return;
-        // Each (query, dimension) folds its chunks (slot = chunk − the
-        // tile's first live chunk) in chunk order.
-        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
-            const uint32_t m = i / d, e = i % d;
-            const uint32_t r = m / G, h = kvh * G + m % G;
-            const uint32_t p = p_first + (seqs ? 0u : r);
-            const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
-            bool live = false;
-            float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
-            for (uint32_t c = c0; c <= c1; ++c) {
+        // The chunks (slot = chunk − the tile's first live chunk) folded in
+        // chunk order.
+        fold_chunks(
+            Q, d, ps, stat, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+                const uint32_t p = p_first + (seqs ? 0u : m / G);
+                *c0 = earliest_of(p, a.window) / kChunk;
+                *c1 = p / kChunk;
+            },
+            [&](uint32_t c, uint32_t m, float* cm, float* cl) {
                 const uint32_t slot = c - live_first;
-                fold_step(fold_part[(slot * G + m) * d + e], fold_stat[(slot * G + m) * 2u],
-                          fold_stat[(slot * G + m) * 2u + 1u], live, run_m, run_l, o);
-            }
-            a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
-        }
+                *cm = fold_stat[(slot * G + m) * 2u];
+                *cl = fold_stat[(slot * G + m) * 2u + 1u];
+            },
+            [&](uint32_t c, uint32_t m, uint32_t e) { return fold_part[((c - live_first) * G + m) * d + e]; },
+            [&](uint32_t m, uint32_t e, float v) {
+                a.out[(static_cast<size_t>(row0 + m / G) * a.query_heads + kvh * G + m % G) * d + e] = v;
+            },
+            lane, wid);
         return;
     }
     if (failed) return;   // without a ticket: the step reports failure
@@ -514,33 +533,26 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Each (query, dimension) loads its chunks' partials and (m, l) together,
-    // eight chunks in flight at once, and folds them in chunk order.
-    for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
-        const uint32_t m = i / d, e = i % d;
-        const uint32_t r = m / G, h = kvh * G + m % G;
-        const uint32_t p = p_first + (seqs ? 0u : r);
-        const uint32_t c0 = earliest_of(p, a.window) / kChunk, c1 = p / kChunk;
-        bool live = false;
-        float run_m = 0.0f, run_l = 0.0f, o = 0.0f;
-        for (uint32_t cc = c0; cc <= c1; cc += 8u) {
-            float co[8], cms[8], cls[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const size_t at = (static_cast<size_t>(cc + k) * a.tokens + row0 + r) * a.query_heads + h;
-                const bool in = cc + k <= c1;
-                co[k] = in ? __ldcg(a.partials + at * d + e) : 0.0f;
-                cms[k] = in ? __ldcg(a.stats + at * 2u) : 0.0f;
-                cls[k] = in ? __ldcg(a.stats + at * 2u + 1u) : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (cc + k > c1) break;
-                fold_step(co[k], cms[k], cls[k], live, run_m, run_l, o);
-            }
-        }
-        a.out[(static_cast<size_t>(row0 + r) * a.query_heads + h) * d + e] = live ? o / run_l : 0.0f;
-    }
+    // The chunks' partials (global memory, through L2) folded in chunk order.
+    auto at_of = [&](uint32_t c, uint32_t m) {
+        return (static_cast<size_t>(c) * a.tokens + row0 + m / G) * a.query_heads + kvh * G + m % G;
+    };
+    fold_chunks(
+        Q, d, ps, stat, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+            const uint32_t p = p_first + (seqs ? 0u : m / G);
+            *c0 = earliest_of(p, a.window) / kChunk;
+            *c1 = p / kChunk;
+        },
+        [&](uint32_t c, uint32_t m, float* cm, float* cl) {
+            const size_t at = at_of(c, m);
+            *cm = __ldcg(a.stats + at * 2u);
+            *cl = __ldcg(a.stats + at * 2u + 1u);
+        },
+        [&](uint32_t c, uint32_t m, uint32_t e) { return __ldcg(a.partials + at_of(c, m) * d + e); },
+        [&](uint32_t m, uint32_t e, float v) {
+            a.out[(static_cast<size_t>(row0 + m / G) * a.query_heads + kvh * G + m % G) * d + e] = v;
+        },
+        lane, wid);
 }
 
 }  // namespace
