@@ -114,15 +114,16 @@ __device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_
 // o_c·fb). The factors depend on the partials only through that running
 // top, a prefix maximum, so here a warp a query finds every chunk's
 // (fa, fb) of a block of 32 chunks at once (a scan of maxima across lanes,
-// then each lane's exp2) and runs the l chain, and then every (query,
-// dimension) runs its o chain in chunk order — the same operations on the
-// same operands as one chunk after the other, so the same bits.
+// then each lane's exp2), and then every (query, dimension) runs its o and
+// l chains in chunk order — the same operations on the same operands as one
+// chunk after the other, so the same bits.
 // `stat_of(c, m, &cm, &cl)` gives chunk c's (m, l) for query m,
 // `part_of(c, m, e)` its partial; queries' chunk ranges from
 // `range_of(m, &c0, &c1)`; `write(m, e, o / l)` takes each output. `fac`
-// holds Q·64 floats of scratch, `carry` Q·4.
+// holds Q·64 floats of scratch, `lfac` Q·32; the CTA must have met a
+// barrier since their last readers.
 template <typename Range, typename Stat, typename Part, typename Write>
-__device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, float* carry, Range range_of,
+__device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, float* lfac, Range range_of,
                                             Stat stat_of, Part part_of, Write write, uint32_t lane, uint32_t wid) {
     uint32_t lo = 0xFFFFFFFFu, hi = 0;
     for (uint32_t m = 0; m < Q; ++m) {
@@ -131,20 +132,23 @@ __device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, 
         lo = min(lo, c0);
         hi = max(hi, c1);
     }
-    const uint32_t warps = blockDim.x / 32u;
-    // Outputs in groups of the CTA's threads, each one thread's o chain.
-    for (uint32_t i0 = 0; i0 < Q * d; i0 += blockDim.x) {
+    constexpr uint32_t warps = kAttnThreads / 32u;
+    // Outputs in groups of the CTA's threads, each one thread's o and l chains.
+    for (uint32_t i0 = 0; i0 < Q * d; i0 += kAttnThreads) {
+        if (i0) __syncthreads();   // the last group's reads of the factors are done
         const uint32_t i = i0 + threadIdx.x;
         const uint32_t me = i / d, e = i % d;
         uint32_t mc0 = 0, mc1 = 0;
         if (i < Q * d) range_of(me, &mc0, &mc1);
-        float o = 0.0f;
-        __syncthreads();   // the last group's reads of carry and fac are done
-        for (uint32_t m = wid; m < Q; m += warps)
-            if (lane == 0) { carry[m * 4u] = -INFINITY; carry[m * 4u + 1u] = 0.0f; }
-        __syncthreads();
+        float o = 0.0f, l = 0.0f;
+        float carry[kMaxQueries / warps];   // the running top of each of this warp's queries
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxQueries / warps; ++k) carry[k] = -INFINITY;
         for (uint32_t base = lo; base <= hi; base += 32u) {
-            for (uint32_t m = wid; m < Q; m += warps) {
+#pragma unroll
+            for (uint32_t k = 0; k < kMaxQueries / warps; ++k) {
+                const uint32_t m = wid + k * warps;
+                if (m >= Q) break;
                 uint32_t c0, c1;
                 range_of(m, &c0, &c1);
                 const uint32_t c = base + lane;
@@ -158,7 +162,7 @@ __device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, 
                     if (lane >= static_cast<uint32_t>(off)) incl = fmaxf(incl, v);
                 }
                 const float before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-                const float top = fmaxf(carry[m * 4u], lane ? before : -INFINITY);   // the running top before c
+                const float top = fmaxf(carry[k], lane ? before : -INFINITY);   // the running top before c
                 float fa = 1.0f, fb = 1.0f;
                 if (in) {
                     if (c == c0) { fa = 0.0f; fb = 1.0f; }
@@ -168,48 +172,41 @@ __device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, 
                 }
                 fac[(m * 32u + lane) * 2u] = fa;
                 fac[(m * 32u + lane) * 2u + 1u] = fb;
-                // l in chunk order (every lane alike; lane 0 keeps it)
-                float run_l = carry[m * 4u + 1u];
-                for (uint32_t j = 0; j < 32u; ++j) {
-                    const float fa_j = __shfl_sync(0xFFFFFFFFu, fa, j), fb_j = __shfl_sync(0xFFFFFFFFu, fb, j);
-                    const float cl_j = __shfl_sync(0xFFFFFFFFu, cl, j);
-                    if (base + j >= c0 && base + j <= c1) run_l = fmaf(run_l, fa_j, cl_j * fb_j);
-                }
-                const float block_top = __shfl_sync(0xFFFFFFFFu, incl, 31);
-                __syncwarp();
-                if (lane == 0) {
-                    carry[m * 4u] = fmaxf(carry[m * 4u], block_top);
-                    carry[m * 4u + 1u] = run_l;
-                }
+                lfac[m * 32u + lane] = cl * fb;
+                carry[k] = fmaxf(carry[k], __shfl_sync(0xFFFFFFFFu, incl, 31));
             }
             __syncthreads();
             if (i < Q * d) {
                 const uint32_t n = mc1 + 1u > base ? min(32u, mc1 + 1u - base) : 0u;
                 const uint32_t j0 = mc0 > base ? mc0 - base : 0u;
-                float co[8];
                 for (uint32_t j = j0; j < n; j += 8u) {
+                    float co[8];
 #pragma unroll
                     for (uint32_t k = 0; k < 8u; ++k) co[k] = j + k < n ? part_of(base + j + k, me, e) : 0.0f;
 #pragma unroll
                     for (uint32_t k = 0; k < 8u; ++k)
-                        if (j + k < n)
-                            o = fmaf(o, fac[(me * 32u + j + k) * 2u], co[k] * fac[(me * 32u + j + k) * 2u + 1u]);
+                        if (j + k < n) {
+                            const float fa = fac[(me * 32u + j + k) * 2u];
+                            o = fmaf(o, fa, co[k] * fac[(me * 32u + j + k) * 2u + 1u]);
+                            l = fmaf(l, fa, lfac[me * 32u + j + k]);
+                        }
                 }
             }
-            __syncthreads();
+            if (base + 32u <= hi) __syncthreads();   // before the next block's factors
         }
-        if (i < Q * d) write(me, e, o / carry[me * 4u + 1u]);
+        if (i < Q * d) write(me, e, o / l);
     }
 }
 
 // The step's rope done in the prologue (decode shapes, `fused`): r is that
 // rope step's arguments.
+template <uint32_t D>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a, RopeArgs r, uint32_t fused,
                                                                  unsigned int* fault) {
     extern __shared__ __align__(16) uint8_t smem[];
-    const uint32_t d = a.head_dim;
-    const uint32_t B = 2048u / d;
-    const uint32_t tiles = kChunk / B;
+    constexpr uint32_t d = D;
+    constexpr uint32_t B = 2048u / D;           // a tile's keys
+    constexpr uint32_t tiles = kChunk / B;
     const bool seqs = a.rows_are_sequences != 0;
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, seqs);
     const uint32_t G = geo.G;
@@ -410,9 +407,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
                 const bool live = lane < B && j <= p && j >= earliest_of(p, a.window);
                 bool chunk_live = false;
                 float chunk_m = 0.0f, al = 1.0f;
-                for (uint32_t u = 0; u <= t; ++u) {
+#pragma unroll
+                for (uint32_t u = 0; u < tiles; ++u) {
                     const float tt = tops[m * 8u + u];
-                    if (tt == -INFINITY) continue;   // no live key in tile u
+                    if (u > t || tt == -INFINITY) continue;   // past tile t, or no live key in tile u
                     const float old = chunk_live ? chunk_m : tt;
                     const float top = fmaxf(old, tt);
                     if (u == t) al = old == top ? 1.0f : exp2_np(old - top);
@@ -423,6 +421,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
                 __syncwarp();
                 if (lane < B) ps[m * kChunk + t * B + lane] = e;
                 float sum = 0.0f;   // in key order
+#pragma unroll
                 for (uint32_t b = 0; b < B; ++b) sum = sum + __shfl_sync(0xFFFFFFFFu, e, b);
                 if (lane == 0) {
                     alpha[m * 8u + t] = al;
@@ -433,6 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             for (uint32_t m = threadIdx.x; m < Q; m += kAttnThreads) {
                 bool chunk_live = false;
                 float chunk_m = 0.0f, chunk_l = 0.0f;
+#pragma unroll
                 for (uint32_t u = 0; u < tiles; ++u) {
                     const float tt = tops[m * 8u + u];
                     if (tt == -INFINITY) continue;
@@ -459,9 +459,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
             // at a tile's first key O·a_t, then the keys' fmas in key order
             // — their weights (two 16-byte reads) and values loaded first,
             // unconditionally (every row of the stage is in bounds), keys
-            // from `valid` on (never staged) skipped. Fully unrolled, so the
-            // loads of later keys go ahead of the chain.
-#pragma unroll
+            // from `valid` on (never staged) skipped.
+#pragma unroll 2
             for (uint32_t b0 = 0; b0 < kChunk; b0 += 8u) {
                 const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
                 const float4 pa = p4[0], pb = p4[1];
@@ -501,7 +500,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         // The chunks (slot = chunk − the tile's first live chunk) folded in
         // chunk order.
         fold_chunks(
-            Q, d, ps, stat, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+            Q, d, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
                 const uint32_t p = p_first + (seqs ? 0u : m / G);
                 *c0 = earliest_of(p, a.window) / kChunk;
                 *c1 = p / kChunk;
@@ -538,7 +537,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         return (static_cast<size_t>(c) * a.tokens + row0 + m / G) * a.query_heads + kvh * G + m % G;
     };
     fold_chunks(
-        Q, d, ps, stat, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+        Q, d, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
             const uint32_t p = p_first + (seqs ? 0u : m / G);
             *c0 = earliest_of(p, a.window) / kChunk;
             *c1 = p / kChunk;
@@ -562,31 +561,18 @@ uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_
     return (tokens + g.rows_per_tile - 1) / g.rows_per_tile;
 }
 
-cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
-    if (!a.rows_are_sequences && a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a))
-        return attention_prefill_run(a, stream, pdl);
+namespace {
+
+template <uint32_t D>
+cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl, size_t base_smem,
+                             size_t cluster_smem, bool decode_shape) {
+    auto kernel = attention_kernel<D>;
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
-    if (a.rope && (geo.G + 2u) * (a.head_dim / 8u) > kAttnThreads) {
-        // More heads than one CTA's threads hold: the rope launch first, then
-        // the attention over its output, as without the fused form.
-        if (cudaError_t e = rope_run(*a.rope, stream, pdl); e != cudaSuccess) return e;
-        AttentionArgs b = a;
-        b.query = a.rope->query;
-        b.rope = nullptr;
-        return attention_run(b, stream, pdl);
-    }
-    const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
-    if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
-    // A one-token decode step may fold over a cluster, with room in rank 0
-    // for every chunk's partial. Batched sequences keep the global fold: the
-    // fold room would halve the CTAs an SM holds across their many row tiles.
-    const bool decode_shape = a.tokens == 1u;
-    const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
         configured = true;
     }
@@ -612,7 +598,7 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
         cfg.numAttrs = 2;
         cfg.dynamicSmemBytes = cluster_smem;
         int clusters = 0;
-        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel, &cfg);   // any arguments
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);   // any arguments
         if (e != cudaSuccess) cudaGetLastError();
         cluster_fits[slots] = e == cudaSuccess && clusters >= 1 ? 1 : -1;
     }
@@ -621,7 +607,34 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     cfg.dynamicSmemBytes = cluster ? cluster_smem : base_smem;
     RopeArgs r{};
     if (a.rope) r = *a.rope;
-    return cudaLaunchKernelEx(&cfg, attention_kernel, a, r, a.rope ? 1u : 0u, fault_word());
+    return cudaLaunchKernelEx(&cfg, kernel, a, r, a.rope ? 1u : 0u, fault_word());
+}
+
+}  // namespace
+
+cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+    if (!a.rows_are_sequences && a.tokens >= kPrefillAttentionRows && attention_prefill_fits(a))
+        return attention_prefill_run(a, stream, pdl);
+    const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
+    if (a.rope && (geo.G + 2u) * (a.head_dim / 8u) > kAttnThreads) {
+        // More heads than one CTA's threads hold: the rope launch first, then
+        // the attention over its output, as without the fused form.
+        if (cudaError_t e = rope_run(*a.rope, stream, pdl); e != cudaSuccess) return e;
+        AttentionArgs b = a;
+        b.query = a.rope->query;
+        b.rope = nullptr;
+        return attention_run(b, stream, pdl);
+    }
+    const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
+    if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
+    // A one-token decode step may fold over a cluster, with room in rank 0
+    // for every chunk's partial. Batched sequences keep the global fold: the
+    // fold room would halve the CTAs an SM holds across their many row tiles.
+    const bool decode_shape = a.tokens == 1u;
+    const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
+    return a.head_dim == 64 ? launch_attention<64>(a, stream, pdl, base_smem, cluster_smem, decode_shape)
+           : a.head_dim == 128 ? launch_attention<128>(a, stream, pdl, base_smem, cluster_smem, decode_shape)
+                               : launch_attention<256>(a, stream, pdl, base_smem, cluster_smem, decode_shape);
 }
 
 }  // namespace cb
