@@ -823,15 +823,21 @@ def run_reference(args):
 
 def run_case(spec, iters):
     """One product launched `iters` times (for profiling): spec is
-    format:rows:K[:tokens[:tensor]], e.g. q4_0:1024:2048, q4_0:4096:1024:512 or
-    q4_0:4096:1024:2048:tensor."""
+    format:rows:K[:tokens[:form]], form one of tensor, split, tiled, streamed,
+    e.g. q4_0:1024:2048, q4_0:4096:1024:512, q4_0:4096:1024:2048:tensor or
+    q4_0:1152:6912:64:split."""
     import torch
     import charlotte_b200 as cb
     fmt_name, rows, K, *rest = spec.split(":")
     fmt = {"q4_0": Q4_0, "q6_k": Q6_K, "q8_0": 8}[fmt_name]
     rows, K = int(rows), int(K)
     tokens = int(rest[0]) if rest else 1
-    flags = 2 if len(rest) > 1 and rest[1] == "tensor" else 0
+    form = rest[1] if len(rest) > 1 else ""
+    flags = {"tensor": cb.MATMUL_TENSOR, "split": cb.MATMUL_SPLIT, "tiled": cb.MATMUL_TILED,
+             "streamed": cb.MATMUL_STREAMED}.get(form, 0)
+    scratch = None
+    if form == "split":
+        scratch = torch.empty(cb.lib().cb_matmul_split_bytes(tokens, rows) // 4, dtype=torch.float32, device="cuda")
     torch.cuda.set_device(0)
     rng = np.random.default_rng(SEED)
     stored = synth.blocks(rng, fmt, rows, K)
@@ -840,7 +846,7 @@ def run_case(spec, iters):
     x = torch.from_numpy(synth.activations(rng, tokens, K)).cuda()
     y = torch.zeros((tokens, rows), dtype=torch.float32, device="cuda")
     for _ in range(iters):
-        cb.matmul(fmt, K, [(piece, nb, 0, rows, 0)], x, [y], flags=flags)
+        cb.matmul(fmt, K, [(piece, nb, 0, rows, 0)], x, [y], flags=flags, scratch=scratch)
     torch.cuda.synchronize()
     cb.check(cb.lib().cb_fault_check(None))
     print(json.dumps({"case": spec, "iters": iters, "ok": True}))
