@@ -97,6 +97,7 @@ class SelectMerge(ctypes.Structure):
 
 
 RUN_PDL = 1
+RUN_TENSOR = 2   # cb_attention_run: the tensor-core form (tolerance tier)
 _lib = None
 
 

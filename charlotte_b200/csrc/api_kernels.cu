@@ -111,6 +111,9 @@ int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream) {
             return fail(CB_ERROR_INVALID, "cb_attention_run: fused rope: both norm gains or neither");
     }
     if (a->tokens == 0) return CB_OK;
+    if ((flags & CB_RUN_TENSOR) && !a->rope && attention_tensor_fits(*a))
+        return launched(attention_tensor_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL),
+                        "cb_attention_run");
     return launched(attention_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_attention_run");
 }
 

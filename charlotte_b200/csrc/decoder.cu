@@ -339,7 +339,10 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         at.window = L.window;
         at.max_chunks = d->max_chunks;
         at.scale_log2e = static_cast<float>(static_cast<double>(m.attention_scale) * 1.4426950408889634);
-        if (int rc = launched(attention_run(at, d->stream, true), "step: attention")) return rc;
+        const bool tensor_attention = d->tensor_prefill && tokens >= kDecoderTensorTokens && attention_tensor_fits(at);
+        if (int rc = launched(tensor_attention ? attention_tensor_run(at, d->stream, true) : attention_run(at, d->stream, true),
+                              "step: attention"))
+            return rc;
         {
             float* outs[3] = {d->out, nullptr, nullptr};
             const uint32_t strides[3] = {H, 0, 0};

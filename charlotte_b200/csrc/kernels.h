@@ -25,6 +25,10 @@ uint32_t attention_row_tiles(uint32_t tokens, uint32_t query_heads, uint32_t kv_
 // The many-query form (attention_prefill.cu): same bits, a CTA per query tile.
 bool attention_prefill_fits(const AttentionArgs& a);
 cudaError_t attention_prefill_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+// The tensor-core form (attention_tensor.cu), the tolerance tier: steps of
+// 16 positions or more, head dimensions 64 and 128, 1, 2, 4 or 8 query heads a kv head.
+bool attention_tensor_fits(const AttentionArgs& a);
+cudaError_t attention_tensor_run(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 // Steps of at least this many rows take the many-query form.
 constexpr uint32_t kPrefillAttentionRows = 32;
 cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl);

@@ -353,8 +353,13 @@ typedef struct cb_select_merge {
 } cb_select_merge;
 CB_API int cb_select_merge_run(const cb_select_merge* m, uint32_t flags, void* stream);
 
-/* Flags of the kernel entry points above. */
-enum { CB_RUN_PDL = 1u };
+/* Flags of the kernel entry points above. CB_RUN_TENSOR (cb_attention_run
+ * only): steps of 16 positions or more (not rows_are_sequences, no fused rope)
+ * with head dimension 64 or 128 and 1, 2, 4 or 8 query heads a kv head run
+ * on the tensor cores — f16 queries and weights, f32 sums in the tensor
+ * cores' order: the tolerance tier, not the reference's bits (no counterpart
+ * in the reference); other shapes keep the exact form. */
+enum { CB_RUN_PDL = 1u, CB_RUN_TENSOR = 2u };
 
 /* ---- weight layout ------------------------------------------------------------
  * The device layout of a weight piece (src/core/formats/device_layout.h:
@@ -418,8 +423,9 @@ typedef struct cb_sampling {
 typedef struct cb_decoder cb_decoder;
 
 enum {
-    /* Steps of 128 tokens or more run their products in the tensor-core
-     * form (CB_MATMUL_TENSOR, tolerance tier) instead of the exact forms;
+    /* Steps of 128 tokens or more run their products (CB_MATMUL_TENSOR)
+     * and, where it fits, their attention (CB_RUN_TENSOR) in the
+     * tensor-core forms, the tolerance tier, instead of the exact forms;
      * shorter steps (decode) and the head's last-token product stay exact.
      * No counterpart in the reference. */
     CB_DECODER_TENSOR_PREFILL = 1u
