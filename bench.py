@@ -458,7 +458,7 @@ def decode_bench(steps, prompt_len, seed, world):
     }
 
 
-def llama_bench(decode_steps, seed, cpu=True):
+def llama_bench(decode_steps, seed, cpu=True, forms=(True, False), profile=False):
     """Llama-3.2-1B shapes, random-init weights, a 2,048-token
     prompt as four 512-token steps on the tcgen05 path
     (CB_DECODER_TENSOR_PREFILL), then `decode_steps` greedy decode steps
@@ -483,9 +483,11 @@ def llama_bench(decode_steps, seed, cpu=True):
     flops = 2.0 * P * layer_params + attention_flops + 2.0 * head.rows * head.cols
     peaks = read_peaks()
     tensor_peak = peaks.get("bf16_tflops_sustained", 1370.0)
-    for tensor in (True, False):
+    for tensor in forms:
         dec = M.Decoder(m, max_step_tokens=512, tensor_prefill=tensor)
         dec.prefill(prompt)   # warm
+        if profile:
+            profiled_region(lambda: dec.prefill(prompt))
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         rec = dec.prefill(prompt)
@@ -513,7 +515,20 @@ def llama_bench(decode_steps, seed, cpu=True):
     return out
 
 
-def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024, cpu=True):
+def profiled_region(fn):
+    """Runs fn() between cudaProfilerStart and cudaProfilerStop: the one
+    region an `ncu --profile-from-start off` launch list captures."""
+    import torch
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    try:
+        return fn()
+    finally:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+
+
+def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024, cpu=True, profile=False):
     """Gemma-3-1B shapes, random-init weights; 64 independent
     sequences with random 1,024-token prompts, sharded over the ranks (64/N
     each, no collective on the data path: strong scaling of a fixed batch);
@@ -539,6 +554,8 @@ def gemma_batch_bench(steps, world, rank, sequences=64, prompt_len=1024, cpu=Tru
     toks, failed, dev_ms = bd.generate(steps, timed=True)
     dev_local = dev_ms
     dev_ms = max_over_ranks(dev_ms, world)
+    if profile:
+        profiled_region(lambda: bd.generate(1))
     bd.close()
     out = {"workload": "gemma-3-1b shapes (configs[4]): %d sequences x %d-token prompts, %d batched steps" % (
                 sequences, prompt_len, steps),
@@ -986,6 +1003,9 @@ def main():
     ap.add_argument("--batch-prompt", type=int, default=1024)
     ap.add_argument("--case", default=None, help="profile one product (format:rows:K) or 'decode'")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-region", action="store_true",
+                    help="--case llama / gemma: bracket one prefill / one batched step with "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.case in ("sweep", "sweep-tensor"):
         print(json.dumps(sweep_bench(flags=2 if args.case == "sweep-tensor" else 0)))
@@ -995,7 +1015,8 @@ def main():
             print(json.dumps(sweep_bench(flags=f, ms=ms, formats=(2,), head=False)))
     elif args.case == "gemma":
         rank, world, local = dist_setup(args.gpus)
-        r = gemma_batch_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt)
+        r = gemma_batch_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt,
+                              cpu=not args.profile_region, profile=args.profile_region)
         if rank == 0:
             print(json.dumps(r))
         if world > 1:
@@ -1016,7 +1037,10 @@ def main():
     elif args.case == "llama":
         import torch
         torch.cuda.set_device(0)
-        print(json.dumps(llama_bench(128, SEED + 11)))
+        if args.profile_region:   # the tensor form's prefill alone, for a launch list
+            print(json.dumps(llama_bench(4, SEED + 11, cpu=False, forms=(True,), profile=True)))
+        else:
+            print(json.dumps(llama_bench(128, SEED + 11)))
     elif args.case == "decode":
         import torch
         torch.cuda.set_device(0)

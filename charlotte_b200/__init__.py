@@ -39,7 +39,7 @@ class Matmul(ctypes.Structure):
                 ("epilogue", ctypes.c_uint32), ("activation", ctypes.c_uint32), ("member", Member * 3),
                 ("gate_input", ctypes.c_void_p), ("gate_input_stride", ctypes.c_uint32),
                 ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32),
-                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64)]
+                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64), ("dense", ctypes.c_void_p)]
 
 
 class Norm(ctypes.Structure):
@@ -142,6 +142,10 @@ def lib() -> ctypes.CDLL:
         L.cb_matmul_scratch_bytes.argtypes = [ctypes.c_uint32] * 3
         L.cb_matmul_split_bytes.restype = ctypes.c_uint64
         L.cb_matmul_split_bytes.argtypes = [ctypes.c_uint32] * 2
+        L.cb_matmul_dense_bytes.restype = ctypes.c_uint64
+        L.cb_matmul_dense_bytes.argtypes = [ctypes.POINTER(Matmul)]
+        L.cb_matmul_densify.restype = ctypes.c_int
+        L.cb_matmul_densify.argtypes = [ctypes.POINTER(Matmul), ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
         _lib = L
     return _lib
 
@@ -167,14 +171,7 @@ def _ptr(t) -> int:
     return 0 if t is None else t.data_ptr()
 
 
-def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, activation: int = SILU,
-           tokens: int | None = None, x_stride: int | None = None, out_stride=None, flags: int = 0,
-           gate_input=None, gate_input_stride: int = 0, gate_input_column: int = 0, gate_input_token: int = 0,
-           stream=None, scratch=None) -> None:
-    """Runs cb_matmul_run. `members`: list of (piece tensor (uint8, cuda), blocks,
-    first_row, rows, out_offset). `x`: f32 cuda tensor [tokens, x_stride].
-    `out`: list of up to 3 f32 cuda tensors. With MATMUL_TENSOR, `scratch`
-    (a cuda tensor of cb_matmul_scratch_bytes) or one allocated here."""
+def _product(fmt, columns, members, epilogue, activation) -> "Matmul":
     m = Matmul()
     m.format = fmt
     m.columns = columns
@@ -183,6 +180,33 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
     m.activation = activation
     for i, (piece, blocks, first_row, rows, out_offset) in enumerate(members):
         m.member[i] = Member(piece.data_ptr(), blocks, first_row, rows, out_offset)
+    return m
+
+
+def densify(fmt: int, columns: int, members, *, epilogue: int = WRITE, activation: int = SILU, stream=None):
+    """cb_matmul_densify: the product's weights as f16 rows in the dense
+    form's slot order (a uint8 cuda tensor), for matmul(..., dense=)."""
+    import torch
+    m = _product(fmt, columns, members, epilogue, activation)
+    n = lib().cb_matmul_dense_bytes(ctypes.byref(m))
+    if n == 0:
+        raise CharlotteError(ERROR_INVALID, last_error())
+    out = torch.empty(n, dtype=torch.uint8, device=members[0][0].device)
+    check(lib().cb_matmul_densify(ctypes.byref(m), out.data_ptr(), n, _stream(stream)))
+    return out
+
+
+def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, activation: int = SILU,
+           tokens: int | None = None, x_stride: int | None = None, out_stride=None, flags: int = 0,
+           gate_input=None, gate_input_stride: int = 0, gate_input_column: int = 0, gate_input_token: int = 0,
+           stream=None, scratch=None, dense=None) -> None:
+    """Runs cb_matmul_run. `members`: list of (piece tensor (uint8, cuda), blocks,
+    first_row, rows, out_offset). `x`: f32 cuda tensor [tokens, x_stride].
+    `out`: list of up to 3 f32 cuda tensors. With MATMUL_TENSOR, `scratch`
+    (a cuda tensor of cb_matmul_scratch_bytes) or one allocated here, and
+    `dense` (densify's tensor for the same product) for the dense form."""
+    m = _product(fmt, columns, members, epilogue, activation)
+    m.dense = _ptr(dense)
     m.gate_input = _ptr(gate_input)
     m.gate_input_stride = gate_input_stride
     m.gate_input_column = gate_input_column

@@ -120,37 +120,81 @@ uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t colum
     return (flags & CB_MATMUL_TENSOR) ? cb::matmul_tensor_scratch_bytes(tokens, columns) : 0u;
 }
 
+namespace {
+
+// The product's description checked and copied into `a` (members, rows,
+// epilogue); `who` names the entry point in messages.
+int product_of(const cb_matmul* m, cb::MatmulArgs& a, const char* who) {
+    using namespace cb;
+    if (!m) return fail(CB_ERROR_INVALID, "%s: null argument", who);
+    if (m->format != CB_Q4_0 && m->format != CB_Q4_1 && m->format != CB_Q8_0 && m->format != CB_Q6_K &&
+        m->format != CB_BF16)
+        return fail(CB_ERROR_INVALID, "%s: format %u has no matmul kernel", who, m->format);
+    if (m->columns == 0 || m->columns % 32 != 0)
+        return fail(CB_ERROR_INVALID, "%s: columns %u is not a whole number of 32-weight groups", who, m->columns);
+    if (m->format == CB_Q6_K && m->columns % 256 != 0)
+        return fail(CB_ERROR_INVALID, "%s: Q6_K rows of %u are not whole 256-weight super-blocks", who, m->columns);
+    if (m->members < 1 || m->members > 3) return fail(CB_ERROR_INVALID, "%s: %u members", who, m->members);
+    if (m->epilogue > CB_EPILOGUE_GATED_BY_INPUT) return fail(CB_ERROR_INVALID, "%s: epilogue %u", who, m->epilogue);
+    if (m->activation > CB_ACT_SIGMOID) return fail(CB_ERROR_INVALID, "%s: activation %u", who, m->activation);
+    if (m->epilogue == CB_EPILOGUE_GATED && (m->members != 2 || m->member[0].rows != m->member[1].rows))
+        return fail(CB_ERROR_INVALID, "%s: a gated product is a gate and an up of equal rows", who);
+    a.format = m->format;
+    a.columns = m->columns;
+    a.members = m->members;
+    a.epilogue = m->epilogue;
+    a.activation = m->activation;
+    uint32_t total = 0;
+    for (uint32_t i = 0; i < m->members; ++i) {
+        const cb_member& s = m->member[i];
+        if (!s.piece || !aligned16(s.piece))
+            return fail(CB_ERROR_INVALID, "%s: member %u's piece is null or not 16-byte aligned", who, i);
+        if (s.rows == 0) return fail(CB_ERROR_INVALID, "%s: member %u has no rows", who, i);
+        const uint64_t groups = static_cast<uint64_t>(s.first_row + s.rows) * (m->columns / 32);
+        // stored blocks: a Q6_K super-block holds 8 groups, a BF16 block one value
+        const uint64_t needed_blocks = m->format == CB_Q6_K ? groups / 8 : (m->format == CB_BF16 ? groups * 32 : groups);
+        if (needed_blocks > s.blocks)
+            return fail(CB_ERROR_INVALID, "%s: member %u reads rows past its piece (%llu of %u blocks)", who, i,
+                        static_cast<unsigned long long>(needed_blocks), s.blocks);
+        a.member[i] = {static_cast<const uint8_t*>(s.piece), s.blocks, s.first_row, s.rows, s.out_offset};
+        total += s.rows;
+    }
+    a.total_rows = m->epilogue == CB_EPILOGUE_GATED ? m->member[0].rows : total;
+    return CB_OK;
+}
+
+}  // namespace
+
+uint64_t cb_matmul_dense_bytes(const cb_matmul* m) {
+    cb::MatmulArgs a{};
+    if (product_of(m, a, "cb_matmul_dense_bytes") != CB_OK) return 0;
+    return cb::matmul_dense_bytes(a);
+}
+
+int cb_matmul_densify(const cb_matmul* m, void* dense, uint64_t dense_bytes, void* stream) {
+    using namespace cb;
+    MatmulArgs a{};
+    if (int rc = product_of(m, a, "cb_matmul_densify")) return rc;
+    if (!dense || !aligned16(dense) || dense_bytes < matmul_dense_bytes(a))
+        return fail(CB_ERROR_INVALID, "cb_matmul_densify: needs %llu bytes of 16-byte aligned memory",
+                    static_cast<unsigned long long>(matmul_dense_bytes(a)));
+    if (cudaError_t e = matmul_densify(a, dense, static_cast<cudaStream_t>(stream)); e != cudaSuccess)
+        return fail_cuda(e, "cb_matmul_densify: launch");
+    return CB_OK;
+}
+
 int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_t tokens, float* const out[3],
                   const uint32_t out_stride[3], uint32_t flags, void* stream) {
     using namespace cb;
     if (!m || !x || !out) return fail(CB_ERROR_INVALID, "cb_matmul_run: null argument");
-    if (m->format != CB_Q4_0 && m->format != CB_Q4_1 && m->format != CB_Q8_0 && m->format != CB_Q6_K &&
-        m->format != CB_BF16)
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: format %u has no matmul kernel", m->format);
-    if (m->columns == 0 || m->columns % 32 != 0)
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: columns %u is not a whole number of 32-weight groups",
-                    m->columns);
-    if (m->format == CB_Q6_K && m->columns % 256 != 0)
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: Q6_K rows of %u are not whole 256-weight super-blocks",
-                    m->columns);
-    if (m->members < 1 || m->members > 3) return fail(CB_ERROR_INVALID, "cb_matmul_run: %u members", m->members);
-    if (m->epilogue > CB_EPILOGUE_GATED_BY_INPUT)
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: epilogue %u", m->epilogue);
-    if (m->activation > CB_ACT_SIGMOID) return fail(CB_ERROR_INVALID, "cb_matmul_run: activation %u", m->activation);
-    if (m->epilogue == CB_EPILOGUE_GATED && (m->members != 2 || m->member[0].rows != m->member[1].rows))
-        return fail(CB_ERROR_INVALID, "cb_matmul_run: a gated product is a gate and an up of equal rows");
+    MatmulArgs a{};
+    if (int rc = product_of(m, a, "cb_matmul_run")) return rc;
     if (m->epilogue == CB_EPILOGUE_GATED_BY_INPUT && !m->gate_input)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: GATED_BY_INPUT without its input u");
     if (tokens == 0) return CB_OK;
     if (x_stride < m->columns) return fail(CB_ERROR_INVALID, "cb_matmul_run: x_stride %u < columns", x_stride);
     if (!aligned16(x) || x_stride % 4 != 0)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: x must be 16-byte aligned with a stride of whole float4s");
-    MatmulArgs a{};
-    a.format = m->format;
-    a.columns = m->columns;
-    a.members = m->members;
-    a.epilogue = m->epilogue;
-    a.activation = m->activation;
     a.token = m->gate_input_token;
     a.tokens = tokens;
     a.x = x;
@@ -161,22 +205,7 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
     a.fault = fault_word();
     if (matmul_decode_smem_bytes(m->format, m->columns) > 220u * 1024u)
         return fail(CB_ERROR_INVALID, "cb_matmul_run: rows of %u are wider than the decode form stages", m->columns);
-    uint32_t total = 0;
-    for (uint32_t i = 0; i < m->members; ++i) {
-        const cb_member& s = m->member[i];
-        if (!s.piece || !aligned16(s.piece))
-            return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u's piece is null or not 16-byte aligned", i);
-        if (s.rows == 0) return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u has no rows", i);
-        const uint64_t groups = static_cast<uint64_t>(s.first_row + s.rows) * (m->columns / 32);
-        // stored blocks: a Q6_K super-block holds 8 groups, a BF16 block one value
-        const uint64_t needed_blocks = m->format == CB_Q6_K ? groups / 8 : (m->format == CB_BF16 ? groups * 32 : groups);
-        if (needed_blocks > s.blocks)
-            return fail(CB_ERROR_INVALID, "cb_matmul_run: member %u reads rows past its piece (%llu of %u blocks)", i,
-                        static_cast<unsigned long long>(needed_blocks), s.blocks);
-        a.member[i] = {static_cast<const uint8_t*>(s.piece), s.blocks, s.first_row, s.rows, s.out_offset};
-        total += s.rows;
-    }
-    a.total_rows = m->epilogue == CB_EPILOGUE_GATED ? m->member[0].rows : total;
+    const uint32_t total = m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : a.total_rows;
     const uint32_t outputs = m->epilogue == CB_EPILOGUE_QKV ? m->members : 1;
     for (uint32_t i = 0; i < outputs; ++i) {
         if (!out[i]) return fail(CB_ERROR_INVALID, "cb_matmul_run: output %u is null", i);
@@ -191,11 +220,17 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
             return fail(CB_ERROR_INVALID, "cb_matmul_run: the tensor form needs %llu bytes of 16-byte aligned scratch",
                         static_cast<unsigned long long>(need));
         a.scratch = m->scratch;
+        a.scratch_bytes = m->scratch_bytes;
+        if (m->dense) {
+            if (!aligned16(m->dense))
+                return fail(CB_ERROR_INVALID, "cb_matmul_run: the dense weights must be 16-byte aligned");
+            a.dense = m->dense;
+        }
     }
     const int sms = sm_count();
     if (sms <= 0) return fail(CB_ERROR_STEP, "cb_matmul_run: no CUDA device");
     const bool pdl = (flags & CB_MATMUL_PDL) != 0;
-    const uint32_t slots = m->epilogue == CB_EPILOGUE_GATED ? 2 * m->member[0].rows : total;
+    const uint32_t slots = total;
     bool tiled = tiled_form(tokens, slots);
     if (flags & CB_MATMUL_STREAMED) tiled = false;
     if (flags & CB_MATMUL_TILED) tiled = true;
@@ -213,7 +248,7 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
         split = true;
     if (split) a.range_sums = static_cast<float*>(m->scratch);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = (flags & CB_MATMUL_TENSOR) ? matmul_tensor(a, st, pdl)
+    cudaError_t e = (flags & CB_MATMUL_TENSOR) ? (a.dense ? matmul_dense(a, sms, st, pdl) : matmul_tensor(a, st, pdl))
                     : split                    ? matmul_split(a, sms, st, pdl)
                     : tiled                    ? matmul_tiled(a, sms, st, pdl)
                                                : matmul_decode(a, sms, st, pdl);

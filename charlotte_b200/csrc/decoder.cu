@@ -61,6 +61,12 @@ struct DevLayer {
     uint16_t* value_cache = nullptr;
     uint32_t window = 0, slots = 0;
     uint64_t sequence_stride = 0;      // elements between sequences' caches
+    // CB_DECODER_TENSOR_PREFILL: each product's weights densified to f16
+    // once at creation (cb_matmul_densify), read by its tensor-form steps.
+    void* dense_qkv = nullptr;
+    void* dense_o = nullptr;
+    void* dense_gate_up = nullptr;
+    void* dense_down = nullptr;
 };
 
 // Records each row's drawn token and advances the step's position (decode
@@ -184,9 +190,8 @@ int launched(cudaError_t e, const char* what) { return e == cudaSuccess ? CB_OK 
 // CB_DECODER_TENSOR_PREFILL.
 constexpr uint32_t kDecoderTensorTokens = 128;
 
-// One matmul launch through the same path as cb_matmul_run.
-int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, const float* x,
-            uint32_t x_stride, uint32_t tokens, float* const outs[3], const uint32_t strides[3]) {
+// A product's description: its members, epilogue and activation.
+cb_matmul description(const cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue) {
     cb_matmul m{};
     const DevWeight* first = *ws.begin();
     m.format = first->format;
@@ -196,11 +201,21 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
     m.activation = d->model.activation;
     uint32_t i = 0;
     for (const DevWeight* w : ws) m.member[i++] = member_of(*w);
+    return m;
+}
+
+// One matmul launch through the same path as cb_matmul_run; `dense`: the
+// product's densified weights for the tensor form (or NULL).
+int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, const float* x,
+            uint32_t x_stride, uint32_t tokens, float* const outs[3], const uint32_t strides[3],
+            const void* dense = nullptr) {
+    cb_matmul m = description(d, ws, epilogue);
     uint32_t flags = CB_MATMUL_PDL;
     if (d->tensor_prefill && tokens >= kDecoderTensorTokens) {
         flags |= CB_MATMUL_TENSOR;
         m.scratch = d->tensor_scratch;
         m.scratch_bytes = d->tensor_scratch_bytes;
+        m.dense = dense;
     } else if (tokens > 1) {
         // range-sum scratch: cb_matmul_run takes the split form where it pays
         m.scratch = d->split_scratch;
@@ -290,7 +305,8 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
             if (int rc = launched(norm_run(n, d->stream, true), "step: attention norm")) return rc;
             float* outs[3] = {d->q, d->k, d->v};
             const uint32_t strides[3] = {qd, kvd, kvd};
-            if (int rc = product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, d->normed, H, tokens, outs, strides))
+            if (int rc = product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, d->normed, H, tokens, outs, strides,
+                                 L.dense_qkv))
                 return rc;
         }
         cb_rope r{};
@@ -346,7 +362,8 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         {
             float* outs[3] = {d->out, nullptr, nullptr};
             const uint32_t strides[3] = {H, 0, 0};
-            if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides)) return rc;
+            if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides, L.dense_o))
+                return rc;
         }
         if (fold) {
             float* outs[3] = {d->act, nullptr, nullptr};
@@ -359,13 +376,16 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
             if (int rc = launched(norm_run(n2, d->stream, true), "step: feed-forward norm")) return rc;
             float* outs[3] = {d->act, nullptr, nullptr};
             const uint32_t strides[3] = {m.ffn, 0, 0};
-            if (int rc = product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, d->normed, H, tokens, outs, strides))
+            if (int rc = product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, d->normed, H, tokens, outs, strides,
+                                 L.dense_gate_up))
                 return rc;
         }
         {
             float* outs[3] = {d->out, nullptr, nullptr};
             const uint32_t strides[3] = {H, 0, 0};
-            if (int rc = product(d, {&L.down}, CB_EPILOGUE_WRITE, d->act, m.ffn, tokens, outs, strides)) return rc;
+            if (int rc = product(d, {&L.down}, CB_EPILOGUE_WRITE, d->act, m.ffn, tokens, outs, strides,
+                                 L.dense_down))
+                return rc;
         }
         pending_add = true;
         pending_post = L.post_ffn_norm;
@@ -586,12 +606,35 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
         }
     }
     if (flags & CB_DECODER_TENSOR_PREFILL) {
+        // x16 for the widest K, then room for the dense form's split-K
+        // partials of the non-gated products (up to 8 splits).
         const uint32_t widest = std::max<uint32_t>(std::max<uint32_t>(H, static_cast<uint32_t>(qd)), m->ffn);
-        d->tensor_scratch_bytes = cb_matmul_scratch_bytes(CB_MATMUL_TENSOR, T, widest);
+        const uint64_t slots = std::max<uint64_t>(H, static_cast<uint64_t>(qd) + 2ull * kvd);
+        d->tensor_scratch_bytes = cb_matmul_scratch_bytes(CB_MATMUL_TENSOR, T, widest) + 8ull * T * slots * 4ull;
         uint8_t* p = nullptr;
         if (int rc = dalloc(d, &p, d->tensor_scratch_bytes)) return bail(rc);
         d->tensor_scratch = p;
         d->tensor_prefill = true;
+        // Every layer product's weights densified once.
+        for (DevLayer& L : d->layers) {
+            struct Want {
+                cb_matmul m;
+                void** dst;
+            } wants[4] = {{description(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV), &L.dense_qkv},
+                          {description(d, {&L.o}, CB_EPILOGUE_WRITE), &L.dense_o},
+                          {description(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED), &L.dense_gate_up},
+                          {description(d, {&L.down}, CB_EPILOGUE_WRITE), &L.dense_down}};
+            for (Want& w : wants) {
+                const uint64_t bytes = cb_matmul_dense_bytes(&w.m);
+                if (bytes == 0) return bail(CB_ERROR_BUILD);
+                uint8_t* q = nullptr;
+                if (int rc = dalloc(d, &q, bytes)) return bail(rc);
+                if (int rc = cb_matmul_densify(&w.m, q, bytes, d->stream)) return bail(rc);
+                *w.dst = q;
+            }
+        }
+        if (cudaError_t se = cudaStreamSynchronize(d->stream); se != cudaSuccess)
+            return bail(fail_cuda(se, "cb_decoder_create: densify"));
     }
     e = cudaMemset(d->tickets, 0, tickets * sizeof(unsigned int));
     if (e == cudaSuccess)

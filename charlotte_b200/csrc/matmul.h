@@ -40,6 +40,8 @@ struct MatmulArgs {
     uint32_t gate_input_column;
     unsigned int* fault;    // device word: a bounded wait that ran out sets a bit
     void* scratch;          // tensor form: x rounded to f16, [tokens][columns]
+    uint64_t scratch_bytes; // tensor form: the dense form's split-K partials follow x16 when they fit
+    const void* dense;      // tensor form: the weights as f16 in the dense layout (matmul_densify)
     // Split form (matmul_split): range r's sum of product row p for token t
     // at range_sums[(r·tokens + t)·total_rows + p] (matmul.wgsl range_sum_at).
     float* range_sums;
@@ -76,6 +78,12 @@ bool split_form(uint32_t tokens, uint32_t slots, uint32_t columns, uint32_t epil
 
 // Tensor-core form (tolerance tier, f16 operands, f32 accumulation in TMEM).
 cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl);
+// The dense tensor form: the product's weights already decoded to f16 rows
+// (matmul_densify, once), so both operands come by TMA; `sms` sizes the
+// tiles and the split of K.
+uint64_t matmul_dense_bytes(const MatmulArgs& a);
+cudaError_t matmul_densify(const MatmulArgs& a, void* dense, cudaStream_t stream);
+cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool pdl);
 uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns);
 
 // Which exact form a step takes by default: the streamed (decode-layout)

@@ -347,41 +347,30 @@ cudaError_t launch_tensor(const MatmulArgs& a, const CUtensorMap& map, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, a, map);
 }
 
-}  // namespace
-
-uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns) {
-    return (static_cast<uint64_t>(tokens) * columns * 2u + 255u) / 256u * 256u;
+// x rounded to f16 into the scratch.
+cudaError_t launch_to_f16(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
+    const uint32_t quads = a.tokens * (a.columns / 4u);
+    uint32_t blocks = (quads + 255u) / 256u;
+    if (blocks > 4096u) blocks = 4096u;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, to_f16_kernel, a.x, a.x_stride, a.columns, a.tokens,
+                              static_cast<__half2*>(a.scratch));
 }
 
-cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
-    // 1. x to f16 in the scratch.
-    {
-        const uint32_t quads = a.tokens * (a.columns / 4u);
-        uint32_t blocks = (quads + 255u) / 256u;
-        if (blocks > 4096u) blocks = 4096u;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(blocks);
-        cfg.blockDim = dim3(256);
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, to_f16_kernel, a.x, a.x_stride, a.columns, a.tokens,
-                                           static_cast<__half2*>(a.scratch));
-        if (e != cudaSuccess) return e;
-    }
-    // 2. The map of x16: [tokens][K] f16, boxes of 64 × 128 with the 128-byte
-    //    swizzle; rows past `tokens` and columns past K read as zero.
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {a.columns, a.tokens};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.columns) * 2u};
-    const cuuint32_t box[2] = {kBK, kBM};
-    const cuuint32_t elem[2] = {1, 1};
-    // The driver's encoder, looked up through the runtime once (the library
-    // does not link the driver library, so it still loads where there is no
-    // GPU driver).
+// The map of an f16 [rows][K] matrix: boxes of 64 × box_rows with the
+// 128-byte swizzle; rows past `rows` and columns past K read as zero. The
+// driver's encoder is looked up through the runtime once (the library does
+// not link the driver library, so it still loads where there is no GPU
+// driver).
+cudaError_t encode_f16_map(CUtensorMap* map, const void* base, uint32_t K, uint32_t rows, uint32_t box_rows) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
@@ -391,10 +380,348 @@ cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
             return cudaErrorNotSupported;
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
-    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.scratch, dims, strides, box,
-                                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2u};
+    const cuuint32_t box[2] = {kBK, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+
+// ---- the dense form ----------------------------------------------------------
+//
+// The product's weights are decoded once (exactly, then rounded to f16) into
+// a dense [slots][K] matrix — at load time by a runtime that keeps it, or
+// once per call — so the GEMM streams both operands by TMA and the tensor
+// core is fed without producer warps. Slot order: the members' rows one
+// after another; a gated product interleaves 64-slot units, 64 outputs'
+// gate rows then the same outputs' up rows, so any 128-slot-aligned tile
+// holds whole (gate, up) pairs. Padding slots are zero rows.
+
+// Slot s's member (-1: a zero row) and weight row.
+struct SlotRow {
+    int q;
+    uint32_t row;
+};
+__device__ __forceinline__ SlotRow slot_row(const MatmulArgs& a, uint32_t s) {
+    if (a.epilogue == kGated) {
+        const uint32_t unit = s / 64u, o = (unit / 2u) * 64u + s % 64u;
+        if (o >= a.member[0].rows) return {-1, 0u};
+        return (unit & 1u) ? SlotRow{1, a.member[1].first_row + o} : SlotRow{0, a.member[0].first_row + o};
+    }
+    uint32_t n = s;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        if (i < static_cast<int>(a.members)) {
+            const uint32_t rows = i == 0 ? a.member[0].rows : (i == 1 ? a.member[1].rows : a.member[2].rows);
+            if (n < rows) {
+                const uint32_t first = i == 0 ? a.member[0].first_row : (i == 1 ? a.member[1].first_row : a.member[2].first_row);
+                return {i, first + n};
+            }
+            n -= rows;
+        }
+    }
+    return {-1, 0u};
+}
+
+__host__ __device__ __forceinline__ uint32_t dense_slot_count(const MatmulArgs& a) {
+    return a.epilogue == kGated ? 128u * ((a.member[0].rows + 63u) / 64u) : a.total_rows;
+}
+
+// A warp a slot row: each lane decodes 32-weight groups and stores them as
+// 64 contiguous bytes of f16.
+template <typename F>
+__global__ void __launch_bounds__(256) densify_kernel(const MatmulArgs a, uint32_t slots, uint4* dense) {
+    const uint32_t G = a.columns / 32u, lane = threadIdx.x & 31u;
+    const uint32_t warps = blockDim.x / 32u;
+    for (uint32_t s = blockIdx.x * warps + threadIdx.x / 32u; s < slots; s += gridDim.x * warps) {
+        uint4* dst = dense + static_cast<size_t>(s) * (a.columns / 8u);
+        const SlotRow sr = slot_row(a, s);
+        if (sr.q < 0) {
+            for (uint32_t g = lane; g < G; g += 32u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dst[4u * g + i] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+        }
+        const uint8_t* piece = sr.q == 1 ? a.member[1].piece : (sr.q == 2 ? a.member[2].piece : a.member[0].piece);
+        const uint32_t blocks = sr.q == 1 ? a.member[1].blocks : (sr.q == 2 ? a.member[2].blocks : a.member[0].blocks);
+        const uint8_t* sp[F::kStreams];
+#pragma unroll
+        for (int q = 0; q < F::kStreams; ++q)
+            sp[q] = piece + RowStreams<F>::base(q, blocks) + static_cast<uint64_t>(sr.row) * RowStreams<F>::row_bytes(q, G);
+        for (uint32_t g = lane; g < G; g += 32u) {
+            F f;
+            f.load(sp, g);
+            const typename F::Consts c = f.consts();
+            uint32_t lo[8], hi[8];
+            decode16<F, 0>(f, c, lo, std::make_integer_sequence<int, 16>{});
+            decode16<F, 16>(f, c, hi, std::make_integer_sequence<int, 16>{});
+            dst[4u * g + 0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            dst[4u * g + 1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+            dst[4u * g + 2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            dst[4u * g + 3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+        }
+    }
+}
+
+// Output of non-gated slot n for token t: its member's output and column.
+__device__ __forceinline__ void put_slot(const MatmulArgs& a, uint32_t t, uint32_t n, float v) {
+    int q = -1;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        if (q < 0 && m < static_cast<int>(a.members)) {
+            const uint32_t rows = m == 0 ? a.member[0].rows : (m == 1 ? a.member[1].rows : a.member[2].rows);
+            if (n < rows) q = m;
+            else n -= rows;
+        }
+    }
+    if (q < 0) return;
+    const uint32_t o = (q == 1 ? a.member[1].out_offset : (q == 2 ? a.member[2].out_offset : a.member[0].out_offset)) + n;
+    if (a.epilogue == kQKV) {
+        float* out = q == 1 ? a.out[1] : (q == 2 ? a.out[2] : a.out[0]);
+        const uint32_t st = q == 1 ? a.out_stride[1] : (q == 2 ? a.out_stride[2] : a.out_stride[0]);
+        out[static_cast<size_t>(t) * st + o] = v;
+    } else if (a.epilogue == kWrite) {
+        a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = v;
+    } else {   // kGatedByInput
+        const float u =
+            a.gate_input[static_cast<size_t>(a.token + t) * a.gate_input_stride + a.gate_input_column + o];
+        a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, v) * u;
+    }
+}
+
+__device__ __forceinline__ void put_gated(const MatmulArgs& a, uint32_t t, uint32_t o, float g, float u) {
+    a.out[0][static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o] = activate(a.activation, g) * u;
+}
+
+template <uint32_t BN>
+struct Dense {
+    static constexpr uint32_t kA = kBM * kBK * 2;                 // 16 KB of x16
+    static constexpr uint32_t kB = BN * kBK * 2;                  // 16 or 32 KB of weights
+    static constexpr uint32_t kStage = kA + kB;
+    static constexpr uint32_t kStages = (192u * 1024u) / kStage;  // 6 or 4
+    static constexpr uint32_t kCs = BN + 1;                       // floats a staged row
+    static constexpr size_t kSmem = 1024 + kStages * kStage + 256;
+    static_assert(kBM * kCs * 4 <= kStages * kStage, "the staged tile fits the drained ring");
+};
+
+// One CTA a 128-token × BN-slot tile over K blocks [kb0, kb1) of split z:
+// warp 0's lane 0 loads both operands by TMA (the first stages' weights
+// before the wait on the previous kernel, which they do not depend on),
+// warp 1's lane 0 issues the MMAs (M = 128, N = BN, K = 16, four a block)
+// into a BN-column f32 accumulator in tensor memory, and all four warps
+// read it back (warp w: lanes 32w ...) through shared memory into
+// coalesced row writes: the epilogue, or split z's raw partial tile.
+template <uint32_t BN>
+__global__ void __launch_bounds__(128, 1)
+    dense_kernel(const MatmulArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                 uint32_t splits, float* partials) {
+    using S = Dense<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStages * S::kStage);
+    uint64_t* empty = full + S::kStages;
+    uint64_t* done = empty + S::kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t all_blocks = (a.columns + kBK - 1u) / kBK;
+    const uint32_t kb0 = all_blocks * blockIdx.z / splits, kb1 = all_blocks * (blockIdx.z + 1u) / splits;
+    const uint32_t kblocks = kb1 - kb0;
+    const uint32_t m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+    const uint32_t slots = dense_slot_count(a);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < S::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t pre = kblocks < S::kStages ? kblocks : S::kStages;
+            for (uint32_t i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&full[i], S::kStage);
+                tma_load_2d(base + i * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + i) * kBK),
+                            static_cast<int32_t>(n0), &full[i]);
+            }
+            grid_dependency_wait();   // x16 is the previous kernel's output
+            for (uint32_t i = 0; i < pre; ++i)
+                tma_load_2d(base + i * S::kStage, &xmap, static_cast<int32_t>((kb0 + i) * kBK), static_cast<int32_t>(m0),
+                            &full[i]);
+            uint32_t issued = pre;
+            for (uint32_t kb = pre; kb < kblocks; ++kb) {
+                const uint32_t s = kb % S::kStages;
+                if (!mbar_wait(&empty[s], ((kb / S::kStages) - 1u) & 1u, a.fault)) break;
+                mbar_arrive_expect_tx(&full[s], S::kStage);
+                tma_load_2d(base + s * S::kStage, &xmap, static_cast<int32_t>((kb0 + kb) * kBK), static_cast<int32_t>(m0),
+                            &full[s]);
+                tma_load_2d(base + s * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + kb) * kBK),
+                            static_cast<int32_t>(n0), &full[s]);
+                issued = kb + 1u;
+            }
+            // Every copy issued has landed before this CTA's shared memory is
+            // reused or released (immediate unless a wait above ran out).
+            for (uint32_t kb = issued > S::kStages ? issued - S::kStages : 0u; kb < issued; ++kb)
+                mbar_wait(&full[kb % S::kStages], (kb / S::kStages) & 1u, nullptr);
+        }
+        __syncwarp();
+    } else {
+        grid_dependency_wait();
+        if (warp == 1) {
+            constexpr uint32_t idesc = umma_idesc_f16(kBM, BN);
+            for (uint32_t kb = 0; kb < kblocks; ++kb) {
+                const uint32_t s = kb % S::kStages;
+                if (!mbar_wait(&full[s], (kb / S::kStages) & 1u, a.fault)) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_addr = smem_addr(base + s * S::kStage);
+                    const uint64_t da = umma_desc_sw128(a_addr), db = umma_desc_sw128(a_addr + S::kA);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / 16u; ++kk)
+                        umma_f16(tmem, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0u ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) umma_commit(done);
+            __syncwarp();
+        }
+    }
+    grid_dependents_launch();
+
+    const bool ok = mbar_wait(done, 0u, a.fault);
+    float* cs = reinterpret_cast<float*>(base);
+    if (ok) {
+        tc_fence_after();
+        fence_proxy_async();   // the ring was last written by the copy engine
+        const uint32_t row = 32u * warp + lane;
+        const uint32_t taddr = tmem + ((32u * warp) << 16);
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < BN; c0 += 32u) {
+            float v[32];
+            tmem_ld32(taddr + c0, v);
+#pragma unroll
+            for (uint32_t i = 0; i < 32u; ++i) cs[row * S::kCs + c0 + i] = v[i];
+        }
+    }
+    __syncthreads();
+    if (ok) {
+        if (splits > 1u) {
+            // split z's raw sums: partials[(z·tokens + t)·slots + n]
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
+                float* dst = partials + (static_cast<size_t>(blockIdx.z) * a.tokens + m0 + r) * slots;
+#pragma unroll
+                for (uint32_t j = 0; j < BN / 32u; ++j) {
+                    const uint32_t n = n0 + lane + 32u * j;
+                    if (n < slots) dst[n] = cs[r * S::kCs + lane + 32u * j];
+                }
+            }
+        } else if (a.epilogue == kGated) {
+            // the tile's outputs: BN/2, unit pairs (gate 64, up 64)
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
+#pragma unroll
+                for (uint32_t j = 0; j < BN / 64u; ++j) {
+                    const uint32_t c = lane + 32u * j, gc = (c / 64u) * 128u + c % 64u;
+                    const uint32_t o = n0 / 2u + c;
+                    if (o < a.member[0].rows)
+                        put_gated(a, m0 + r, o, cs[r * S::kCs + gc], cs[r * S::kCs + gc + 64u]);
+                }
+            }
+        } else {
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
+#pragma unroll
+                for (uint32_t j = 0; j < BN / 32u; ++j) {
+                    const uint32_t n = n0 + lane + 32u * j;
+                    if (n < slots) put_slot(a, m0 + r, n, cs[r * S::kCs + lane + 32u * j]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+// The splits' partial sums added in order (split 0 first), then the
+// epilogue. A thread an output of a token.
+__global__ void dense_combine_kernel(const MatmulArgs a, uint32_t splits, const float* partials) {
+    grid_dependency_wait();
+    const uint32_t slots = dense_slot_count(a);
+    const bool gated = a.epilogue == kGated;
+    const uint32_t outputs = gated ? a.member[0].rows : slots;
+    const size_t plane = static_cast<size_t>(a.tokens) * slots;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.tokens * outputs; i += gridDim.x * blockDim.x) {
+        const uint32_t t = i / outputs, o = i % outputs;
+        const uint32_t n = gated ? (o / 64u) * 128u + o % 64u : o;
+        const float* p = partials + static_cast<size_t>(t) * slots + n;
+        float v = p[0];
+        for (uint32_t z = 1; z < splits; ++z) v += p[z * plane];
+        if (gated) {
+            float u = p[64];
+            for (uint32_t z = 1; z < splits; ++z) u += p[z * plane + 64];
+            put_gated(a, t, o, v, u);
+        } else {
+            put_slot(a, t, n, v);
+        }
+    }
+    grid_dependents_launch();
+}
+
+template <uint32_t BN>
+cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUtensorMap& wmap, uint32_t splits,
+                         float* partials, cudaStream_t stream, bool pdl) {
+    using S = Dense<BN>;
+    auto kernel = dense_kernel<BN>;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(S::kSmem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.tokens + kBM - 1) / kBM, (dense_slot_count(a) + BN - 1) / BN, splits);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a, xmap, wmap, splits, partials);
+}
+
+}  // namespace
+
+uint64_t matmul_tensor_scratch_bytes(uint32_t tokens, uint32_t columns) {
+    return (static_cast<uint64_t>(tokens) * columns * 2u + 255u) / 256u * 256u;
+}
+
+cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
+    // 1. x to f16 in the scratch.
+    if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
+    // 2. The map of x16: [tokens][K] f16, boxes of 64 × 128.
+    CUtensorMap map;
+    if (cudaError_t e = encode_f16_map(&map, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
     switch (a.format) {
         case kQ4_0: return launch_tensor<Q4_0>(a, map, stream, pdl);
         case kQ8_0: return launch_tensor<Q8_0>(a, map, stream, pdl);
@@ -403,6 +730,73 @@ cudaError_t matmul_tensor(const MatmulArgs& a, cudaStream_t stream, bool pdl) {
         case kBF16: return launch_tensor<BF16>(a, map, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
+}
+
+
+uint64_t matmul_dense_bytes(const MatmulArgs& a) {
+    return static_cast<uint64_t>(dense_slot_count(a)) * a.columns * 2u;
+}
+
+cudaError_t matmul_densify(const MatmulArgs& a, void* dense, cudaStream_t stream) {
+    const uint32_t slots = dense_slot_count(a);
+    const uint32_t blocks = (slots + 7u) / 8u < 4096u ? (slots + 7u) / 8u : 4096u;
+    uint4* d = static_cast<uint4*>(dense);
+    switch (a.format) {
+        case kQ4_0: densify_kernel<Q4_0><<<blocks, 256, 0, stream>>>(a, slots, d); break;
+        case kQ8_0: densify_kernel<Q8_0><<<blocks, 256, 0, stream>>>(a, slots, d); break;
+        case kQ6_K: densify_kernel<Q6_K><<<blocks, 256, 0, stream>>>(a, slots, d); break;
+        case kQ4_1: densify_kernel<Q4_1><<<blocks, 256, 0, stream>>>(a, slots, d); break;
+        case kBF16: densify_kernel<BF16><<<blocks, 256, 0, stream>>>(a, slots, d); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool pdl) {
+    const uint32_t slots = dense_slot_count(a);
+    const uint32_t mt = (a.tokens + kBM - 1u) / kBM;
+    const uint32_t sm = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
+    // N = 256 tiles (fewer operand bytes a flop) when they fill the GPU;
+    // else 128, for more CTAs.
+    const uint32_t bn = mt * ((slots + 255u) / 256u) >= sm ? 256u : 128u;
+    const uint32_t tiles = mt * ((slots + bn - 1u) / bn);
+    // Split K when the tiles leave SMs idle: the split count with the fewest
+    // waves a split (ties: fewer splits), each split at least 8 K blocks,
+    // its partials where the scratch has room after x16.
+    const uint32_t kblocks = (a.columns + kBK - 1u) / kBK;
+    const uint64_t x16 = matmul_tensor_scratch_bytes(a.tokens, a.columns);
+    uint32_t splits = 1;
+    double best = static_cast<double>((tiles + sm - 1u) / sm);
+    for (uint32_t z = 2; z <= 8u && kblocks / z >= 8u; ++z) {
+        if (x16 + static_cast<uint64_t>(z) * a.tokens * slots * 4u > a.scratch_bytes) break;
+        const double cost = static_cast<double>((tiles * z + sm - 1u) / sm) / z;
+        if (cost < best - 1e-9) {
+            best = cost;
+            splits = z;
+        }
+    }
+    float* partials = splits > 1u ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.scratch) + x16) : nullptr;
+
+    if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
+    CUtensorMap xmap, wmap;
+    if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
+    if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, bn); e != cudaSuccess) return e;
+    cudaError_t e = bn == 256u ? launch_dense<256>(a, xmap, wmap, splits, partials, stream, pdl)
+                               : launch_dense<128>(a, xmap, wmap, splits, partials, stream, pdl);
+    if (e != cudaSuccess || splits == 1u) return e;
+    const uint32_t outputs = a.epilogue == kGated ? a.member[0].rows : slots;
+    const uint64_t n = static_cast<uint64_t>(a.tokens) * outputs;
+    const uint32_t blocks = static_cast<uint32_t>((n + 255u) / 256u < 4096u ? (n + 255u) / 256u : 4096u);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dense_combine_kernel, a, splits, static_cast<const float*>(partials));
 }
 
 }  // namespace cb

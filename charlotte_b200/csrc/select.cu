@@ -11,8 +11,9 @@
 // descending, padding 0. Any exact selection of the 64 largest keys gives
 // the reference's candidates, in its order.
 //
-// B200 mapping: one launch. Each CTA sorts a tile of 1,024 keys (bitonic, in
-// shared memory) and writes its top 64. The last CTA of each group of 16
+// B200 mapping: one launch. Each CTA takes a tile of 1,024 keys and writes
+// its top 64, sorted (bitonic networks in registers: warps sort 32 keys,
+// lists of 64 halve by top-64 merges). The last CTA of each group of 16
 // tiles to finish (an atomic ticket, no waiting) merges the group's sorted
 // lists pairwise by rank; the last group to finish merges the groups' lists
 // the same way and runs the draw on the 64 candidates, writing the 16-byte
@@ -45,41 +46,68 @@ __device__ __forceinline__ void entry_pair(uint64_t k, uint32_t* out) {
     out[1] = 0xFFFFFFFFu - static_cast<uint32_t>(k);
 }
 
-// Bitonic sort of 1,024 keys, descending, thread t holding position t: the
-// stages whose partner (t ^ j, j < 32) is in the same warp run in registers
-// with shuffles; the wider stages compare and swap in shared memory, one
-// barrier a stage. The sorted keys are left in `keys`.
-__device__ void sort_tile(uint64_t* keys) {
-    const uint32_t t = threadIdx.x;
-    uint64_t v = keys[t];
-    for (uint32_t k = 2; k <= kTile; k <<= 1) {
-        if (k > 32u) {
-            keys[t] = v;
-            __syncthreads();
-            for (uint32_t j = k >> 1; j >= 32u; j >>= 1) {
-                const uint32_t ixj = t ^ j;
-                if (ixj > t) {
-                    const uint64_t a = keys[t], b = keys[ixj];
-                    const bool descending = (t & k) == 0;
-                    if (descending ? a < b : a > b) {
-                        keys[t] = b;
-                        keys[ixj] = a;
-                    }
-                }
-                __syncthreads();
-            }
-            v = keys[t];
+// One compare-exchange of a bitonic network between lanes `lane` and
+// `lane ^ j` of a warp (one register each): the lower lane keeps the larger
+// key when the run is descending, the smaller when ascending.
+__device__ __forceinline__ uint64_t exchange(uint64_t v, uint32_t j, bool descending, uint32_t lane) {
+    const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, j);
+    return (((lane & j) == 0) == descending) ? (v > w ? v : w) : (v < w ? v : w);
+}
+
+// Sorts a bitonic 64-key list held as (r0: positions 0..31, r1: 32..63,
+// position = lane + 32·register) descending.
+__device__ __forceinline__ void bitonic_merge64(uint64_t& r0, uint64_t& r1, uint32_t lane) {
+    const uint64_t hi = r0 > r1 ? r0 : r1, lo = r0 > r1 ? r1 : r0;
+    r0 = hi;
+    r1 = lo;
+#pragma unroll
+    for (uint32_t j = 16; j > 0; j >>= 1) {
+        r0 = exchange(r0, j, true, lane);
+        r1 = exchange(r1, j, true, lane);
+    }
+}
+
+// The 64 largest of the tile's 1,024 keys (thread t holding `v`, position
+// t), sorted descending, into buf[0..63]. Each warp sorts its 32 keys in
+// registers (a bitonic sort over the lanes); warp w < 16 joins its list
+// with warp w + 16's into a sorted 64; then the lists halve four times,
+// warp w keeping the top 64 of its list and list w + n/2's: the larger of
+// A[i] and B[63 − i] at each position is a bitonic sequence holding exactly
+// the union's top 64, which one bitonic merge sorts. Lists pass through
+// `buf` (1,024 keys), one barrier a level.
+__device__ void top_of_tile(uint64_t v, uint64_t* buf) {
+    const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+#pragma unroll
+    for (uint32_t k = 2; k <= 32u; k <<= 1)
+#pragma unroll
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) v = exchange(v, j, (lane & k) == 0, lane);
+    if (warp >= 16u) buf[(warp - 16u) * 64u + 32u + lane] = v;
+    __syncthreads();
+    uint64_t r0 = v, r1 = 0;
+    if (warp < 16u) {
+        r1 = buf[warp * 64u + 32u + (31u - lane)];   // the other list reversed: ascending
+        bitonic_merge64(r0, r1, lane);
+    }
+    for (uint32_t n = 16; n > 1u; n >>= 1) {
+        __syncthreads();   // the last level's reads of buf are done
+        if (warp >= n / 2u && warp < n) {
+            buf[warp * 64u + lane] = r0;
+            buf[warp * 64u + 32u + lane] = r1;
         }
-        for (uint32_t j = min(k >> 1, 16u); j > 0; j >>= 1) {
-            const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, j);
-            // The lower position of a pair keeps the larger key in a
-            // descending run, the smaller in an ascending one.
-            const bool keep_larger = ((t & k) == 0) == ((t & j) == 0);
-            v = keep_larger ? (v > w ? v : w) : (v < w ? v : w);
+        __syncthreads();
+        if (warp < n / 2u) {
+            const uint64_t* b = buf + (warp + n / 2u) * 64u;
+            const uint64_t b0 = b[63u - lane], b1 = b[31u - lane];
+            r0 = r0 > b0 ? r0 : b0;
+            r1 = r1 > b1 ? r1 : b1;
+            bitonic_merge64(r0, r1, lane);
         }
     }
-    __syncthreads();   // every thread's reads of `keys` are done
-    keys[t] = v;
+    __syncthreads();
+    if (warp == 0u) {
+        buf[lane] = r0;
+        buf[32u + lane] = r1;
+    }
     __syncthreads();
 }
 
@@ -251,10 +279,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectArgs a) {
         const uint32_t e = tile * kTile + t;
         uint64_t k = 0;
         if (e < a.count) k = entry_key(__float_as_uint(a.logits[e]), e + a.id_offset);
-        buf[t] = k;
+        top_of_tile(k, buf);
     }
-    __syncthreads();
-    sort_tile(buf);
     if (t < kKeep) entry_pair(buf[t], a.partials + 2u * (tile * kKeep + t));
     grid_dependents_launch();
 

@@ -129,8 +129,15 @@ typedef struct cb_matmul {
     uint32_t gate_input_token;     /* u's row of the first token                         */
     void* scratch;                 /* CB_MATMUL_TENSOR: cb_matmul_scratch_bytes() of
                                       device memory, 16-byte aligned (x rounded to f16);
-                                      the exact forms ignore it                          */
+                                      with `dense`, room after that lets the product
+                                      split K (up to 8·tokens·slots floats); the exact
+                                      forms take the split form's range sums here        */
     uint64_t scratch_bytes;
+    const void* dense;             /* CB_MATMUL_TENSOR: NULL, or the product's weights
+                                      as f16 rows written by cb_matmul_densify for these
+                                      same members and epilogue (16-byte aligned): the
+                                      dense form, both operands fed to the tensor cores
+                                      by TMA; the pieces are then not read               */
 } cb_matmul;
 
 /* y[t][o] = Σ_k W[o][k]·x[t][k] for tokens t in [0, tokens), each output
@@ -143,6 +150,14 @@ CB_API int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, 
  * (0 for the exact forms). No counterpart in the reference (its prefill is
  * exact f32 only). */
 CB_API uint64_t cb_matmul_scratch_bytes(uint32_t flags, uint32_t tokens, uint32_t columns);
+/* The dense form's weights (no counterpart in the reference): each weight
+ * of the product decoded exactly and rounded to f16 (nearest even), as
+ * [slots][columns] rows — the members' rows in order; a gated product's in
+ * 64-row units alternating gate and up rows of the same outputs, padded
+ * with zero rows to whole 128-row pairs. A runtime writes them once (at
+ * load) and passes them with every tensor-form call of the product. */
+CB_API uint64_t cb_matmul_dense_bytes(const cb_matmul* m);
+CB_API int cb_matmul_densify(const cb_matmul* m, void* dense, uint64_t dense_bytes, void* stream);
 /* The split form's range-sum scratch for `tokens` rows of a product of
  * `rows` outputs: 32·tokens·rows floats, laid out as the reference's
  * range_sums (range_sum_at: (r·tokens + t)·rows + p, matmul.wgsl:600). */
