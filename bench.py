@@ -840,9 +840,10 @@ def run_reference(args):
 
 def run_case(spec, iters):
     """One product launched `iters` times (for profiling): spec is
-    format:rows:K[:tokens[:form]], form one of tensor, split, tiled, streamed,
-    e.g. q4_0:1024:2048, q4_0:4096:1024:512, q4_0:4096:1024:2048:tensor or
-    q4_0:1152:6912:64:split."""
+    format:rows:K[:tokens[:form]], form one of tensor, dense (the tensor form
+    over weights densified first), split, tiled, streamed, e.g.
+    q4_0:1024:2048, q4_0:4096:1024:512, q4_0:4096:1024:2048:tensor or
+    q4_0:1152:6912:64:split. Prints the mean device time a launch."""
     import torch
     import charlotte_b200 as cb
     fmt_name, rows, K, *rest = spec.split(":")
@@ -850,23 +851,34 @@ def run_case(spec, iters):
     rows, K = int(rows), int(K)
     tokens = int(rest[0]) if rest else 1
     form = rest[1] if len(rest) > 1 else ""
-    flags = {"tensor": cb.MATMUL_TENSOR, "split": cb.MATMUL_SPLIT, "tiled": cb.MATMUL_TILED,
-             "streamed": cb.MATMUL_STREAMED}.get(form, 0)
+    flags = {"tensor": cb.MATMUL_TENSOR, "dense": cb.MATMUL_TENSOR, "split": cb.MATMUL_SPLIT,
+             "tiled": cb.MATMUL_TILED, "streamed": cb.MATMUL_STREAMED}.get(form, 0)
     scratch = None
     if form == "split":
         scratch = torch.empty(cb.lib().cb_matmul_split_bytes(tokens, rows) // 4, dtype=torch.float32, device="cuda")
+    if form == "dense":
+        n = cb.lib().cb_matmul_scratch_bytes(flags, tokens, K) + 8 * tokens * rows * 4
+        scratch = torch.empty(n, dtype=torch.uint8, device="cuda")
     torch.cuda.set_device(0)
     rng = np.random.default_rng(SEED)
     stored = synth.blocks(rng, fmt, rows, K)
     nb = stored.size // synth.BLOCK_BYTES[fmt]
     piece = torch.from_numpy(synth.to_piece(fmt, stored)).cuda()
+    members = [(piece, nb, 0, rows, 0)]
+    dense = cb.densify(fmt, K, members) if form == "dense" else None
     x = torch.from_numpy(synth.activations(rng, tokens, K)).cuda()
     y = torch.zeros((tokens, rows), dtype=torch.float32, device="cuda")
-    for _ in range(iters):
-        cb.matmul(fmt, K, [(piece, nb, 0, rows, 0)], x, [y], flags=flags, scratch=scratch)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(iters):
+        if i == 1:
+            e0.record()
+        cb.matmul(fmt, K, members, x, [y], flags=flags | cb.MATMUL_PDL, scratch=scratch, dense=dense)
+    e1.record()
     torch.cuda.synchronize()
     cb.check(cb.lib().cb_fault_check(None))
-    print(json.dumps({"case": spec, "iters": iters, "ok": True}))
+    us = e0.elapsed_time(e1) * 1e3 / max(iters - 1, 1)
+    print(json.dumps({"case": spec, "iters": iters, "ok": True, "us": round(us, 2),
+                      "tflops": round(2.0 * tokens * rows * K / us / 1e6, 1)}))
 
 
 SWEEP_SHAPES = [("qkv", 4096, 1024), ("o", 1024, 2048), ("gate_up", 6144, 1024), ("down", 1024, 3072)]

@@ -497,29 +497,33 @@ __device__ __forceinline__ void put_gated(const MatmulArgs& a, uint32_t t, uint3
     a.out[0][static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o] = activate(a.activation, g) * u;
 }
 
-template <uint32_t BN>
+template <uint32_t BN, uint32_t MT>
 struct Dense {
-    static constexpr uint32_t kA = kBM * kBK * 2;                 // 16 KB of x16
+    static constexpr uint32_t kA = kBM * kBK * 2;                 // 16 KB of x16 a 128-token subtile
     static constexpr uint32_t kB = BN * kBK * 2;                  // 16 or 32 KB of weights
-    static constexpr uint32_t kStage = kA + kB;
-    static constexpr uint32_t kStages = (192u * 1024u) / kStage;  // 6 or 4
+    static constexpr uint32_t kStage = MT * kA + kB;
+    static constexpr uint32_t kStages = (192u * 1024u) / kStage;  // 6, 4 or 3
     static constexpr uint32_t kCs = BN + 1;                       // floats a staged row
+    static constexpr uint32_t kWarps = 8;
     static constexpr size_t kSmem = 1024 + kStages * kStage + 256;
-    static_assert(kBM * kCs * 4 <= kStages * kStage, "the staged tile fits the drained ring");
+    static_assert(kBM * kCs * 4 <= kStages * kStage, "a staged subtile fits the drained ring");
+    static_assert(MT * BN <= 512, "the accumulators fit tensor memory");
 };
 
-// One CTA a 128-token × BN-slot tile over K blocks [kb0, kb1) of split z:
-// warp 0's lane 0 loads both operands by TMA (the first stages' weights
-// before the wait on the previous kernel, which they do not depend on),
-// warp 1's lane 0 issues the MMAs (M = 128, N = BN, K = 16, four a block)
-// into a BN-column f32 accumulator in tensor memory, and all four warps
-// read it back (warp w: lanes 32w ...) through shared memory into
-// coalesced row writes: the epilogue, or split z's raw partial tile.
-template <uint32_t BN>
-__global__ void __launch_bounds__(128, 1)
+// One CTA a (128·MT)-token × BN-slot tile over K blocks [kb0, kb1) of split
+// z: MT accumulators of 128 × BN f32 in tensor memory share each staged
+// weight tile (a weight read once for 128·MT tokens). Warp 0's lane 0 loads
+// the operands by TMA (the first stages' weights before the wait on the
+// previous kernel, which they do not depend on), warp 1's lane 0 issues the
+// MMAs (M = 128, N = BN, K = 16; four a block and subtile), and the eight
+// warps read each accumulator back (warp w: lanes 32·(w mod 4), half w/4 of
+// the columns) through shared memory into coalesced row writes: the
+// epilogue, or split z's raw partial tile.
+template <uint32_t BN, uint32_t MT>
+__global__ void __launch_bounds__(256, 1)
     dense_kernel(const MatmulArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  uint32_t splits, float* partials) {
-    using S = Dense<BN>;
+    using S = Dense<BN, MT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStages * S::kStage);
@@ -531,8 +535,9 @@ __global__ void __launch_bounds__(128, 1)
     const uint32_t all_blocks = (a.columns + kBK - 1u) / kBK;
     const uint32_t kb0 = all_blocks * blockIdx.z / splits, kb1 = all_blocks * (blockIdx.z + 1u) / splits;
     const uint32_t kblocks = kb1 - kb0;
-    const uint32_t m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+    const uint32_t m0 = blockIdx.x * kBM * MT, n0 = blockIdx.y * BN;
     const uint32_t slots = dense_slot_count(a);
+    constexpr uint32_t kColumns = MT * BN < 32u ? 32u : MT * BN;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S::kStages; ++s) {
@@ -543,7 +548,7 @@ __global__ void __launch_bounds__(128, 1)
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, BN);
+        tmem_alloc(tmem_slot, kColumns);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -553,24 +558,27 @@ __global__ void __launch_bounds__(128, 1)
 
     if (warp == 0) {
         if (lane == 0) {
+            auto load_x = [&](uint32_t s, uint32_t kb) {
+#pragma unroll
+                for (uint32_t mt = 0; mt < MT; ++mt)
+                    tma_load_2d(base + s * S::kStage + mt * S::kA, &xmap, static_cast<int32_t>((kb0 + kb) * kBK),
+                                static_cast<int32_t>(m0 + mt * kBM), &full[s]);
+            };
             const uint32_t pre = kblocks < S::kStages ? kblocks : S::kStages;
             for (uint32_t i = 0; i < pre; ++i) {
                 mbar_arrive_expect_tx(&full[i], S::kStage);
-                tma_load_2d(base + i * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + i) * kBK),
+                tma_load_2d(base + i * S::kStage + MT * S::kA, &wmap, static_cast<int32_t>((kb0 + i) * kBK),
                             static_cast<int32_t>(n0), &full[i]);
             }
             grid_dependency_wait();   // x16 is the previous kernel's output
-            for (uint32_t i = 0; i < pre; ++i)
-                tma_load_2d(base + i * S::kStage, &xmap, static_cast<int32_t>((kb0 + i) * kBK), static_cast<int32_t>(m0),
-                            &full[i]);
+            for (uint32_t i = 0; i < pre; ++i) load_x(i, i);
             uint32_t issued = pre;
             for (uint32_t kb = pre; kb < kblocks; ++kb) {
                 const uint32_t s = kb % S::kStages;
                 if (!mbar_wait(&empty[s], ((kb / S::kStages) - 1u) & 1u, a.fault)) break;
                 mbar_arrive_expect_tx(&full[s], S::kStage);
-                tma_load_2d(base + s * S::kStage, &xmap, static_cast<int32_t>((kb0 + kb) * kBK), static_cast<int32_t>(m0),
-                            &full[s]);
-                tma_load_2d(base + s * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + kb) * kBK),
+                load_x(s, kb);
+                tma_load_2d(base + s * S::kStage + MT * S::kA, &wmap, static_cast<int32_t>((kb0 + kb) * kBK),
                             static_cast<int32_t>(n0), &full[s]);
                 issued = kb + 1u;
             }
@@ -589,11 +597,14 @@ __global__ void __launch_bounds__(128, 1)
                 if (!mbar_wait(&full[s], (kb / S::kStages) & 1u, a.fault)) break;
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t a_addr = smem_addr(base + s * S::kStage);
-                    const uint64_t da = umma_desc_sw128(a_addr), db = umma_desc_sw128(a_addr + S::kA);
+                    const uint32_t stage = smem_addr(base + s * S::kStage);
+                    const uint64_t db = umma_desc_sw128(stage + MT * S::kA);
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; ++kk)
-                        umma_f16(tmem, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0u ? 1u : 0u);
+#pragma unroll
+                        for (uint32_t mt = 0; mt < MT; ++mt)
+                            umma_f16(tmem + mt * BN, umma_desc_sw128(stage + mt * S::kA) + 2u * kk, db + 2u * kk, idesc,
+                                     (kb | kk) != 0u ? 1u : 0u);
                     umma_commit(&empty[s]);
                 }
                 __syncwarp();
@@ -606,57 +617,65 @@ __global__ void __launch_bounds__(128, 1)
 
     const bool ok = mbar_wait(done, 0u, a.fault);
     float* cs = reinterpret_cast<float*>(base);
+    const uint32_t quarter = warp & 3u, half = warp >> 2;
     if (ok) {
         tc_fence_after();
         fence_proxy_async();   // the ring was last written by the copy engine
-        const uint32_t row = 32u * warp + lane;
-        const uint32_t taddr = tmem + ((32u * warp) << 16);
-#pragma unroll 1
-        for (uint32_t c0 = 0; c0 < BN; c0 += 32u) {
-            float v[32];
-            tmem_ld32(taddr + c0, v);
-#pragma unroll
-            for (uint32_t i = 0; i < 32u; ++i) cs[row * S::kCs + c0 + i] = v[i];
-        }
     }
-    __syncthreads();
-    if (ok) {
-        if (splits > 1u) {
-            // split z's raw sums: partials[(z·tokens + t)·slots + n]
-            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
-                float* dst = partials + (static_cast<size_t>(blockIdx.z) * a.tokens + m0 + r) * slots;
+#pragma unroll 1
+    for (uint32_t mt = 0; mt < MT; ++mt) {
+        const uint32_t r0 = m0 + mt * kBM;   // the subtile's first token
+        if (ok) {
+            const uint32_t row = 32u * quarter + lane;
+            const uint32_t taddr = tmem + ((32u * quarter) << 16) + mt * BN;
+#pragma unroll 1
+            for (uint32_t c0 = half * (BN / 2u); c0 < (half + 1u) * (BN / 2u); c0 += 32u) {
+                float v[32];
+                tmem_ld32(taddr + c0, v);
 #pragma unroll
-                for (uint32_t j = 0; j < BN / 32u; ++j) {
-                    const uint32_t n = n0 + lane + 32u * j;
-                    if (n < slots) dst[n] = cs[r * S::kCs + lane + 32u * j];
-                }
+                for (uint32_t i = 0; i < 32u; ++i) cs[row * S::kCs + c0 + i] = v[i];
             }
-        } else if (a.epilogue == kGated) {
-            // the tile's outputs: BN/2, unit pairs (gate 64, up 64)
-            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
+        }
+        __syncthreads();
+        if (ok && r0 < a.tokens) {
+            if (splits > 1u) {
+                // split z's raw sums: partials[(z·tokens + t)·slots + n]
+                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
+                    float* dst = partials + (static_cast<size_t>(blockIdx.z) * a.tokens + r0 + r) * slots;
 #pragma unroll
-                for (uint32_t j = 0; j < BN / 64u; ++j) {
-                    const uint32_t c = lane + 32u * j, gc = (c / 64u) * 128u + c % 64u;
-                    const uint32_t o = n0 / 2u + c;
-                    if (o < a.member[0].rows)
-                        put_gated(a, m0 + r, o, cs[r * S::kCs + gc], cs[r * S::kCs + gc + 64u]);
+                    for (uint32_t j = 0; j < BN / 32u; ++j) {
+                        const uint32_t n = n0 + lane + 32u * j;
+                        if (n < slots) dst[n] = cs[r * S::kCs + lane + 32u * j];
+                    }
                 }
-            }
-        } else {
-            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += 4u) {
+            } else if (a.epilogue == kGated) {
+                // the tile's outputs: BN/2, unit pairs (gate 64, up 64)
+                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
 #pragma unroll
-                for (uint32_t j = 0; j < BN / 32u; ++j) {
-                    const uint32_t n = n0 + lane + 32u * j;
-                    if (n < slots) put_slot(a, m0 + r, n, cs[r * S::kCs + lane + 32u * j]);
+                    for (uint32_t j = 0; j < BN / 64u; ++j) {
+                        const uint32_t c = lane + 32u * j, gc = (c / 64u) * 128u + c % 64u;
+                        const uint32_t o = n0 / 2u + c;
+                        if (o < a.member[0].rows)
+                            put_gated(a, r0 + r, o, cs[r * S::kCs + gc], cs[r * S::kCs + gc + 64u]);
+                    }
+                }
+            } else {
+                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
+#pragma unroll
+                    for (uint32_t j = 0; j < BN / 32u; ++j) {
+                        const uint32_t n = n0 + lane + 32u * j;
+                        if (n < slots) put_slot(a, r0 + r, n, cs[r * S::kCs + lane + 32u * j]);
+                    }
                 }
             }
         }
+        __syncthreads();   // the staged subtile is written out before the next is staged
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, kColumns);
     }
 }
 
@@ -685,11 +704,11 @@ __global__ void dense_combine_kernel(const MatmulArgs a, uint32_t splits, const 
     grid_dependents_launch();
 }
 
-template <uint32_t BN>
+template <uint32_t BN, uint32_t MT>
 cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUtensorMap& wmap, uint32_t splits,
                          float* partials, cudaStream_t stream, bool pdl) {
-    using S = Dense<BN>;
-    auto kernel = dense_kernel<BN>;
+    using S = Dense<BN, MT>;
+    auto kernel = dense_kernel<BN, MT>;
     static bool configured = false;
     if (!configured) {
         const cudaError_t e =
@@ -698,8 +717,8 @@ cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUt
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.tokens + kBM - 1) / kBM, (dense_slot_count(a) + BN - 1) / BN, splits);
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3((a.tokens + kBM * MT - 1) / (kBM * MT), (dense_slot_count(a) + BN - 1) / BN, splits);
+    cfg.blockDim = dim3(32 * S::kWarps);
     cfg.dynamicSmemBytes = S::kSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -754,26 +773,31 @@ cudaError_t matmul_densify(const MatmulArgs& a, void* dense, cudaStream_t stream
 
 cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool pdl) {
     const uint32_t slots = dense_slot_count(a);
-    const uint32_t mt = (a.tokens + kBM - 1u) / kBM;
     const uint32_t sm = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
-    // N = 256 tiles (fewer operand bytes a flop) when they fill the GPU;
-    // else 128, for more CTAs.
-    const uint32_t bn = mt * ((slots + 255u) / 256u) >= sm ? 256u : 128u;
-    const uint32_t tiles = mt * ((slots + bn - 1u) / bn);
-    // Split K when the tiles leave SMs idle: the split count with the fewest
-    // waves a split (ties: fewer splits), each split at least 8 K blocks,
-    // its partials where the scratch has room after x16.
-    const uint32_t kblocks = (a.columns + kBK - 1u) / kBK;
+    auto ceil_div = [](uint32_t n, uint32_t d) { return (n + d - 1u) / d; };
+    // The tile: 256 tokens × 256 slots (two accumulators sharing each weight
+    // tile: the fewest operand bytes a flop) when those tiles nearly fill the
+    // GPU; else 128 × 256 when they do; else 128 × 128, the most CTAs.
+    uint32_t bn = 128, mt = 1;
+    if (ceil_div(a.tokens, 256) * ceil_div(slots, 256) * 4u >= sm * 3u) {
+        bn = 256;
+        mt = 2;
+    } else if (ceil_div(a.tokens, 128) * ceil_div(slots, 256) >= sm) {
+        bn = 256;
+    }
+    const uint32_t tiles = ceil_div(a.tokens, 128 * mt) * ceil_div(slots, bn);
+    // Split K only when the tiles leave most SMs idle: as many splits as
+    // still fit one wave, each at least 8 K blocks, their partials where the
+    // scratch has room after x16 (a second launch adds them in order).
+    const uint32_t kblocks = ceil_div(a.columns, kBK);
     const uint64_t x16 = matmul_tensor_scratch_bytes(a.tokens, a.columns);
     uint32_t splits = 1;
-    double best = static_cast<double>((tiles + sm - 1u) / sm);
-    for (uint32_t z = 2; z <= 8u && kblocks / z >= 8u; ++z) {
-        if (x16 + static_cast<uint64_t>(z) * a.tokens * slots * 4u > a.scratch_bytes) break;
-        const double cost = static_cast<double>((tiles * z + sm - 1u) / sm) / z;
-        if (cost < best - 1e-9) {
-            best = cost;
-            splits = z;
-        }
+    if (tiles * 2u <= sm) {
+        splits = sm / tiles;
+        if (splits > 8u) splits = 8u;
+        while (splits > 1u && (kblocks / splits < 8u ||
+                               x16 + static_cast<uint64_t>(splits) * a.tokens * slots * 4u > a.scratch_bytes))
+            --splits;
     }
     float* partials = splits > 1u ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.scratch) + x16) : nullptr;
 
@@ -781,8 +805,9 @@ cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool
     CUtensorMap xmap, wmap;
     if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
     if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, bn); e != cudaSuccess) return e;
-    cudaError_t e = bn == 256u ? launch_dense<256>(a, xmap, wmap, splits, partials, stream, pdl)
-                               : launch_dense<128>(a, xmap, wmap, splits, partials, stream, pdl);
+    cudaError_t e = mt == 2u   ? launch_dense<256, 2>(a, xmap, wmap, splits, partials, stream, pdl)
+                    : bn == 256u ? launch_dense<256, 1>(a, xmap, wmap, splits, partials, stream, pdl)
+                                 : launch_dense<128, 1>(a, xmap, wmap, splits, partials, stream, pdl);
     if (e != cudaSuccess || splits == 1u) return e;
     const uint32_t outputs = a.epilogue == kGated ? a.member[0].rows : slots;
     const uint64_t n = static_cast<uint64_t>(a.tokens) * outputs;
