@@ -497,33 +497,31 @@ __device__ __forceinline__ void put_gated(const MatmulArgs& a, uint32_t t, uint3
     a.out[0][static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o] = activate(a.activation, g) * u;
 }
 
-template <uint32_t BN, uint32_t MT>
+template <uint32_t BN>
 struct Dense {
-    static constexpr uint32_t kA = kBM * kBK * 2;                 // 16 KB of x16 a 128-token subtile
-    static constexpr uint32_t kB = BN * kBK * 2;                  // 16 or 32 KB of weights
-    static constexpr uint32_t kStage = MT * kA + kB;
-    static constexpr uint32_t kStages = (192u * 1024u) / kStage;  // 6, 4 or 3
+    static constexpr uint32_t kA = kBM * kBK * 2;                 // 16 KB of x16
+    static constexpr uint32_t kB = BN * kBK * 2;                  // 16 KB of weights (BN = 128)
+    static constexpr uint32_t kStage = kA + kB;
+    static constexpr uint32_t kStages = (192u * 1024u) / kStage;
     static constexpr uint32_t kCs = BN + 1;                       // floats a staged row
     static constexpr uint32_t kWarps = 8;
     static constexpr size_t kSmem = 1024 + kStages * kStage + 256;
-    static_assert(kBM * kCs * 4 <= kStages * kStage, "a staged subtile fits the drained ring");
-    static_assert(MT * BN <= 512, "the accumulators fit tensor memory");
+    static_assert(kBM * kCs * 4 <= kStages * kStage, "the staged tile fits the drained ring");
 };
 
-// One CTA a (128·MT)-token × BN-slot tile over K blocks [kb0, kb1) of split
-// z: MT accumulators of 128 × BN f32 in tensor memory share each staged
-// weight tile (a weight read once for 128·MT tokens). Warp 0's lane 0 loads
-// the operands by TMA (the first stages' weights before the wait on the
-// previous kernel, which they do not depend on), warp 1's lane 0 issues the
-// MMAs (M = 128, N = BN, K = 16; four a block and subtile), and the eight
-// warps read each accumulator back (warp w: lanes 32·(w mod 4), half w/4 of
-// the columns) through shared memory into coalesced row writes: the
-// epilogue, or split z's raw partial tile.
-template <uint32_t BN, uint32_t MT>
+// One CTA a 128-token × BN-slot tile over K blocks [kb0, kb1) of split z,
+// for products of too few tiles for the persistent form. Warp 0's lane 0
+// loads the operands by TMA (the first stages' weights before the wait on
+// the previous kernel, which they do not depend on), warp 1's lane 0 issues
+// the MMAs (M = 128, N = BN, K = 16; four a block) into a BN-column f32
+// accumulator in tensor memory, and the eight warps read it back (warp w:
+// lanes 32·(w mod 4), half w/4 of the columns) through shared memory into
+// coalesced row writes: the epilogue, or split z's raw partial tile.
+template <uint32_t BN>
 __global__ void __launch_bounds__(256, 1)
     dense_kernel(const MatmulArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                  uint32_t splits, float* partials) {
-    using S = Dense<BN, MT>;
+    using S = Dense<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kStages * S::kStage);
@@ -535,9 +533,8 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t all_blocks = (a.columns + kBK - 1u) / kBK;
     const uint32_t kb0 = all_blocks * blockIdx.z / splits, kb1 = all_blocks * (blockIdx.z + 1u) / splits;
     const uint32_t kblocks = kb1 - kb0;
-    const uint32_t m0 = blockIdx.x * kBM * MT, n0 = blockIdx.y * BN;
+    const uint32_t m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
     const uint32_t slots = dense_slot_count(a);
-    constexpr uint32_t kColumns = MT * BN < 32u ? 32u : MT * BN;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S::kStages; ++s) {
@@ -548,7 +545,7 @@ __global__ void __launch_bounds__(256, 1)
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, kColumns);
+        tmem_alloc(tmem_slot, BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -559,15 +556,13 @@ __global__ void __launch_bounds__(256, 1)
     if (warp == 0) {
         if (lane == 0) {
             auto load_x = [&](uint32_t s, uint32_t kb) {
-#pragma unroll
-                for (uint32_t mt = 0; mt < MT; ++mt)
-                    tma_load_2d(base + s * S::kStage + mt * S::kA, &xmap, static_cast<int32_t>((kb0 + kb) * kBK),
-                                static_cast<int32_t>(m0 + mt * kBM), &full[s]);
+                tma_load_2d(base + s * S::kStage, &xmap, static_cast<int32_t>((kb0 + kb) * kBK), static_cast<int32_t>(m0),
+                            &full[s]);
             };
             const uint32_t pre = kblocks < S::kStages ? kblocks : S::kStages;
             for (uint32_t i = 0; i < pre; ++i) {
                 mbar_arrive_expect_tx(&full[i], S::kStage);
-                tma_load_2d(base + i * S::kStage + MT * S::kA, &wmap, static_cast<int32_t>((kb0 + i) * kBK),
+                tma_load_2d(base + i * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + i) * kBK),
                             static_cast<int32_t>(n0), &full[i]);
             }
             grid_dependency_wait();   // x16 is the previous kernel's output
@@ -578,7 +573,7 @@ __global__ void __launch_bounds__(256, 1)
                 if (!mbar_wait(&empty[s], ((kb / S::kStages) - 1u) & 1u, a.fault)) break;
                 mbar_arrive_expect_tx(&full[s], S::kStage);
                 load_x(s, kb);
-                tma_load_2d(base + s * S::kStage + MT * S::kA, &wmap, static_cast<int32_t>((kb0 + kb) * kBK),
+                tma_load_2d(base + s * S::kStage + S::kA, &wmap, static_cast<int32_t>((kb0 + kb) * kBK),
                             static_cast<int32_t>(n0), &full[s]);
                 issued = kb + 1u;
             }
@@ -598,13 +593,10 @@ __global__ void __launch_bounds__(256, 1)
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t stage = smem_addr(base + s * S::kStage);
-                    const uint64_t db = umma_desc_sw128(stage + MT * S::kA);
+                    const uint64_t da = umma_desc_sw128(stage), db = umma_desc_sw128(stage + S::kA);
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; ++kk)
-#pragma unroll
-                        for (uint32_t mt = 0; mt < MT; ++mt)
-                            umma_f16(tmem + mt * BN, umma_desc_sw128(stage + mt * S::kA) + 2u * kk, db + 2u * kk, idesc,
-                                     (kb | kk) != 0u ? 1u : 0u);
+                        umma_f16(tmem, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0u ? 1u : 0u);
                     umma_commit(&empty[s]);
                 }
                 __syncwarp();
@@ -621,61 +613,295 @@ __global__ void __launch_bounds__(256, 1)
     if (ok) {
         tc_fence_after();
         fence_proxy_async();   // the ring was last written by the copy engine
+        const uint32_t row = 32u * quarter + lane;
+        const uint32_t taddr = tmem + ((32u * quarter) << 16);
+#pragma unroll 1
+        for (uint32_t c0 = half * (BN / 2u); c0 < (half + 1u) * (BN / 2u); c0 += 32u) {
+            float v[32];
+            tmem_ld32(taddr + c0, v);
+#pragma unroll
+            for (uint32_t i = 0; i < 32u; ++i) cs[row * S::kCs + c0 + i] = v[i];
+        }
     }
-#pragma unroll 1
-    for (uint32_t mt = 0; mt < MT; ++mt) {
-        const uint32_t r0 = m0 + mt * kBM;   // the subtile's first token
-        if (ok) {
-            const uint32_t row = 32u * quarter + lane;
-            const uint32_t taddr = tmem + ((32u * quarter) << 16) + mt * BN;
-#pragma unroll 1
-            for (uint32_t c0 = half * (BN / 2u); c0 < (half + 1u) * (BN / 2u); c0 += 32u) {
-                float v[32];
-                tmem_ld32(taddr + c0, v);
+    __syncthreads();
+    if (ok && m0 < a.tokens) {
+        if (splits > 1u) {
+            // split z's raw sums: partials[(z·tokens + t)·slots + n]
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += S::kWarps) {
+                float* dst = partials + (static_cast<size_t>(blockIdx.z) * a.tokens + m0 + r) * slots;
 #pragma unroll
-                for (uint32_t i = 0; i < 32u; ++i) cs[row * S::kCs + c0 + i] = v[i];
+                for (uint32_t j = 0; j < BN / 32u; ++j) {
+                    const uint32_t n = n0 + lane + 32u * j;
+                    if (n < slots) dst[n] = cs[r * S::kCs + lane + 32u * j];
+                }
             }
-        }
-        __syncthreads();
-        if (ok && r0 < a.tokens) {
-            if (splits > 1u) {
-                // split z's raw sums: partials[(z·tokens + t)·slots + n]
-                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
-                    float* dst = partials + (static_cast<size_t>(blockIdx.z) * a.tokens + r0 + r) * slots;
+        } else if (a.epilogue == kGated) {
+            // the tile's outputs: BN/2, unit pairs (gate 64, up 64)
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += S::kWarps) {
 #pragma unroll
-                    for (uint32_t j = 0; j < BN / 32u; ++j) {
-                        const uint32_t n = n0 + lane + 32u * j;
-                        if (n < slots) dst[n] = cs[r * S::kCs + lane + 32u * j];
-                    }
+                for (uint32_t j = 0; j < BN / 64u; ++j) {
+                    const uint32_t c = lane + 32u * j, gc = (c / 64u) * 128u + c % 64u;
+                    const uint32_t o = n0 / 2u + c;
+                    if (o < a.member[0].rows)
+                        put_gated(a, m0 + r, o, cs[r * S::kCs + gc], cs[r * S::kCs + gc + 64u]);
                 }
-            } else if (a.epilogue == kGated) {
-                // the tile's outputs: BN/2, unit pairs (gate 64, up 64)
-                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
+            }
+        } else {
+            for (uint32_t r = warp; r < kBM && m0 + r < a.tokens; r += S::kWarps) {
 #pragma unroll
-                    for (uint32_t j = 0; j < BN / 64u; ++j) {
-                        const uint32_t c = lane + 32u * j, gc = (c / 64u) * 128u + c % 64u;
-                        const uint32_t o = n0 / 2u + c;
-                        if (o < a.member[0].rows)
-                            put_gated(a, r0 + r, o, cs[r * S::kCs + gc], cs[r * S::kCs + gc + 64u]);
-                    }
-                }
-            } else {
-                for (uint32_t r = warp; r < kBM && r0 + r < a.tokens; r += S::kWarps) {
-#pragma unroll
-                    for (uint32_t j = 0; j < BN / 32u; ++j) {
-                        const uint32_t n = n0 + lane + 32u * j;
-                        if (n < slots) put_slot(a, r0 + r, n, cs[r * S::kCs + lane + 32u * j]);
-                    }
+                for (uint32_t j = 0; j < BN / 32u; ++j) {
+                    const uint32_t n = n0 + lane + 32u * j;
+                    if (n < slots) put_slot(a, m0 + r, n, cs[r * S::kCs + lane + 32u * j]);
                 }
             }
         }
-        __syncthreads();   // the staged subtile is written out before the next is staged
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kColumns);
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+// ---- the persistent dense form: products of at least a wave of tiles ------
+
+// Waits like mbar_wait, and gives up early once another role of the CTA has
+// given up (`abort`, in shared memory): a wait that runs out sets the fault
+// word and `abort`, so the other roles leave within a few hundred polls.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, unsigned int* fault,
+                                          volatile uint32_t* abort) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && *abort) return false;
+    }
+    if (fault) atomicOr(fault, kFaultTimeout);
+    *abort = 1u;
+    return false;
+}
+
+// A 32 × 32 block of outputs — tokens t0 + r (r = 0..31) × slots
+// [n, n + 32) — from registers (lane r holding its token's 32 values) to
+// the outputs through the warp's staging buffer `stg` (32 rows of 33
+// floats: conflict-free both ways), so each store instruction writes 32
+// consecutive floats of one token's row. The Write and QKV epilogues write
+// straight when one member holds the 32 slots; otherwise each slot takes
+// put_slot.
+__device__ __forceinline__ void store_block(const MatmulArgs& a, uint32_t t0, uint32_t n, const float (&v)[32],
+                                            uint32_t slots, float* stg, uint32_t lane) {
+#pragma unroll
+    for (uint32_t i = 0; i < 32u; ++i) stg[lane * 33u + i] = v[i];
+    __syncwarp();
+    int q = -1;
+    uint32_t local = n, rows = 0;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        if (q < 0 && m < static_cast<int>(a.members)) {
+            const uint32_t r = m == 0 ? a.member[0].rows : (m == 1 ? a.member[1].rows : a.member[2].rows);
+            if (local < r) {
+                q = m;
+                rows = r;
+            } else {
+                local -= r;
+            }
+        }
+    }
+    const uint32_t live = a.tokens > t0 ? (a.tokens - t0 < 32u ? a.tokens - t0 : 32u) : 0u;
+    if (q >= 0 && local + 32u <= rows && a.epilogue != kGatedByInput) {
+        const bool qkv = a.epilogue == kQKV;
+        float* out = qkv ? (q == 1 ? a.out[1] : (q == 2 ? a.out[2] : a.out[0])) : a.out[0];
+        const uint32_t st = qkv ? (q == 1 ? a.out_stride[1] : (q == 2 ? a.out_stride[2] : a.out_stride[0])) : a.out_stride[0];
+        const uint32_t off = q == 1 ? a.member[1].out_offset : (q == 2 ? a.member[2].out_offset : a.member[0].out_offset);
+        float* dst = out + static_cast<size_t>(t0) * st + off + local + lane;
+        for (uint32_t r = 0; r < live; ++r) dst[static_cast<size_t>(r) * st] = stg[r * 33u + lane];
+    } else if (n + lane < slots) {
+        for (uint32_t r = 0; r < live; ++r) put_slot(a, t0 + r, n + lane, stg[r * 33u + lane]);
+    }
+    __syncwarp();   // the staging buffer is read before the next block
+}
+
+struct Persist {
+    static constexpr uint32_t kBN = 256;
+    static constexpr uint32_t kA = kBM * kBK * 2;      // 16 KB of x16
+    static constexpr uint32_t kB = kBN * kBK * 2;      // 32 KB of weights
+    static constexpr uint32_t kStage = kA + kB;
+    static constexpr uint32_t kStages = 4;
+    static constexpr uint32_t kEpilogueWarps = 8;
+    static constexpr uint32_t kThreads = 32u * (2u + kEpilogueWarps);
+    static constexpr uint32_t kStaging = 32u * 33u * 4u;   // bytes an epilogue warp stages a block in
+    static constexpr size_t kSmem = 1024 + kStages * kStage + 256 + kEpilogueWarps * kStaging;
+};
+
+// A CTA an SM, looping over the product's 128-token × 256-slot tiles (tile
+// blockIdx.x, then every gridDim.x-th; token tiles fastest, so the CTAs at
+// work together share weight tiles in L2). Warp 0's lane 0 streams both
+// operands by TMA through a 4-stage ring across tiles; warp 1's lane 0
+// issues the MMAs into one of two 256-column accumulators in tensor memory,
+// alternating by tile; warps 2-9 drain the other accumulator at the same
+// time (warp w: lanes 32·(w mod 4), half (w − 2)/4 of the columns), from
+// registers straight to the outputs, then hand it back.
+__global__ void __launch_bounds__(Persist::kThreads, 1)
+    dense_persistent_kernel(const MatmulArgs a, const __grid_constant__ CUtensorMap xmap,
+                            const __grid_constant__ CUtensorMap wmap) {
+    using P = Persist;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + P::kStages * P::kStage);
+    uint64_t* empty = full + P::kStages;
+    uint64_t* acc_full = empty + P::kStages;   // [2]: an accumulator is complete
+    uint64_t* acc_empty = acc_full + 2;        // [2]: an accumulator is drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    volatile uint32_t* abort = tmem_slot + 1;
+    float* staging = reinterpret_cast<float*>(base + P::kStages * P::kStage + 256);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t slots = dense_slot_count(a);
+    const uint32_t kblocks = (a.columns + kBK - 1u) / kBK;
+    const uint32_t m_tiles = (a.tokens + kBM - 1u) / kBM, n_tiles = (slots + P::kBN - 1u) / P::kBN;
+    const uint32_t tiles = m_tiles * n_tiles;
+    const uint32_t mine = tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < P::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], P::kEpilogueWarps);
+        }
+        *abort = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 2u * P::kBN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t total = mine * kblocks;
+            auto tile_of = [&](uint32_t g) { return blockIdx.x + (g / kblocks) * gridDim.x; };
+            auto load_w = [&](uint32_t g, uint32_t s) {
+                tma_load_2d(base + s * P::kStage + P::kA, &wmap, static_cast<int32_t>((g % kblocks) * kBK),
+                            static_cast<int32_t>((tile_of(g) / m_tiles) * P::kBN), &full[s]);
+            };
+            auto load_x = [&](uint32_t g, uint32_t s) {
+                tma_load_2d(base + s * P::kStage, &xmap, static_cast<int32_t>((g % kblocks) * kBK),
+                            static_cast<int32_t>((tile_of(g) % m_tiles) * kBM), &full[s]);
+            };
+            // The first stages' weights before the wait on the previous
+            // kernel (x16 is its output; the weights do not depend on it).
+            const uint32_t pre = total < P::kStages ? total : P::kStages;
+            for (uint32_t g = 0; g < pre; ++g) {
+                mbar_arrive_expect_tx(&full[g], P::kStage);
+                load_w(g, g);
+            }
+            grid_dependency_wait();
+            for (uint32_t g = 0; g < pre; ++g) load_x(g, g);
+            uint32_t issued = pre;
+            for (uint32_t g = pre; g < total; ++g) {
+                const uint32_t s = g % P::kStages;
+                if (!role_wait(&empty[s], ((g / P::kStages) - 1u) & 1u, a.fault, abort)) break;
+                mbar_arrive_expect_tx(&full[s], P::kStage);
+                load_x(g, s);
+                load_w(g, s);
+                issued = g + 1u;
+            }
+            // Every copy issued has landed before the CTA leaves.
+            for (uint32_t g = issued > P::kStages ? issued - P::kStages : 0u; g < issued; ++g)
+                mbar_wait(&full[g % P::kStages], (g / P::kStages) & 1u, nullptr);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = umma_idesc_f16(kBM, P::kBN);
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t i = 0; i < mine && ok; ++i) {
+            const uint32_t b = i & 1u;
+            if (i >= 2u) {
+                bool got = lane == 0 ? role_wait(&acc_empty[b], ((i >> 1) - 1u) & 1u, a.fault, abort) : false;
+                if (!__shfl_sync(0xFFFFFFFFu, got, 0)) break;
+                tc_fence_after();
+            }
+            for (uint32_t kb = 0; kb < kblocks; ++kb, ++g) {
+                const uint32_t s = g % P::kStages;
+                bool got = lane == 0 ? role_wait(&full[s], (g / P::kStages) & 1u, a.fault, abort) : false;
+                if (!__shfl_sync(0xFFFFFFFFu, got, 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t stage = smem_addr(base + s * P::kStage);
+                    const uint64_t da = umma_desc_sw128(stage), db = umma_desc_sw128(stage + P::kA);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / 16u; ++kk)
+                        umma_f16(tmem + b * P::kBN, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0u ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            // Complete even after a failed wait: the epilogue's wait ends.
+            if (lane == 0) umma_commit(&acc_full[b]);
+            __syncwarp();
+        }
+    } else {
+        grid_dependency_wait();
+        const uint32_t quarter = warp & 3u, part = (warp - 2u) / 4u;
+        for (uint32_t i = 0; i < mine; ++i) {
+            const uint32_t b = i & 1u;
+            const uint32_t tile = blockIdx.x + i * gridDim.x;
+            const uint32_t m0 = (tile % m_tiles) * kBM, n0 = (tile / m_tiles) * P::kBN;
+            bool got = lane == 0 ? role_wait(&acc_full[b], (i >> 1) & 1u, a.fault, abort) : false;
+            if (!__shfl_sync(0xFFFFFFFFu, got, 0)) break;
+            tc_fence_after();
+            const uint32_t t0 = m0 + 32u * quarter;   // the warp's 32 tokens, lane = token
+            const uint32_t taddr = tmem + ((32u * quarter) << 16) + b * P::kBN;
+            float* stg = staging + (warp - 2u) * (32u * 33u);
+            if (a.epilogue == kGated) {
+                // columns [128·part, +128): 64 gate then the same outputs' 64 up
+#pragma unroll 1
+                for (uint32_t h = 0; h < 2u; ++h) {
+                    float g[32], u[32];
+                    tmem_ld32(taddr + 128u * part + 32u * h, g);
+                    tmem_ld32(taddr + 128u * part + 64u + 32u * h, u);
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; ++j) g[j] = activate(a.activation, g[j]) * u[j];
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; ++j) stg[lane * 33u + j] = g[j];
+                    __syncwarp();
+                    const uint32_t o = n0 / 2u + 64u * part + 32u * h + lane;
+                    if (o < a.member[0].rows) {
+                        float* dst = a.out[0] + static_cast<size_t>(t0) * a.out_stride[0] + a.member[0].out_offset + o;
+                        for (uint32_t r = 0; r < 32u && t0 + r < a.tokens; ++r)
+                            dst[static_cast<size_t>(r) * a.out_stride[0]] = stg[r * 33u + lane];
+                    }
+                    __syncwarp();
+                }
+            } else {
+#pragma unroll 1
+                for (uint32_t c0 = 128u * part; c0 < 128u * part + 128u; c0 += 32u) {
+                    float v[32];
+                    tmem_ld32(taddr + c0, v);
+                    store_block(a, t0, n0 + c0, v, slots, stg, lane);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+    }
+    grid_dependents_launch();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2u * P::kBN);
     }
 }
 
@@ -704,11 +930,11 @@ __global__ void dense_combine_kernel(const MatmulArgs a, uint32_t splits, const 
     grid_dependents_launch();
 }
 
-template <uint32_t BN, uint32_t MT>
+template <uint32_t BN>
 cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUtensorMap& wmap, uint32_t splits,
                          float* partials, cudaStream_t stream, bool pdl) {
-    using S = Dense<BN, MT>;
-    auto kernel = dense_kernel<BN, MT>;
+    using S = Dense<BN>;
+    auto kernel = dense_kernel<BN>;
     static bool configured = false;
     if (!configured) {
         const cudaError_t e =
@@ -717,7 +943,7 @@ cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUt
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.tokens + kBM * MT - 1) / (kBM * MT), (dense_slot_count(a) + BN - 1) / BN, splits);
+    cfg.gridDim = dim3((a.tokens + kBM - 1) / kBM, (dense_slot_count(a) + BN - 1) / BN, splits);
     cfg.blockDim = dim3(32 * S::kWarps);
     cfg.dynamicSmemBytes = S::kSmem;
     cfg.stream = stream;
@@ -727,6 +953,28 @@ cudaError_t launch_dense(const MatmulArgs& a, const CUtensorMap& xmap, const CUt
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, a, xmap, wmap, splits, partials);
+}
+
+cudaError_t launch_persistent(const MatmulArgs& a, const CUtensorMap& xmap, const CUtensorMap& wmap, uint32_t ctas,
+                              cudaStream_t stream, bool pdl) {
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(dense_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(Persist::kSmem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(Persist::kThreads);
+    cfg.dynamicSmemBytes = Persist::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dense_persistent_kernel, a, xmap, wmap);
 }
 
 }  // namespace
@@ -775,17 +1023,18 @@ cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool
     const uint32_t slots = dense_slot_count(a);
     const uint32_t sm = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
     auto ceil_div = [](uint32_t n, uint32_t d) { return (n + d - 1u) / d; };
-    // The tile: 256 tokens × 256 slots (two accumulators sharing each weight
-    // tile: the fewest operand bytes a flop) when those tiles nearly fill the
-    // GPU; else 128 × 256 when they do; else 128 × 128, the most CTAs.
-    uint32_t bn = 128, mt = 1;
-    if (ceil_div(a.tokens, 256) * ceil_div(slots, 256) * 4u >= sm * 3u) {
-        bn = 256;
-        mt = 2;
-    } else if (ceil_div(a.tokens, 128) * ceil_div(slots, 256) >= sm) {
-        bn = 256;
+    // A wave or more of 128 × 256 tiles: the persistent form, a CTA an SM.
+    const uint32_t wide_tiles = ceil_div(a.tokens, 128) * ceil_div(slots, 256);
+    if (wide_tiles >= sm) {
+        if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
+        CUtensorMap xmap, wmap;
+        if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
+        if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, Persist::kBN); e != cudaSuccess) return e;
+        return launch_persistent(a, xmap, wmap, sm, stream, pdl);
     }
-    const uint32_t tiles = ceil_div(a.tokens, 128 * mt) * ceil_div(slots, bn);
+    // Fewer: 128 × 128 tiles, one a CTA, K split when they leave SMs idle.
+    constexpr uint32_t bn = 128;
+    const uint32_t tiles = ceil_div(a.tokens, 128) * ceil_div(slots, bn);
     // Split K only when the tiles leave most SMs idle: as many splits as
     // still fit one wave, each at least 8 K blocks, their partials where the
     // scratch has room after x16 (a second launch adds them in order).
@@ -805,9 +1054,7 @@ cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool
     CUtensorMap xmap, wmap;
     if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
     if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, bn); e != cudaSuccess) return e;
-    cudaError_t e = mt == 2u   ? launch_dense<256, 2>(a, xmap, wmap, splits, partials, stream, pdl)
-                    : bn == 256u ? launch_dense<256, 1>(a, xmap, wmap, splits, partials, stream, pdl)
-                                 : launch_dense<128, 1>(a, xmap, wmap, splits, partials, stream, pdl);
+    cudaError_t e = launch_dense<bn>(a, xmap, wmap, splits, partials, stream, pdl);
     if (e != cudaSuccess || splits == 1u) return e;
     const uint32_t outputs = a.epilogue == kGated ? a.member[0].rows : slots;
     const uint64_t n = static_cast<uint64_t>(a.tokens) * outputs;
