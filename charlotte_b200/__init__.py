@@ -46,7 +46,8 @@ class Norm(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_void_p), ("output", ctypes.c_void_p), ("gain", ctypes.c_void_p),
                 ("post_gain", ctypes.c_void_p), ("normed", ctypes.c_void_p), ("width", ctypes.c_uint32),
                 ("tokens", ctypes.c_uint32), ("add", ctypes.c_uint32), ("last_token", ctypes.c_uint32),
-                ("epsilon", ctypes.c_float)]
+                ("epsilon", ctypes.c_float), ("scale", ctypes.c_void_p), ("add_only", ctypes.c_uint32),
+                ("rows_per_token", ctypes.c_uint32)]
 
 
 class Rope(ctypes.Structure):
@@ -56,7 +57,23 @@ class Rope(ctypes.Structure):
                 ("position", ctypes.c_void_p), ("position0", ctypes.c_uint32), ("tokens", ctypes.c_uint32),
                 ("head_dim", ctypes.c_uint32), ("query_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
                 ("halves", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("epsilon", ctypes.c_float),
-                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64)]
+                ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64),
+                ("encode", ctypes.c_uint32), ("value_norm", ctypes.c_uint32)]
+
+
+class BlockAttention(ctypes.Structure):
+    _fields_ = [("query", ctypes.c_void_p), ("key", ctypes.c_void_p), ("value", ctypes.c_void_p),
+                ("out", ctypes.c_void_p), ("tokens", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+                ("query_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32), ("half_window", ctypes.c_uint32),
+                ("scale_log2e", ctypes.c_float)]
+
+
+class Pool(ctypes.Structure):
+    _fields_ = [("input", ctypes.c_void_p), ("output", ctypes.c_void_p), ("width", ctypes.c_uint32),
+                ("tokens", ctypes.c_uint32), ("kind", ctypes.c_uint32)]
+
+
+POOL_MEAN, POOL_UNIT = 0, 1
 
 
 class Attention(ctypes.Structure):
@@ -126,6 +143,7 @@ def lib() -> ctypes.CDLL:
                                     ctypes.POINTER(ctypes.c_void_p * 3), ctypes.POINTER(ctypes.c_uint32 * 3),
                                     ctypes.c_uint32, ctypes.c_void_p]
         for name, struct in (("cb_norm_run", Norm), ("cb_rope_run", Rope), ("cb_attention_run", Attention),
+                             ("cb_block_attention_run", BlockAttention), ("cb_pool_run", Pool),
                              ("cb_gather_run", Gather), ("cb_select_run", Select),
                              ("cb_select_run_static", Select), ("cb_select_merge_run", SelectMerge)):
             fn = getattr(L, name)
@@ -230,13 +248,14 @@ def matmul(fmt: int, columns: int, members, x, out, *, epilogue: int = WRITE, ac
                               ctypes.byref(strides), flags, _stream(stream)))
 
 
-def run(kind: str, **fields) -> None:
-    """Runs one kernel entry point: kind in norm, rope, attention, gather,
-    select, select_static; fields are the C struct's (tensors become device
-    pointers)."""
+def run(entry: str, **fields) -> None:
+    """Runs one kernel entry point: `entry` in norm, rope, attention, gather,
+    select, select_static, select_merge, block_attention, pool; fields are the
+    C struct's (tensors become device pointers)."""
     struct = {"norm": Norm, "rope": Rope, "attention": Attention, "gather": Gather, "select": Select,
-              "select_static": Select, "select_merge": SelectMerge}[kind]
-    fn = {"select_static": "cb_select_run_static"}.get(kind, f"cb_{kind}_run")
+              "select_static": Select, "select_merge": SelectMerge, "block_attention": BlockAttention,
+              "pool": Pool}[entry]
+    fn = {"select_static": "cb_select_run_static"}.get(entry, f"cb_{entry}_run")
     stream = fields.pop("stream", None)
     flags = fields.pop("flags", 0)
     v = struct()

@@ -39,7 +39,11 @@ int select_arguments(const cb_select* s, const char* who, bool own_scratch) {
 extern "C" {
 
 int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream) {
-    if (!n || !n->hidden || !n->gain || !n->normed) return fail(CB_ERROR_INVALID, "cb_norm_run: null argument");
+    if (!n || !n->hidden || (!n->normed && !n->add_only)) return fail(CB_ERROR_INVALID, "cb_norm_run: null argument");
+    if ((n->scale || n->add_only) && !n->add)
+        return fail(CB_ERROR_INVALID, "cb_norm_run: a scale or an add alone needs the add");
+    if (n->rows_per_token > 1 && n->last_token)
+        return fail(CB_ERROR_INVALID, "cb_norm_run: several rows a token with the last token's norm");
     if (n->width == 0 || n->width % 4 != 0 || n->width > 4096)
         return fail(CB_ERROR_INVALID, "cb_norm_run: width %u is not a multiple of 4 up to 4096", n->width);
     if (n->add && !n->output) return fail(CB_ERROR_INVALID, "cb_norm_run: add without the block's output");
@@ -56,8 +60,11 @@ void cb_rope_turns(double base, uint32_t head_dim, float* turns) {
 }
 
 int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream) {
-    if (!r || !r->query || !r->key || !r->value || !r->key_cache || !r->value_cache || !r->turns)
+    if (!r || !r->query || !r->key || !r->value || !r->turns || (!r->encode && (!r->key_cache || !r->value_cache)))
         return fail(CB_ERROR_INVALID, "cb_rope_run: null argument");
+    if (r->encode && r->rows_are_sequences)
+        return fail(CB_ERROR_INVALID, "cb_rope_run: the encode form takes the rows of one step");
+    if (r->value_norm && !r->encode) return fail(CB_ERROR_INVALID, "cb_rope_run: value_norm is the encode form's");
     if (!head_dim_ok(r->head_dim)) return fail(CB_ERROR_INVALID, "cb_rope_run: head dimension %u", r->head_dim);
     if (r->kv_heads == 0 || r->query_heads % r->kv_heads != 0)
         return fail(CB_ERROR_INVALID, "cb_rope_run: %u query heads over %u kv heads", r->query_heads, r->kv_heads);
@@ -67,11 +74,40 @@ int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream) {
         return fail(CB_ERROR_INVALID, "cb_rope_run: more than 1024 lanes a token");
     if ((r->query_gain == nullptr) != (r->key_gain == nullptr))
         return fail(CB_ERROR_INVALID, "cb_rope_run: QK-norm on queries or keys alone");
-    if (r->slots == 0) return fail(CB_ERROR_INVALID, "cb_rope_run: no cache slots");
+    if (r->slots == 0 && !r->encode) return fail(CB_ERROR_INVALID, "cb_rope_run: no cache slots");
     if (r->rows_are_sequences && r->sequence_stride < static_cast<uint64_t>(r->slots) * r->kv_heads * r->head_dim)
         return fail(CB_ERROR_INVALID, "cb_rope_run: sequences' caches overlap (stride below one cache)");
     if (r->tokens == 0) return CB_OK;
     return launched(rope_run(*r, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_rope_run");
+}
+
+int cb_block_attention_run(const cb_block_attention* a, uint32_t flags, void* stream) {
+    if (!a || !a->query || !a->key || !a->value || !a->out)
+        return fail(CB_ERROR_INVALID, "cb_block_attention_run: null argument");
+    if (a->head_dim == 0 || a->head_dim % 64 != 0 || a->head_dim > 512)
+        return fail(CB_ERROR_INVALID, "cb_block_attention_run: head dimension %u", a->head_dim);
+    if (a->kv_heads == 0 || a->query_heads % a->kv_heads != 0 || 16 % (a->query_heads / a->kv_heads) != 0)
+        return fail(CB_ERROR_INVALID, "cb_block_attention_run: %u query heads over %u kv heads", a->query_heads,
+                    a->kv_heads);
+    if (!aligned16(a->query) || !aligned16(a->key) || !aligned16(a->value) || !aligned16(a->out))
+        return fail(CB_ERROR_INVALID, "cb_block_attention_run: rows must be 16-byte aligned");
+    if (a->tokens == 0) return CB_OK;
+    if (!block_attention_fits(*a))
+        return fail(CB_ERROR_INVALID, "cb_block_attention_run: %u tokens of head dimension %u do not fit", a->tokens,
+                    a->head_dim);
+    return launched(block_attention_run(*a, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL),
+                    "cb_block_attention_run");
+}
+
+int cb_pool_run(const cb_pool* p, uint32_t flags, void* stream) {
+    if (!p || !p->input || !p->output) return fail(CB_ERROR_INVALID, "cb_pool_run: null argument");
+    if (p->kind != CB_POOL_MEAN && p->kind != CB_POOL_UNIT) return fail(CB_ERROR_INVALID, "cb_pool_run: kind %u", p->kind);
+    if (p->width == 0 || p->width % 4 != 0 || p->width > 4096)
+        return fail(CB_ERROR_INVALID, "cb_pool_run: width %u is not a multiple of 4 up to 4096", p->width);
+    if (!aligned16(p->input) || !aligned16(p->output))
+        return fail(CB_ERROR_INVALID, "cb_pool_run: rows must be 16-byte aligned");
+    if (p->tokens == 0) return CB_OK;
+    return launched(pool_run(*p, static_cast<cudaStream_t>(stream), flags & CB_RUN_PDL), "cb_pool_run");
 }
 
 uint32_t cb_attention_tickets(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads) {

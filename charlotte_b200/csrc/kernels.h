@@ -32,6 +32,10 @@ cudaError_t attention_tensor_run(const AttentionArgs& a, cudaStream_t stream, bo
 // Steps of at least this many rows take the many-query form.
 constexpr uint32_t kPrefillAttentionRows = 32;
 cudaError_t gather_run(const GatherArgs& a, cudaStream_t stream, bool pdl);
+// An encoder's (encoder.cu): block attention and pooling.
+bool block_attention_fits(const cb_block_attention& a);
+cudaError_t block_attention_run(const cb_block_attention& a, cudaStream_t stream, bool pdl);
+cudaError_t pool_run(const cb_pool& p, cudaStream_t stream, bool pdl);
 cudaError_t select_merge_run(const cb_select_merge& a, cudaStream_t stream, bool pdl);
 cudaError_t select_run(const SelectArgs& a, cudaStream_t stream, bool pdl);
 uint32_t select_tiles(uint32_t count);

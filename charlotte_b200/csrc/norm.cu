@@ -10,9 +10,12 @@
 // r = 1/sqrt(total/n + eps) and normed = (x·r)·g.
 //
 // With `add`, y (the block's output) is added first — post-normed with its
-// own gain when the layer has a post-norm (Gemma 3) — and the new hidden row
-// written back. `last_token` normalizes only the step's last row (the final
-// norm). Rows ≤ 4096 wide, a multiple of 4.
+// own gain when the layer has a post-norm (Gemma 3) — then x times `scale`
+// when given (Gemma 4's layer output scale), and the new hidden row written
+// back; `add_only` stops there. `last_token` normalizes only the step's last
+// row (the final norm); `rows_per_token` rows a token are each their own
+// row (the per-layer inputs); without a gain, normed = x·r (unit_gain).
+// Rows ≤ 4096 wide, a multiple of 4.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -91,13 +94,19 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(NormArgs a) {
                 }
             }
         }
+        const float sc = a.scale ? *a.scale : 1.0f;
 #pragma unroll
         for (int k = 0; k < kMaxVec4; ++k) {
             const uint32_t i = threadIdx.x + k * kNormThreads;
             if (i < vec4s) {
                 x[k] = make_float4(x[k].x + y[k].x, x[k].y + y[k].y, x[k].z + y[k].z, x[k].w + y[k].w);
+                if (a.scale) x[k] = make_float4(x[k].x * sc, x[k].y * sc, x[k].z * sc, x[k].w * sc);
                 hidden[i] = x[k];
             }
+        }
+        if (a.add_only) {
+            grid_dependents_launch();
+            return;
         }
     }
     float squares = 0.0f;
@@ -111,8 +120,12 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(NormArgs a) {
     for (int k = 0; k < kMaxVec4; ++k) {
         const uint32_t i = threadIdx.x + k * kNormThreads;
         if (i < vec4s) {
-            const float4 g = gain[i];
-            normed[i] = make_float4((x[k].x * r) * g.x, (x[k].y * r) * g.y, (x[k].z * r) * g.z, (x[k].w * r) * g.w);
+            if (gain) {
+                const float4 g = gain[i];
+                normed[i] = make_float4((x[k].x * r) * g.x, (x[k].y * r) * g.y, (x[k].z * r) * g.z, (x[k].w * r) * g.w);
+            } else {
+                normed[i] = make_float4(x[k].x * r, x[k].y * r, x[k].z * r, x[k].w * r);
+            }
         }
     }
 }
@@ -121,7 +134,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(NormArgs a) {
 
 cudaError_t norm_run(const NormArgs& a, cudaStream_t stream, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.last_token ? 1u : a.tokens);
+    cfg.gridDim = dim3(a.last_token ? 1u : a.tokens * (a.rows_per_token > 1u ? a.rows_per_token : 1u));
     cfg.blockDim = dim3(kNormThreads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

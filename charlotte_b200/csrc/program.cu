@@ -398,8 +398,8 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
             r.key_gain = qk ? static_cast<const float*>(ptr[1]) : nullptr;
             r.factors = factors ? static_cast<const float*>(ptr[2]) : nullptr;
             r.query = static_cast<float*>(ptr[3]);
-            r.key = static_cast<const float*>(ptr[4]);
-            r.value = static_cast<const float*>(ptr[5]);
+            r.key = static_cast<float*>(ptr[4]);
+            r.value = static_cast<float*>(ptr[5]);
             r.key_cache = static_cast<uint16_t*>(ptr[6]);
             r.value_cache = static_cast<uint16_t*>(ptr[7]);
             r.turns = static_cast<const float*>(turns);

@@ -12,7 +12,10 @@
 // `stride` within the head's lanes pairs the same elements), then
 // (x·r)·g. Query and key pairs turn by their angle — NEOX halves or
 // adjacent pairs — queries written back f32, keys and values packed f16
-// (saturated, round-to-nearest-even) into slot p mod slots.
+// (saturated, round-to-nearest-even) into slot p mod slots. The encode form
+// (rope_encode.wgsl, an encoder's) writes keys back f32 in place instead,
+// and with value_norm scales each value head by its 1/sqrt(mean square +
+// epsilon); no cache.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -55,6 +58,31 @@ __global__ void rope_kernel(RopeArgs a) {
     float4 x0 = src[lane];
     float4 x1 = src[lane + lanes];
 
+    if (a.encode) {
+        // rope_encode.wgsl: keys turned like queries and written back in
+        // place; value heads normalized without a gain (value_norm). The
+        // reduce runs on every lane where either needs it (uniform).
+        const bool qk = a.query_gain != nullptr, vn = a.value_norm != 0;
+        float r = 1.0f;
+        if (qk || vn) r = head_norm_factor(x0, x1, lanes, d, a.epsilon);
+        if (!is_value) {
+            if (qk) {   // (x·r)·g, then the turn: the decoder form's steps
+                const float4* g = reinterpret_cast<const float4*>(is_query ? a.query_gain : a.key_gain);
+                const float4 g0 = g[lane], g1 = g[lane + lanes];
+                x0 = make_float4((x0.x * r) * g0.x, (x0.y * r) * g0.y, (x0.z * r) * g0.z, (x0.w * r) * g0.w);
+                x1 = make_float4((x1.x * r) * g1.x, (x1.y * r) * g1.y, (x1.z * r) * g1.z, (x1.w * r) * g1.w);
+            }
+            rope_head(x0, x1, lane, lanes, d, false, a.epsilon, nullptr, true, a.halves != 0, cosines, sines);
+        } else if (vn) {
+            x0 = make_float4(x0.x * r, x0.y * r, x0.z * r, x0.w * r);
+            x1 = make_float4(x1.x * r, x1.y * r, x1.z * r, x1.w * r);
+        }
+        float* base = is_query ? a.query + (static_cast<size_t>(row) * hq + head) * d
+                               : (is_value ? a.value : a.key) + (static_cast<size_t>(row) * hkv + kvh) * d;
+        reinterpret_cast<float4*>(base)[lane] = x0;
+        reinterpret_cast<float4*>(base)[lane + lanes] = x1;
+        return;
+    }
     // QK-norm (uniform over the CTA: both gains or neither). Every lane takes
     // part in the shuffles — a warp may hold a key head and a value head —
     // and value heads discard the result.

@@ -32,17 +32,20 @@ __device__ __forceinline__ void rope_angles(uint32_t p, const float* turns, cons
 // with `gain` (x·r)·g; with `turn`, the pairs turned by their angle — NEOX
 // halves or adjacent pairs. Every lane of the warp calls it (the shuffles
 // span the warp); value heads pass no gain and no turn.
+// A head's 1/sqrt(mean square + epsilon) from its lanes' vec4 pairs, the
+// sum in reduce_head's tree; every lane of the warp takes part.
+__device__ __forceinline__ float head_norm_factor(float4 x0, float4 x1, uint32_t lanes, uint32_t d, float epsilon) {
+    float v = dot4(x0, x0) + dot4(x1, x1);
+    for (uint32_t stride = lanes / 2u; stride > 0; stride >>= 1) v = v + __shfl_down_sync(0xFFFFFFFFu, v, stride, lanes);
+    const float total = __shfl_sync(0xFFFFFFFFu, v, 0, lanes);
+    return 1.0f / sqrtf(total / static_cast<float>(d) + epsilon);
+}
+
 __device__ __forceinline__ void rope_head(float4& x0, float4& x1, uint32_t lane, uint32_t lanes, uint32_t d,
                                           bool norm, float epsilon, const float* gain, bool turn, bool halves,
                                           const float* cosines, const float* sines) {
     float r = 1.0f;
-    if (norm) {
-        float v = dot4(x0, x0) + dot4(x1, x1);
-        for (uint32_t stride = lanes / 2u; stride > 0; stride >>= 1)
-            v = v + __shfl_down_sync(0xFFFFFFFFu, v, stride, lanes);
-        const float total = __shfl_sync(0xFFFFFFFFu, v, 0, lanes);
-        r = 1.0f / sqrtf(total / static_cast<float>(d) + epsilon);
-    }
+    if (norm) r = head_norm_factor(x0, x1, lanes, d, epsilon);
     if (!turn) return;
     if (gain) {
         const float4 g0 = reinterpret_cast<const float4*>(gain)[lane];

@@ -174,7 +174,7 @@ CB_API uint64_t cb_matmul_split_bytes(uint32_t tokens, uint32_t rows);
 typedef struct cb_norm {
     float* hidden;            /* [tokens][width]                          */
     const float* output;      /* y, [tokens][width], with add             */
-    const float* gain;        /* [width]                                  */
+    const float* gain;        /* [width]; NULL: no gain (norm.h unit_gain) */
     const float* post_gain;   /* [width] or NULL                          */
     float* normed;            /* [tokens][width]                          */
     uint32_t width;
@@ -182,6 +182,15 @@ typedef struct cb_norm {
     uint32_t add;
     uint32_t last_token;
     float epsilon;
+    /* An encoder's variants (norm.h:69-82; zero leaves each off):
+     * `scale`: one float multiplying x after the add (Gemma 4's layer output
+     * scale; needs add); `add_only`: the add and x written back, nothing
+     * normalized (needs add); `rows_per_token`: the launch covers tokens ×
+     * rows_per_token rows, each normalized on its own (not with
+     * last_token). */
+    const float* scale;
+    uint32_t add_only;
+    uint32_t rows_per_token;
 } cb_norm;
 CB_API int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream);
 
@@ -196,8 +205,8 @@ CB_API int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream);
  * must be a multiple of 32; d is 64, 128 or 256. */
 typedef struct cb_rope {
     float* query;
-    const float* key;
-    const float* value;
+    float* key;                 /* read; written in place with `encode`    */
+    float* value;               /* read; written in place with value_norm  */
     uint16_t* key_cache;
     uint16_t* value_cache;
     const float* query_gain;
@@ -219,6 +228,12 @@ typedef struct cb_rope {
      * t·sequence_stride elements. Zero: rows are consecutive positions. */
     uint32_t rows_are_sequences;
     uint64_t sequence_stride;
+    /* rope's encode form (rope_encode.wgsl, an encoder's): every head
+     * written back in place, f32 — keys QK-normed and turned like queries —
+     * and no cache (key_cache, value_cache, slots unused); with value_norm,
+     * each value head also scaled by 1/sqrt(mean square + epsilon). */
+    uint32_t encode;
+    uint32_t value_norm;
 } cb_rope;
 CB_API int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream);
 /* θ_k / 2π for k < d/2, base^(−2k/d) in f64 rounded once to f32 (host). */
@@ -270,6 +285,46 @@ typedef struct cb_attention {
 CB_API int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream);
 /* Ticket words cb_attention needs for `tokens` rows. */
 CB_API uint32_t cb_attention_tickets(uint32_t tokens, uint32_t query_heads, uint32_t kv_heads);
+
+/* ---- block attention (an encoder's) -----------------------------------------------
+ * Replaces block_attention.wgsl scores_of + weigh behind
+ * block_attention_launches (src/core/kernels/block_attention/
+ * block_attention.h:333): every row i of a step at position 0 attends the
+ * step's own keys j with |i − j| ≤ half_window (the layer's window / 2),
+ * f32 queries, keys and values as rope's encode form left them; the same
+ * scores, maxima, weights and in-order sums, bit for bit, in one launch (no
+ * scores buffer). tokens ≤ 1,024 at head_dim 512, head_dim a multiple of 64,
+ * query_heads / kv_heads dividing 16. */
+typedef struct cb_block_attention {
+    const float* query;   /* [tokens][query_heads][head_dim] */
+    const float* key;     /* [tokens][kv_heads][head_dim]    */
+    const float* value;   /* [tokens][kv_heads][head_dim]    */
+    float* out;           /* [tokens][query_heads][head_dim] */
+    uint32_t tokens;
+    uint32_t head_dim;
+    uint32_t query_heads;
+    uint32_t kv_heads;
+    uint32_t half_window;
+    float scale_log2e;
+} cb_block_attention;
+CB_API int cb_block_attention_run(const cb_block_attention* a, uint32_t flags, void* stream);
+
+/* ---- pooling (an encoder's) -----------------------------------------------------
+ * Replaces pool.wgsl mean and unit behind mean_launch and unit_launch
+ * (src/core/kernels/pool/pool.h:107-121). MEAN: the mean of input rows
+ * 0..tokens−1 ([tokens][width]), each column a chain of adds in row order
+ * times 1/tokens, written at row tokens − 1 of output. UNIT: input's one row
+ * over its Euclidean length into output (a zero row stays zero). width ≤
+ * 4,096, a multiple of 4. */
+enum { CB_POOL_MEAN = 0, CB_POOL_UNIT = 1 };
+typedef struct cb_pool {
+    const float* input;
+    float* output;
+    uint32_t width;
+    uint32_t tokens;
+    uint32_t kind;
+} cb_pool;
+CB_API int cb_pool_run(const cb_pool* p, uint32_t flags, void* stream);
 
 /* ---- embedding gather -----------------------------------------------------------
  * Replaces gather.wgsl:25 behind gather_launches (src/core/kernels/gather/

@@ -163,6 +163,71 @@ def norm_row(hidden: np.ndarray, output, gain: np.ndarray, post_gain, epsilon: f
     return h, normed
 
 
+def norm_row_ex(hidden, output, gain, *, epsilon, add=True, post_gain=None, post_scale=1.0, scale=None,
+                normalize=True):
+    """norm.wgsl with the encoder's variants (or_norm_row_ex), one row:
+    returns (new hidden, normed or None). gain None: no gain."""
+    h = np.array(hidden, np.float32, copy=True)
+    width = h.size
+    normed = np.empty(width, np.float32)
+    out = np.ascontiguousarray(output if output is not None else np.zeros(width), np.float32)
+    keep = [np.ascontiguousarray(a, np.float32) if a is not None else None for a in (gain, post_gain, scale)]
+    L = lib()
+    L.or_norm_row_ex.argtypes = [c_f32p, c_f32p, c_f32p, c_f32p, ctypes.c_float, c_f32p, ctypes.c_uint32,
+                                 ctypes.c_float, ctypes.c_int, ctypes.c_int, c_f32p]
+    L.or_norm_row_ex(ptr(h, ctypes.c_float), ptr(out, ctypes.c_float),
+                     *[ptr(a, ctypes.c_float) if a is not None else None for a in keep[:2]], post_scale,
+                     ptr(keep[2], ctypes.c_float) if keep[2] is not None else None, width, epsilon, int(add),
+                     int(normalize), ptr(normed, ctypes.c_float))
+    return h, (normed if normalize else None)
+
+
+def rope_encode_token(q, k, v, p, *, head_dim, query_heads, kv_heads, halves, epsilon, turns, factors=None,
+                      query_gain=None, key_gain=None, value_norm=False):
+    """rope_encode.wgsl for one token, q, k and v (f32 [heads*d]) in place."""
+    keep = [np.ascontiguousarray(a, np.float32) if a is not None else None
+            for a in (turns, factors, query_gain, key_gain)]
+    s = RopeShape(head_dim, query_heads, kv_heads, int(halves), int(query_gain is not None), 1, epsilon,
+                  *[ptr(a, ctypes.c_float) if a is not None else None for a in keep])
+    L = lib()
+    L.or_rope_encode_token.argtypes = [ctypes.POINTER(RopeShape), ctypes.c_uint32, ctypes.c_int, c_f32p, c_f32p,
+                                       c_f32p]
+    L.or_rope_encode_token(ctypes.byref(s), p, int(value_norm), ptr(q, ctypes.c_float), ptr(k, ctypes.c_float),
+                           ptr(v, ctypes.c_float))
+
+
+def block_attention(q, k, v, *, tokens, head_dim, query_heads, kv_heads, half_window, scale_log2e):
+    """block_attention.wgsl scores_of + weigh over a step: q [n][hq*d], k, v
+    [n][hkv*d] -> out [n][hq*d]."""
+    qq, kk, vv = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    out = np.empty((tokens, query_heads * head_dim), np.float32)
+    L = lib()
+    L.or_block_attention.argtypes = [c_f32p, c_f32p, c_f32p] + [ctypes.c_uint32] * 5 + [ctypes.c_float, c_f32p]
+    L.or_block_attention(ptr(qq, ctypes.c_float), ptr(kk, ctypes.c_float), ptr(vv, ctypes.c_float), tokens,
+                         head_dim, query_heads, kv_heads, half_window, scale_log2e, ptr(out, ctypes.c_float))
+    return out
+
+
+def pool_mean(rows):
+    """pool.wgsl mean over the rows of a [n][width] array."""
+    r = np.ascontiguousarray(rows, np.float32)
+    out = np.empty(r.shape[1], np.float32)
+    L = lib()
+    L.or_pool_mean.argtypes = [c_f32p, ctypes.c_uint32, ctypes.c_uint32, c_f32p]
+    L.or_pool_mean(ptr(r, ctypes.c_float), r.shape[0], r.shape[1], ptr(out, ctypes.c_float))
+    return out
+
+
+def pool_unit(row):
+    """pool.wgsl unit: the row over its Euclidean length."""
+    r = np.ascontiguousarray(row, np.float32)
+    out = np.empty(r.size, np.float32)
+    L = lib()
+    L.or_pool_unit.argtypes = [c_f32p, ctypes.c_uint32, c_f32p]
+    L.or_pool_unit(ptr(r, ctypes.c_float), r.size, ptr(out, ctypes.c_float))
+    return out
+
+
 def rope_turns(base: float, head_dim: int) -> np.ndarray:
     t = np.empty(head_dim // 2, np.float32)
     lib().or_rope_turns(base, head_dim, ptr(t, ctypes.c_float))

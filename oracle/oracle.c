@@ -528,6 +528,131 @@ void or_rope_token(const or_rope_shape* s, uint32_t p, float* q, const float* k,
     }
 }
 
+/* ---- an encoder's kernels --------------------------------------------------- */
+
+/* norm.wgsl:80-198 with the `scaled`, `normalize`, post_scale and unit-gain
+ * variants (norm.h:69-99), one row. */
+void or_norm_row_ex(float* hidden, const float* output, const float* gain, const float* post_gain, float post_scale,
+                    const float* scale, uint32_t width, float epsilon, int add, int normalize, float* normed) {
+    const float n = (float)width;
+    if (add) {
+        float y[4096];
+        memcpy(y, output, width * sizeof(float));
+        if (post_gain) {
+            float r = 1.0f / sqrtf(norm_squares(y, width) / n + epsilon);
+            for (uint32_t j = 0; j < width; ++j) y[j] = ((y[j] * r) * post_gain[j]) * post_scale;
+        }
+        const float s = scale ? scale[0] : 1.0f;
+        for (uint32_t j = 0; j < width; ++j) {
+            float x = hidden[j] + y[j];
+            if (scale) x = x * s;
+            hidden[j] = x;
+        }
+    }
+    if (!normalize) return;
+    float r = 1.0f / sqrtf(norm_squares(hidden, width) / n + epsilon);
+    for (uint32_t j = 0; j < width; ++j) normed[j] = gain ? (hidden[j] * r) * gain[j] : hidden[j] * r;
+}
+
+/* rope_encode.wgsl:8-76: the decoder form's angles, QK-norm and turn, every
+ * head in place; value heads x·r with value_norm (the head's reduce_head,
+ * no gain), not turned. */
+void or_rope_encode_token(const or_rope_shape* s, uint32_t p, int value_norm, float* q, float* k, float* v) {
+    const uint32_t d = s->head_dim;
+    float cosines[256], sines[256];
+    for (uint32_t j = 0; j < d / 2; ++j) {
+        float t = (float)p * s->turns[j];
+        if (s->factors) t = t / s->factors[j];
+        float angle = 6.283185307179586f * (t - rintf(t));
+        or_sincos(angle, &sines[j], &cosines[j]);
+    }
+    for (uint32_t h = 0; h < s->query_heads; ++h) {
+        float* x = q + (size_t)h * d;
+        if (s->qk_norm) norm_head(x, d, s->query_gain, s->epsilon);
+        rotate_head(x, d, s->halves, cosines, sines);
+    }
+    for (uint32_t h = 0; h < s->kv_heads; ++h) {
+        float* x = k + (size_t)h * d;
+        if (s->qk_norm) norm_head(x, d, s->key_gain, s->epsilon);
+        rotate_head(x, d, s->halves, cosines, sines);
+    }
+    if (value_norm) {
+        const uint32_t lanes = d / 8;
+        for (uint32_t h = 0; h < s->kv_heads; ++h) {
+            float* x = v + (size_t)h * d;
+            float partial[64];
+            for (uint32_t i = 0; i < lanes; ++i)
+                partial[i] = or_dot4(x + 4 * i, x + 4 * i) + or_dot4(x + 4 * (i + lanes), x + 4 * (i + lanes));
+            float r = 1.0f / sqrtf(head_reduce(partial, lanes) / (float)d + s->epsilon);
+            for (uint32_t j = 0; j < d; ++j) x[j] = x[j] * r;
+        }
+    }
+}
+
+/* block_attention.wgsl: scores_of (:95-190) — s_ij = (the chain of dot4s
+ * along d in order) × scale·log2e — and weigh (:205-326) — m the largest live
+ * score of the row, p = exp2(s − m) for live keys, O = fma(p, v, O) and
+ * l = l + p in key order, out = O / l. A key not live adds an exact zero
+ * (fma(0, v, O) = O; O is never −0), so it is skipped here. */
+void or_block_attention(const float* q, const float* k, const float* v, uint32_t n, uint32_t d, uint32_t query_heads,
+                        uint32_t kv_heads, uint32_t half_window, float scale_log2e, float* out) {
+    const uint32_t G = query_heads / kv_heads;
+    float* s = (float*)malloc((size_t)n * sizeof(float));
+    float o[512];
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t lo = i > half_window ? i - half_window : 0;
+        const uint32_t hi = i + half_window < n - 1 ? i + half_window : n - 1;
+        for (uint32_t h = 0; h < query_heads; ++h) {
+            const uint32_t kv = h / G;
+            const float* qv = q + ((size_t)i * query_heads + h) * d;
+            float m = 0.0f;
+            int seen = 0;
+            for (uint32_t j = lo; j <= hi; ++j) {
+                const float* kj = k + ((size_t)j * kv_heads + kv) * d;
+                float acc = 0.0f;
+                for (uint32_t c = 0; c < d; c += 4) acc = acc + or_dot4(qv + c, kj + c);
+                s[j] = acc * scale_log2e;
+                m = seen ? fmaxf(m, s[j]) : s[j];
+                seen = 1;
+            }
+            float l = 0.0f;
+            for (uint32_t c = 0; c < d; ++c) o[c] = 0.0f;
+            for (uint32_t j = lo; j <= hi; ++j) {
+                const float p = or_exp2(s[j] - m);
+                const float* vj = v + ((size_t)j * kv_heads + kv) * d;
+                for (uint32_t c = 0; c < d; ++c) o[c] = fmaf(p, vj[c], o[c]);
+                l = l + p;
+            }
+            float* dst = out + ((size_t)i * query_heads + h) * d;
+            for (uint32_t c = 0; c < d; ++c) dst[c] = o[c] / l;
+        }
+    }
+    free(s);
+}
+
+/* pool.wgsl mean (:49-61) and unit (:63-100). */
+void or_pool_mean(const float* rows, uint32_t n, uint32_t width, float* mean) {
+    const float inverse = 1.0f / (float)n;
+    for (uint32_t c = 0; c < width; ++c) {
+        float sum = 0.0f;
+        for (uint32_t r = 0; r < n; ++r) sum = sum + rows[(size_t)r * width + c];
+        mean[c] = sum * inverse;
+    }
+}
+
+void or_pool_unit(const float* row, uint32_t width, float* unit) {
+    float partial[OR_NORM_WG];
+    const uint32_t vec4s = width / 4;
+    for (uint32_t i = 0; i < OR_NORM_WG; ++i) {
+        float squares = 0.0f;
+        for (uint32_t c = i; c < vec4s; c += OR_NORM_WG) squares = squares + or_dot4(row + 4 * c, row + 4 * c);
+        partial[i] = squares;
+    }
+    const float total = norm_reduce(partial);
+    const float r = total > 0.0f ? 1.0f / sqrtf(total) : 0.0f;
+    for (uint32_t c = 0; c < width; ++c) unit[c] = row[c] * r;
+}
+
 /* ---- attention ------------------------------------------------------------- */
 
 #define OR_CHUNK_KEYS 64

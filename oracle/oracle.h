@@ -106,6 +106,28 @@ void or_attention_row(const float* q, uint32_t p, const uint16_t* key_cache, con
                       uint32_t slots, uint32_t window, float scale_log2e, uint32_t head_dim,
                       uint32_t query_heads, uint32_t kv_heads, float* out);
 
+/* ---- an encoder's kernels (graph/encoder.h) -------------------------------- */
+/* norm.wgsl:80-198 with the encoder's variants for one row: the add (y
+ * post-normed first with post_gain, times post_scale), x = (x + y)·scale[0]
+ * when `scale`, the new hidden row written back; without `normalize` nothing
+ * more; else normed = (x·r)·gain, or x·r when gain is NULL. */
+void or_norm_row_ex(float* hidden, const float* output, const float* gain, const float* post_gain, float post_scale,
+                    const float* scale, uint32_t width, float epsilon, int add, int normalize, float* normed);
+/* rope_encode.wgsl for one token at position p, in place: query and key
+ * heads QK-normed (qk_norm) and turned, value heads normalized without a
+ * gain when value_norm; no cache. */
+void or_rope_encode_token(const or_rope_shape* s, uint32_t p, int value_norm, float* q, float* k, float* v);
+/* block_attention.wgsl scores_of + weigh for the whole step of n rows:
+ * q [n][hq][d], k and v [n][hkv][d], out [n][hq][d]; key j live for row i
+ * when |i - j| <= half_window. */
+void or_block_attention(const float* q, const float* k, const float* v, uint32_t n, uint32_t d, uint32_t query_heads,
+                        uint32_t kv_heads, uint32_t half_window, float scale_log2e, float* out);
+/* pool.wgsl mean: the mean of n rows of `width` (a chain of adds a column in
+ * row order, times 1/n); unit: a row over its Euclidean length (zeros stay
+ * zeros). */
+void or_pool_mean(const float* rows, uint32_t n, uint32_t width, float* mean);
+void or_pool_unit(const float* row, uint32_t width, float* unit);
+
 /* ---- selection and draw (topk.wgsl, draw.wgsl) ----------------------------- */
 uint32_t or_key_of(uint32_t bits);   /* topk.wgsl:28 */
 uint32_t or_bits_of(uint32_t key);   /* topk.wgsl:43 */
