@@ -57,7 +57,7 @@ constexpr uint32_t kStepHead = 64;             // interface.h kStepHead
 constexpr uint64_t kMaxReadback = 4096;        // program.h kMaxReadback
 constexpr uint32_t kGgufF16 = 1;
 
-enum class Kind { Matmul, Norm, Rope, Attention, Gather, Select, Draw };
+enum class Kind { Matmul, Norm, Rope, Attention, Gather, Select, Draw, BlockAttention, Pool };
 
 // One operation: the launches [first_launch, last_launch] of the graph.
 struct Op {
@@ -80,6 +80,8 @@ struct Op {
     cb_select sel{};
     bool select_draws = false;
     cb_select_merge draw{};
+    cb_block_attention block{};
+    cb_pool pool{};
 };
 
 struct Graph {
@@ -344,21 +346,20 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
         case CB_KERNEL_NORM: {
             if (!is(entry, "main")) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: norm entry %s", i, entry);
             if (l.binding_count < 5) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: norm bindings", i);
-            for (const char* v : {"scaled", "renorm", "unit_gain"})
-                if (override_or(l, v, 0.0) != 0.0)
-                    return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: the norm variant '%s' has no CUDA form",
-                                i, v);
-            if (override_or(l, "normalize", 1.0) == 0.0 || override_or(l, "rows_per_token", 1.0) != 1.0 ||
-                constant_at<float>(l, 4) != 1.0f)
-                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: a norm form (add-only, several rows a "
-                            "token, or a post scale) with no CUDA form", i);
-            void* ptr[5];
-            for (uint32_t b = 0; b < 5; ++b)
+            // The audio encoder's forms (a re-norm, a post scale) have no CUDA form.
+            if (override_or(l, "renorm", 0.0) != 0.0 || constant_at<float>(l, 4) != 1.0f)
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: a norm with a re-norm or a post scale has "
+                            "no CUDA form", i);
+            const bool scaled = override_or(l, "scaled", 0.0) != 0.0;
+            if (scaled && l.binding_count < 6) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: norm scale", i);
+            void* ptr[6] = {};
+            for (uint32_t b = 0; b < (scaled ? 6u : 5u); ++b)
                 if (int rc = resolve(p, l.bindings[b], i, &ptr[b])) return rc;
             const bool add = override_or(l, "add", 0.0) != 0.0;
             const bool post = override_or(l, "post_norm", 0.0) != 0.0;
+            const bool unit = override_or(l, "unit_gain", 0.0) != 0.0;
             cb_norm& n = op.norm;
-            n.gain = static_cast<const float*>(ptr[0]);
+            n.gain = unit ? nullptr : static_cast<const float*>(ptr[0]);
             n.post_gain = post ? static_cast<const float*>(ptr[1]) : nullptr;
             n.output = add ? static_cast<const float*>(ptr[2]) : nullptr;
             n.hidden = static_cast<float*>(ptr[3]);
@@ -367,6 +368,9 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
             n.add = add ? 1u : 0u;
             n.last_token = op.last_token ? 1u : 0u;
             n.epsilon = constant_at<float>(l, 0);
+            n.scale = scaled ? static_cast<const float*>(ptr[5]) : nullptr;
+            n.add_only = override_or(l, "normalize", 1.0) == 0.0 ? 1u : 0u;
+            n.rows_per_token = static_cast<uint32_t>(override_or(l, "rows_per_token", 1.0));
             op.kind = Kind::Norm;
             ops.push_back(op);
             return CB_OK;
@@ -410,6 +414,99 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
             r.slots = constant_at<uint32_t>(l, 0);
             r.epsilon = constant_at<float>(l, 4);
             op.kind = Kind::Rope;
+            ops.push_back(op);
+            return CB_OK;
+        }
+        case CB_KERNEL_ROPE_ENCODE: {
+            // rope_encode_launch (rope.cpp): bindings {query gain, key gain,
+            // factors, query, key, value}; constants {slots, ε, turns at 16}.
+            if (!is(entry, "main")) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope entry %s", i, entry);
+            if (l.binding_count < 6) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope bindings", i);
+            const uint32_t d = static_cast<uint32_t>(override_or(l, "head_dimension", 0.0));
+            if (override_or(l, "axial", 0.0) != 0.0 || (d != 64 && d != 128 && d != 256))
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope's encode form %s has no CUDA form", i,
+                            d == 512 ? "at head dimension 512" : "in the axial pairing");
+            if (l.constants_bytes < 16 + 4 * (d / 2))
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope constants", i);
+            void* ptr[6];
+            for (uint32_t b = 0; b < 6; ++b)
+                if (int rc = resolve(p, l.bindings[b], i, &ptr[b])) return rc;
+            void* turns = nullptr;
+            if (int rc = dev_alloc(p, &turns, 4 * (d / 2))) return rc;
+            const cudaError_t e = cudaMemcpy(turns, l.constants + 16, 4 * (d / 2), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return fail_cuda(e, "cb_program_build: rope turns");
+            const bool qk = override_or(l, "qk_norm", 0.0) != 0.0;
+            const bool factors = override_or(l, "factors", 0.0) != 0.0;
+            cb_rope& r = op.rope;
+            r.query_gain = qk ? static_cast<const float*>(ptr[0]) : nullptr;
+            r.key_gain = qk ? static_cast<const float*>(ptr[1]) : nullptr;
+            r.factors = factors ? static_cast<const float*>(ptr[2]) : nullptr;
+            r.query = static_cast<float*>(ptr[3]);
+            r.key = static_cast<float*>(ptr[4]);
+            r.value = static_cast<float*>(ptr[5]);
+            r.turns = static_cast<const float*>(turns);
+            r.head_dim = d;
+            r.query_heads = static_cast<uint32_t>(override_or(l, "query_heads", 0.0));
+            r.kv_heads = static_cast<uint32_t>(override_or(l, "key_value_heads", 0.0));
+            r.halves = override_or(l, "halves", 0.0) != 0.0 ? 1u : 0u;
+            r.epsilon = constant_at<float>(l, 4);
+            r.encode = 1;
+            r.value_norm = override_or(l, "value_norm", 0.0) != 0.0 ? 1u : 0u;
+            op.kind = Kind::Rope;
+            ops.push_back(op);
+            return CB_OK;
+        }
+        case CB_KERNEL_BLOCK_ATTENTION: {
+            // block_attention_launches (block_attention.cpp): scores_of
+            // {query, key, scores, maxima} then weigh {scores, maxima, value,
+            // attention}, one launch here; constants {half window, scale·log2e}.
+            if (!is(entry, "scores_of"))
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: block attention entry %s without its scores",
+                            i, entry);
+            if (i + 1 >= count || launches[i + 1].kernel != CB_KERNEL_BLOCK_ATTENTION ||
+                !is(launches[i + 1].entry_point, "weigh") || l.binding_count < 2 || launches[i + 1].binding_count < 4)
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: block attention's scores without its weigh", i);
+            void* ptr[4];
+            for (uint32_t b = 0; b < 2; ++b)
+                if (int rc = resolve(p, l.bindings[b], i, &ptr[b])) return rc;
+            for (uint32_t b = 2; b < 4; ++b)
+                if (int rc = resolve(p, launches[i + 1].bindings[b], i + 1, &ptr[b])) return rc;
+            cb_block_attention& a = op.block;
+            a.query = static_cast<const float*>(ptr[0]);
+            a.key = static_cast<const float*>(ptr[1]);
+            a.value = static_cast<const float*>(ptr[2]);
+            a.out = static_cast<float*>(ptr[3]);
+            a.head_dim = static_cast<uint32_t>(override_or(l, "head_dimension", 0.0));
+            a.query_heads = static_cast<uint32_t>(override_or(l, "query_heads", 0.0));
+            a.kv_heads = static_cast<uint32_t>(override_or(l, "key_value_heads", 0.0));
+            a.half_window = constant_at<uint32_t>(l, 0);
+            a.scale_log2e = constant_at<float>(l, 4);
+            if (a.kv_heads == 0 || a.query_heads % a.kv_heads != 0 || 16 % (a.query_heads / a.kv_heads) != 0 ||
+                a.head_dim % 64 != 0 || a.head_dim > 512)
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: block attention of %u/%u heads of %u", i,
+                            a.query_heads, a.kv_heads, a.head_dim);
+            op.kind = Kind::BlockAttention;
+            op.last_launch = i + 1;
+            ops.push_back(op);
+            i = i + 1;
+            return CB_OK;
+        }
+        case CB_KERNEL_POOL: {
+            // mean_launch / unit_launch (pool.cpp): {input, output};
+            // constants {vec4s, pooling, ε}.
+            const bool mean = is(entry, "mean");
+            if (!mean && !is(entry, "unit"))
+                return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: pooling entry %s has no CUDA form", i, entry);
+            if (l.binding_count < 2) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: pool bindings", i);
+            void* ptr[2];
+            for (uint32_t b = 0; b < 2; ++b)
+                if (int rc = resolve(p, l.bindings[b], i, &ptr[b])) return rc;
+            cb_pool& q = op.pool;
+            q.input = static_cast<const float*>(ptr[0]);
+            q.output = static_cast<float*>(ptr[1]);
+            q.width = 4u * constant_at<uint32_t>(l, 0);
+            q.kind = mean ? CB_POOL_MEAN : CB_POOL_UNIT;
+            op.kind = Kind::Pool;
             ops.push_back(op);
             return CB_OK;
         }
@@ -578,6 +675,16 @@ int launch_op(cb_program* p, const Op& op, const cb_step& s) {
             a.tickets = p->tickets;
             a.max_chunks = p->max_chunks;
             return cb_attention_run(&a, CB_RUN_PDL, stream);
+        }
+        case Kind::BlockAttention: {
+            cb_block_attention a = op.block;
+            a.tokens = T;
+            return cb_block_attention_run(&a, CB_RUN_PDL, stream);
+        }
+        case Kind::Pool: {
+            cb_pool q = op.pool;
+            q.tokens = T;
+            return cb_pool_run(&q, CB_RUN_PDL, stream);
         }
         case Kind::Gather: {
             cb_gather g = op.gather;

@@ -595,7 +595,10 @@ enum {
     CB_KERNEL_ATTENTION = 4,
     CB_KERNEL_GATHER = 5,
     CB_KERNEL_TOPK = 6,
-    CB_KERNEL_DRAW = 7
+    CB_KERNEL_DRAW = 7,
+    CB_KERNEL_ROPE_ENCODE = 8,       /* rope.wgsl + rope_encode.wgsl (an encoder's)  */
+    CB_KERNEL_BLOCK_ATTENTION = 9,   /* block_attention.wgsl (scores_of, weigh)      */
+    CB_KERNEL_POOL = 10              /* pool.wgsl (mean, unit)                       */
 };
 enum { CB_ROWS_EVERY_TOKEN = 0, CB_ROWS_LAST_TOKEN = 1 };            /* interface.h Rows      */
 enum { CB_KEY_SPLIT_NONE = 0, CB_KEY_SPLIT_PER_CHUNK = 1, CB_KEY_SPLIT_WHEN_SPLIT = 2 };   /* KeySplit */

@@ -25,6 +25,7 @@
 #include "core/capability/capability.h"
 #include "core/gguf/byte_source.h"
 #include "core/gguf/reader.h"
+#include "core/graph/encoder.h"
 #include "core/graph/graph.h"
 #include "core/policy/policy.h"
 #include "program_cuda.h"
@@ -53,7 +54,8 @@ struct cbh {
     residency::ResidencyPlan plan;
     std::unique_ptr<residency::cuda::Upload> upload;
     std::unique_ptr<kernels::cuda::Program> program;
-    residency::BufferRange logits{}, sampled{};
+    residency::BufferRange logits{}, sampled{}, embedding{};
+    bool encoder = false;
     std::uint32_t launches = 0;
     std::vector<Result> results;
     std::string message;
@@ -146,10 +148,14 @@ __attribute__((visibility("default"))) int cbh_open(const char* path, std::uint3
     if (h->index.read_string("general.architecture", name) != gguf::MetadataError::Ok)
         return fail(h, err, err_len, "no general.architecture");
     const arch::Architecture* a = capability::find_architecture(name);
-    if (!a || !arch::decoder_graph(*a)) return fail(h, err, err_len, "no decoder architecture " + std::string(name));
+    if (!a || (!arch::decoder_graph(*a) && !arch::encoder_graph(*a)))
+        return fail(h, err, err_len, "no architecture " + std::string(name));
+    h->encoder = arch::encoder_graph(*a) != nullptr;
     if (const auto r = a->describe(h->index, h->model); !r.ok()) return fail(h, err, err_len, "describe: " + r.subject);
     if (const auto r = residency::plan_residency(h->index, h->model, kLimits, policy::LoadPolicy{},
-                                                 graph::decoder_working_set(h->model), h->plan);
+                                                 h->encoder ? graph::encoder_working_set(h->model)
+                                                            : graph::decoder_working_set(h->model),
+                                                 h->plan);
         !r.ok())
         return fail(h, err, err_len, "plan: " + r.subject);
     if (const auto r = residency::cuda::Upload::begin(h->index, h->plan, h->file.size(), capability::find_format, {},
@@ -167,17 +173,22 @@ __attribute__((visibility("default"))) int cbh_open(const char* path, std::uint3
     const residency::ResidencyPlan& plan = h->upload->plan();
     std::vector<kernels::Launch> launches;
     const formats::Format* f16 = capability::find_format(gguf::TensorType::F16);
-    if (const auto r = arch::decoder_graph(*a)(h->model, plan, *f16, launches); !r.ok())
+    // An encoder's one step ends in the pooled, unit-length vector, which it
+    // reads back (runtime/embedder.h); a decoder's in the sampled record.
+    if (const auto r = h->encoder ? arch::encoder_graph(*a)(h->model, plan, launches)
+                                  : arch::decoder_graph(*a)(h->model, plan, *f16, launches);
+        !r.ok())
         return fail(h, err, err_len, "graph: " + r.subject);
     for (const residency::PlannedScratch& s : plan.scratch) {
         if (s.purpose == "logits") h->logits = s.range;
         if (s.purpose == "sampled") h->sampled = s.range;
+        if (s.purpose == "embedding") h->embedding = s.range;
     }
     h->launches = static_cast<std::uint32_t>(launches.size());
+    const residency::BufferRange& back = h->encoder ? h->embedding : h->sampled;
     Built built;
     kernels::cuda::Program::build(*h->upload, std::move(launches),
-                                  kernels::Binding{h->sampled.buffer, h->sampled.offset, h->sampled.length}, on_built,
-                                  &built);
+                                  kernels::Binding{back.buffer, back.offset, back.length}, on_built, &built);
     if (!built.program) return fail(h, err, err_len, "build: " + built.message);
     h->program = std::move(built.program);
     *out = h;
@@ -185,6 +196,10 @@ __attribute__((visibility("default"))) int cbh_open(const char* path, std::uint3
 }
 
 __attribute__((visibility("default"))) std::uint32_t cbh_vocab(const cbh* h) { return h->model.vocabulary_size; }
+// An encoder's embedding length (0 for a decoder).
+__attribute__((visibility("default"))) std::uint32_t cbh_embedding_length(const cbh* h) {
+    return h->encoder ? h->model.encoder->embedding_length : 0u;
+}
 __attribute__((visibility("default"))) std::uint32_t cbh_launches(const cbh* h) { return h->launches; }
 __attribute__((visibility("default"))) std::uint32_t cbh_context(const cbh* h) { return h->plan.context_offered; }
 
@@ -224,6 +239,25 @@ __attribute__((visibility("default"))) const char* cbh_message(const cbh* h) { r
 __attribute__((visibility("default"))) int cbh_logits(cbh* h, float* out) {
     return cb_buffers_read(h->upload->buffers(), static_cast<std::uint32_t>(h->logits.buffer), h->logits.offset, out,
                            std::uint64_t{h->model.vocabulary_size} * 4);
+}
+
+// An encoder's last step's embedding (the plan's embedding buffer) to host
+// memory, embedding-length floats.
+__attribute__((visibility("default"))) int cbh_embedding(cbh* h, float* out) {
+    if (!h->encoder) return CB_ERROR_INVALID;
+    return cb_buffers_read(h->upload->buffers(), static_cast<std::uint32_t>(h->embedding.buffer), h->embedding.offset,
+                           out, std::uint64_t{h->model.encoder->embedding_length} * 4);
+}
+
+// Any scratch buffer of the plan by its purpose ("hidden", "per_layer", …):
+// `count` floats from its start to host memory (for tests that check a step
+// part of the way).
+__attribute__((visibility("default"))) int cbh_scratch(cbh* h, const char* purpose, float* out, std::uint64_t count) {
+    for (const residency::PlannedScratch& s : h->upload->plan().scratch)
+        if (s.purpose == purpose)
+            return cb_buffers_read(h->upload->buffers(), static_cast<std::uint32_t>(s.range.buffer), s.range.offset,
+                                   out, std::min<std::uint64_t>(count * 4, s.range.length));
+    return CB_ERROR_INVALID;
 }
 
 // A profiled step of its first `launches` launches, waited on: the number

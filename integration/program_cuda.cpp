@@ -152,6 +152,11 @@ std::uint32_t kernel_of(const Launch& l) noexcept {
     if (l.kernel.size() == shaders::rope.size() + shaders::rope_cache.size() && l.kernel.starts_with(shaders::rope) &&
         l.kernel.ends_with(shaders::rope_cache))
         return CB_KERNEL_ROPE_CACHE;
+    if (l.kernel.size() == shaders::rope.size() + shaders::rope_encode.size() && l.kernel.starts_with(shaders::rope) &&
+        l.kernel.ends_with(shaders::rope_encode))
+        return CB_KERNEL_ROPE_ENCODE;
+    if (l.kernel == shaders::block_attention) return CB_KERNEL_BLOCK_ATTENTION;
+    if (l.kernel == shaders::pool) return CB_KERNEL_POOL;
     return CB_KERNEL_UNKNOWN;
 }
 
