@@ -39,7 +39,8 @@ class Matmul(ctypes.Structure):
                 ("epilogue", ctypes.c_uint32), ("activation", ctypes.c_uint32), ("member", Member * 3),
                 ("gate_input", ctypes.c_void_p), ("gate_input_stride", ctypes.c_uint32),
                 ("gate_input_column", ctypes.c_uint32), ("gate_input_token", ctypes.c_uint32),
-                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64), ("dense", ctypes.c_void_p)]
+                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64), ("dense", ctypes.c_void_p),
+                ("x16", ctypes.c_void_p), ("out16", ctypes.c_void_p)]
 
 
 class Norm(ctypes.Structure):
@@ -47,7 +48,7 @@ class Norm(ctypes.Structure):
                 ("post_gain", ctypes.c_void_p), ("normed", ctypes.c_void_p), ("width", ctypes.c_uint32),
                 ("tokens", ctypes.c_uint32), ("add", ctypes.c_uint32), ("last_token", ctypes.c_uint32),
                 ("epsilon", ctypes.c_float), ("scale", ctypes.c_void_p), ("add_only", ctypes.c_uint32),
-                ("rows_per_token", ctypes.c_uint32)]
+                ("rows_per_token", ctypes.c_uint32), ("normed16", ctypes.c_void_p)]
 
 
 class Rope(ctypes.Structure):
@@ -84,7 +85,7 @@ class Attention(ctypes.Structure):
                 ("kv_heads", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("window", ctypes.c_uint32),
                 ("max_chunks", ctypes.c_uint32), ("scale_log2e", ctypes.c_float),
                 ("rows_are_sequences", ctypes.c_uint32), ("sequence_stride", ctypes.c_uint64),
-                ("rope", ctypes.c_void_p)]
+                ("rope", ctypes.c_void_p), ("out16", ctypes.c_void_p)]
 
 
 class Gather(ctypes.Structure):

@@ -225,6 +225,14 @@ int cb_matmul_run(const cb_matmul* m, const float* x, uint32_t x_stride, uint32_
             if (!aligned16(m->dense))
                 return fail(CB_ERROR_INVALID, "cb_matmul_run: the dense weights must be 16-byte aligned");
             a.dense = m->dense;
+            if (m->x16 && !aligned16(m->x16))
+                return fail(CB_ERROR_INVALID, "cb_matmul_run: x16 must be 16-byte aligned");
+            if (m->out16 && m->epilogue != CB_EPILOGUE_GATED)
+                return fail(CB_ERROR_INVALID, "cb_matmul_run: out16 is the gated epilogue's");
+            a.x16 = m->x16;
+            a.out16 = m->out16;
+        } else if (m->x16 || m->out16) {
+            return fail(CB_ERROR_INVALID, "cb_matmul_run: x16 and out16 are the dense form's");
         }
     }
     const int sms = sm_count();

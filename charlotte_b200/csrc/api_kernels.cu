@@ -65,7 +65,8 @@ int cb_rope_run(const cb_rope* r, uint32_t flags, void* stream) {
     if (r->encode && r->rows_are_sequences)
         return fail(CB_ERROR_INVALID, "cb_rope_run: the encode form takes the rows of one step");
     if (r->value_norm && !r->encode) return fail(CB_ERROR_INVALID, "cb_rope_run: value_norm is the encode form's");
-    if (!head_dim_ok(r->head_dim)) return fail(CB_ERROR_INVALID, "cb_rope_run: head dimension %u", r->head_dim);
+    if (!head_dim_ok(r->head_dim) && !(r->encode && r->head_dim == 512))
+        return fail(CB_ERROR_INVALID, "cb_rope_run: head dimension %u", r->head_dim);
     if (r->kv_heads == 0 || r->query_heads % r->kv_heads != 0)
         return fail(CB_ERROR_INVALID, "cb_rope_run: %u query heads over %u kv heads", r->query_heads, r->kv_heads);
     if ((r->query_heads + 2 * r->kv_heads) * (r->head_dim / 8) % 32 != 0)

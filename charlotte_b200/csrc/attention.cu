@@ -122,9 +122,9 @@ __device__ __forceinline__ void stage_keys(const AttentionArgs& a, const uint16_
 // `range_of(m, &c0, &c1)`; `write(m, e, o / l)` takes each output. `fac`
 // holds Q·64 floats of scratch, `lfac` Q·32; the CTA must have met a
 // barrier since their last readers.
-template <typename Range, typename Stat, typename Part, typename Write>
-__device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, float* lfac, Range range_of,
-                                            Stat stat_of, Part part_of, Write write, uint32_t lane, uint32_t wid) {
+template <uint32_t D, typename Range, typename Stat, typename Part, typename Write>
+__device__ __forceinline__ void fold_chunks(uint32_t Q, float* fac, float* lfac, Range range_of, Stat stat_of,
+                                            Part part_of, Write write, uint32_t lane, uint32_t wid) {
     uint32_t lo = 0xFFFFFFFFu, hi = 0;
     for (uint32_t m = 0; m < Q; ++m) {
         uint32_t c0, c1;
@@ -133,68 +133,97 @@ __device__ __forceinline__ void fold_chunks(uint32_t Q, uint32_t d, float* fac, 
         hi = max(hi, c1);
     }
     constexpr uint32_t warps = kAttnThreads / 32u;
-    // Outputs in groups of the CTA's threads, each one thread's o and l chains.
-    for (uint32_t i0 = 0; i0 < Q * d; i0 += kAttnThreads) {
-        if (i0) __syncthreads();   // the last group's reads of the factors are done
+    // Every chunk's (fa, fb) of a block of 32 chunks, a warp a query.
+    float carry[kMaxQueries / warps];   // the running top of each of this warp's queries
+#pragma unroll
+    for (uint32_t k = 0; k < kMaxQueries / warps; ++k) carry[k] = -INFINITY;
+    auto factors = [&](uint32_t base) {
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxQueries / warps; ++k) {
+            const uint32_t m = wid + k * warps;
+            if (m >= Q) break;
+            uint32_t c0, c1;
+            range_of(m, &c0, &c1);
+            const uint32_t c = base + lane;
+            const bool in = c >= c0 && c <= c1;
+            float cm = -INFINITY, cl = 0.0f;
+            if (in) stat_of(c, m, &cm, &cl);
+            float incl = cm;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+                if (lane >= static_cast<uint32_t>(off)) incl = fmaxf(incl, v);
+            }
+            const float before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+            const float top = fmaxf(carry[k], lane ? before : -INFINITY);   // the running top before c
+            float fa = 1.0f, fb = 1.0f;
+            if (in) {
+                if (c == c0) { fa = 0.0f; fb = 1.0f; }
+                else if (top == cm) { fa = 1.0f; fb = 1.0f; }
+                else if (top > cm) { fa = 1.0f; fb = exp2_np(cm - top); }
+                else { fa = exp2_np(top - cm); fb = 1.0f; }
+            }
+            fac[(m * 32u + lane) * 2u] = fa;
+            fac[(m * 32u + lane) * 2u + 1u] = fb;
+            lfac[m * 32u + lane] = cl * fb;
+            carry[k] = fmaxf(carry[k], __shfl_sync(0xFFFFFFFFu, incl, 31));
+        }
+    };
+    // One output's chains over the block's chunks [c0, c1], its partials
+    // loaded 16 at a time before their fmas.
+    auto chain = [&](uint32_t base, uint32_t m, uint32_t e, uint32_t c0, uint32_t c1, float& o, float& l) {
+#pragma unroll 1
+        for (uint32_t c = c0; c <= c1; c += 16u) {
+            float co[16];
+#pragma unroll
+            for (uint32_t k = 0; k < 16u; ++k) co[k] = c + k <= c1 ? part_of(c + k, m, e) : 0.0f;
+#pragma unroll
+            for (uint32_t k = 0; k < 16u; ++k)
+                if (c + k <= c1) {
+                    const uint32_t f = m * 32u + (c + k - base);
+                    const float fa = fac[2u * f];
+                    o = fmaf(o, fa, co[k] * fac[2u * f + 1u]);
+                    l = fmaf(l, fa, lfac[f]);
+                }
+        }
+    };
+    if (hi - lo < 32u) {
+        // One block (up to 2,048 keys): its factors once, then the outputs
+        // in groups of the CTA's threads.
+        factors(lo);
+        __syncthreads();
+#pragma unroll 1
+        for (uint32_t i = threadIdx.x; i < Q * D; i += kAttnThreads) {
+            const uint32_t m = i / D, e = i % D;
+            uint32_t c0, c1;
+            range_of(m, &c0, &c1);
+            float o = 0.0f, l = 0.0f;
+            chain(lo, m, e, c0, c1, o, l);
+            write(m, e, o / l);
+        }
+        return;
+    }
+    // Longer: the outputs in groups of the CTA's threads, each group
+    // walking the blocks (their factors again for each group).
+    for (uint32_t i0 = 0; i0 < Q * D; i0 += kAttnThreads) {
+        if (i0) {
+            __syncthreads();   // the last group's reads of the factors are done
+#pragma unroll
+            for (uint32_t k = 0; k < kMaxQueries / warps; ++k) carry[k] = -INFINITY;
+        }
         const uint32_t i = i0 + threadIdx.x;
-        const uint32_t me = i / d, e = i % d;
+        const uint32_t m = i / D, e = i % D;
         uint32_t mc0 = 0, mc1 = 0;
-        if (i < Q * d) range_of(me, &mc0, &mc1);
+        if (i < Q * D) range_of(m, &mc0, &mc1);
         float o = 0.0f, l = 0.0f;
-        float carry[kMaxQueries / warps];   // the running top of each of this warp's queries
-#pragma unroll
-        for (uint32_t k = 0; k < kMaxQueries / warps; ++k) carry[k] = -INFINITY;
         for (uint32_t base = lo; base <= hi; base += 32u) {
-#pragma unroll
-            for (uint32_t k = 0; k < kMaxQueries / warps; ++k) {
-                const uint32_t m = wid + k * warps;
-                if (m >= Q) break;
-                uint32_t c0, c1;
-                range_of(m, &c0, &c1);
-                const uint32_t c = base + lane;
-                const bool in = c >= c0 && c <= c1;
-                float cm = -INFINITY, cl = 0.0f;
-                if (in) stat_of(c, m, &cm, &cl);
-                float incl = cm;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const float v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
-                    if (lane >= static_cast<uint32_t>(off)) incl = fmaxf(incl, v);
-                }
-                const float before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-                const float top = fmaxf(carry[k], lane ? before : -INFINITY);   // the running top before c
-                float fa = 1.0f, fb = 1.0f;
-                if (in) {
-                    if (c == c0) { fa = 0.0f; fb = 1.0f; }
-                    else if (top == cm) { fa = 1.0f; fb = 1.0f; }
-                    else if (top > cm) { fa = 1.0f; fb = exp2_np(cm - top); }
-                    else { fa = exp2_np(top - cm); fb = 1.0f; }
-                }
-                fac[(m * 32u + lane) * 2u] = fa;
-                fac[(m * 32u + lane) * 2u + 1u] = fb;
-                lfac[m * 32u + lane] = cl * fb;
-                carry[k] = fmaxf(carry[k], __shfl_sync(0xFFFFFFFFu, incl, 31));
-            }
+            factors(base);
             __syncthreads();
-            if (i < Q * d) {
-                const uint32_t n = mc1 + 1u > base ? min(32u, mc1 + 1u - base) : 0u;
-                const uint32_t j0 = mc0 > base ? mc0 - base : 0u;
-                for (uint32_t j = j0; j < n; j += 8u) {
-                    float co[8];
-#pragma unroll
-                    for (uint32_t k = 0; k < 8u; ++k) co[k] = j + k < n ? part_of(base + j + k, me, e) : 0.0f;
-#pragma unroll
-                    for (uint32_t k = 0; k < 8u; ++k)
-                        if (j + k < n) {
-                            const float fa = fac[(me * 32u + j + k) * 2u];
-                            o = fmaf(o, fa, co[k] * fac[(me * 32u + j + k) * 2u + 1u]);
-                            l = fmaf(l, fa, lfac[me * 32u + j + k]);
-                        }
-                }
-            }
+            if (i < Q * D && mc1 >= base && mc0 <= base + 31u)
+                chain(base, m, e, max(mc0, base), min(mc1, base + 31u), o, l);
             if (base + 32u <= hi) __syncthreads();   // before the next block's factors
         }
-        if (i < Q * d) write(me, e, o / l);
+        if (i < Q * D) write(m, e, o / l);
     }
 }
 
@@ -388,23 +417,29 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         // from zero in key order; then, a thread a query, l = fma(l, a,
         // sum) over the tiles with live keys, in order.
         {
+            // A warp takes 32/B (query, tile) pairs at once, B lanes each
+            // (one a key); the shuffles stay within a pair's lanes.
             const uint32_t pairs = Q * tiles;
-            for (uint32_t w = wid; w < pairs; w += kAttnThreads / 32u) {
-                const uint32_t m = w / tiles, t = w % tiles;
+            constexpr uint32_t kPairs = 32u / B;
+            const uint32_t seg = lane / B, sl = lane % B;
+            for (uint32_t w0 = wid * kPairs; w0 < pairs; w0 += (kAttnThreads / 32u) * kPairs) {
+                const uint32_t w = w0 + seg;
+                const uint32_t m = w < pairs ? w / tiles : 0u, t = w < pairs ? w % tiles : 0u;
                 const uint32_t p = p_first + (seqs ? 0u : m / G);
-                const uint32_t j = key0 + t * B + lane;
-                const bool live = lane < B && j <= p && j >= earliest_of(p, a.window);
-                float top = live ? ps[m * kChunk + t * B + lane] : -INFINITY;
+                const uint32_t j = key0 + t * B + sl;
+                const bool live = w < pairs && j <= p && j >= earliest_of(p, a.window);
+                float top = live ? ps[m * kChunk + t * B + sl] : -INFINITY;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
-                if (lane == 0) tops[m * 8u + t] = top;
+                for (uint32_t o = B / 2u; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o, B));
+                if (sl == 0 && w < pairs) tops[m * 8u + t] = top;
             }
             __syncthreads();
-            for (uint32_t w = wid; w < pairs; w += kAttnThreads / 32u) {
-                const uint32_t m = w / tiles, t = w % tiles;
+            for (uint32_t w0 = wid * kPairs; w0 < pairs; w0 += (kAttnThreads / 32u) * kPairs) {
+                const uint32_t w = w0 + seg;
+                const uint32_t m = w < pairs ? w / tiles : 0u, t = w < pairs ? w % tiles : 0u;
                 const uint32_t p = p_first + (seqs ? 0u : m / G);
-                const uint32_t j = key0 + t * B + lane;
-                const bool live = lane < B && j <= p && j >= earliest_of(p, a.window);
+                const uint32_t j = key0 + t * B + sl;
+                const bool live = w < pairs && j <= p && j >= earliest_of(p, a.window);
                 bool chunk_live = false;
                 float chunk_m = 0.0f, al = 1.0f;
 #pragma unroll
@@ -417,13 +452,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
                     chunk_m = top;
                     chunk_live = true;
                 }
-                const float e = live ? exp2_np(ps[m * kChunk + t * B + lane] - chunk_m) : 0.0f;
+                const float e = live ? exp2_np(ps[m * kChunk + t * B + sl] - chunk_m) : 0.0f;
                 __syncwarp();
-                if (lane < B) ps[m * kChunk + t * B + lane] = e;
+                if (w < pairs) ps[m * kChunk + t * B + sl] = e;
                 float sum = 0.0f;   // in key order
 #pragma unroll
-                for (uint32_t b = 0; b < B; ++b) sum = sum + __shfl_sync(0xFFFFFFFFu, e, b);
-                if (lane == 0) {
+                for (uint32_t b = 0; b < B; ++b) sum = sum + __shfl_sync(0xFFFFFFFFu, e, b, B);
+                if (sl == 0 && w < pairs) {
                     alpha[m * 8u + t] = al;
                     sums[m * 8u + t] = sum;
                 }
@@ -499,8 +534,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         if (cluster_rank() != 0u) return;
         // The chunks (slot = chunk − the tile's first live chunk) folded in
         // chunk order.
-        fold_chunks(
-            Q, d, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+        fold_chunks<D>(
+            Q, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
                 const uint32_t p = p_first + (seqs ? 0u : m / G);
                 *c0 = earliest_of(p, a.window) / kChunk;
                 *c1 = p / kChunk;
@@ -536,8 +571,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     auto at_of = [&](uint32_t c, uint32_t m) {
         return (static_cast<size_t>(c) * a.tokens + row0 + m / G) * a.query_heads + kvh * G + m % G;
     };
-    fold_chunks(
-        Q, d, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
+    fold_chunks<D>(
+        Q, ps, qs, [&](uint32_t m, uint32_t* c0, uint32_t* c1) {
             const uint32_t p = p_first + (seqs ? 0u : m / G);
             *c0 = earliest_of(p, a.window) / kChunk;
             *c1 = p / kChunk;
@@ -628,9 +663,16 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     const size_t base_smem = attention_smem(a.head_dim, kMaxQueries);
     if (base_smem > 200u * 1024u) return cudaErrorInvalidValue;
     // A one-token decode step may fold over a cluster, with room in rank 0
-    // for every chunk's partial. Batched sequences keep the global fold: the
-    // fold room would halve the CTAs an SM holds across their many row tiles.
-    const bool decode_shape = a.tokens == 1u;
+    // for every chunk's partial; so may batched sequences whose CTAs all fit
+    // one wave, on a layer whose window's chunks always fit the cluster (a
+    // step past that would fold globally inside a cluster launch, slower).
+    // Larger batches keep the global fold: the fold room would halve the
+    // CTAs an SM holds across their many row tiles.
+    const uint32_t slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
+    const int sms = sm_count();
+    const bool decode_shape =
+        a.tokens == 1u || (a.rows_are_sequences && sms > 0 && a.window / kChunk + 1u <= slots &&
+                           static_cast<uint64_t>(a.kv_heads) * slots * a.tokens <= static_cast<uint64_t>(sms));
     const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
     return a.head_dim == 64 ? launch_attention<64>(a, stream, pdl, base_smem, cluster_smem, decode_shape)
            : a.head_dim == 128 ? launch_attention<128>(a, stream, pdl, base_smem, cluster_smem, decode_shape)

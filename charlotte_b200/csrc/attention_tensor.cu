@@ -22,6 +22,7 @@
 
 #include <cstdint>
 
+#include "api_common.h"
 #include "kernels.h"
 #include "tma.cuh"
 
@@ -73,7 +74,7 @@ struct TensorAttention {
     static constexpr size_t kSmem = 2ull * 2 * kTile * 2;      // K and V, two stages
 };
 
-// Warps = G·WQ (8): warp w is head w % G of the kv head, positions
+// Warps = G·WQ: warp w is head w % G of the kv head, positions
 // 16·(w / G) .. +15 of the CTA's block of 16·WQ positions.
 template <uint32_t D>
 __global__ void __launch_bounds__(256) attention_tensor_kernel(const AttentionArgs a, uint32_t WQ) {
@@ -241,12 +242,18 @@ __global__ void __launch_bounds__(256) attention_tensor_kernel(const AttentionAr
 #pragma unroll
     for (uint32_t n = 0; n < D / 8; ++n) {
         const uint32_t d0 = n * 8u + 2u * c;
-        if (ra < a.tokens)
-            *reinterpret_cast<float2*>(a.out + (static_cast<size_t>(ra) * a.query_heads + head) * D + d0) =
-                make_float2(o[n][0] * ia, o[n][1] * ia);
-        if (rb < a.tokens)
-            *reinterpret_cast<float2*>(a.out + (static_cast<size_t>(rb) * a.query_heads + head) * D + d0) =
-                make_float2(o[n][2] * ib, o[n][3] * ib);
+        const size_t at_a = (static_cast<size_t>(ra) * a.query_heads + head) * D + d0;
+        const size_t at_b = (static_cast<size_t>(rb) * a.query_heads + head) * D + d0;
+        if (ra < a.tokens) {
+            *reinterpret_cast<float2*>(a.out + at_a) = make_float2(o[n][0] * ia, o[n][1] * ia);
+            if (a.out16) *reinterpret_cast<__half2*>(static_cast<__half*>(a.out16) + at_a) =
+                             __floats2half2_rn(o[n][0] * ia, o[n][1] * ia);
+        }
+        if (rb < a.tokens) {
+            *reinterpret_cast<float2*>(a.out + at_b) = make_float2(o[n][2] * ib, o[n][3] * ib);
+            if (a.out16) *reinterpret_cast<__half2*>(static_cast<__half*>(a.out16) + at_b) =
+                             __floats2half2_rn(o[n][2] * ib, o[n][3] * ib);
+        }
     }
 }
 
@@ -262,7 +269,13 @@ cudaError_t launch_tensor_attention(const AttentionArgs& a, cudaStream_t stream,
         configured = true;
     }
     const uint32_t G = a.query_heads / a.kv_heads;
-    const uint32_t WQ = G >= 8u ? 1u : 8u / G;   // warps a CTA: G·WQ = 8
+    // Warps a CTA: G·WQ, up to 8; fewer row blocks a CTA while the grid is
+    // under two CTAs an SM (the causal triangle makes the late blocks long:
+    // more, shorter CTAs balance it).
+    const int sms = sm_count();
+    const uint32_t want = 2u * (sms > 0 ? static_cast<uint32_t>(sms) : 148u);
+    uint32_t WQ = G >= 8u ? 1u : 8u / G;
+    while (WQ > 1u && a.kv_heads * ((a.tokens + 16u * WQ - 1u) / (16u * WQ)) < want) WQ /= 2u;
     const uint32_t block_rows = 16u * WQ;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.kv_heads, (a.tokens + block_rows - 1) / block_rows);

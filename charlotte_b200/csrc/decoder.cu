@@ -130,6 +130,11 @@ struct cb_decoder {
     float* hidden2 = nullptr;
     void* tensor_scratch = nullptr;
     uint64_t tensor_scratch_bytes = 0;
+    // f16 copies a tensor-form step's producers write for the next product
+    // (its x16): the norms' rows, the attention's output, gate|up's output.
+    void* normed16 = nullptr;
+    void* att16 = nullptr;
+    void* act16 = nullptr;
     void* split_scratch = nullptr;   // the split form's range sums (few-tile, wide-K products)
     uint64_t split_scratch_bytes = 0;
 };
@@ -206,9 +211,11 @@ cb_matmul description(const cb_decoder* d, std::initializer_list<const DevWeight
 
 // One matmul launch through the same path as cb_matmul_run; `dense`: the
 // product's densified weights for the tensor form (or NULL).
+// `x16`/`out16`: the dense form's f16 copy of x (written by the producer)
+// and of a gated output (for the next product), or NULL.
 int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t epilogue, const float* x,
             uint32_t x_stride, uint32_t tokens, float* const outs[3], const uint32_t strides[3],
-            const void* dense = nullptr) {
+            const void* dense = nullptr, const void* x16 = nullptr, void* out16 = nullptr) {
     cb_matmul m = description(d, ws, epilogue);
     uint32_t flags = CB_MATMUL_PDL;
     if (d->tensor_prefill && tokens >= kDecoderTensorTokens) {
@@ -216,6 +223,8 @@ int product(cb_decoder* d, std::initializer_list<const DevWeight*> ws, uint32_t 
         m.scratch = d->tensor_scratch;
         m.scratch_bytes = d->tensor_scratch_bytes;
         m.dense = dense;
+        m.x16 = dense ? x16 : nullptr;
+        m.out16 = dense ? out16 : nullptr;
     } else if (tokens > 1) {
         // range-sum scratch: cb_matmul_run takes the split form where it pays
         m.scratch = d->split_scratch;
@@ -288,6 +297,9 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
     // A one-token step of one sequence folds each norm into the product after
     // it; the residual stream then alternates between two buffers.
     const bool fold = tokens == 1 && !batch;
+    // A step whose products take the tensor form: its producers also write
+    // f16 copies of the products' inputs.
+    const bool tensor_step = d->tensor_prefill && tokens >= kDecoderTensorTokens;
     float* stream_buf[2] = {d->hidden, d->hidden2};
     uint32_t cur = 0;
     for (uint32_t l = 0; l < m.layers; ++l) {
@@ -302,11 +314,12 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         } else {
             cb_norm n{d->hidden, d->out, L.attn_norm, pending_post, d->normed, H, tokens, pending_add ? 1u : 0u, 0u,
                       m.epsilon};
+            n.normed16 = tensor_step ? d->normed16 : nullptr;
             if (int rc = launched(norm_run(n, d->stream, true), "step: attention norm")) return rc;
             float* outs[3] = {d->q, d->k, d->v};
             const uint32_t strides[3] = {qd, kvd, kvd};
             if (int rc = product(d, {&L.q, &L.k, &L.v}, CB_EPILOGUE_QKV, d->normed, H, tokens, outs, strides,
-                                 L.dense_qkv))
+                                 L.dense_qkv, n.normed16))
                 return rc;
         }
         cb_rope r{};
@@ -355,14 +368,16 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
         at.window = L.window;
         at.max_chunks = d->max_chunks;
         at.scale_log2e = static_cast<float>(static_cast<double>(m.attention_scale) * 1.4426950408889634);
-        const bool tensor_attention = d->tensor_prefill && tokens >= kDecoderTensorTokens && attention_tensor_fits(at);
+        const bool tensor_attention = tensor_step && attention_tensor_fits(at);
+        if (tensor_attention) at.out16 = d->att16;
         if (int rc = launched(tensor_attention ? attention_tensor_run(at, d->stream, true) : attention_run(at, d->stream, true),
                               "step: attention"))
             return rc;
         {
             float* outs[3] = {d->out, nullptr, nullptr};
             const uint32_t strides[3] = {H, 0, 0};
-            if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides, L.dense_o))
+            if (int rc = product(d, {&L.o}, CB_EPILOGUE_WRITE, d->att, qd, tokens, outs, strides, L.dense_o,
+                                 at.out16))
                 return rc;
         }
         if (fold) {
@@ -373,18 +388,19 @@ int enqueue_step(cb_decoder* d, uint32_t tokens, bool fed, bool logits, const cb
             cur ^= 1u;
         } else {
             cb_norm n2{d->hidden, d->out, L.ffn_norm, L.post_attn_norm, d->normed, H, tokens, 1u, 0u, m.epsilon};
+            n2.normed16 = tensor_step ? d->normed16 : nullptr;
             if (int rc = launched(norm_run(n2, d->stream, true), "step: feed-forward norm")) return rc;
             float* outs[3] = {d->act, nullptr, nullptr};
             const uint32_t strides[3] = {m.ffn, 0, 0};
             if (int rc = product(d, {&L.gate, &L.up}, CB_EPILOGUE_GATED, d->normed, H, tokens, outs, strides,
-                                 L.dense_gate_up))
+                                 L.dense_gate_up, n2.normed16, tensor_step ? d->act16 : nullptr))
                 return rc;
         }
         {
             float* outs[3] = {d->out, nullptr, nullptr};
             const uint32_t strides[3] = {H, 0, 0};
             if (int rc = product(d, {&L.down}, CB_EPILOGUE_WRITE, d->act, m.ffn, tokens, outs, strides,
-                                 L.dense_down))
+                                 L.dense_down, tensor_step && !fold ? d->act16 : nullptr))
                 return rc;
         }
         pending_add = true;
@@ -615,6 +631,13 @@ int cb_decoder_create_batch(const cb_model* m, uint32_t max_step_tokens, uint32_
         if (int rc = dalloc(d, &p, d->tensor_scratch_bytes)) return bail(rc);
         d->tensor_scratch = p;
         d->tensor_prefill = true;
+        uint16_t* h16 = nullptr;
+        if (int rc = dalloc(d, &h16, static_cast<size_t>(T) * H)) return bail(rc);
+        d->normed16 = h16;
+        if (int rc = dalloc(d, &h16, static_cast<size_t>(T) * qd)) return bail(rc);
+        d->att16 = h16;
+        if (int rc = dalloc(d, &h16, static_cast<size_t>(T) * m->ffn)) return bail(rc);
+        d->act16 = h16;
         // Every layer product's weights densified once.
         for (DevLayer& L : d->layers) {
             struct Want {

@@ -42,6 +42,8 @@ struct MatmulArgs {
     void* scratch;          // tensor form: x rounded to f16, [tokens][columns]
     uint64_t scratch_bytes; // tensor form: the dense form's split-K partials follow x16 when they fit
     const void* dense;      // tensor form: the weights as f16 in the dense layout (matmul_densify)
+    const void* x16;        // dense form: x already f16 ([tokens][columns]), else rounded into scratch
+    void* out16;            // dense form, gated: each output also f16 at [t·out_stride[0] + o]
     // Split form (matmul_split): range r's sum of product row p for token t
     // at range_sums[(r·tokens + t)·total_rows + p] (matmul.wgsl range_sum_at).
     float* range_sums;

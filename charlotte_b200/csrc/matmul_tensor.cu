@@ -494,7 +494,10 @@ __device__ __forceinline__ void put_slot(const MatmulArgs& a, uint32_t t, uint32
 }
 
 __device__ __forceinline__ void put_gated(const MatmulArgs& a, uint32_t t, uint32_t o, float g, float u) {
-    a.out[0][static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o] = activate(a.activation, g) * u;
+    const size_t at = static_cast<size_t>(t) * a.out_stride[0] + a.member[0].out_offset + o;
+    const float v = activate(a.activation, g) * u;
+    a.out[0][at] = v;
+    if (a.out16) static_cast<__half*>(a.out16)[at] = __float2half_rn(v);
 }
 
 template <uint32_t BN>
@@ -877,9 +880,14 @@ __global__ void __launch_bounds__(Persist::kThreads, 1)
                     __syncwarp();
                     const uint32_t o = n0 / 2u + 64u * part + 32u * h + lane;
                     if (o < a.member[0].rows) {
-                        float* dst = a.out[0] + static_cast<size_t>(t0) * a.out_stride[0] + a.member[0].out_offset + o;
-                        for (uint32_t r = 0; r < 32u && t0 + r < a.tokens; ++r)
-                            dst[static_cast<size_t>(r) * a.out_stride[0]] = stg[r * 33u + lane];
+                        const size_t at = static_cast<size_t>(t0) * a.out_stride[0] + a.member[0].out_offset + o;
+                        float* dst = a.out[0] + at;
+                        __half* dst16 = a.out16 ? static_cast<__half*>(a.out16) + at : nullptr;
+                        for (uint32_t r = 0; r < 32u && t0 + r < a.tokens; ++r) {
+                            const float v = stg[r * 33u + lane];
+                            dst[static_cast<size_t>(r) * a.out_stride[0]] = v;
+                            if (dst16) dst16[static_cast<size_t>(r) * a.out_stride[0]] = __float2half_rn(v);
+                        }
                     }
                     __syncwarp();
                 }
@@ -1024,35 +1032,43 @@ cudaError_t matmul_dense(const MatmulArgs& a, int sms, cudaStream_t stream, bool
     const uint32_t sm = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
     auto ceil_div = [](uint32_t n, uint32_t d) { return (n + d - 1u) / d; };
     // A wave or more of 128 × 256 tiles: the persistent form, a CTA an SM.
+    // x as f16: given (a producer's copy), or rounded into the scratch
+    const void* x16 = a.x16 ? a.x16 : a.scratch;
     const uint32_t wide_tiles = ceil_div(a.tokens, 128) * ceil_div(slots, 256);
     if (wide_tiles >= sm) {
-        if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
+        if (!a.x16)
+            if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
         CUtensorMap xmap, wmap;
-        if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
+        if (cudaError_t e = encode_f16_map(&xmap, x16, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
         if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, Persist::kBN); e != cudaSuccess) return e;
         return launch_persistent(a, xmap, wmap, sm, stream, pdl);
     }
     // Fewer: 128 × 128 tiles, one a CTA, K split when they leave SMs idle.
     constexpr uint32_t bn = 128;
     const uint32_t tiles = ceil_div(a.tokens, 128) * ceil_div(slots, bn);
-    // Split K only when the tiles leave most SMs idle: as many splits as
-    // still fit one wave, each at least 8 K blocks, their partials where the
-    // scratch has room after x16 (a second launch adds them in order).
+    // Split K where it shortens the product: the waves of CTAs a split
+    // costs, over the splits, plus a sixth of an unsplit wave for writing
+    // and adding the partials (a second launch adds them in order); each
+    // split at least 8 K blocks, their partials where the scratch has room
+    // after x16.
     const uint32_t kblocks = ceil_div(a.columns, kBK);
-    const uint64_t x16 = matmul_tensor_scratch_bytes(a.tokens, a.columns);
+    const uint64_t x16_bytes = matmul_tensor_scratch_bytes(a.tokens, a.columns);
     uint32_t splits = 1;
-    if (tiles * 2u <= sm) {
-        splits = sm / tiles;
-        if (splits > 8u) splits = 8u;
-        while (splits > 1u && (kblocks / splits < 8u ||
-                               x16 + static_cast<uint64_t>(splits) * a.tokens * slots * 4u > a.scratch_bytes))
-            --splits;
+    double best = static_cast<double>(ceil_div(tiles, sm));
+    for (uint32_t z = 2; z <= 8u && kblocks / z >= 8u; ++z) {
+        if (x16_bytes + static_cast<uint64_t>(z) * a.tokens * slots * 4u > a.scratch_bytes) break;
+        const double cost = static_cast<double>(ceil_div(tiles * z, sm)) / z + 1.0 / 6.0;
+        if (cost < best - 1e-9) {
+            best = cost;
+            splits = z;
+        }
     }
-    float* partials = splits > 1u ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.scratch) + x16) : nullptr;
+    float* partials = splits > 1u ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.scratch) + x16_bytes) : nullptr;
 
-    if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
+    if (!a.x16)
+        if (cudaError_t e = launch_to_f16(a, stream, pdl); e != cudaSuccess) return e;
     CUtensorMap xmap, wmap;
-    if (cudaError_t e = encode_f16_map(&xmap, a.scratch, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
+    if (cudaError_t e = encode_f16_map(&xmap, x16, a.columns, a.tokens, kBM); e != cudaSuccess) return e;
     if (cudaError_t e = encode_f16_map(&wmap, a.dense, a.columns, slots, bn); e != cudaSuccess) return e;
     cudaError_t e = launch_dense<bn>(a, xmap, wmap, splits, partials, stream, pdl);
     if (e != cudaSuccess || splits == 1u) return e;

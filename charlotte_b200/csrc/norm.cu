@@ -16,6 +16,7 @@
 // row (the final norm); `rows_per_token` rows a token are each their own
 // row (the per-layer inputs); without a gain, normed = x·r (unit_gain).
 // Rows ≤ 4096 wide, a multiple of 4.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -120,11 +121,18 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(NormArgs a) {
     for (int k = 0; k < kMaxVec4; ++k) {
         const uint32_t i = threadIdx.x + k * kNormThreads;
         if (i < vec4s) {
+            float4 v;
             if (gain) {
                 const float4 g = gain[i];
-                normed[i] = make_float4((x[k].x * r) * g.x, (x[k].y * r) * g.y, (x[k].z * r) * g.z, (x[k].w * r) * g.w);
+                v = make_float4((x[k].x * r) * g.x, (x[k].y * r) * g.y, (x[k].z * r) * g.z, (x[k].w * r) * g.w);
             } else {
-                normed[i] = make_float4(x[k].x * r, x[k].y * r, x[k].z * r, x[k].w * r);
+                v = make_float4(x[k].x * r, x[k].y * r, x[k].z * r, x[k].w * r);
+            }
+            normed[i] = v;
+            if (a.normed16) {
+                __half2* h = reinterpret_cast<__half2*>(a.normed16) + 2u * (base + i);
+                h[0] = __floats2half2_rn(v.x, v.y);
+                h[1] = __floats2half2_rn(v.z, v.w);
             }
         }
     }

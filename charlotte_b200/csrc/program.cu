@@ -423,9 +423,9 @@ int build_one(cb_program* p, const cb_launch* launches, uint32_t count, uint32_t
             if (!is(entry, "main")) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope entry %s", i, entry);
             if (l.binding_count < 6) return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope bindings", i);
             const uint32_t d = static_cast<uint32_t>(override_or(l, "head_dimension", 0.0));
-            if (override_or(l, "axial", 0.0) != 0.0 || (d != 64 && d != 128 && d != 256))
+            if (override_or(l, "axial", 0.0) != 0.0 || (d != 64 && d != 128 && d != 256 && d != 512))
                 return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope's encode form %s has no CUDA form", i,
-                            d == 512 ? "at head dimension 512" : "in the axial pairing");
+                            override_or(l, "axial", 0.0) != 0.0 ? "in the axial pairing" : "at this head dimension");
             if (l.constants_bytes < 16 + 4 * (d / 2))
                 return fail(CB_ERROR_BUILD, "cb_program_build: launch %u: rope constants", i);
             void* ptr[6];

@@ -64,7 +64,25 @@ __global__ void rope_kernel(RopeArgs a) {
         // reduce runs on every lane where either needs it (uniform).
         const bool qk = a.query_gain != nullptr, vn = a.value_norm != 0;
         float r = 1.0f;
-        if (qk || vn) r = head_norm_factor(x0, x1, lanes, d, a.epsilon);
+        if ((qk || vn) && lanes <= 32u) {
+            r = head_norm_factor(x0, x1, lanes, d, a.epsilon);
+        } else if (qk || vn) {
+            // Heads of 512: 64 lanes over two warps. reduce_head's first
+            // level (stride 32) through shared memory, the rest within the
+            // head's first warp, the total back through shared memory.
+            float* red = angles + d;                 // a float a thread
+            float* total = red + blockDim.x;         // a float a head
+            float v = dot4(x0, x0) + dot4(x1, x1);
+            red[threadIdx.x] = v;
+            __syncthreads();
+            if (lane < 32u) {
+                v = v + red[threadIdx.x + 32u];
+                for (uint32_t stride = 16u; stride > 0; stride >>= 1) v = v + __shfl_down_sync(0xFFFFFFFFu, v, stride);
+                if (lane == 0) total[head] = v;
+            }
+            __syncthreads();
+            r = 1.0f / sqrtf(total[head] / static_cast<float>(d) + a.epsilon);
+        }
         if (!is_value) {
             if (qk) {   // (x·r)·g, then the turn: the decoder form's steps
                 const float4* g = reinterpret_cast<const float4*>(is_query ? a.query_gain : a.key_gain);
@@ -108,7 +126,9 @@ cudaError_t rope_run(const RopeArgs& a, cudaStream_t stream, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.tokens);
     cfg.blockDim = dim3((threads + 31u) / 32u * 32u);
-    cfg.dynamicSmemBytes = a.head_dim * sizeof(float);
+    // the angles; heads of 512 (encode form) also a reduce float a thread and a total a head
+    cfg.dynamicSmemBytes = (a.head_dim + (a.head_dim > 256u ? threads + a.query_heads + 2u * a.kv_heads : 0u)) *
+                           sizeof(float);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

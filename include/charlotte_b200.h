@@ -138,6 +138,12 @@ typedef struct cb_matmul {
                                       same members and epilogue (16-byte aligned): the
                                       dense form, both operands fed to the tensor cores
                                       by TMA; the pieces are then not read               */
+    const void* x16;               /* with `dense`: NULL, or x already rounded to f16,
+                                      [tokens][columns] (16-byte aligned) — read in place
+                                      of rounding x (a norm's or a product's f16 copy)   */
+    void* out16;                   /* with `dense`, GATED epilogue: NULL, or where each
+                                      output is also written rounded to f16,
+                                      [tokens][out_stride[0]] (the next product's x16)   */
 } cb_matmul;
 
 /* y[t][o] = Σ_k W[o][k]·x[t][k] for tokens t in [0, tokens), each output
@@ -191,6 +197,9 @@ typedef struct cb_norm {
     const float* scale;
     uint32_t add_only;
     uint32_t rows_per_token;
+    /* NULL, or where normed is also written rounded to f16 (nearest even),
+     * [rows][width]: a tensor-form product's x16. */
+    void* normed16;
 } cb_norm;
 CB_API int cb_norm_run(const cb_norm* n, uint32_t flags, void* stream);
 
@@ -231,7 +240,8 @@ typedef struct cb_rope {
     /* rope's encode form (rope_encode.wgsl, an encoder's): every head
      * written back in place, f32 — keys QK-normed and turned like queries —
      * and no cache (key_cache, value_cache, slots unused); with value_norm,
-     * each value head also scaled by 1/sqrt(mean square + epsilon). */
+     * each value head also scaled by 1/sqrt(mean square + epsilon). This
+     * form also takes heads of 512 (EmbeddingGemma 2's global layers). */
     uint32_t encode;
     uint32_t value_norm;
 } cb_rope;
@@ -281,6 +291,9 @@ typedef struct cb_attention {
      * caches, and stages both itself. Its fields must describe the same
      * rows, heads, caches and position as this struct's. */
     const cb_rope* rope;
+    /* CB_RUN_TENSOR's form: NULL, or where out is also written rounded to
+     * f16, [tokens][query_heads·head_dim] (the output product's x16). */
+    void* out16;
 } cb_attention;
 CB_API int cb_attention_run(const cb_attention* a, uint32_t flags, void* stream);
 /* Ticket words cb_attention needs for `tokens` rows. */

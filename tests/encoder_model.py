@@ -36,7 +36,8 @@ class EncoderArch:
     hidden: int = 256          # W
     query_heads: int = 4
     kv_heads: int = 1
-    head_dim: int = 256
+    head_dim: int = 256        # the sliding layers' heads
+    global_head_dim: int = 512  # the global layers' (EmbeddingGemma 2's)
     ffn: int = 512
     vocab: int = 300
     per_layer: int = 64        # P
@@ -61,6 +62,10 @@ class W:
         return self.rows * self.cols // synth.BLOCK_WEIGHTS[self.format]
 
 
+def head_dim_of(a: EncoderArch, layer: int) -> int:
+    return a.head_dim if a.sliding[layer] else a.global_head_dim
+
+
 def synthesize(arch: EncoderArch, seed: int = 0) -> dict:
     rng = np.random.default_rng(seed)
     a = arch
@@ -74,11 +79,12 @@ def synthesize(arch: EncoderArch, seed: int = 0) -> dict:
     m = {"arch": a, "token_embd": w(Q8_0, a.vocab, a.hidden), "output_norm": gain(a.hidden),
          "output": w(Q4_0, a.embedding, a.hidden), "per_layer_proj": w(Q4_0, a.layers * a.per_layer, a.hidden),
          "per_layer_norm": gain(a.per_layer), "layers": []}
-    qd, kvd = a.query_heads * a.head_dim, a.kv_heads * a.head_dim
-    for _ in range(a.layers):
+    for l in range(a.layers):
+        d = head_dim_of(a, l)
+        qd, kvd = a.query_heads * d, a.kv_heads * d
         m["layers"].append({
             "attn_norm": gain(a.hidden), "q": w(Q4_0, qd, a.hidden), "k": w(Q4_0, kvd, a.hidden),
-            "v": w(Q4_0, kvd, a.hidden), "q_norm": gain(a.head_dim), "k_norm": gain(a.head_dim),
+            "v": w(Q4_0, kvd, a.hidden), "q_norm": gain(d), "k_norm": gain(d),
             "o": w(Q4_0, a.hidden, qd), "post_attn_norm": gain(a.hidden), "ffn_norm": gain(a.hidden),
             "gate": w(Q4_0, a.ffn, a.hidden), "up": w(Q4_0, a.ffn, a.hidden), "down": w(Q4_0, a.hidden, a.ffn),
             "post_ffn_norm": gain(a.hidden), "inp_gate": w(Q4_0, a.per_layer, a.hidden),
@@ -98,7 +104,7 @@ def write_gguf(m: dict, path: str) -> None:
           _u32(k("block_count"), a.layers), _u32(k("context_length"), a.context),
           _u32(k("embedding_length"), a.hidden), _u32(k("feed_forward_length"), a.ffn),
           _u32(k("attention.head_count"), a.query_heads), _u32(k("attention.head_count_kv"), a.kv_heads),
-          _u32(k("attention.key_length"), a.head_dim), _u32(k("attention.value_length"), a.head_dim),
+          _u32(k("attention.key_length"), a.global_head_dim), _u32(k("attention.value_length"), a.global_head_dim),
           _f32(k("attention.layer_norm_rms_epsilon"), a.epsilon), _f32(k("rope.freq_base"), a.rope_base),
           _kv(k("attention.causal"), BOOL, b"\x00"), _u32(k("pooling_type"), 1),
           _u32(k("attention.sliding_window"), a.window), _bools(k("attention.sliding_window_pattern"), a.sliding),
@@ -194,8 +200,8 @@ def oracle_embedding(m: dict, ids) -> np.ndarray:
             if normalize:
                 normed[t] = n
 
-    d = a.head_dim
     for l, L in enumerate(m["layers"]):
+        d = head_dim_of(a, l)
         # attention
         norm(L["attn_norm"])
         q, k, v = _mm(L["q"], normed), _mm(L["k"], normed), _mm(L["v"], normed)

@@ -111,6 +111,7 @@ def test_norm_unit_gain(cuda):
 ROPE = [
     # d, Hq, Hkv, halves, qk_norm, value_norm
     (256, 4, 1, True, True, True),     # EmbeddingGemma 2's sliding layers
+    (512, 4, 1, True, True, True),     # its global layers: a head's 64 lanes over two warps
     (256, 4, 1, True, True, False),
     (128, 16, 8, True, False, True),
     (64, 32, 8, False, True, True),

@@ -8,6 +8,8 @@ decoded exactly first (the same decode the exact forms use), then rounded to
 f16 with x. Cases cover each format, each epilogue, ragged token and row
 tails (partial 128-token and 128-slot tiles), a K that ends in half a
 64-wide block, and a step long enough to cycle the 4-stage ring many times."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -208,3 +210,34 @@ def test_tensor_gated_by_input(cuda, form):
         gate_input_token=2, form=form)
     t = exact(O.Q4_0, stored, rows, K, x)
     within(y.cpu().numpy(), t / (1.0 + np.exp(-t)) * u[2:2 + T, 100:100 + rows])
+
+
+def test_dense_reads_x16_and_writes_out16(cuda):
+    """A producer's f16 copy of x (cb_matmul.x16) gives the bits of x rounded
+    by the product itself; a gated product's out16 is its output rounded to
+    f16 (the next product's x16)."""
+    rng = np.random.default_rng(53)
+    F, K, T = 2048, 1024, 300
+    gs, gp, gnb = weight(rng, O.Q4_0, F, K)
+    us, up, unb = weight(rng, O.Q4_0, F, K)
+    x = synth.activations(rng, T, K)
+    members = [(dev(gp), gnb, 0, F, 0), (dev(up), unb, 0, F, 0)]
+    dense = cb.densify(O.Q4_0, K, members, epilogue=cb.GATED)
+    n = cb.lib().cb_matmul_scratch_bytes(cb.MATMUL_TENSOR, T, K) + 8 * T * 2 * F * 4
+    scratch = torch.empty(n, dtype=torch.uint8, device="cuda")
+    y0 = torch.zeros((T, F), dtype=torch.float32, device="cuda")
+    cb.matmul(O.Q4_0, K, members, dev(x), [y0], epilogue=cb.GATED, flags=cb.MATMUL_TENSOR, scratch=scratch,
+              dense=dense)
+    x16 = dev(x).half()
+    y1 = torch.zeros_like(y0)
+    o16 = torch.zeros((T, F), dtype=torch.float16, device="cuda")
+    m = cb._product(O.Q4_0, K, members, cb.GATED, cb.SILU)
+    m.scratch, m.scratch_bytes, m.dense = scratch.data_ptr(), n, dense.data_ptr()
+    m.x16, m.out16 = x16.data_ptr(), o16.data_ptr()
+    outs = (ctypes.c_void_p * 3)(y1.data_ptr(), None, None)
+    strides = (ctypes.c_uint32 * 3)(F, 0, 0)
+    cb.check(cb.lib().cb_matmul_run(ctypes.byref(m), dev(x).data_ptr(), K, T, ctypes.byref(outs),
+                                    ctypes.byref(strides), cb.MATMUL_TENSOR, None))
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    assert torch.equal(o16, y1.half())
