@@ -1013,6 +1013,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip configs[0], the M=16/128 sweep and configs[3]")
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--batch-prompt", type=int, default=1024)
+    ap.add_argument("--batch-sequences", type=int, default=64,
+                    help="--case gemma: sequences in all (8 on one GPU is one rank's share at N = 8)")
     ap.add_argument("--case", default=None, help="profile one product (format:rows:K) or 'decode'")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--profile-region", action="store_true",
@@ -1027,8 +1029,9 @@ def main():
             print(json.dumps(sweep_bench(flags=f, ms=ms, formats=(2,), head=False)))
     elif args.case == "gemma":
         rank, world, local = dist_setup(args.gpus)
-        r = gemma_batch_bench(args.batch_steps, world, rank, prompt_len=args.batch_prompt,
-                              cpu=not args.profile_region, profile=args.profile_region)
+        r = gemma_batch_bench(args.batch_steps, world, rank, sequences=args.batch_sequences,
+                              prompt_len=args.batch_prompt, cpu=not args.profile_region,
+                              profile=args.profile_region)
         if rank == 0:
             print(json.dumps(r))
         if world > 1:

@@ -171,6 +171,27 @@ __device__ __forceinline__ void chain_group2(const F& A, const F& B, const float
     (chain_step2<F, ks>(A, B, c, x2, acc), ...);
 }
 
+// P pairs of rows at once: step k reads x once (doubled) and advances each
+// pair's chain by one paired decode and one paired fma — each row's
+// operations and their order those of chain_step2.
+template <typename F, int P, int k>
+__device__ __forceinline__ void chain_step_rows(const F (&A)[P], const F (&B)[P], const typename F::Consts2 (&c)[P],
+                                                const float4* x2, float2 (&acc)[P]) {
+    const float4 xq = x2[k / 2];
+    const float2 xk = (k % 2 == 0) ? make_float2(xq.x, xq.y) : make_float2(xq.z, xq.w);
+#pragma unroll
+    for (int p = 0; p < P; ++p) acc[p] = __ffma2_rn(F::template weight2<k>(A[p], B[p], c[p]), xk, acc[p]);
+}
+
+template <typename F, int P, int... ks>
+__device__ __forceinline__ void chain_group_rows(const F (&A)[P], const F (&B)[P], const float4* x2, float2 (&acc)[P],
+                                                 std::integer_sequence<int, ks...>) {
+    typename F::Consts2 c[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) c[p] = F::consts2(A[p], B[p]);
+    (chain_step_rows<F, P, ks>(A, B, c, x2, acc), ...);
+}
+
 // One row's chain reading x doubled (x2).
 template <typename F, int k>
 __device__ __forceinline__ void chain_step1d(const F& A, const typename F::Consts& ca, const float4* x2, float& acc) {

@@ -41,6 +41,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 #include <utility>
 
 #include "formats.cuh"
@@ -194,6 +195,13 @@ __device__ __forceinline__ void norm_row128(const MatmulArgs& a, float* xs, uint
         }
 }
 
+// Whether a batch's row pairs run their chains together (chain_group_rows):
+// batches of 4 or more rows of the formats whose decoded state stays in
+// registers for every pair at once (Q4_1 and BF16 would spill).
+template <typename F, int R>
+constexpr bool kRowsTogether = R >= 4 && (std::is_same<F, Q4_0>::value || std::is_same<F, Q8_0>::value ||
+                                          std::is_same<F, Q6_K>::value);
+
 template <typename F, int R, int W>
 __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -304,6 +312,36 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
                 chain_group1d<F>(A, xl + (g - lo) * 16u, acc, std::make_integer_sequence<int, 32>{});
             }
             red[lane] = acc;
+        } else if (kRowsTogether<F, R> && R * W <= 64 && !gated) {   // (R = 8 at 16 warps would spill)
+            // Every pair's chain advanced together, k outermost: one read of x
+            // (doubled) serves all R/2 pairs, and the pairs' fmas are
+            // independent, so a warp has R/2 accumulations in flight at
+            // every step. Slots past the live rows read stale stage bytes;
+            // their sums are never written.
+            float2 acc[R / 2];
+#pragma unroll
+            for (int p = 0; p < R / 2; ++p) acc[p] = make_float2(0.0f, 0.0f);
+            for (uint32_t g = lo; g < hi; ++g) {
+                F A[R / 2], B[R / 2];
+#pragma unroll
+                for (int p = 0; p < R / 2; ++p) {
+                    const uint8_t* pa[F::kStreams];
+                    const uint8_t* pb[F::kStreams];
+#pragma unroll
+                    for (int q = 0; q < F::kStreams; ++q) {
+                        pa[q] = seg[0][q] + (2u * p) * rb[q];
+                        pb[q] = pa[q] + rb[q];
+                    }
+                    A[p].load(pa, g);
+                    B[p].load(pb, g);
+                }
+                chain_group_rows<F, R / 2>(A, B, xl + (g - lo) * 16u, acc, std::make_integer_sequence<int, 32>{});
+            }
+#pragma unroll
+            for (int p = 0; p < R / 2; ++p) {
+                red[(2 * p) * kRedStride + lane] = acc[p].x;
+                red[(2 * p + 1) * kRedStride + lane] = acc[p].y;
+            }
         } else {
         // Pairs of slots: non-gated rows (2p, 2p+1) of the segment. Gated:
         // with R = 2 the pair is the output's gate row and up row; otherwise
@@ -376,41 +414,56 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const MatmulArgs a) {
 }
 
 // ---- several tokens a weight pass ------------------------------------------
-// The same warp layout with R = 2 (a pair of rows, or a gated output's gate
-// and up rows) and MT tokens: each weight is decoded once and multiplied
+// The same warp layout with R = 2 or 4 rows a batch (a pair of rows, or a
+// gated output's gate and up rows; or two pairs: four rows, or two outputs'
+// gate rows then their up rows) and MT tokens: each weight is decoded once and multiplied
 // into MT chains, one per token, each still the reference's chain for that
 // (row, token). Tokens go in pairs through the paired FMA (fma.rn.f32x2,
 // each half one fma, so each chain keeps its bits): one paired fma advances
 // tokens 2p and 2p + 1 of a row, with the row's weight as both halves of one
 // operand. x is staged range-major by token pair, the pair's two floats of
-// each k side by side. The 2·MT range-sum rows meet in shared memory, and
-// lane slot·MT + i adds row `slot`'s range sums for token i in range order.
-template <typename F, int MT, int k>
-__device__ __forceinline__ void chain_step_mt(const F& A, const F& B, const typename F::Consts2& c,
-                                              const float4* x2, uint32_t pair4, float2 (&pa)[MT / 2],
-                                              float2 (&pb)[MT / 2]) {
-    const float2 w = F::template weight2<k>(A, B, c);
-    const float2 wa = make_float2(w.x, w.x), wb = make_float2(w.y, w.y);
+// each k side by side; with two pairs each read of x serves both, halving the
+// shared-memory traffic a fma. The R·MT range-sum rows meet in shared
+// memory, and lane slot·MT + i adds row `slot`'s range sums for token i in
+// range order.
+template <typename F, int MT, int RP, int k>
+__device__ __forceinline__ void chain_step_mt(const F (&A)[RP], const F (&B)[RP], const typename F::Consts2 (&c)[RP],
+                                              const float4* x2, uint32_t pair4, float2 (&pa)[RP][MT / 2],
+                                              float2 (&pb)[RP][MT / 2]) {
+    float2 wa[RP], wb[RP];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+        const float2 w = F::template weight2<k>(A[r], B[r], c[r]);
+        wa[r] = make_float2(w.x, w.x);
+        wb[r] = make_float2(w.y, w.y);
+    }
 #pragma unroll
     for (int p = 0; p < MT / 2; ++p) {
         const float4 xq = x2[p * pair4 + k / 2];
         const float2 xk = (k % 2 == 0) ? make_float2(xq.x, xq.y) : make_float2(xq.z, xq.w);
-        pa[p] = __ffma2_rn(wa, xk, pa[p]);
-        pb[p] = __ffma2_rn(wb, xk, pb[p]);
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+            pa[r][p] = __ffma2_rn(wa[r], xk, pa[r][p]);
+            pb[r][p] = __ffma2_rn(wb[r], xk, pb[r][p]);
+        }
     }
 }
 
-template <typename F, int MT, int... ks>
-__device__ __forceinline__ void chain_group_mt(const F& A, const F& B, const float4* x2, uint32_t pair4,
-                                               float2 (&pa)[MT / 2], float2 (&pb)[MT / 2],
+template <typename F, int MT, int RP, int... ks>
+__device__ __forceinline__ void chain_group_mt(const F (&A)[RP], const F (&B)[RP], const float4* x2, uint32_t pair4,
+                                               float2 (&pa)[RP][MT / 2], float2 (&pb)[RP][MT / 2],
                                                std::integer_sequence<int, ks...>) {
-    const typename F::Consts2 c = F::consts2(A, B);
-    (chain_step_mt<F, MT, ks>(A, B, c, x2, pair4, pa, pb), ...);
+    typename F::Consts2 c[RP];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) c[r] = F::consts2(A[r], B[r]);
+    (chain_step_mt<F, MT, RP, ks>(A, B, c, x2, pair4, pa, pb), ...);
 }
 
-template <typename F, int MT, int W>
+template <typename F, int MT, int W, int R>
 __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
-    constexpr int R = 2;
+    static_assert(R == 2 || R == 4, "one or two pairs of rows a batch");
+    static_assert(R * MT <= 32, "a batch's totals take one lane each");
+    constexpr int RP = R / 2;
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t G = a.columns / 32u;
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
@@ -487,47 +540,74 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
             return;
         }
         const Batch bt = locate_batch<R>(a, b);
-        // Stream pointers of the batch's two rows: non-gated rows 0 and 1 of
-        // one segment; gated the gate row at slot 0 and the up row at slot 1.
-        const uint8_t* pa[F::kStreams];
-        const uint8_t* pb[F::kStreams];
+        // Stream pointers of the batch's slots: non-gated, rows 0..R-1 of one
+        // segment; gated, R = 2: the gate row at slot 0 and the up row at
+        // slot 1; R = 4: the gate rows at slots 0 and 1, the up rows at 2 and 3.
+        // Pair r is slots (2r, 2r + 1).
+        const uint8_t* pa[RP][F::kStreams];
+        const uint8_t* pb[RP][F::kStreams];
         {
             const MemberArgs& m0 = gated ? a.member[0] : a.member[bt.member];
+            const MemberArgs& m1 = a.member[gated ? 1 : bt.member];
 #pragma unroll
             for (int q = 0; q < F::kStreams; ++q) {
-                const uint64_t off = RowStreams<F>::base(q, m0.blocks) +
-                                     static_cast<uint64_t>(m0.first_row + bt.local) * rb[q];
-                pa[q] = stage + reg[q] + static_cast<uint32_t>(off & 15ull);
-                pb[q] = pa[q] + rb[q];
-            }
-            if (gated) {
-                const MemberArgs& m1 = a.member[1];
+                const uint64_t off0 = RowStreams<F>::base(q, m0.blocks) +
+                                      static_cast<uint64_t>(m0.first_row + bt.local) * rb[q];
+                const uint8_t* s0 = stage + reg[q] + static_cast<uint32_t>(off0 & 15ull);
+                if (!gated) {
 #pragma unroll
-                for (int q = 0; q < F::kStreams; ++q) {
-                    const uint64_t off = RowStreams<F>::base(q, m1.blocks) +
-                                         static_cast<uint64_t>(m1.first_row + bt.local) * rb[q];
-                    pb[q] = stage + reg[q] + sl[q] + static_cast<uint32_t>(off & 15ull);
+                    for (int r = 0; r < RP; ++r) {
+                        pa[r][q] = s0 + (2u * r) * rb[q];
+                        pb[r][q] = s0 + (2u * r + 1u) * rb[q];
+                    }
+                } else {
+                    const uint64_t off1 = RowStreams<F>::base(q, m1.blocks) +
+                                          static_cast<uint64_t>(m1.first_row + bt.local) * rb[q];
+                    const uint8_t* s1 = stage + reg[q] + (R / 2) * sl[q] + static_cast<uint32_t>(off1 & 15ull);
+                    if (R == 2) {
+                        pa[0][q] = s0;
+                        pb[0][q] = s1;
+                    } else {
+                        pa[0][q] = s0;
+                        pb[0][q] = s0 + rb[q];
+                        pa[RP - 1][q] = s1;
+                        pb[RP - 1][q] = s1 + rb[q];
+                    }
                 }
             }
         }
         const bool la = bt.live > 0;
         const bool lb = gated ? la : bt.live > 1;
-        float2 aa[MT / 2], ab[MT / 2];
+        float2 aa[RP][MT / 2], ab[RP][MT / 2];
 #pragma unroll
-        for (int p = 0; p < MT / 2; ++p) { aa[p] = make_float2(0.0f, 0.0f); ab[p] = make_float2(0.0f, 0.0f); }
+        for (int r = 0; r < RP; ++r)
+#pragma unroll
+            for (int p = 0; p < MT / 2; ++p) { aa[r][p] = make_float2(0.0f, 0.0f); ab[r][p] = make_float2(0.0f, 0.0f); }
         for (uint32_t g = lo; g < hi; ++g) {
-            F A, B;
-            if (la) A.load(pa, g); else A.zero();
-            if (lb) B.load(pb, g); else B.zero();
-            chain_group_mt<F, MT>(A, B, xl + (g - lo) * 16u, pair4, aa, ab, std::make_integer_sequence<int, 32>{});
+            F A[RP], B[RP];
+            if (R == 2) {
+                if (la) A[0].load(pa[0], g); else A[0].zero();
+                if (lb) B[0].load(pb[0], g); else B[0].zero();
+            } else {
+                // Slots past the live rows read stale stage bytes; their sums
+                // are never written.
+#pragma unroll
+                for (int r = 0; r < RP; ++r) {
+                    A[r].load(pa[r], g);
+                    B[r].load(pb[r], g);
+                }
+            }
+            chain_group_mt<F, MT, RP>(A, B, xl + (g - lo) * 16u, pair4, aa, ab, std::make_integer_sequence<int, 32>{});
         }
 #pragma unroll
-        for (int p = 0; p < MT / 2; ++p) {
-            red[(2 * p) * kRedStride + lane] = aa[p].x;
-            red[(2 * p + 1) * kRedStride + lane] = aa[p].y;
-            red[(MT + 2 * p) * kRedStride + lane] = ab[p].x;
-            red[(MT + 2 * p + 1) * kRedStride + lane] = ab[p].y;
-        }
+        for (int r = 0; r < RP; ++r)
+#pragma unroll
+            for (int p = 0; p < MT / 2; ++p) {
+                red[((2 * r) * MT + 2 * p) * kRedStride + lane] = aa[r][p].x;
+                red[((2 * r) * MT + 2 * p + 1) * kRedStride + lane] = aa[r][p].y;
+                red[((2 * r + 1) * MT + 2 * p) * kRedStride + lane] = ab[r][p].x;
+                red[((2 * r + 1) * MT + 2 * p + 1) * kRedStride + lane] = ab[r][p].y;
+            }
         fence_proxy_async();
         __syncwarp();
         if (b + 2u * stride < batches) issue_batch<F, R>(a, b + 2u * stride, stage, &bars[s], G, lane);
@@ -547,12 +627,12 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
         const uint32_t slot = lane / MT, ti = lane % MT;
         const uint32_t t = t0 + ti;
         if (gated) {
-            const float up = __shfl_down_sync(0xFFFFFFFFu, total, MT);
-            if (slot == 0 && ti < nt && bt.live > 0) {
-                const uint32_t o = a.member[0].out_offset + bt.local;
+            const float up = __shfl_down_sync(0xFFFFFFFFu, total, (R / 2) * MT);
+            if (slot < static_cast<uint32_t>(R / 2) && slot < bt.live && ti < nt) {
+                const uint32_t o = a.member[0].out_offset + bt.local + slot;
                 a.out[0][static_cast<size_t>(t) * a.out_stride[0] + o] = activate(a.activation, total) * up;
             }
-        } else if (slot < min(bt.live, 2u) && lane < static_cast<uint32_t>(R * MT) && ti < nt) {
+        } else if (slot < min(bt.live, static_cast<uint32_t>(R)) && lane < static_cast<uint32_t>(R * MT) && ti < nt) {
             const MemberArgs& m = a.member[bt.member];
             const uint32_t o = m.out_offset + bt.local + slot;
             if (a.epilogue == kWrite) {
@@ -569,20 +649,21 @@ __global__ void __launch_bounds__(W * 32) decode_mt_kernel(const MatmulArgs a) {
     }
 }
 
-template <typename F, int MT, int W = kWarps>
+template <typename F, int MT, int W = kWarps, int R = 2>
 size_t decode_mt_smem(uint32_t G) {
     return static_cast<size_t>(MT / 2) * 32u * x2_lane_stride(G) * 4u +
-           W * (16u + 2u * MT * kRedStride * 4u + 2ull * 2u * RowStreams<F>::row_stage(G));
+           W * (16u + static_cast<size_t>(R) * MT * kRedStride * 4u + 2ull * R * RowStreams<F>::row_stage(G));
 }
 
-template <typename F, int MT, int W>
+template <typename F, int MT, int W, int R>
 cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    const size_t smem = decode_mt_smem<F, MT, W>(G);
+    const size_t smem = decode_mt_smem<F, MT, W, R>(G);
     if (smem > static_cast<size_t>(kMaxDecodeSmem)) return cudaErrorInvalidValue;
-    const uint32_t batches = a.epilogue == kGated ? a.member[0].rows
-                                                  : [&] { uint32_t n = 0; for (uint32_t m = 0; m < a.members; ++m) n += (a.member[m].rows + 1) / 2; return n; }();
-    auto kernel = decode_mt_kernel<F, MT, W>;
+    uint32_t batches = 0;
+    if (a.epilogue == kGated) batches = (a.member[0].rows + R / 2 - 1) / (R / 2);
+    else for (uint32_t m = 0; m < a.members; ++m) batches += (a.member[m].rows + R - 1) / R;
+    auto kernel = decode_mt_kernel<F, MT, W, R>;
     static bool configured = false;   // per instantiation
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDecodeSmem);
@@ -626,13 +707,33 @@ cudaError_t launch_decode_mt(const MatmulArgs& a, int sm_count, cudaStream_t str
 // 16 for longer ones — stepping down while x of that many tokens and the
 // stages do not fit shared memory (wide rows).
 // Eight warps a CTA where they fit (x is staged once a CTA, so more warps
-// share it), else four.
-template <typename F, int MT>
+// share it), else four. Up to 8 tokens a pass, batches of two pairs of rows
+// (each read of x serves both pairs) for the formats whose decoded state
+// fits registers for both (kRowsTogether).
+template <typename F, int MT, int R>
 cudaError_t launch_mt_warps(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
     const uint32_t G = a.columns / 32u;
-    if (decode_mt_smem<F, MT, 8>(G) <= static_cast<size_t>(kMaxDecodeSmem))
-        return launch_decode_mt<F, MT, 8>(a, sm_count, stream, pdl);
-    return launch_decode_mt<F, MT, 4>(a, sm_count, stream, pdl);
+    if (decode_mt_smem<F, MT, 8, R>(G) <= static_cast<size_t>(kMaxDecodeSmem))
+        return launch_decode_mt<F, MT, 8, R>(a, sm_count, stream, pdl);
+    return launch_decode_mt<F, MT, 4, R>(a, sm_count, stream, pdl);
+}
+
+// Two pairs a batch halve the batches (and the CTAs of a product that fills
+// less than a wave) and raise the registers a thread, so they are taken
+// where the product is large enough to keep every SM busy either way
+// (measured on Gemma-3-1B and Qwen3-0.6B shapes at 2-16 tokens, B200): the
+// vocabulary heads at any token count, products of 2,048 slots or more at 8
+// tokens, non-gated ones of 4,096 rows or more at 2-4 tokens.
+template <typename F, int MT>
+cudaError_t launch_mt_rows(const MatmulArgs& a, int sm_count, cudaStream_t stream, bool pdl) {
+    constexpr bool two_pairs = MT <= 8 && kRowsTogether<F, 4>;
+    const bool gated = a.epilogue == kGated;
+    const uint64_t slots = gated ? 2ull * a.member[0].rows : a.total_rows;
+    const bool large = slots >= 65536u || (MT == 8 && slots >= 2048u) || (MT <= 4 && !gated && slots >= 4096u);
+    if (two_pairs && large &&
+        decode_mt_smem<F, MT, 4, two_pairs ? 4 : 2>(a.columns / 32u) <= static_cast<size_t>(kMaxDecodeSmem))
+        return launch_mt_warps<F, MT, two_pairs ? 4 : 2>(a, sm_count, stream, pdl);
+    return launch_mt_warps<F, MT, 2>(a, sm_count, stream, pdl);
 }
 
 template <typename F>
@@ -640,10 +741,10 @@ cudaError_t dispatch_mt(const MatmulArgs& a, int sm_count, cudaStream_t stream, 
     const uint32_t G = a.columns / 32u;
     const size_t budget = static_cast<size_t>(kMaxDecodeSmem);
     const uint32_t want = a.tokens > 8 ? 16u : (a.tokens > 4 ? 8u : (a.tokens > 2 ? 4u : 2u));
-    if (want >= 16 && decode_mt_smem<F, 16>(G) <= budget) return launch_mt_warps<F, 16>(a, sm_count, stream, pdl);
-    if (want >= 8 && decode_mt_smem<F, 8>(G) <= budget) return launch_mt_warps<F, 8>(a, sm_count, stream, pdl);
-    if (want >= 4 && decode_mt_smem<F, 4>(G) <= budget) return launch_mt_warps<F, 4>(a, sm_count, stream, pdl);
-    if (decode_mt_smem<F, 2>(G) <= budget) return launch_mt_warps<F, 2>(a, sm_count, stream, pdl);
+    if (want >= 16 && decode_mt_smem<F, 16>(G) <= budget) return launch_mt_rows<F, 16>(a, sm_count, stream, pdl);
+    if (want >= 8 && decode_mt_smem<F, 8>(G) <= budget) return launch_mt_rows<F, 8>(a, sm_count, stream, pdl);
+    if (want >= 4 && decode_mt_smem<F, 4>(G) <= budget) return launch_mt_rows<F, 4>(a, sm_count, stream, pdl);
+    if (decode_mt_smem<F, 2>(G) <= budget) return launch_mt_rows<F, 2>(a, sm_count, stream, pdl);
     return cudaErrorInvalidValue;
 }
 
