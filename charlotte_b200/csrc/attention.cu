@@ -195,14 +195,63 @@ __device__ __forceinline__ void fold_chunks(uint32_t Q, float* fac, float* lfac,
         // in groups of the CTA's threads.
         factors(lo);
         __syncthreads();
+        // A thread's outputs (threadIdx.x + 256·j) share the dimension e
+        // (the CTA's threads are a whole number of D). With more than one,
+        // four at a time run their chains together, chunk by chunk in order,
+        // each over its own query's chunks, four chunks' partials of each
+        // loaded before their fmas — the operations of `chain`, interleaved.
+        static_assert(kAttnThreads % D == 0, "a thread's outputs share one dimension");
+        constexpr uint32_t kStep = kAttnThreads / D;   // queries between a thread's outputs
+        if (Q <= kStep) {
+            const uint32_t m = threadIdx.x / D, e = threadIdx.x % D;
+            if (m < Q) {
+                uint32_t c0, c1;
+                range_of(m, &c0, &c1);
+                float o = 0.0f, l = 0.0f;
+                chain(lo, m, e, c0, c1, o, l);
+                write(m, e, o / l);
+            }
+            return;
+        }
+        const uint32_t e = threadIdx.x % D;
 #pragma unroll 1
-        for (uint32_t i = threadIdx.x; i < Q * D; i += kAttnThreads) {
-            const uint32_t m = i / D, e = i % D;
-            uint32_t c0, c1;
-            range_of(m, &c0, &c1);
-            float o = 0.0f, l = 0.0f;
-            chain(lo, m, e, c0, c1, o, l);
-            write(m, e, o / l);
+        for (uint32_t mb = threadIdx.x / D; mb < Q; mb += 4u * kStep) {
+            uint32_t c0[4], c1[4];
+            float o[4], l[4];
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; ++j) {
+                c0[j] = 1u;
+                c1[j] = 0u;   // no chunks: past the CTA's queries
+                if (mb + j * kStep < Q) range_of(mb + j * kStep, &c0[j], &c1[j]);
+                o[j] = 0.0f;
+                l[j] = 0.0f;
+            }
+#pragma unroll 1
+            for (uint32_t c = lo; c <= hi; c += 4u) {
+                float co[4][4];
+#pragma unroll
+                for (uint32_t j = 0; j < 4u; ++j)
+#pragma unroll
+                    for (uint32_t k = 0; k < 4u; ++k) {
+                        const uint32_t cc = c + k;
+                        co[j][k] = cc >= c0[j] && cc <= c1[j] ? part_of(cc, mb + j * kStep, e) : 0.0f;
+                    }
+#pragma unroll
+                for (uint32_t k = 0; k < 4u; ++k)
+#pragma unroll
+                    for (uint32_t j = 0; j < 4u; ++j) {
+                        const uint32_t cc = c + k;
+                        if (cc >= c0[j] && cc <= c1[j]) {
+                            const uint32_t f = (mb + j * kStep) * 32u + (cc - lo);
+                            const float fa = fac[2u * f];
+                            o[j] = fmaf(o[j], fa, co[j][k] * fac[2u * f + 1u]);
+                            l[j] = fmaf(l[j], fa, lfac[f]);
+                        }
+                    }
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; ++j)
+                if (mb + j * kStep < Q) write(mb + j * kStep, e, o[j] / l[j]);
         }
         return;
     }
@@ -253,6 +302,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     // (by the host, or by the last step's closing launch), so it is read
     // before the dependency wait, as are the keys of earlier steps.
     const uint32_t pos0 = a.position ? *a.position : a.position0;
+    // The fused rope's turn (and llama3 factor) of this thread's angle (d/2
+    // angles, one a thread), loaded beside the position so the two loads
+    // share one round trip.
+    static_assert(D / 2u <= kAttnThreads, "one angle a thread");
+    const bool angle_thread = fused && threadIdx.x < D / 2u;
+    const float turn_k = angle_thread ? __ldg(r.turns + threadIdx.x) : 0.0f;
+    const float factor_k = angle_thread && r.factors ? __ldg(r.factors + threadIdx.x) : 1.0f;
     const uint32_t row0 = rt * geo.rows_per_tile;
     const uint32_t rows = min(geo.rows_per_tile, a.tokens - row0);
     const uint32_t Q = rows * G;
@@ -306,7 +362,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
     // position a tile), into the score buffer, free until the scores.
     float* cosines = ps;
     float* sines = ps + d / 2u;
-    if (fused && working) rope_angles(p_first, r.turns, r.factors, d, cosines, sines, threadIdx.x, kAttnThreads);
+    if (working && angle_thread)
+        rope_angle(p_first, turn_k, factor_k, r.factors != nullptr, &cosines[threadIdx.x], &sines[threadIdx.x]);
     grid_dependency_wait();
 
     // The fused rope: G query heads (and, in the CTA whose chunks hold the
@@ -485,34 +542,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
         }
         __syncthreads();
         // O = O·a_t, then fma(p_b, v_b, O) in key order; the chunk's partial.
-        for (uint32_t i = threadIdx.x; i < Q * d; i += kAttnThreads) {
-            const uint32_t m = i / d, e = i % d;
-            float o = 0.0f;
-            // A key of weight 0 (not live for this query) adds exactly
-            // nothing — fma(0, v, o) = o for the finite values the cache
-            // holds — so the loop needs no test; keys past p_last, never
-            // staged, are left out.
-            const uint32_t valid = min(kChunk, p_last + 1u - key0);
-            // Eight keys at a time (every tile is a whole number of eights):
-            // at a tile's first key O·a_t, then the keys' fmas in key order
-            // — their weights (two 16-byte reads) and values loaded first,
-            // unconditionally (every row of the stage is in bounds), keys
-            // from `valid` on (never staged) skipped.
-#pragma unroll 2
-            for (uint32_t b0 = 0; b0 < kChunk; b0 += 8u) {
-                const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
-                const float4 pa = p4[0], pb = p4[1];
-                const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-                float vv[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
-                if (b0 % B == 0) o = o * alpha[m * 8u + b0 / B];
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    if (b0 + k < valid) o = fmaf(pw[k], vv[k], o);
-            }
+        // A key of weight 0 (not live for this query) adds exactly nothing —
+        // fma(0, v, o) = o for the finite values the cache holds — so the
+        // loop needs no test; keys past p_last, never staged, are left out.
+        const uint32_t valid = min(kChunk, p_last + 1u - key0);
+        // Output (m, e) into rank 0's slot for this CTA's chunk (slot =
+        // rank), or to the partials in global memory.
+        auto put = [&](uint32_t m, uint32_t e, float o) {
             if (cluster_fold) {
-                // Into rank 0's slot for this CTA's chunk (slot = rank).
                 const uint32_t slot = blockIdx.y;
                 st_cluster_f32(cluster_map(fold_part + (slot * G + m) * d + e, 0u), o);
                 if (e == 0) {
@@ -527,6 +564,63 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttentionArgs a
                     a.stats[at * 2u] = stat[m * 4u];
                     a.stats[at * 2u + 1u] = stat[m * 4u + 1u];
                 }
+            }
+        };
+        if (Q * d <= kAttnThreads) {
+            // One output a thread.
+            const uint32_t m = threadIdx.x / d, e = threadIdx.x % d;
+            if (m < Q) {
+                float o = 0.0f;
+                // Eight keys at a time (every tile is a whole number of
+                // eights): at a tile's first key O·a_t, then the keys' fmas
+                // in key order — their weights (two 16-byte reads) and values
+                // loaded first, unconditionally (every row of the stage is in
+                // bounds), keys from `valid` on (never staged) skipped.
+#pragma unroll 2
+                for (uint32_t b0 = 0; b0 < kChunk; b0 += 8u) {
+                    const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
+                    const float4 pa = p4[0], pb = p4[1];
+                    const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                    float vv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
+                    if (b0 % B == 0) o = o * alpha[m * 8u + b0 / B];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (b0 + k < valid) o = fmaf(pw[k], vv[k], o);
+                }
+                put(m, e, o);
+            }
+        } else {
+            // A thread's outputs share the dimension e (the CTA's threads are
+            // a whole number of d): four at a time, each value loaded once
+            // for all four, their chains — independent — advancing together.
+            constexpr uint32_t kStep = kAttnThreads / D;
+            const uint32_t e = threadIdx.x % d;
+#pragma unroll 1
+            for (uint32_t mb = threadIdx.x / d; mb < Q; mb += 4u * kStep) {
+                float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+                for (uint32_t b0 = 0; b0 < kChunk; b0 += 8u) {
+                    float vv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) vv[k] = fp16_bits_to_f32(vs[(b0 + k) * pitch + e]);
+#pragma unroll
+                    for (uint32_t j = 0; j < 4u; ++j) {
+                        // Queries past the CTA's last read its row (results discarded).
+                        const uint32_t m = min(mb + j * kStep, Q - 1u);
+                        const float4* p4 = reinterpret_cast<const float4*>(ps + m * kChunk + b0);
+                        const float4 pa = p4[0], pb = p4[1];
+                        const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                        if (b0 % B == 0) o[j] = o[j] * alpha[m * 8u + b0 / B];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k)
+                            if (b0 + k < valid) o[j] = fmaf(pw[k], vv[k], o[j]);
+                    }
+                }
+#pragma unroll
+                for (uint32_t j = 0; j < 4u; ++j)
+                    if (mb + j * kStep < Q) put(mb + j * kStep, e, o[j]);
             }
         }
     }

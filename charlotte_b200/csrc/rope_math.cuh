@@ -14,14 +14,19 @@ namespace cb {
 // The token's angle table for position p: t = p·turn_k (then t/factor_k
 // with llama3 factors), angle = 2π·(t − round_even(t)), and its sine and
 // cosine (Cody–Waite/Taylor, numerics.cuh); entries k = first, first+step, ...
+// Entry k from its turn and factor (factor used only when `scaled`).
+__device__ __forceinline__ void rope_angle(uint32_t p, float turn, float factor, bool scaled, float* cosine,
+                                           float* sine) {
+    float t = static_cast<float>(p) * turn;
+    if (scaled) t = t / factor;
+    const float angle = 6.283185307179586f * (t - rintf(t));
+    sincos_turn(angle, sine, cosine);
+}
+
 __device__ __forceinline__ void rope_angles(uint32_t p, const float* turns, const float* factors, uint32_t d,
                                             float* cosines, float* sines, uint32_t first, uint32_t step) {
-    for (uint32_t k = first; k < d / 2u; k += step) {
-        float t = static_cast<float>(p) * turns[k];
-        if (factors) t = t / factors[k];
-        const float angle = 6.283185307179586f * (t - rintf(t));
-        sincos_turn(angle, &sines[k], &cosines[k]);
-    }
+    for (uint32_t k = first; k < d / 2u; k += step)
+        rope_angle(p, turns[k], factors ? factors[k] : 1.0f, factors != nullptr, &cosines[k], &sines[k]);
 }
 
 // One head held by `lanes` = d/8 threads, lane i holding vec4s i and
