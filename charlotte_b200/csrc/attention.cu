@@ -697,7 +697,7 @@ namespace {
 
 template <uint32_t D>
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl, size_t base_smem,
-                             size_t cluster_smem, bool decode_shape) {
+                             size_t cluster_smem, bool decode_shape, uint32_t slots) {
     auto kernel = attention_kernel<D>;
     const Geometry geo = geometry_of(a.query_heads, a.kv_heads, a.rows_are_sequences != 0);
     static bool configured = false;
@@ -708,7 +708,6 @@ cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool p
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    const uint32_t slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.kv_heads, slots, (a.tokens + geo.rows_per_tile - 1) / geo.rows_per_tile);
     cfg.blockDim = dim3(kAttnThreads);
@@ -716,25 +715,29 @@ cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool p
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-    // A (kv head, row tile)'s chunk CTAs as one cluster, when a cluster of
-    // that many CTAs can be resident at this shared-memory size (asked of
-    // the occupancy calculator once a size).
-    static int cluster_fits[kChunkSlots + 1] = {};   // 0 unknown, 1 yes, -1 no
+    // A (kv head, row tile)'s chunk CTAs as one cluster, when every one of
+    // the launch's clusters can be resident at once at this shared-memory
+    // size (the occupancy calculator asked once a cluster size): clusters
+    // past that would wait for a whole cluster to finish, doubling the
+    // launch (measured: 8 clusters of 16 CTAs at head dimension 256, one
+    // of them a second wave).
+    static int cluster_room[kChunkSlots + 1] = {};   // 0 unknown, else 1 + the clusters resident at once
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
     attr[1].val.clusterDim.y = slots;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     const bool can_cluster = decode_shape && slots > 1 && cluster_smem <= 200u * 1024u;
-    if (can_cluster && cluster_fits[slots] == 0) {
+    if (can_cluster && cluster_room[slots] == 0) {
         cfg.numAttrs = 2;
         cfg.dynamicSmemBytes = cluster_smem;
         int clusters = 0;
         const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);   // any arguments
         if (e != cudaSuccess) cudaGetLastError();
-        cluster_fits[slots] = e == cudaSuccess && clusters >= 1 ? 1 : -1;
+        cluster_room[slots] = 1 + (e == cudaSuccess && clusters > 0 ? clusters : 0);
     }
-    const bool cluster = can_cluster && cluster_fits[slots] > 0;
+    const uint64_t clusters_needed = static_cast<uint64_t>(cfg.gridDim.x) * cfg.gridDim.z;
+    const bool cluster = can_cluster && static_cast<uint64_t>(cluster_room[slots] - 1) >= clusters_needed;
     cfg.numAttrs = cluster ? 2 : 1;
     cfg.dynamicSmemBytes = cluster ? cluster_smem : base_smem;
     RopeArgs r{};
@@ -765,15 +768,21 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     // step past that would fold globally inside a cluster launch, slower).
     // Larger batches keep the global fold: the fold room would halve the
     // CTAs an SM holds across their many row tiles.
-    const uint32_t slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
+    // Decode shapes on a sliding-window layer take only as many chunk slots
+    // as the window's keys can span (a 512-key window: 9), so a cluster holds
+    // no CTA that can never have a chunk.
+    const uint32_t all_slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
+    const uint32_t window_chunks = a.window / kChunk + 1u + (a.window % kChunk ? 1u : 0u);
+    const uint32_t slots = window_chunks < all_slots ? window_chunks : all_slots;
     const int sms = sm_count();
     const bool decode_shape =
         a.tokens == 1u || (a.rows_are_sequences && sms > 0 && a.window / kChunk + 1u <= slots &&
                            static_cast<uint64_t>(a.kv_heads) * slots * a.tokens <= static_cast<uint64_t>(sms));
+    const uint32_t launch_slots = decode_shape ? slots : all_slots;
     const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
-    return a.head_dim == 64 ? launch_attention<64>(a, stream, pdl, base_smem, cluster_smem, decode_shape)
-           : a.head_dim == 128 ? launch_attention<128>(a, stream, pdl, base_smem, cluster_smem, decode_shape)
-                               : launch_attention<256>(a, stream, pdl, base_smem, cluster_smem, decode_shape);
+    return a.head_dim == 64 ? launch_attention<64>(a, stream, pdl, base_smem, cluster_smem, decode_shape, launch_slots)
+           : a.head_dim == 128 ? launch_attention<128>(a, stream, pdl, base_smem, cluster_smem, decode_shape, launch_slots)
+                               : launch_attention<256>(a, stream, pdl, base_smem, cluster_smem, decode_shape, launch_slots);
 }
 
 }  // namespace cb
