@@ -73,21 +73,23 @@ def test_batch_step_from_host_ids(cuda):
         dec.close()
 
 
-def test_gemma_3_1b_batch_of_64_rows_match_sequences_alone(cuda):
+@pytest.mark.parametrize("S,rows", [(64, (0, 21, 42, 63)), (8, (0, 3, 7))])
+def test_gemma_3_1b_batch_rows_match_sequences_alone(cuda, S, rows):
     """configs[4]'s shape at full size: 64 sequences batched (each with its
     own caches, a windowed layer's ring of 512 + 64 slots wrapping over the
-    620 positions), 8 batched greedy steps; rows 0, 21, 42 and 63 give the
-    tokens and logits of their sequences decoded alone (themselves bit-exact
-    with the oracle at full size)."""
+    620 positions), 8 batched greedy steps; the given rows give the tokens
+    and logits of their sequences decoded alone (themselves bit-exact with
+    the oracle at full size). 8 sequences (one GPU's share at N = 8) take the
+    streamed products with two row pairs a batch and the windowed layers'
+    attention over clusters of 9 chunk CTAs."""
     m = M.synthesize(M.gemma_3_1b(context=1024), seed=23)
     rng = np.random.default_rng(9)
-    S, P, steps = 64, 612, 8
+    P, steps = 612, 8
     prompts = [rng.integers(0, m.arch.vocab, P).astype(np.uint32) for _ in range(S)]
     bd = M.BatchDecoder(m, S, max_step_tokens=64)
     firsts = [int(bd.prefill_sequence(s, p)[0]) for s, p in enumerate(prompts)]
     toks, failed = bd.generate(steps)
     assert not failed.any()
-    rows = (0, 21, 42, 63)
     last = {r: bd.logits_row(r) for r in rows}
     bd.close()
     for r in rows:

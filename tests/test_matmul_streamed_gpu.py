@@ -51,6 +51,10 @@ CASES = [
     (O.Q6_K, 300, 2048, 64),
     (O.Q4_1, 1024, 3072, 5),
     (O.BF16, 333, 1024, 40),
+    # two row pairs a batch (large products), the last batch one row live
+    (O.Q4_0, 4097, 1024, 3),
+    (O.Q8_0, 2049, 1152, 8),
+    (O.Q6_K, 65537, 256, 2),
 ]
 
 
@@ -94,10 +98,12 @@ def test_streamed_qkv(cuda):
 
 
 @pytest.mark.parametrize("activation", [cb.SILU, cb.GELU_TANH])
-@pytest.mark.parametrize("T", [3, 16, 21])
-def test_streamed_gated(cuda, activation, T):
+@pytest.mark.parametrize("T,F", [(3, 3072), (7, 3072), (8, 2049), (16, 3072), (21, 3072)])
+def test_streamed_gated(cuda, activation, T, F):
+    """T = 7, 8 at 2,048+ slots: batches of two outputs' gate rows then their up
+    rows (F = 2,049: the last batch one output live)."""
     rng = np.random.default_rng(T + activation)
-    F, K = 3072, 1024
+    K = 1024
     gs, gp, gnb = weight(rng, O.Q4_0, F, K)
     us, up, unb = weight(rng, O.Q4_0, F, K)
     x = synth.activations(rng, T, K) * 4
