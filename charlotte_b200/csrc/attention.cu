@@ -770,7 +770,7 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     // CTAs an SM holds across their many row tiles.
     // Decode shapes on a sliding-window layer take only as many chunk slots
     // as the window's keys can span (a 512-key window: 9), so a cluster holds
-    // no CTA that can never have a chunk.
+    // no CTA that can never have a chunk, and a launch no CTA that only leaves.
     const uint32_t all_slots = a.max_chunks < kChunkSlots ? a.max_chunks : kChunkSlots;
     const uint32_t window_chunks = a.window / kChunk + 1u + (a.window % kChunk ? 1u : 0u);
     const uint32_t slots = window_chunks < all_slots ? window_chunks : all_slots;
@@ -778,7 +778,10 @@ cudaError_t attention_run(const AttentionArgs& a, cudaStream_t stream, bool pdl)
     const bool decode_shape =
         a.tokens == 1u || (a.rows_are_sequences && sms > 0 && a.window / kChunk + 1u <= slots &&
                            static_cast<uint64_t>(a.kv_heads) * slots * a.tokens <= static_cast<uint64_t>(sms));
-    const uint32_t launch_slots = decode_shape ? slots : all_slots;
+    // Batched sequences keep the window's slots in the global fold too (a
+    // row a tile: its live chunks never span more); tiles of several rows
+    // take every slot.
+    const uint32_t launch_slots = decode_shape || a.rows_are_sequences ? slots : all_slots;
     const size_t cluster_smem = base_smem + cluster_fold_floats(a.head_dim, geo.G) * 4u;
     return a.head_dim == 64 ? launch_attention<64>(a, stream, pdl, base_smem, cluster_smem, decode_shape, launch_slots)
            : a.head_dim == 128 ? launch_attention<128>(a, stream, pdl, base_smem, cluster_smem, decode_shape, launch_slots)
