@@ -30,7 +30,9 @@
 //  - Rows are worked two at a time: one paired fma (fma.rn.f32x2, two fmas
 //    each rounded once) decodes a weight of each row exactly (formats.cuh),
 //    one accumulates both, with x held doubled ((x_k, x_k)) in shared memory
-//    as the pair's operand.
+//    as the pair's operand. In batches of four or more rows the pairs'
+//    chains advance together, k outermost: one read of x serves every pair
+//    (chain_group_rows).
 //  - Batches never straddle members, so a batch's rows come in one bulk copy
 //    per stream (two for a gated batch: its gate rows and its up rows).
 //  - x is staged once per CTA in shared memory range-major, a 16-byte skew
